@@ -1,0 +1,408 @@
+// GQA flash-decode attention over a paged fp16 KV cache.
+//
+// Replaces the attention inside candle-transformers 0.8.4 quantized_llama
+// (q.k^T / sqrt(hd) -> softmax_last_dim -> .v over an f32 KV cache that grows
+// by concatenation; called from crates/ferrite-wasm-host/src/adapter.rs:
+// 61-70) and the reference's own stub kernel
+// crates/ferrite-core/kernels/flash_attention.cu:166-225 (f32, hd <= 64,
+// never launched).
+//
+// B200 design (HBM-bound: 2 * ctx * n_kv * hd * 2 bytes per layer and token):
+//  * split-K: CTA (kv head, split of 2 pages, sequence); every CTA of the
+//    grid issues its K and V page copies at once with cp.async.bulk (TMA,
+//    one 16 KB copy per page, no multicast) onto per-page mbarriers, so each
+//    SM keeps >64 KB in flight;
+//  * the G = n_heads / n_kv query heads of the kv head share each K/V row
+//    read from shared memory;
+//  * scores: lane owns 4 dims of hd, a 32-value butterfly reduce-scatter
+//    turns (32/G tokens x G heads) per-lane partials into one full dot per
+//    lane (31 shuffles per 32 dots);
+//  * partial (max, sum, o) per split go to a scratch buffer; a combine kernel
+//    merges the splits (log-sum-exp) and, fused into the model path,
+//    quantizes the result to Q8_K for the output projection.
+// All mbarrier waits are bounded: on timeout the kernel raises
+// ERRBIT_WAIT_TIMEOUT in the context's error word and returns.
+#include <math.h>
+
+#include "fb_internal.h"
+#include "kq_common.cuh"
+
+namespace fb {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (~1 s of SM clock).  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > 2000000000LL) return false;
+    }
+    return true;
+}
+
+constexpr int ATT_HD = 128;
+constexpr int ATT_WARPS = 4;
+
+__device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
+    return A.seq_lens ? A.seq_lens[b] : A.pos[b] + 1;
+}
+
+// Dynamic shared memory: K[2*page][hd] half, V[2*page][hd] half,
+// q[G][hd] f32, s[G][2*page] f32, red[ATT_WARPS][G][hd] f32.
+template <int G>
+__global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[4];  // K page 0, K page 1, V page 0, V page 1
+    const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P = A.page_size, ST = 2 * P;
+    pdl_wait();
+    const int len = seq_len_of(A, b);
+    const int t0 = split * ST;
+    if (t0 >= len) {
+        pdl_launch();
+        return;
+    }
+    const int ntok = min(ST, len - t0);
+    __half *Ks = reinterpret_cast<__half *>(smem);
+    __half *Vs = Ks + (size_t)ST * ATT_HD;
+    float *qs = reinterpret_cast<float *>(Vs + (size_t)ST * ATT_HD);
+    float *ss = qs + G * ATT_HD;
+    float *red = ss + G * ST;
+    const uint32_t page_bytes = (uint32_t)P * ATT_HD * 2;
+    const int npages = (ntok + P - 1) / P;  // 1 or 2
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 4; i++) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    bool ok_pages = true;
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < npages; j++) {
+            const int lp = t0 / P + j;
+            int page = lp < A.max_pages ? A.block_table[(int64_t)b * A.max_pages + lp] : -1;
+            if (page < 0 || page >= A.num_pages) {
+                atomicOr(A.err, ERRBIT_BAD_PAGE);
+                page = -1;
+            }
+            if (page >= 0) {
+                const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
+                mbar_expect_tx(&bars[j], page_bytes);
+                bulk_g2s(Ks + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes, &bars[j]);
+                mbar_expect_tx(&bars[2 + j], page_bytes);
+                bulk_g2s(Vs + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes, &bars[2 + j]);
+            } else {
+                // complete the phases without data; the page reads as zero
+                mbar_expect_tx(&bars[j], 0);
+                mbar_expect_tx(&bars[2 + j], 0);
+                ok_pages = false;
+            }
+        }
+    }
+    // q of the G heads of this kv head (already RoPE'd)
+    const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
+    for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) qs[i] = qg[i];
+    __syncthreads();
+    (void)ok_pages;
+
+    // ---- scores: warp w handles tokens [32w, 32w+32) of the split
+    constexpr int TCH = 32 / G;  // tokens per reduce-scatter chunk
+    const int tw0 = warp * 32;
+    bool waited_ok = true;
+    if (tw0 < ntok) {
+        waited_ok = mbar_wait_bounded(&bars[tw0 / P], 0);
+        float qv[G][4];
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) qv[g][e] = qs[g * ATT_HD + 4 * lane + e];
+#pragma unroll 1
+        for (int c = 0; c < G; c++) {
+            const int tc0 = tw0 + c * TCH;
+            float v[32];
+#pragma unroll
+            for (int t = 0; t < TCH; t++) {
+                const int tok = tc0 + t;
+                const uint2 kr = *reinterpret_cast<const uint2 *>(Ks + (size_t)tok * ATT_HD + 4 * lane);
+                const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
+                const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    float acc = qv[g][0] * k01.x;
+                    acc = fmaf(qv[g][1], k01.y, acc);
+                    acc = fmaf(qv[g][2], k23.x, acc);
+                    acc = fmaf(qv[g][3], k23.y, acc);
+                    v[t * G + g] = acc;
+                }
+            }
+            // butterfly reduce-scatter: lane l ends with the sum of index l
+#pragma unroll
+            for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+                const bool up = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < n / 2; i++) {
+                    const float send = up ? v[i] : v[i + n / 2];
+                    const float keep = up ? v[i + n / 2] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            const int t = lane / G, g = lane % G;
+            const int tok = tc0 + t;
+            ss[g * ST + tok] = tok < ntok ? v[0] * A.scale : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // ---- softmax statistics per head (one warp per head)
+    float *ml = red;  // reuse: [G][2] before the PV reduction
+    for (int g = warp; g < G; g += ATT_WARPS) {
+        float mx = -INFINITY;
+        for (int t = lane; t < ntok; t += 32) mx = fmaxf(mx, ss[g * ST + t]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float sum = 0.f;
+        for (int t = lane; t < ST; t += 32) {
+            const float p = t < ntok ? expf(ss[g * ST + t] - mx) : 0.f;
+            ss[g * ST + t] = p;
+            sum += p;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (lane == 0) {
+            ml[2 * g] = mx;
+            ml[2 * g + 1] = sum;
+        }
+    }
+    __syncthreads();
+    float mls[G][2];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mls[g][0] = ml[2 * g];
+        mls[g][1] = ml[2 * g + 1];
+    }
+    __syncthreads();
+    // ---- o = sum_t p_t * v_t; warp w over tokens [32w, 32w+32), lane owns 4 dims
+    float o[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[g][e] = 0.f;
+    if (tw0 < ntok) {
+        waited_ok = mbar_wait_bounded(&bars[2 + tw0 / P], 0) && waited_ok;
+        const int tend = min(tw0 + 32, ntok);
+        for (int tok = tw0; tok < tend; tok++) {
+            const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)tok * ATT_HD + 4 * lane);
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float p = ss[g * ST + tok];
+                o[g][0] = fmaf(p, v01.x, o[g][0]);
+                o[g][1] = fmaf(p, v01.y, o[g][1]);
+                o[g][2] = fmaf(p, v23.x, o[g][2]);
+                o[g][3] = fmaf(p, v23.y, o[g][3]);
+            }
+        }
+    }
+    if (!waited_ok) {
+        atomicOr(A.err, ERRBIT_WAIT_TIMEOUT);
+        // let any copy still in flight land before the CTA's shared memory
+        // is released (bounded as well)
+        for (int j = 0; j < 4; j++) mbar_wait_bounded(&bars[j], 0);
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) {
+        const int g = i / ATT_HD, d = i % ATT_HD;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < ATT_WARPS; w++) s += red[(w * G + g) * ATT_HD + d];
+        const int64_t hrow = ((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * A.nsplit_max + split;
+        A.part_o[hrow * ATT_HD + d] = s;
+        if (d == 0) {
+            A.part_ml[2 * hrow] = mls[g][0];
+            A.part_ml[2 * hrow + 1] = mls[g][1];
+        }
+    }
+    pdl_launch();
+}
+
+// Merge the splits of each head.  One CTA per (256-value block of the
+// [n_heads * hd] output row, sequence); out_q8 != null quantizes the block to
+// Q8_K (input of the output projection), out_f32 != null stores f32.
+__device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
+                                                   int64_t blk);
+
+__global__ void __launch_bounds__(256) k_attn_combine(AttnArgs A, float *__restrict__ out_f32, Q8Act aq,
+                                                      int use_q8) {
+    pdl_wait();
+    const int blk = blockIdx.x, b = blockIdx.y;
+    const int len = seq_len_of(A, b);
+    const int nsplit = (len + 2 * A.page_size - 1) / (2 * A.page_size);
+    const int tid = threadIdx.x;
+    const int i = blk * 256 + tid;  // value index in [n_heads * hd]
+    const int h = i / ATT_HD, d = i % ATT_HD;
+    const int64_t hbase = ((int64_t)b * A.n_heads + h) * A.nsplit_max;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; s++) M = fmaxf(M, A.part_ml[2 * (hbase + s)]);
+    float L = 0.f, acc = 0.f;
+    for (int s = 0; s < nsplit; s++) {
+        const float w = expf(A.part_ml[2 * (hbase + s)] - M);
+        L = fmaf(A.part_ml[2 * (hbase + s) + 1], w, L);
+        acc = fmaf(A.part_o[(hbase + s) * ATT_HD + d], w, acc);
+    }
+    const float val = acc / L;
+    if (out_f32) out_f32[(int64_t)b * A.n_heads * ATT_HD + i] = val;
+    if (use_q8) {
+        __shared__ float vals[256];
+        vals[tid] = val;
+        __syncthreads();
+        if (tid < 32) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = vals[8 * tid + e];
+            q8k_store_warp_ext(v, tid, aq, b, blk);
+        }
+    }
+    pdl_launch();
+}
+
+// (same arithmetic as the Q8_K store in ops.cu)
+__device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
+                                                   int64_t blk) {
+    float amax = 0.f, piv = 0.f;
+    int idx = 1 << 30;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const float av = fabsf(v[e]);
+        if (amax < av) {
+            amax = av;
+            piv = v[e];
+            idx = 8 * lane + e;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float op = __shfl_xor_sync(0xffffffffu, piv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            piv = op;
+            idx = oi;
+        }
+    }
+    uint32_t w0 = 0, w1 = 0;
+    int s = 0;
+    float d = 0.f;
+    if (amax != 0.f) {
+        const float iscale = __fdiv_rn(-128.f, piv);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            int q = (int)roundf(__fmul_rn(iscale, v[e]));
+            q = q > 127 ? 127 : q;
+            s += q;
+            if (e < 4) w0 |= ((uint32_t)(uint8_t)q) << (8 * e);
+            else w1 |= ((uint32_t)(uint8_t)q) << (8 * (e - 4));
+        }
+        d = __fdiv_rn(1.f, iscale);
+    }
+    const int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+    const int64_t k = a.k;
+    *reinterpret_cast<uint2 *>(a.qs + row * k + blk * QK + 64 * (lane & 3) + 8 * (lane >> 2)) = make_uint2(w0, w1);
+    if ((lane & 1) == 0) a.bs16[row * (k / 16) + blk * 16 + (lane >> 1)] = (int16_t)s16;
+    if ((lane & 3) == 0) a.bs32[row * (k / 32) + blk * 8 + (lane >> 2)] = (int16_t)s32;
+    if (lane == 0) a.d[row * (k / QK) + blk] = d;
+}
+
+size_t attn_smem_bytes(int G, int page_size) {
+    const int ST = 2 * page_size;
+    return (size_t)2 * ST * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * ST * 4 +
+           (size_t)ATT_WARPS * G * ATT_HD * 4;
+}
+
+template <typename K>
+static void launch_ex(fb_ctx *ctx, K kernel, dim3 grid, dim3 block, size_t smem, AttnArgs A) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, A));
+}
+
+// Split pass + combine.  out_f32 and/or (use_q8, aq) receive the result.
+void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A0, int batch, int max_seq_len, float *out_f32,
+                        const Q8Act *aq) {
+    AttnArgs A = A0;
+    const int G = A.n_heads / A.n_kv;
+    FB_REQUIRE(A.n_heads % A.n_kv == 0, "attn: n_heads must be a multiple of n_kv_heads");
+    FB_REQUIRE(A.page_size >= 16 && A.page_size <= 64 && A.page_size % 16 == 0,
+               "attn: page_size must be 16, 32, 48 or 64");
+    const int nsplit = (max_seq_len + 2 * A.page_size - 1) / (2 * A.page_size);
+    FB_REQUIRE(nsplit <= A.nsplit_max, "attn: max_seq_len exceeds the split scratch");
+    const size_t smem = attn_smem_bytes(G, A.page_size);
+    dim3 grid(A.n_kv, nsplit, batch);
+    switch (G) {
+#define FB_ATT_CASE(GG)                                                                                     \
+    case GG:                                                                                                \
+        FB_CUDA(cudaFuncSetAttribute(k_attn_split<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        launch_ex(ctx, k_attn_split<GG>, grid, dim3(ATT_WARPS * 32), smem, A);                              \
+        break;
+        FB_ATT_CASE(1)
+        FB_ATT_CASE(2)
+        FB_ATT_CASE(4)
+        FB_ATT_CASE(8)
+#undef FB_ATT_CASE
+    default:
+        fail(FB_ERR_INVALID, "attn: GQA group size must be 1, 2, 4 or 8");
+    }
+    FB_REQUIRE((A.n_heads * ATT_HD) % 256 == 0, "attn: n_heads * head_dim must be a multiple of 256");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    cfg.gridDim = dim3((A.n_heads * ATT_HD) / 256, batch);
+    cfg.blockDim = dim3(256);
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
+    FB_CUDA(cudaLaunchKernelEx(&cfg, k_attn_combine, A, out_f32, q, aq ? 1 : 0));
+}
+
+}  // namespace fb

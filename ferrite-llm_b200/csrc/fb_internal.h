@@ -1,0 +1,173 @@
+// Host-side internals shared by the C ABI, the kernels' launchers and the
+// model runtime.  Not part of the public interface.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/ferrite_b200.h"
+
+namespace fb {
+
+// Exception carrying a status code; caught at the C boundary.
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const std::string &msg);
+void set_last_error(const std::string &msg);
+
+// Runs f, converting exceptions into a status code + thread-local message.
+template <class F> int guarded(F &&f) {
+    try {
+        f();
+        return FB_OK;
+    } catch (const Error &e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        set_last_error("host allocation failed");
+        return FB_ERR_OOM;
+    } catch (const std::exception &e) {
+        set_last_error(e.what());
+        return FB_ERR_INVALID;
+    }
+}
+void check_cuda(cudaError_t e, const char *what, const char *file, int line);
+#define FB_CUDA(call) ::fb::check_cuda((call), #call, __FILE__, __LINE__)
+#define FB_REQUIRE(cond, msg)                                              \
+    do {                                                                   \
+        if (!(cond)) ::fb::fail(FB_ERR_INVALID, std::string(msg));         \
+    } while (0)
+
+// Device error-word bits (set by kernels, read by fb_ctx_error_word).
+enum : uint32_t {
+    ERRBIT_WAIT_TIMEOUT = 1u << 0,  // a bounded spin-wait gave up
+    ERRBIT_BAD_TOKEN = 1u << 1,     // token id outside [0, vocab)
+    ERRBIT_BAD_POS = 1u << 2,       // position outside the KV capacity
+    ERRBIT_BAD_PAGE = 1u << 3,      // block-table entry outside the pool
+};
+
+// A device buffer owned by the library.
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    ~DevBuf();
+    void alloc(size_t n);
+    void release();
+    template <class T> T *as() const { return reinterpret_cast<T *>(ptr); }
+};
+
+}  // namespace fb
+
+struct fb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    bool pdl = true;
+    int num_sms = 148;
+    uint32_t *err_word = nullptr;          // device, zero-initialised
+    fb::DevBuf scratch;                    // grow-only workspace
+    void *ensure_scratch(size_t bytes);
+};
+
+// Device layouts (all 16-byte aligned):
+//  Q4_K: n*nb blocks of 144 B in row order; each block keeps the GGUF
+//        header (d, dmin, scales[12]) in bytes 0..15 and stores the 128
+//        quant bytes permuted so that MMA quad lane t reads bytes
+//        [16+32t, 48+32t): for g = 0..3, GGUF qs[32g + 8t .. 32g + 8t + 7].
+//  Q6_K: "main" n*nb blocks of 208 B: bytes [48t, 48t+48) for quad lane t
+//        hold 8 ql words (h, j, x) = GGUF ql[64h + 32j + 8t + 4x .. +3] and
+//        4 qh words (h, x) = GGUF qh[32h + 8t + 4x .. +3]; bytes 192..207 are
+//        the 16 int8 scales.  The fp16 super-block scales d live in a
+//        separate [n, nb] array after the main area.
+struct fb_qtensor {
+    int dtype = 0;
+    int64_t n = 0, k = 0;
+    fb::DevBuf buf;
+    int64_t nb() const { return k / 256; }
+    const uint8_t *main() const { return buf.as<uint8_t>(); }
+    // Q6_K: fp16 d array after the 208-byte blocks.
+    const uint16_t *q6_d() const {
+        return reinterpret_cast<const uint16_t *>(buf.as<uint8_t>() + (size_t)n * nb() * 208);
+    }
+    static size_t device_bytes(int dtype, int64_t n, int64_t k);
+};
+
+namespace fb {
+
+// Q8_K activations in the device's SoA form for m rows of k values:
+//  qs  [m][k] int8, each 256-block permuted so quad lane t reads bytes
+//      [64t, 64t+64): for s = 0..7, the values 32s + 8t .. 32s + 8t + 7;
+//  d   [m][k/256] f32;  bs16 [m][k/16] int16;  bs32 [m][k/32] int16.
+struct Q8Act {
+    int8_t *qs;
+    float *d;
+    int16_t *bs16;
+    int16_t *bs32;
+    int64_t k;
+};
+size_t q8act_bytes(int64_t m, int64_t k);
+Q8Act q8act_view(void *base, int64_t m, int64_t k);
+
+// ---- kernel launchers (stream-ordered, no sync) ----
+void launch_quantize_q8k(fb_ctx *ctx, const float *x, int64_t m, int64_t k, const Q8Act &a);
+void launch_quantize_q8k_gguf(fb_ctx *ctx, const float *x, int64_t m, int64_t k, void *out);
+void launch_repack(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *gguf, void *dev);
+void launch_unpack(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *dev, void *gguf);
+void launch_synth(fb_ctx *ctx, int dtype, int64_t nblocks, uint64_t seed, float sigma, void *gguf_out);
+void launch_synth_f32(fb_ctx *ctx, float *out, int64_t n, uint64_t seed, float mean, float stddev);
+void launch_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out, int out_dtype);
+// y[m, n] (+)= x.W^T for m <= 16 from pre-quantized activations.
+void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy);
+// m > 16 QMatMul (prefill form).
+void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m);
+void launch_block_dots(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int32_t *out_sc, int32_t *out_min);
+void launch_rmsnorm(fb_ctx *ctx, const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps);
+void launch_rope(fb_ctx *ctx, float *x, int64_t n_tok, int64_t n_heads, int64_t hd, int64_t pos0,
+                 const float *cos_tab, const float *sin_tab, int mode);
+void launch_swiglu(fb_ctx *ctx, const float *g, const float *u, float *out, int64_t m, int64_t f);
+
+// Fused decode-step kernels (ops.cu).
+void launch_residual_rmsnorm_q8k(fb_ctx *ctx, float *x, const float *add, const float *g, int rows, int dim, float eps,
+                                 const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab);
+void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
+                       const float *kn, float eps, const float *cos_t, const float *sin_t, int mode,
+                       const int32_t *pos, int max_ctx, float *q_out, void *kpool, void *vpool,
+                       const int32_t *block_table, int max_pages, int page_size, int num_pages);
+void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a);
+void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out);
+void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
+                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale);
+
+// Paged flash-decode attention (attention.cu).
+struct AttnArgs {
+    const float *q;              // [b, n_heads, hd]
+    const void *kpool;           // fp16 [num_pages, n_kv, page, hd]
+    const void *vpool;
+    const int32_t *block_table;  // [b, max_pages]
+    const int32_t *seq_lens;     // [b] or null (then pos[b] + 1)
+    const int32_t *pos;          // [b]
+    float *part_o;               // [b, n_heads, nsplit_max, hd]
+    float *part_ml;              // [b, n_heads, nsplit_max, 2]
+    int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
+    float scale;
+    uint32_t *err;
+};
+void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
+                        const Q8Act *aq);
+
+// RoPE tables [max_pos][hd/2] computed on the host exactly as the oracle does
+// (candle precompute_freqs_cis: angle = pos * theta^(-2i/hd) in f32).
+void rope_tables(int max_pos, int head_dim, float theta, std::vector<float> &cos_t,
+                 std::vector<float> &sin_t);
+
+}  // namespace fb

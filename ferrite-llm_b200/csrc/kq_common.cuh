@@ -1,0 +1,70 @@
+// Device-side helpers shared by the sm_100a kernels: PDL controls, cache-hinted
+// loads, 8-bit integer MMA wrappers and the k-quant field decoders.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace fb {
+
+constexpr int QK = 256;
+
+// Programmatic dependent launch: wait for the preceding grid's results /
+// allow the next grid to start its prologue.  Both are no-ops when the
+// kernel was launched without the PDL attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Streaming weight loads: read once, keep out of L1.
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ld_stream_u16(const void *p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+// Activation loads: shared by every warp of the grid, keep in L1.
+__device__ __forceinline__ uint4 ld_act16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// D = A(16x32 s8, row) * B(32x8 s8, col) + C, int32 accumulate.
+__device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Q4_K: 8 six-bit scales (sc) and mins (mn) packed as 4 bytes per word:
+// sc_lo/hi hold j = 0..3 / 4..7, mn_lo/hi likewise (format of
+// get_scale_min_k4 in the GGUF Q4_K block).
+struct Q4Scales {
+    uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
+};
+__device__ __forceinline__ Q4Scales q4k_unpack_scales(uint32_t s0, uint32_t s1, uint32_t s2) {
+    Q4Scales r;
+    r.sc_lo = s0 & 0x3F3F3F3Fu;
+    r.mn_lo = s1 & 0x3F3F3F3Fu;
+    r.sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+    r.mn_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+    return r;
+}
+__device__ __forceinline__ int byte_of(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); }
+__device__ __forceinline__ int sbyte_of(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xFFu); }
+
+}  // namespace fb

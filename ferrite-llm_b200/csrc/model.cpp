@@ -1,0 +1,565 @@
+// Quantized Llama / Qwen3 decode runtime behind fb_model_* — the B200
+// counterpart of ferrite-core's InferenceModel implemented for candle at
+// crates/ferrite-wasm-host/src/adapter.rs:60-93 (forward / prefill /
+// clear_cache), with greedy sampling kept on the device like
+// Sampler::argmax (crates/ferrite-core/src/sampling.rs:108-112).
+//
+// One decode step for a batch of b sequences is a fixed chain of kernels:
+//   [embed + RMSNorm + Q8_K]
+//   per layer: QKV GEMV -> QK-norm + RoPE + KV write -> flash-decode split
+//              -> combine + Q8_K -> O GEMV -> residual + RMSNorm + Q8_K
+//              -> gate/up GEMV -> SwiGLU + Q8_K -> down GEMV
+//              -> residual + RMSNorm (next layer or final) + Q8_K
+//   lm_head GEMV -> argmax
+// launched with programmatic dependent launch and captured once per batch
+// size into a CUDA graph.  All buffers are allocated up front; the step reads
+// token ids and positions from device buffers, so replays need no host work.
+#include <cuda_fp16.h>
+#include <math.h>
+#include <string.h>
+
+#include <map>
+#include <memory>
+#include <string>
+
+#include "fb_internal.h"
+
+using namespace fb;
+
+namespace {
+
+constexpr int kPage = 64;
+
+enum TensorKind {
+    T_TOKEN_EMBD = 1, T_OUTPUT_NORM = 2, T_OUTPUT = 3,
+    T_ATTN_NORM = 10, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUTPUT, T_ATTN_Q_NORM, T_ATTN_K_NORM,
+    T_FFN_NORM, T_FFN_GATE, T_FFN_UP, T_FFN_DOWN
+};
+
+int kind_of(const char *name) {
+    static const std::map<std::string, int> m = {
+        {"token_embd", T_TOKEN_EMBD},   {"output_norm", T_OUTPUT_NORM}, {"output", T_OUTPUT},
+        {"attn_norm", T_ATTN_NORM},     {"attn_q", T_ATTN_Q},           {"attn_k", T_ATTN_K},
+        {"attn_v", T_ATTN_V},           {"attn_output", T_ATTN_OUTPUT}, {"attn_q_norm", T_ATTN_Q_NORM},
+        {"attn_k_norm", T_ATTN_K_NORM}, {"ffn_norm", T_FFN_NORM},       {"ffn_gate", T_FFN_GATE},
+        {"ffn_up", T_FFN_UP},           {"ffn_down", T_FFN_DOWN}};
+    auto it = m.find(name ? name : "");
+    return it == m.end() ? 0 : it->second;
+}
+
+struct QT {
+    fb_qtensor *t = nullptr;
+    QT() = default;
+    QT(const QT &) = delete;
+    QT &operator=(const QT &) = delete;
+    ~QT() { fb_qtensor_destroy(t); }
+    void reset(fb_qtensor *n = nullptr) {
+        fb_qtensor_destroy(t);
+        t = n;
+    }
+};
+
+struct Layer {
+    QT wq, wk, wv, wo, wgate, wup, wdown;  // as set
+    QT wqkv, wgu;                          // fused by finalize
+    DevBuf attn_norm, ffn_norm, q_norm, k_norm;
+};
+
+// Per-tensor seed of the random-init model: seed + 0x1000 * (layer + 1) + kind
+// (layer = -1 for the global tensors).
+uint64_t tensor_seed(uint64_t seed, int layer, int kind) {
+    return seed + 0x1000ull * (uint64_t)(layer + 1) + (uint64_t)kind;
+}
+
+}  // namespace
+
+struct fb_model {
+    fb_ctx *ctx = nullptr;
+    fb_model_config c{};
+    std::vector<std::unique_ptr<Layer>> layers;
+    QT tok_embd, output;
+    DevBuf out_norm;
+    bool finalized = false;
+    // KV cache and tables
+    int pages_per_seq = 0, num_pages = 0, nsplit_max = 0;
+    DevBuf kv;  // [L][K|V][num_pages][n_kv][page][hd] fp16
+    DevBuf block_table, rope_cos, rope_sin;
+    // step buffers
+    DevBuf x, y_qkv, q, y_o, y_gu, y_d, logits, part_o, part_ml;
+    DevBuf act_h, act_a, act_f;
+    DevBuf tok, pos, next;
+    int32_t *pinned = nullptr;  // host staging [3 * max_batch]
+    std::map<int, cudaGraphExec_t> graphs;
+    int len0 = 0;  // tokens held by sequence slot 0 (forward / prefill API)
+
+    size_t kv_half_layer() const { return (size_t)num_pages * c.n_kv_heads * kPage * c.head_dim; }
+    __half *kpool(int l) const { return kv.as<__half>() + (size_t)l * 2 * kv_half_layer(); }
+    __half *vpool(int l) const { return kpool(l) + kv_half_layer(); }
+
+    ~fb_model() {
+        for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+        if (pinned) cudaFreeHost(pinned);
+    }
+};
+
+static void upload_f32(fb_ctx *ctx, DevBuf &buf, const void *host, size_t n) {
+    buf.alloc(n * 4);
+    FB_CUDA(cudaMemcpyAsync(buf.ptr, host, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+}
+
+static void step(fb_model *m, int b) {
+    fb_ctx *ctx = m->ctx;
+    const fb_model_config &c = m->c;
+    const int H = c.hidden, qd = c.n_heads * c.head_dim, F = c.ffn;
+    const Q8Act ah = q8act_view(m->act_h.ptr, b, H);
+    const Q8Act aa = q8act_view(m->act_a.ptr, b, qd);
+    const Q8Act af = q8act_view(m->act_f.ptr, b, F);
+    float *x = m->x.as<float>();
+    launch_residual_rmsnorm_q8k(ctx, x, nullptr, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
+                                m->tok_embd.t, m->tok.as<int32_t>(), c.vocab);
+    AttnArgs A{};
+    A.q = m->q.as<float>();
+    A.block_table = m->block_table.as<int32_t>();
+    A.seq_lens = nullptr;
+    A.pos = m->pos.as<int32_t>();
+    A.part_o = m->part_o.as<float>();
+    A.part_ml = m->part_ml.as<float>();
+    A.n_heads = c.n_heads;
+    A.n_kv = c.n_kv_heads;
+    A.page_size = kPage;
+    A.max_pages = m->pages_per_seq;
+    A.num_pages = m->num_pages;
+    A.nsplit_max = m->nsplit_max;
+    A.scale = (float)(1.0 / sqrt((double)c.head_dim));
+    A.err = ctx->err_word;
+    for (int l = 0; l < c.n_layers; l++) {
+        Layer &L = *m->layers[l];
+        launch_gemv(ctx, L.wqkv.t, ah, b, m->y_qkv.as<float>(), L.wqkv.t->n);
+        launch_qk_rope_kv(ctx, m->y_qkv.as<float>(), b, c.n_heads, c.n_kv_heads, c.head_dim,
+                          c.qk_norm ? L.q_norm.as<float>() : nullptr, c.qk_norm ? L.k_norm.as<float>() : nullptr,
+                          c.eps, m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.rope_mode, m->pos.as<int32_t>(),
+                          c.max_ctx, m->q.as<float>(), m->kpool(l), m->vpool(l), m->block_table.as<int32_t>(),
+                          m->pages_per_seq, kPage, m->num_pages);
+        A.kpool = m->kpool(l);
+        A.vpool = m->vpool(l);
+        launch_attn_decode(ctx, A, b, c.max_ctx, nullptr, &aa);
+        launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
+        launch_residual_rmsnorm_q8k(ctx, x, m->y_o.as<float>(), L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
+                                    nullptr, c.vocab);
+        launch_gemv(ctx, L.wgu.t, ah, b, m->y_gu.as<float>(), 2 * F);
+        launch_swiglu_q8k(ctx, m->y_gu.as<float>(), F, b, af);
+        launch_gemv(ctx, L.wdown.t, af, b, m->y_d.as<float>(), H);
+        const float *gn = (l + 1 < c.n_layers) ? m->layers[l + 1]->attn_norm.as<float>() : m->out_norm.as<float>();
+        launch_residual_rmsnorm_q8k(ctx, x, m->y_d.as<float>(), gn, b, H, c.eps, ah, nullptr, nullptr, c.vocab);
+    }
+    launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), c.vocab);
+    launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>());
+}
+
+// Runs one step; the first call for a batch size runs eagerly and then
+// captures the chain into a CUDA graph for later replays.
+static void run_step(fb_model *m, int b) {
+    fb_ctx *ctx = m->ctx;
+    auto it = m->graphs.find(b);
+    if (it != m->graphs.end()) {
+        FB_CUDA(cudaGraphLaunch(it->second, ctx->stream));
+        return;
+    }
+    step(m, b);
+    cudaGraph_t g = nullptr;
+    FB_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+        step(m, b);
+    } catch (...) {
+        cudaStreamEndCapture(ctx->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    FB_CUDA(cudaStreamEndCapture(ctx->stream, &g));
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    FB_CUDA(e);
+    m->graphs[b] = ge;
+}
+
+static void require_ready(const fb_model *m) {
+    if (!m->finalized) fail(FB_ERR_STATE, "model not finalized (call fb_model_finalize after setting tensors)");
+}
+
+static void check_no_device_error(fb_model *m) {
+    uint32_t flags = 0;
+    FB_CUDA(cudaMemcpyAsync(&flags, m->ctx->err_word, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (flags) {
+        FB_CUDA(cudaMemsetAsync(m->ctx->err_word, 0, 4, m->ctx->stream));
+        fail(FB_ERR_DEVICE, "device error word set: 0x" + std::to_string(flags));
+    }
+}
+
+extern "C" {
+
+int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
+    return guarded([&] {
+        FB_REQUIRE(ctx && cfg && out, "null argument");
+        *out = nullptr;
+        const fb_model_config &c = *cfg;
+        FB_REQUIRE(c.n_layers > 0 && c.hidden > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.ffn > 0 && c.vocab > 0,
+                   "model dims must be positive");
+        FB_REQUIRE(c.head_dim == 128, "head_dim must be 128");
+        FB_REQUIRE(c.hidden % 256 == 0 && c.ffn % 256 == 0 && (c.n_heads * c.head_dim) % 256 == 0,
+                   "hidden, ffn and n_heads*head_dim must be multiples of 256");
+        FB_REQUIRE(c.n_heads % c.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
+        const int G = c.n_heads / c.n_kv_heads;
+        FB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "GQA group must be 1, 2, 4 or 8");
+        FB_REQUIRE(c.max_ctx >= 1 && c.max_batch >= 1 && c.max_batch <= 16, "need max_ctx >= 1, 1 <= max_batch <= 16");
+        FB_REQUIRE(c.rope_mode == 0 || c.rope_mode == 1, "rope_mode must be 0 or 1");
+        auto m = std::make_unique<fb_model>();
+        m->ctx = ctx;
+        m->c = c;
+        for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
+        m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
+        m->num_pages = m->pages_per_seq * c.max_batch;
+        m->nsplit_max = (m->pages_per_seq + 1) / 2;
+        m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
+        FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
+        std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);
+        for (size_t i = 0; i < bt.size(); i++) bt[i] = (int32_t)i;  // slot s owns pages [s*pps, (s+1)*pps)
+        m->block_table.alloc(bt.size() * 4);
+        FB_CUDA(cudaMemcpyAsync(m->block_table.ptr, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+        std::vector<float> ct, st;
+        rope_tables(c.max_ctx, c.head_dim, c.rope_theta, ct, st);
+        upload_f32(ctx, m->rope_cos, ct.data(), ct.size());
+        upload_f32(ctx, m->rope_sin, st.data(), st.size());
+        const int B = c.max_batch, H = c.hidden, qd = c.n_heads * c.head_dim;
+        const int kd = c.n_kv_heads * c.head_dim;
+        m->x.alloc((size_t)B * H * 4);
+        m->y_qkv.alloc((size_t)B * (qd + 2 * kd) * 4);
+        m->q.alloc((size_t)B * qd * 4);
+        m->y_o.alloc((size_t)B * H * 4);
+        m->y_gu.alloc((size_t)B * 2 * c.ffn * 4);
+        m->y_d.alloc((size_t)B * H * 4);
+        m->logits.alloc((size_t)B * c.vocab * 4);
+        m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 4);
+        m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 4);
+        m->act_h.alloc(q8act_bytes(B, H));
+        m->act_a.alloc(q8act_bytes(B, qd));
+        m->act_f.alloc(q8act_bytes(B, c.ffn));
+        m->tok.alloc((size_t)B * 4);
+        m->pos.alloc((size_t)B * 4);
+        m->next.alloc((size_t)B * 4);
+        FB_CUDA(cudaMemsetAsync(m->tok.ptr, 0, (size_t)B * 4, ctx->stream));
+        FB_CUDA(cudaMemsetAsync(m->pos.ptr, 0, (size_t)B * 4, ctx->stream));
+        FB_CUDA(cudaMallocHost(&m->pinned, (size_t)3 * B * 4));
+        FB_CUDA(cudaStreamSynchronize(ctx->stream));
+        *out = m.release();
+    });
+}
+
+int fb_model_destroy(fb_model *m) {
+    return guarded([&] {
+        if (!m) return;
+        cudaStreamSynchronize(m->ctx->stream);
+        delete m;
+    });
+}
+
+int fb_model_set_tensor(fb_model *m, const char *name, int layer, int dtype, int64_t rows, int64_t cols,
+                        const void *data_host) {
+    return guarded([&] {
+        FB_REQUIRE(m && name && data_host, "null argument");
+        FB_REQUIRE(!m->finalized, "model already finalized");
+        const fb_model_config &c = m->c;
+        const int kind = kind_of(name);
+        FB_REQUIRE(kind != 0, std::string("unknown tensor name: ") + name);
+        const bool global = kind < T_ATTN_NORM;
+        if (global) FB_REQUIRE(layer < 0, "global tensors take layer = -1");
+        else FB_REQUIRE(layer >= 0 && layer < c.n_layers, "layer index out of range");
+        const int qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+        auto vec = [&](DevBuf &buf, int64_t n) {
+            FB_REQUIRE(dtype == FB_F32 && rows * cols == n, std::string(name) + ": expected f32 vector");
+            upload_f32(m->ctx, buf, data_host, (size_t)n);
+        };
+        auto mat = [&](QT &slot, int64_t r, int64_t k, bool allow_q6, bool allow_q4) {
+            FB_REQUIRE(rows == r && cols == k, std::string(name) + ": shape mismatch");
+            FB_REQUIRE((dtype == FB_Q6_K && allow_q6) || (dtype == FB_Q4_K && allow_q4),
+                       std::string(name) + ": unsupported dtype");
+            fb_qtensor *t = nullptr;
+            const int rc = fb_qtensor_upload(m->ctx, dtype, r, k, data_host, &t);
+            if (rc != FB_OK) fail(rc, fb_last_error());
+            slot.reset(t);
+        };
+        switch (kind) {
+        case T_TOKEN_EMBD: mat(m->tok_embd, c.vocab, c.hidden, false, true); break;
+        case T_OUTPUT_NORM: vec(m->out_norm, c.hidden); break;
+        case T_OUTPUT: mat(m->output, c.vocab, c.hidden, true, true); break;
+        default: {
+            Layer &L = *m->layers[layer];
+            switch (kind) {
+            case T_ATTN_NORM: vec(L.attn_norm, c.hidden); break;
+            case T_ATTN_Q: mat(L.wq, qd, c.hidden, true, true); break;
+            case T_ATTN_K: mat(L.wk, kd, c.hidden, true, true); break;
+            case T_ATTN_V: mat(L.wv, kd, c.hidden, true, true); break;
+            case T_ATTN_OUTPUT: mat(L.wo, c.hidden, qd, true, true); break;
+            case T_ATTN_Q_NORM: vec(L.q_norm, c.head_dim); break;
+            case T_ATTN_K_NORM: vec(L.k_norm, c.head_dim); break;
+            case T_FFN_NORM: vec(L.ffn_norm, c.hidden); break;
+            case T_FFN_GATE: mat(L.wgate, c.ffn, c.hidden, true, true); break;
+            case T_FFN_UP: mat(L.wup, c.ffn, c.hidden, true, true); break;
+            case T_FFN_DOWN: mat(L.wdown, c.hidden, c.ffn, true, true); break;
+            }
+        }
+        }
+    });
+}
+
+int fb_model_synth(fb_model *m, uint64_t seed) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        FB_REQUIRE(!m->finalized, "model already finalized");
+        fb_ctx *ctx = m->ctx;
+        const fb_model_config &c = m->c;
+        const int qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+        const float sigma = 0.02f;
+        auto mat = [&](QT &slot, int dtype, int64_t r, int64_t k, uint64_t s) {
+            fb_qtensor *t = nullptr;
+            const int rc = fb_qtensor_synth(ctx, dtype, r, k, s, sigma, &t);
+            if (rc != FB_OK) fail(rc, fb_last_error());
+            slot.reset(t);
+        };
+        auto vec = [&](DevBuf &buf, int64_t n, uint64_t s) {
+            buf.alloc((size_t)n * 4);
+            launch_synth_f32(ctx, buf.as<float>(), n, s, 1.0f, 0.02f);
+        };
+        mat(m->tok_embd, FB_Q4_K, c.vocab, c.hidden, tensor_seed(seed, -1, T_TOKEN_EMBD));
+        vec(m->out_norm, c.hidden, tensor_seed(seed, -1, T_OUTPUT_NORM));
+        mat(m->output, FB_Q6_K, c.vocab, c.hidden, tensor_seed(seed, -1, T_OUTPUT));
+        for (int l = 0; l < c.n_layers; l++) {
+            Layer &L = *m->layers[l];
+            vec(L.attn_norm, c.hidden, tensor_seed(seed, l, T_ATTN_NORM));
+            mat(L.wq, FB_Q4_K, qd, c.hidden, tensor_seed(seed, l, T_ATTN_Q));
+            mat(L.wk, FB_Q4_K, kd, c.hidden, tensor_seed(seed, l, T_ATTN_K));
+            mat(L.wv, FB_Q4_K, kd, c.hidden, tensor_seed(seed, l, T_ATTN_V));
+            mat(L.wo, FB_Q4_K, c.hidden, qd, tensor_seed(seed, l, T_ATTN_OUTPUT));
+            vec(L.q_norm, c.head_dim, tensor_seed(seed, l, T_ATTN_Q_NORM));
+            vec(L.k_norm, c.head_dim, tensor_seed(seed, l, T_ATTN_K_NORM));
+            vec(L.ffn_norm, c.hidden, tensor_seed(seed, l, T_FFN_NORM));
+            mat(L.wgate, FB_Q4_K, c.ffn, c.hidden, tensor_seed(seed, l, T_FFN_GATE));
+            mat(L.wup, FB_Q4_K, c.ffn, c.hidden, tensor_seed(seed, l, T_FFN_UP));
+            mat(L.wdown, FB_Q6_K, c.hidden, c.ffn, tensor_seed(seed, l, T_FFN_DOWN));
+        }
+        FB_CUDA(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int fb_model_finalize(fb_model *m) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        if (m->finalized) return;
+        fb_ctx *ctx = m->ctx;
+        const fb_model_config &c = m->c;
+        FB_REQUIRE(m->tok_embd.t && m->output.t && m->out_norm.ptr, "token_embd, output and output_norm are required");
+        for (int l = 0; l < c.n_layers; l++) {
+            Layer &L = *m->layers[l];
+            FB_REQUIRE(L.wq.t && L.wk.t && L.wv.t && L.wo.t && L.wgate.t && L.wup.t && L.wdown.t && L.attn_norm.ptr &&
+                           L.ffn_norm.ptr,
+                       "layer " + std::to_string(l) + " is missing tensors");
+            if (c.qk_norm) FB_REQUIRE(L.q_norm.ptr && L.k_norm.ptr, "qk_norm needs attn_q_norm / attn_k_norm");
+            FB_REQUIRE(L.wq.t->dtype == L.wk.t->dtype && L.wq.t->dtype == L.wv.t->dtype,
+                       "attn_q/k/v must share a dtype");
+            FB_REQUIRE(L.wgate.t->dtype == L.wup.t->dtype, "ffn_gate/up must share a dtype");
+            const fb_qtensor *qkv[3] = {L.wq.t, L.wk.t, L.wv.t};
+            fb_qtensor *f = nullptr;
+            int rc = fb_qtensor_concat_rows(ctx, qkv, 3, &f);
+            if (rc != FB_OK) fail(rc, fb_last_error());
+            L.wqkv.reset(f);
+            const fb_qtensor *gu[2] = {L.wgate.t, L.wup.t};
+            rc = fb_qtensor_concat_rows(ctx, gu, 2, &f);
+            if (rc != FB_OK) fail(rc, fb_last_error());
+            L.wgu.reset(f);
+            L.wq.reset();
+            L.wk.reset();
+            L.wv.reset();
+            L.wgate.reset();
+            L.wup.reset();
+        }
+        m->finalized = true;
+    });
+}
+
+int fb_model_decode_dev(fb_model *m, const int32_t *tokens_dev, const int32_t *pos_dev, int batch, int32_t *next_dev,
+                        float *logits_dev) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_dev && pos_dev, "null argument");
+        require_ready(m);
+        FB_REQUIRE(batch >= 1 && batch <= m->c.max_batch, "batch out of range");
+        cudaStream_t s = m->ctx->stream;
+        FB_CUDA(cudaMemcpyAsync(m->tok.ptr, tokens_dev, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+        FB_CUDA(cudaMemcpyAsync(m->pos.ptr, pos_dev, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+        run_step(m, batch);
+        if (next_dev) FB_CUDA(cudaMemcpyAsync(next_dev, m->next.ptr, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+        if (logits_dev)
+            FB_CUDA(cudaMemcpyAsync(logits_dev, m->logits.ptr, (size_t)batch * m->c.vocab * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+    });
+}
+
+int fb_model_decode_greedy(fb_model *m, const int32_t *tokens_host, const int32_t *pos_host, int batch,
+                           int32_t *next_host) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_host && pos_host && next_host, "null argument");
+        require_ready(m);
+        FB_REQUIRE(batch >= 1 && batch <= m->c.max_batch, "batch out of range");
+        for (int i = 0; i < batch; i++) {
+            FB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->c.vocab, "token id out of range");
+            FB_REQUIRE(pos_host[i] >= 0 && pos_host[i] < m->c.max_ctx, "position out of range");
+        }
+        cudaStream_t s = m->ctx->stream;
+        int32_t *pt = m->pinned, *pp = m->pinned + m->c.max_batch, *pn = m->pinned + 2 * m->c.max_batch;
+        memcpy(pt, tokens_host, (size_t)batch * 4);
+        memcpy(pp, pos_host, (size_t)batch * 4);
+        FB_CUDA(cudaMemcpyAsync(m->tok.ptr, pt, (size_t)batch * 4, cudaMemcpyHostToDevice, s));
+        FB_CUDA(cudaMemcpyAsync(m->pos.ptr, pp, (size_t)batch * 4, cudaMemcpyHostToDevice, s));
+        run_step(m, batch);
+        FB_CUDA(cudaMemcpyAsync(pn, m->next.ptr, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+        FB_CUDA(cudaStreamSynchronize(s));
+        memcpy(next_host, pn, (size_t)batch * 4);
+        if (pos_host[0] + 1 > m->len0) m->len0 = pos_host[0] + 1;
+        check_no_device_error(m);
+    });
+}
+
+int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos, float *logits_host) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_host, "null argument");
+        require_ready(m);
+        FB_REQUIRE(n >= 1 && pos >= 0 && pos + n <= m->c.max_ctx, "tokens do not fit the KV capacity");
+        FB_REQUIRE(pos <= m->len0, "pos beyond the cached sequence");
+        for (int i = 0; i < n; i++)
+            FB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->c.vocab, "token id out of range");
+        cudaStream_t s = m->ctx->stream;
+        // token by token through the decode step (causal by construction)
+        for (int i = 0; i < n; i++) {
+            m->pinned[0] = tokens_host[i];
+            m->pinned[1] = pos + i;
+            FB_CUDA(cudaMemcpyAsync(m->tok.ptr, &m->pinned[0], 4, cudaMemcpyHostToDevice, s));
+            FB_CUDA(cudaMemcpyAsync(m->pos.ptr, &m->pinned[1], 4, cudaMemcpyHostToDevice, s));
+            run_step(m, 1);
+            FB_CUDA(cudaStreamSynchronize(s));  // pinned staging is reused next iteration
+        }
+        m->len0 = pos + n;
+        if (logits_host)
+            FB_CUDA(cudaMemcpyAsync(logits_host, m->logits.ptr, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, s));
+        FB_CUDA(cudaStreamSynchronize(s));
+        check_no_device_error(m);
+    });
+}
+
+int fb_model_prefill(fb_model *m, const int32_t *tokens_host, int n, float *logits_host) {
+    return fb_model_forward(m, tokens_host, n, 0, logits_host);
+}
+
+int fb_model_clear_cache(fb_model *m) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        m->len0 = 0;
+    });
+}
+
+int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        FB_REQUIRE(ctx >= 0 && ctx <= m->c.max_ctx, "ctx out of range");
+        const fb_model_config &c = m->c;
+        for (int l = 0; l < c.n_layers; l++)
+            for (int which = 0; which < 2; which++)
+                launch_synth_kv(m->ctx, which ? (void *)m->vpool(l) : (void *)m->kpool(l), l, which, ctx,
+                                c.n_kv_heads, c.head_dim, kPage, m->block_table.as<int32_t>(), m->pages_per_seq,
+                                c.max_batch, seed, scale);
+        FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+        m->len0 = ctx;
+    });
+}
+
+int fb_model_read_kv(fb_model *m, int layer, int which, int pos, float *out_host) {
+    return guarded([&] {
+        FB_REQUIRE(m && out_host, "null argument");
+        const fb_model_config &c = m->c;
+        FB_REQUIRE(layer >= 0 && layer < c.n_layers && (which == 0 || which == 1) && pos >= 0 && pos < c.max_ctx,
+                   "index out of range");
+        const __half *pool = which ? m->vpool(layer) : m->kpool(layer);
+        const int page = pos / kPage;  // slot 0 uses pages [0, pages_per_seq)
+        std::vector<__half> tmp((size_t)c.head_dim);
+        for (int h = 0; h < c.n_kv_heads; h++) {
+            const __half *src = pool + (((size_t)page * c.n_kv_heads + h) * kPage + (pos % kPage)) * c.head_dim;
+            FB_CUDA(cudaMemcpyAsync(tmp.data(), src, (size_t)c.head_dim * 2, cudaMemcpyDeviceToHost, m->ctx->stream));
+            FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+            for (int d = 0; d < c.head_dim; d++) out_host[h * c.head_dim + d] = __half2float(tmp[d]);
+        }
+    });
+}
+
+int fb_model_weight_bytes(const fb_model *m, int64_t *bytes) {
+    return guarded([&] {
+        FB_REQUIRE(m && bytes, "null argument");
+        int64_t tot = 0;
+        auto add = [&](const QT &q) {
+            if (q.t) tot += (int64_t)q.t->buf.bytes;
+        };
+        add(m->tok_embd);
+        add(m->output);
+        for (const auto &Lp : m->layers) {
+            const Layer &L = *Lp;
+            add(L.wq), add(L.wk), add(L.wv), add(L.wo), add(L.wgate), add(L.wup), add(L.wdown);
+            add(L.wqkv), add(L.wgu);
+        }
+        *bytes = tot;
+    });
+}
+
+// ---------------------------------------------------------------------------
+int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, const void *v_pages_dev,
+                   const int32_t *block_table_dev, const int32_t *seq_lens_dev, float *out_dev, int batch,
+                   int n_heads, int n_kv_heads, int head_dim, int page_size, int max_pages, int max_seq_len,
+                   float scale) {
+    return guarded([&] {
+        FB_REQUIRE(ctx && q_dev && k_pages_dev && v_pages_dev && block_table_dev && seq_lens_dev && out_dev,
+                   "null argument");
+        FB_REQUIRE(head_dim == 128, "head_dim must be 128");
+        FB_REQUIRE(page_size == 32 || page_size == 64, "page_size must be 32 or 64");
+        FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
+                   "bad shape");
+        FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
+        const int nsplit = (max_seq_len + 2 * page_size - 1) / (2 * page_size);
+        void *base = ctx->ensure_scratch((size_t)batch * n_heads * nsplit * (head_dim + 2) * 4);
+        AttnArgs A{};
+        A.q = q_dev;
+        A.kpool = k_pages_dev;
+        A.vpool = v_pages_dev;
+        A.block_table = block_table_dev;
+        A.seq_lens = seq_lens_dev;
+        A.pos = nullptr;
+        A.part_o = (float *)base;
+        A.part_ml = (float *)base + (size_t)batch * n_heads * nsplit * head_dim;
+        A.n_heads = n_heads;
+        A.n_kv = n_kv_heads;
+        A.page_size = page_size;
+        A.max_pages = max_pages;
+        A.num_pages = 0x7fffffff;  // caller-owned pool: ids are trusted up to int range
+        A.nsplit_max = nsplit;
+        A.scale = scale;
+        A.err = ctx->err_word;
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr);
+    });
+}
+
+}  // extern "C"
+
+namespace fb {
+// Until the tensor-core prefill GEMM is in place, m > 16 runs the Q8_K
+// integer path in chunks of 16 rows.
+void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
+    const int rc = fb_qmatmul_q8k(ctx, w, x, y, m);
+    if (rc != FB_OK) fail(rc, fb_last_error());
+}
+}  // namespace fb

@@ -1,0 +1,477 @@
+// Norm / RoPE / SwiGLU / embedding / argmax kernels of the decode step, in
+// standalone form (C-ABI ops) and fused with the Q8_K quantization of the
+// next QMatMul's input.
+//
+// Semantics (candle-nn 0.8.4 CPU ops as used by quantized_llama; CUDA forms
+// in the reference's vendored ptx-kernels/kernels/candle/reduce.cu):
+//   rms_norm  y = x / sqrt(mean(x^2) + eps) * g          (reduce.cu:189-230)
+//   rope_i    interleaved pairs (x[2i], x[2i+1])         (reduce.cu:275-292)
+//   rope      rotate-half pairs (x[i], x[i + d/2])       (reduce.cu:294-318)
+//   silu      v / (1 + exp(-v))                          (unary.cu:59)
+// Elementwise float steps use round-to-nearest intrinsics (no contraction)
+// so values match the CPU arithmetic bit for bit; only reductions differ in
+// summation order.
+#include <math.h>
+
+#include "fb_internal.h"
+#include "kq_common.cuh"
+
+namespace fb {
+
+// Q8_K quantization helpers shared with quant.cu are re-stated here for
+// values already in registers (one warp per 256-value block, lane l owns
+// values 8l..8l+7).
+__device__ __forceinline__ void q8k_store_warp(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
+                                               int64_t blk) {
+    float amax = 0.f, piv = 0.f;
+    int idx = 1 << 30;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float av = fabsf(v[e]);
+        if (amax < av) {
+            amax = av;
+            piv = v[e];
+            idx = 8 * lane + e;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        float op = __shfl_xor_sync(0xffffffffu, piv, off);
+        int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            piv = op;
+            idx = oi;
+        }
+    }
+    uint32_t w0 = 0, w1 = 0;
+    int s = 0;
+    float d = 0.f;
+    if (amax != 0.f) {
+        const float iscale = __fdiv_rn(-128.f, piv);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            int q = (int)roundf(__fmul_rn(iscale, v[e]));
+            q = q > 127 ? 127 : q;
+            s += q;
+            if (e < 4) w0 |= ((uint32_t)(uint8_t)q) << (8 * e);
+            else w1 |= ((uint32_t)(uint8_t)q) << (8 * (e - 4));
+        }
+        d = __fdiv_rn(1.f, iscale);
+    }
+    const int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+    const int64_t k = a.k;
+    *reinterpret_cast<uint2 *>(a.qs + row * k + blk * QK + 64 * (lane & 3) + 8 * (lane >> 2)) = make_uint2(w0, w1);
+    if ((lane & 1) == 0) a.bs16[row * (k / 16) + blk * 16 + (lane >> 1)] = (int16_t)s16;
+    if ((lane & 3) == 0) a.bs32[row * (k / 32) + blk * 8 + (lane >> 2)] = (int16_t)s32;
+    if (lane == 0) a.d[row * (k / QK) + blk] = d;
+}
+
+template <int NW>
+__device__ __forceinline__ float block_sum(float v, float *sh) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) t += sh[w];
+    return t;
+}
+
+// ------------------------------------------------------------------------
+// Residual add + RMSNorm + Q8_K, one CTA (NW warps) per row of width dim.
+// x[row] (+= add[row] when add != null) is written back when x_out != null;
+// emb_tab != null replaces x by the dequantized embedding row of token[row].
+constexpr int NORM_WARPS = 16;
+
+__device__ __forceinline__ float q4k_value(const uint8_t *blk, int i) {
+    const uint32_t *hw = reinterpret_cast<const uint32_t *>(blk);
+    const Q4Scales s = q4k_unpack_scales(hw[1], hw[2], hw[3]);
+    const float d = h2f((uint16_t)(hw[0] & 0xFFFF)), dmin = h2f((uint16_t)(hw[0] >> 16));
+    const int g = i >> 6, r = i & 63, hi = r >> 5, l = r & 31;
+    const int j = 2 * g + hi;
+    const int sc = byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
+    const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
+    const int t = l >> 3, e = l & 7;
+    const int nib = (blk[16 + 32 * t + 8 * g + e] >> (4 * hi)) & 0xF;
+    return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)nib), __fmul_rn(dmin, (float)mn));
+}
+
+__global__ void __launch_bounds__(NORM_WARPS * 32)
+    k_residual_rmsnorm_q8k(float *__restrict__ x, const float *__restrict__ add, const float *__restrict__ g,
+                           int dim, float eps, Q8Act a, const uint8_t *__restrict__ emb_tab,
+                           const int32_t *__restrict__ tokens, int vocab, uint32_t *err) {
+    __shared__ float sh[NORM_WARPS];
+    extern __shared__ float xs[];  // dim floats
+    pdl_wait();
+    const int64_t row = blockIdx.x;
+    float *xr = x + row * dim;
+    float ss = 0.f;
+    if (emb_tab) {
+        int tok = tokens[row];
+        if (tok < 0 || tok >= vocab) {
+            if (threadIdx.x == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
+            tok = 0;
+        }
+        const uint8_t *er = emb_tab + (int64_t)tok * (dim / QK) * 144;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+            const float v = q4k_value(er + (i / QK) * 144, i % QK);
+            xs[i] = v;
+            xr[i] = v;
+            ss += v * v;
+        }
+    } else {
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+            float v = xr[i];
+            if (add) {
+                v = __fadd_rn(add[row * dim + i], v);
+                xr[i] = v;
+            }
+            xs[i] = v;
+            ss += v * v;
+        }
+    }
+    ss = block_sum<NORM_WARPS>(ss, sh);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int blk = warp; blk < dim / QK; blk += NORM_WARPS) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int i = blk * QK + 8 * lane + e;
+            v[e] = __fmul_rn(__fdiv_rn(xs[i], m), g[i]);
+        }
+        q8k_store_warp(v, lane, a, row, blk);
+    }
+    pdl_launch();
+}
+
+// ------------------------------------------------------------------------
+// After the fused QKV GEMV: y[row] = [q (nq*hd) | k (nkv*hd) | v (nkv*hd)].
+// Per head (one warp): optional QK RMSNorm, RoPE at pos[row]; q -> q_out
+// (f32), k/v -> fp16 KV pages of sequence `row` at position pos[row].
+__global__ void __launch_bounds__(256)
+    k_qk_rope_kv(const float *__restrict__ y, int nq, int nkv, int hd, const float *__restrict__ qn,
+                 const float *__restrict__ kn, float eps, const float *__restrict__ cos_t,
+                 const float *__restrict__ sin_t, int mode, const int32_t *__restrict__ pos, int max_ctx,
+                 float *__restrict__ q_out, __half *__restrict__ kpool, __half *__restrict__ vpool,
+                 const int32_t *__restrict__ block_table, int max_pages, int page_size, int num_pages,
+                 uint32_t *err) {
+    pdl_wait();
+    const int row = blockIdx.y;
+    const int head = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int nh = nq + 2 * nkv;
+    if (head >= nh) return;
+    int p = pos[row];
+    if (p < 0 || p >= max_ctx) {
+        if (lane == 0) atomicOr(err, ERRBIT_BAD_POS);
+        return;
+    }
+    const float *src = y + (int64_t)row * nh * hd + (int64_t)head * hd;
+    const int per = hd / 32;  // values per lane (4 for hd = 128)
+    float v[8];
+    for (int e = 0; e < per; e++) v[e] = src[lane * per + e];
+    const bool is_q = head < nq, is_k = !is_q && head < nq + nkv;
+    if ((is_q || is_k) && qn) {
+        float ss = 0.f;
+        for (int e = 0; e < per; e++) ss += v[e] * v[e];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
+        const float *gw = is_q ? qn : kn;
+        for (int e = 0; e < per; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), gw[lane * per + e]);
+    }
+    if (is_q || is_k) {
+        const int half = hd / 2;
+        const float *ct = cos_t + (int64_t)p * half, *st = sin_t + (int64_t)p * half;
+        if (mode == 0) {
+            // interleaved: lane owns pairs (2i, 2i+1) inside its own values
+            for (int e = 0; e < per; e += 2) {
+                const int i = (lane * per + e) >> 1;
+                const float c = ct[i], s = st[i], x0 = v[e], x1 = v[e + 1];
+                v[e] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                v[e + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+            }
+        } else {
+            // rotate-half: partner value lives in lane ^ 16 (same e)
+            for (int e = 0; e < per; e++) {
+                const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+                const int d = lane * per + e;
+                const int i = d < half ? d : d - half;
+                const float c = ct[i], s = st[i];
+                if (d < half) v[e] = __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s));
+                else v[e] = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
+            }
+        }
+    }
+    if (is_q) {
+        float *dst = q_out + ((int64_t)row * nq + head) * hd + lane * per;
+        for (int e = 0; e < per; e++) dst[e] = v[e];
+    } else {
+        const int kvh = is_k ? head - nq : head - nq - nkv;
+        const int lp = p / page_size;
+        const int page = lp < max_pages ? block_table[(int64_t)row * max_pages + lp] : -1;
+        if (page < 0 || page >= num_pages) {
+            if (lane == 0) atomicOr(err, ERRBIT_BAD_PAGE);
+            return;
+        }
+        __half *pool = is_k ? kpool : vpool;
+        __half *dst = pool + (((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + lane * per;
+        for (int e = 0; e < per; e++) dst[e] = __float2half_rn(v[e]);
+    }
+    pdl_launch();
+}
+
+// ------------------------------------------------------------------------
+// SwiGLU + Q8_K: y[row] = [gate (f) | up (f)] -> act = Q8K(silu(gate) * up).
+__global__ void __launch_bounds__(256) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t nbk = f / QK;
+    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (wid < rows * nbk) {
+        const int64_t row = wid / nbk, blk = wid % nbk;
+        const float *gp = y + row * 2 * f + blk * QK + 8 * lane;
+        const float *up = gp + f;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float gv = gp[e];
+            const float sg = __fdiv_rn(gv, __fadd_rn(expf(-gv), 1.0f));
+            v[e] = __fmul_rn(sg, up[e]);
+        }
+        q8k_store_warp(v, lane, a, row, blk);
+    }
+    pdl_launch();
+}
+
+// ------------------------------------------------------------------------
+// Greedy argmax over each logits row (first index of the maximum, like the
+// CPU oracle); one CTA per row.
+__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ logits, int64_t vocab,
+                                                 int32_t *__restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_wait();
+    const float *r = logits + (int64_t)blockIdx.x * vocab;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float v = r[i];
+        if (v > best) {
+            best = v;
+            bi = (int)i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        best = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > best || (ov == best && oi < bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+    pdl_launch();
+}
+
+// ------------------------------------------------------------------------
+// Standalone ops for the C ABI.
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ g, float *__restrict__ y, int64_t dim,
+                          float eps) {
+    __shared__ float sh[8];
+    const float *xr = x + (int64_t)blockIdx.x * dim;
+    float *yr = y + (int64_t)blockIdx.x * dim;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum<8>(ss, sh);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
+}
+
+__global__ void k_rope(float *__restrict__ x, int64_t n_tok, int64_t n_heads, int64_t hd, int64_t pos0,
+                       const float *__restrict__ cos_t, const float *__restrict__ sin_t, int mode) {
+    const int64_t half = hd / 2;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over tok*heads*half
+    if (idx >= n_tok * n_heads * half) return;
+    const int64_t i = idx % half, th = idx / half, t = th / n_heads;
+    float *xh = x + th * hd;
+    const int64_t a = mode ? i : 2 * i, b = mode ? i + half : 2 * i + 1;
+    const float c = cos_t[(pos0 + t) * half + i], s = sin_t[(pos0 + t) * half + i];
+    const float x0 = xh[a], x1 = xh[b];
+    xh[a] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    xh[b] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+__global__ void k_swiglu(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ o, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float gv = g[i];
+    o[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(expf(-gv), 1.0f)), u[i]);
+}
+
+void launch_rmsnorm(fb_ctx *ctx, const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps) {
+    k_rmsnorm<<<(unsigned)rows, 256, 0, ctx->stream>>>(x, g, y, dim, eps);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_rope(fb_ctx *ctx, float *x, int64_t n_tok, int64_t n_heads, int64_t hd, int64_t pos0,
+                 const float *cos_tab, const float *sin_tab, int mode) {
+    const int64_t n = n_tok * n_heads * (hd / 2);
+    k_rope<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(x, n_tok, n_heads, hd, pos0, cos_tab, sin_tab, mode);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_swiglu(fb_ctx *ctx, const float *g, const float *u, float *out, int64_t m, int64_t f) {
+    const int64_t n = m * f;
+    k_swiglu<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(g, u, out, n);
+    FB_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------
+// PDL launch helper for the fused step kernels.
+template <typename K, typename... Args>
+static void launch_k(fb_ctx *ctx, K kernel, dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
+void launch_residual_rmsnorm_q8k(fb_ctx *ctx, float *x, const float *add, const float *g, int rows, int dim, float eps,
+                                 const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab) {
+    FB_REQUIRE(dim % QK == 0, "rmsnorm_q8k: dim must be a multiple of 256");
+    const size_t smem = (size_t)dim * 4;
+    if (smem > 48 * 1024)
+        FB_CUDA(cudaFuncSetAttribute(k_residual_rmsnorm_q8k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const uint8_t *tab = nullptr;
+    if (emb) {
+        FB_REQUIRE(emb->dtype == FB_Q4_K && emb->k == dim, "embedding table must be Q4_K [vocab, hidden]");
+        tab = emb->main();
+    }
+    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(rows), dim3(NORM_WARPS * 32), smem, x, add, g, dim, eps, a, tab,
+             tokens, vocab, ctx->err_word);
+}
+
+void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
+                       const float *kn, float eps, const float *cos_t, const float *sin_t, int mode,
+                       const int32_t *pos, int max_ctx, float *q_out, void *kpool, void *vpool,
+                       const int32_t *block_table, int max_pages, int page_size, int num_pages) {
+    FB_REQUIRE(hd == 64 || hd == 128, "qk_rope_kv: head_dim must be 64 or 128");
+    const int nh = nq + 2 * nkv;
+    launch_k(ctx, k_qk_rope_kv, dim3((nh + 7) / 8, rows), dim3(256), 0, y, nq, nkv, hd, qn, kn, eps, cos_t, sin_t,
+             mode, pos, max_ctx, q_out, (__half *)kpool, (__half *)vpool, block_table, max_pages, page_size,
+             num_pages, ctx->err_word);
+}
+
+void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a) {
+    FB_REQUIRE(f % QK == 0, "swiglu_q8k: ffn must be a multiple of 256");
+    const int64_t warps = (int64_t)rows * (f / QK);
+    launch_k(ctx, k_swiglu_q8k, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, y, f, (int64_t)rows, a);
+}
+
+void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out) {
+    launch_k(ctx, k_argmax, dim3(rows), dim3(1024), 0, logits, vocab, out);
+}
+
+void rope_tables(int max_pos, int head_dim, float theta, std::vector<float> &cos_t, std::vector<float> &sin_t) {
+    const int half = head_dim / 2;
+    cos_t.resize((size_t)max_pos * half);
+    sin_t.resize((size_t)max_pos * half);
+    for (int i = 0; i < half; i++) {
+        // same expression as the oracle's rope_inv_freq / or_rope
+        const float inv = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
+        for (int p = 0; p < max_pos; p++) {
+            const float ang = (float)p * inv;
+            cos_t[(size_t)p * half + i] = cosf(ang);
+            sin_t[(size_t)p * half + i] = sinf(ang);
+        }
+    }
+}
+
+}  // namespace fb
+
+namespace fb {
+
+static uint64_t kv_mix64_host(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Synthetic KV fill (bench / parity setup): value of (layer, K|V, position p,
+// element e = kv_head*hd + d) = fp16(scale*sqrt(3)*(2u - 1)), u the 24-bit
+// uniform of splitmix64(mix(seed) ^ ((layer*2 + which) << 40 | p << 20 | e)).
+// The CPU oracle's or_model_synth_kv uses the same function.
+__device__ __forceinline__ uint64_t kv_mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void k_synth_kv(__half *__restrict__ pool, int layer, int which, int ctx, int nkv, int hd, int page_size,
+                           const int32_t *__restrict__ block_table, int max_pages, int slots, uint64_t sm,
+                           float s3) {
+    const int64_t kd = (int64_t)nkv * hd;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over ctx * kd
+    if (i >= (int64_t)ctx * kd) return;
+    const int p = (int)(i / kd);
+    const int e = (int)(i % kd);
+    const uint64_t idx = (((uint64_t)layer * 2u + (uint64_t)which) << 40) | ((uint64_t)p << 20) | (uint64_t)e;
+    const uint64_t h = kv_mix64(sm ^ idx);
+    const float u = (float)(h >> 40) * (1.0f / 16777216.0f);
+    const __half v = __float2half_rn(__fmul_rn(s3, __fsub_rn(__fmul_rn(2.0f, u), 1.0f)));
+    const int kvh = e / hd, d = e % hd;
+    for (int s = 0; s < slots; s++) {
+        const int page = block_table[(int64_t)s * max_pages + p / page_size];
+        pool[(((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + d] = v;
+    }
+}
+
+void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
+                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale) {
+    const int64_t n = (int64_t)nctx * nkv * hd;
+    if (n == 0) return;
+    k_synth_kv<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+        (__half *)pool, layer, which, nctx, nkv, hd, page_size, block_table, max_pages, slots, kv_mix64_host(seed),
+        scale * 1.7320508f);
+    FB_CUDA(cudaGetLastError());
+}
+
+}  // namespace fb

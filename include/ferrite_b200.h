@@ -1,0 +1,201 @@
+/*
+ * ferrite_b200 — C ABI of the B200 (sm_100a) quantized decode/prefill path.
+ *
+ * The entry points replace the arithmetic behind ferrite-llm's candle-backend
+ * quantized Llama/Qwen forward.  Reference interfaces they stand in for:
+ *   - QTensor / QMatMul (candle-core 0.8.4, quantized/mod.rs; constructed by
+ *     quantized_llama::ModelWeights::from_gguf at
+ *     crates/ferrite-wasm-host/src/adapter.rs:47-55, called per layer from
+ *     the forward at adapter.rs:61-70)            -> fb_qtensor_*, fb_qmatmul
+ *   - GGUF k-quant blocks block_q4_K / block_q6_K / block_q8_K
+ *     (ferrite-os/crates/internal/ptx-kernels/kernels/candle/
+ *      quantized.cu:388-393, :419-424, :428-432)  -> FB_Q4_K / FB_Q6_K / FB_Q8_K
+ *   - QTensor::dequantize / dequantize_block_q4_K|q6_K_{f32,f16}
+ *     (quantized.cu:936-1151)                      -> fb_dequantize
+ *   - candle-nn rms_norm / rope_i / rope / softmax / silu
+ *     (ptx-kernels/kernels/candle/reduce.cu:189-345, unary.cu:59)
+ *                                                  -> fb_rmsnorm, fb_rope,
+ *                                                     fb_attn_decode, fb_swiglu
+ *   - ferrite_core::InferenceModel { forward, prefill, clear_cache }
+ *     (crates/ferrite-core/src/generation.rs:187-195; implemented for candle
+ *      at adapter.rs:60-93)                        -> fb_model_forward,
+ *                                                     fb_model_prefill,
+ *                                                     fb_model_clear_cache
+ *   - Sampler::argmax greedy path (crates/ferrite-core/src/sampling.rs:108-112)
+ *                                                  -> fb_model_decode_greedy
+ *
+ * Conventions: every function returns 0 (FB_OK) or a negative FB_ERR_* code
+ * and records a message readable with fb_last_error() (thread-local).  No
+ * call aborts or exits.  Pointers named *_dev are device pointers; *_host are
+ * host pointers.  All device work is ordered on the context's stream; only
+ * fb_sync and the *_host model calls synchronise.  One context per host
+ * thread / stream; handles are not thread-safe.
+ */
+#ifndef FERRITE_B200_H
+#define FERRITE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FB_ABI_VERSION 1
+
+enum fb_status {
+    FB_OK = 0,
+    FB_ERR_INVALID = -1,   /* bad argument (shape, dtype, null pointer) */
+    FB_ERR_CUDA = -2,      /* a CUDA runtime call failed */
+    FB_ERR_OOM = -3,       /* device allocation failed */
+    FB_ERR_DEVICE = -4,    /* a kernel reported an error through the error word */
+    FB_ERR_NCCL = -5,      /* a collective failed or timed out */
+    FB_ERR_STATE = -6      /* call not valid in the current state */
+};
+
+/* dtype ids follow the GGML type numbering for the k-quants. */
+enum fb_dtype {
+    FB_F32 = 0,
+    FB_F16 = 1,
+    FB_Q4_K = 12,
+    FB_Q6_K = 14,
+    FB_Q8_K = 15,
+    FB_BF16 = 30
+};
+
+typedef struct fb_ctx fb_ctx;
+typedef struct fb_qtensor fb_qtensor;
+typedef struct fb_model fb_model;
+
+/* ------------------------------------------------------------ context --- */
+const char *fb_last_error(void);
+int fb_abi_version(void);
+/* stream: a cudaStream_t (NULL = create a private non-blocking stream). */
+int fb_ctx_create(int device, void *stream, fb_ctx **out);
+int fb_ctx_destroy(fb_ctx *ctx);
+int fb_ctx_set_stream(fb_ctx *ctx, void *stream);
+void *fb_ctx_stream(fb_ctx *ctx);
+int fb_sync(fb_ctx *ctx);
+/* Reads and clears the device error word (bit flags set by kernels whose
+ * bounded waits ran out or whose inputs failed a device-side check). */
+int fb_ctx_error_word(fb_ctx *ctx, uint32_t *flags);
+/* Programmatic dependent launch between consecutive kernels (default on). */
+int fb_ctx_set_pdl(fb_ctx *ctx, int enable);
+
+/* ------------------------------------------------------------ QTensor --- */
+/* A weight matrix W[n, k] (n output features, k inputs, k % 256 == 0 for
+ * k-quants) held in device memory.  host_blocks holds GGUF blocks in row
+ * order (n * k/256 blocks).  The device copy is re-laid out for the GEMV;
+ * fb_qtensor_download returns the original GGUF bytes. */
+int fb_qtensor_upload(fb_ctx *ctx, int dtype, int64_t n, int64_t k,
+                      const void *host_blocks, fb_qtensor **out);
+int fb_qtensor_upload_dev(fb_ctx *ctx, int dtype, int64_t n, int64_t k,
+                          const void *dev_blocks, fb_qtensor **out);
+/* Random-init weights generated on the device (counter-based hash of
+ * (seed, block index); sigma = target standard deviation). */
+int fb_qtensor_synth(fb_ctx *ctx, int dtype, int64_t n, int64_t k,
+                     uint64_t seed, float sigma, fb_qtensor **out);
+/* Stacks the rows of several tensors of one dtype and k (fused QKV, gate/up). */
+int fb_qtensor_concat_rows(fb_ctx *ctx, const fb_qtensor *const *parts,
+                           int nparts, fb_qtensor **out);
+int fb_qtensor_info(const fb_qtensor *t, int *dtype, int64_t *n, int64_t *k,
+                    int64_t *device_bytes);
+int fb_qtensor_download(fb_ctx *ctx, const fb_qtensor *t, void *host_blocks);
+int fb_qtensor_destroy(fb_qtensor *t);
+/* W -> dense [n, k] in out_dtype (FB_F32, FB_F16 or FB_BF16). */
+int fb_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out_dev,
+                  int out_dtype);
+
+/* ------------------------------------------------------------ QMatMul --- */
+/* y[m, n] = x[m, k] . W[n, k]^T, f32 in and out.  m <= 16: activations are
+ * quantized to Q8_K and dotted in integer arithmetic (candle's CPU QMatMul);
+ * m > 16: the prefill path (W dequantized to 16-bit tiles on chip, tensor-core
+ * MMA with f32 accumulation). */
+int fb_qmatmul(fb_ctx *ctx, const fb_qtensor *w, const float *x_dev,
+               float *y_dev, int64_t m);
+/* Forces the Q8_K integer path for any m (chunks of 16 rows). */
+int fb_qmatmul_q8k(fb_ctx *ctx, const fb_qtensor *w, const float *x_dev,
+                   float *y_dev, int64_t m);
+/* f32 [m, k] -> GGUF block_q8_K array (m * k/256 blocks of 292 bytes). */
+int fb_quantize_q8k(fb_ctx *ctx, const float *x_dev, int64_t m, int64_t k,
+                    void *q8k_dev);
+/* Integer partials of W[n, k] against one activation row x[k] (quantized to
+ * Q8_K on the device): per (row, super-block) sum_j sc_j*dot_j and, for
+ * Q4_K, sum_j m_j*bsum_j.  out_* are int32 [n, k/256]. */
+int fb_block_dots(fb_ctx *ctx, const fb_qtensor *w, const float *x_dev,
+                  int32_t *out_sc_dev, int32_t *out_min_dev);
+
+/* ---------------------------------------------------------------- ops --- */
+/* y = x / sqrt(mean(x^2) + eps) * g, rows of length dim. */
+int fb_rmsnorm(fb_ctx *ctx, const float *x_dev, const float *g_dev,
+               float *y_dev, int64_t rows, int64_t dim, float eps);
+/* In-place RoPE of x[n_tok, n_heads, head_dim] at positions pos0 + t.
+ * mode 0 = interleaved pairs (candle rope_i), 1 = rotate-half (NEOX). */
+int fb_rope(fb_ctx *ctx, float *x_dev, int64_t n_tok, int64_t n_heads,
+            int64_t head_dim, int64_t pos0, float theta, int mode);
+/* out[m, f] = silu(gate[m, f]) * up[m, f]. */
+int fb_swiglu(fb_ctx *ctx, const float *gate_dev, const float *up_dev,
+              float *out_dev, int64_t m, int64_t f);
+/* GQA decode attention of one query token per sequence over a paged fp16 KV
+ * cache.  q[b, n_heads, head_dim] f32; k/v pages fp16
+ * [num_pages, n_kv_heads, page_size, head_dim]; block_table[b, max_pages]
+ * int32 physical page ids; seq_lens[b] int32 (tokens to attend, including
+ * the current one); out[b, n_heads, head_dim] f32.  scale = 1/sqrt(hd). */
+int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
+                   const void *v_pages_dev, const int32_t *block_table_dev,
+                   const int32_t *seq_lens_dev, float *out_dev, int batch,
+                   int n_heads, int n_kv_heads, int head_dim, int page_size,
+                   int max_pages, int max_seq_len, float scale);
+
+/* -------------------------------------------------------------- model --- */
+typedef struct {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+    int max_ctx;      /* KV capacity per sequence (tokens) */
+    int max_batch;    /* decode batch capacity */
+    float rope_theta, eps;
+    int qk_norm;      /* 1: Qwen3 per-head RMSNorm on q and k */
+    int rope_mode;    /* 0 interleaved (llama), 1 rotate-half (qwen3) */
+} fb_model_config;
+
+int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out);
+int fb_model_destroy(fb_model *m);
+/* GGUF tensor names: "token_embd", "output_norm", "output", and per layer
+ * "attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm",
+ * "attn_k_norm", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down" (layer >= 0).
+ * data_host: GGUF blocks for k-quants, f32 values for FB_F32. */
+int fb_model_set_tensor(fb_model *m, const char *name, int layer, int dtype,
+                        int64_t rows, int64_t cols, const void *data_host);
+/* Random-init every tensor on the device: linear layers Q4_K except
+ * ffn_down / output (Q6_K), i.e. a Q4_K_M-like mix; norms 1 + U(+-0.02*sqrt3). */
+int fb_model_synth(fb_model *m, uint64_t seed);
+/* Must be called after all tensors are set (fuses QKV and gate/up). */
+int fb_model_finalize(fb_model *m);
+/* InferenceModel::forward for one sequence: tokens_host[n] at positions
+ * pos..pos+n-1; logits of the last token -> logits_host[vocab] (may be NULL). */
+int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos,
+                     float *logits_host);
+/* Greedy decode step for a batch: tokens_host[b] at positions pos_host[b]
+ * (sequence i uses KV slot i); writes argmax ids to next_host[b]. */
+int fb_model_decode_greedy(fb_model *m, const int32_t *tokens_host,
+                           const int32_t *pos_host, int batch,
+                           int32_t *next_host);
+/* Device-resident form of the same step (inputs and outputs on the device,
+ * no synchronisation; replays a captured CUDA graph when available). */
+int fb_model_decode_dev(fb_model *m, const int32_t *tokens_dev,
+                        const int32_t *pos_dev, int batch, int32_t *next_dev,
+                        float *logits_dev);
+int fb_model_prefill(fb_model *m, const int32_t *tokens_host, int n,
+                     float *logits_host);
+int fb_model_clear_cache(fb_model *m);
+/* Fill the first ctx positions of every sequence slot's KV cache with
+ * synthetic fp16 values (bench / parity setup). */
+int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale);
+/* Reads one KV row (which 0 = K, 1 = V) of slot 0 as f32 [n_kv*head_dim]. */
+int fb_model_read_kv(fb_model *m, int layer, int which, int pos,
+                     float *out_host);
+int fb_model_weight_bytes(const fb_model *m, int64_t *bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,86 @@
+"""GPU RMSNorm / RoPE / SwiGLU / paged flash-decode attention vs CPU
+references (oracle for the elementwise ops, float64 numpy for attention)."""
+import math
+
+import numpy as np
+import pytest
+
+import ferrite_b200 as fb
+from conftest import O, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def test_rmsnorm(fbctx, torch_cuda):
+    torch = torch_cuda
+    x = np.random.default_rng(1).normal(0, 3, (6, 4096)).astype(np.float32)
+    g = (1 + np.random.default_rng(2).normal(0, 0.02, 4096)).astype(np.float32)
+    xd, gd = torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda()
+    yd = torch.empty_like(xd)
+    fb.rmsnorm(fbctx, xd.data_ptr(), gd.data_ptr(), yd.data_ptr(), 6, 4096, 1e-6)
+    ref = np.zeros_like(x)
+    O.lib().or_rmsnorm(O._p(x), O._p(g), O._p(ref), 6, 4096, 1e-6)
+    np.testing.assert_allclose(yd.cpu().numpy(), ref, rtol=2e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_rope(fbctx, torch_cuda, mode):
+    torch = torch_cuda
+    x = np.random.default_rng(mode).normal(0, 1, (3, 8, 128)).astype(np.float32)
+    xd = torch.from_numpy(x.copy()).cuda()
+    fb.rope(fbctx, xd.data_ptr(), 3, 8, 128, 4090, 1e6, mode)
+    ref = x.copy()
+    for t in range(3):
+        O.lib().or_rope(O._p(ref[t]), 8, 128, 4090 + t, 1e6, mode)
+    assert np.array_equal(xd.cpu().numpy(), ref)  # same tables, same rounding
+
+
+def test_swiglu(fbctx, torch_cuda):
+    torch = torch_cuda
+    g = np.random.default_rng(3).normal(0, 2, (4, 1024)).astype(np.float32)
+    u = np.random.default_rng(4).normal(0, 2, (4, 1024)).astype(np.float32)
+    gd, ud = torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()
+    od = torch.empty_like(gd)
+    fb.swiglu(fbctx, gd.data_ptr(), ud.data_ptr(), od.data_ptr(), 4, 1024)
+    ref = (g / (np.exp(-g) + 1.0)) * u
+    np.testing.assert_allclose(od.cpu().numpy(), ref, rtol=1e-6, atol=1e-6)
+
+
+def attn_reference(q, kp, vp, bt, lens, page):
+    b, nh, hd = q.shape
+    nkv = kp.shape[1]
+    g = nh // nkv
+    out = np.zeros_like(q, dtype=np.float64)
+    for s in range(b):
+        L = lens[s]
+        pages = [bt[s, i // page] for i in range(L)]
+        K = np.stack([kp[pages[i], :, i % page] for i in range(L)]).astype(np.float64)  # [L, nkv, hd]
+        V = np.stack([vp[pages[i], :, i % page] for i in range(L)]).astype(np.float64)
+        for h in range(nh):
+            sc = K[:, h // g] @ q[s, h].astype(np.float64) / math.sqrt(hd)
+            p = np.exp(sc - sc.max())
+            out[s, h] = (p / p.sum()) @ V[:, h // g]
+    return out
+
+
+@pytest.mark.parametrize("nh,nkv", [(32, 8), (64, 8), (8, 8), (16, 8)])
+@pytest.mark.parametrize("page", [32, 64])
+def test_attn_decode_paged(fbctx, torch_cuda, nh, nkv, page):
+    torch = torch_cuda
+    rng = np.random.default_rng(nh + page)
+    hd, b = 128, 5
+    lens = np.array([1, page - 1, page + 1, 2 * page + 3, 700], dtype=np.int32)
+    max_pages = int(math.ceil(lens.max() / page))
+    num_pages = b * max_pages + 3
+    perm = rng.permutation(num_pages)[: b * max_pages].reshape(b, max_pages).astype(np.int32)
+    kp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    vp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    qd, kd, vd, btd, ld = t(q), t(kp), t(vp), t(perm), t(lens)
+    out = torch.zeros((b, nh, hd), dtype=torch.float32, device="cuda")
+    fb.attn_decode(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(),
+                   out.data_ptr(), b, nh, nkv, hd, page, max_pages, int(lens.max()), 1.0 / math.sqrt(hd))
+    ref = attn_reference(q, kp, vp, perm, lens, page)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=1e-5)
+    assert fbctx.error_word() == 0
