@@ -19,7 +19,10 @@
 //    lane (31 shuffles per 32 dots);
 //  * partial (max, sum, o) per split go to a scratch buffer; a combine kernel
 //    merges the splits (log-sum-exp) and, fused into the model path,
-//    quantizes the result to Q8_K for the output projection.
+//    quantizes the result to Q8_K for the output projection;
+//  * dots, exponentials and sums run in binary64 with one rounding to f32
+//    at the end, so the result equals the CPU oracle's single-pass softmax
+//    bit for bit whatever the split layout.
 // All mbarrier waits are bounded: on timeout the kernel raises
 // ERRBIT_WAIT_TIMEOUT in the context's error word and returns.
 #include <math.h>
@@ -73,7 +76,13 @@ __device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
 }
 
 // Dynamic shared memory: K[2*page][hd] half, V[2*page][hd] half,
-// q[G][hd] f32, s[G][2*page] f32, red[ATT_WARPS][G][hd] f32.
+// q[G][hd] f32, s[G][2*page] f32, p[G][2*page] f64, red[ATT_WARPS][G][hd] f64.
+//
+// Numerics (identical to the CPU oracle up to binary64 rounding):
+//   s_t = f32(sum_e q_e * k_te in binary64) * scale
+//   per split: m = max_t s_t, p_t = exp64(s_t - m), l = sum p_t,
+//              o = sum p_t v_t              (binary64)
+//   combine:   M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
 template <int G>
 __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -93,7 +102,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
     __half *Vs = Ks + (size_t)ST * ATT_HD;
     float *qs = reinterpret_cast<float *>(Vs + (size_t)ST * ATT_HD);
     float *ss = qs + G * ATT_HD;
-    float *red = ss + G * ST;
+    double *ps = reinterpret_cast<double *>(ss + G * ST);
+    double *red = ps + G * ST;
     const uint32_t page_bytes = (uint32_t)P * ATT_HD * 2;
     const int npages = (ntok + P - 1) / P;  // 1 or 2
 
@@ -102,7 +112,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
         mbar_fence_init();
     }
     __syncthreads();
-    bool ok_pages = true;
     if (threadIdx.x == 0) {
         for (int j = 0; j < npages; j++) {
             const int lp = t0 / P + j;
@@ -114,14 +123,15 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
             if (page >= 0) {
                 const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
                 mbar_expect_tx(&bars[j], page_bytes);
-                bulk_g2s(Ks + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes, &bars[j]);
+                bulk_g2s(Ks + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes,
+                         &bars[j]);
                 mbar_expect_tx(&bars[2 + j], page_bytes);
-                bulk_g2s(Vs + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes, &bars[2 + j]);
+                bulk_g2s(Vs + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes,
+                         &bars[2 + j]);
             } else {
-                // complete the phases without data; the page reads as zero
+                // complete the phases without data (the error word is set)
                 mbar_expect_tx(&bars[j], 0);
                 mbar_expect_tx(&bars[2 + j], 0);
-                ok_pages = false;
             }
         }
     }
@@ -129,7 +139,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
     const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
     for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) qs[i] = qg[i];
     __syncthreads();
-    (void)ok_pages;
 
     // ---- scores: warp w handles tokens [32w, 32w+32) of the split
     constexpr int TCH = 32 / G;  // tokens per reduce-scatter chunk
@@ -145,7 +154,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
 #pragma unroll 1
         for (int c = 0; c < G; c++) {
             const int tc0 = tw0 + c * TCH;
-            float v[32];
+            double v[32];
 #pragma unroll
             for (int t = 0; t < TCH; t++) {
                 const int tok = tc0 + t;
@@ -154,10 +163,11 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
                 const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
 #pragma unroll
                 for (int g = 0; g < G; g++) {
-                    float acc = qv[g][0] * k01.x;
-                    acc = fmaf(qv[g][1], k01.y, acc);
-                    acc = fmaf(qv[g][2], k23.x, acc);
-                    acc = fmaf(qv[g][3], k23.y, acc);
+                    // f32 x fp16 products are exact in binary64
+                    double acc = __dmul_rn((double)qv[g][0], (double)k01.x);
+                    acc = __fma_rn((double)qv[g][1], (double)k01.y, acc);
+                    acc = __fma_rn((double)qv[g][2], (double)k23.x, acc);
+                    acc = __fma_rn((double)qv[g][3], (double)k23.y, acc);
                     v[t * G + g] = acc;
                 }
             }
@@ -167,39 +177,38 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
                 const bool up = (lane & o) != 0;
 #pragma unroll
                 for (int i = 0; i < n / 2; i++) {
-                    const float send = up ? v[i] : v[i + n / 2];
-                    const float keep = up ? v[i + n / 2] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                    const double send = up ? v[i] : v[i + n / 2];
+                    const double keep = up ? v[i + n / 2] : v[i];
+                    v[i] = __dadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
                 }
             }
             const int t = lane / G, g = lane % G;
             const int tok = tc0 + t;
-            ss[g * ST + tok] = tok < ntok ? v[0] * A.scale : -INFINITY;
+            ss[g * ST + tok] = tok < ntok ? __fmul_rn(__double2float_rn(v[0]), A.scale) : -INFINITY;
         }
     }
     __syncthreads();
-    // ---- softmax statistics per head (one warp per head)
-    float *ml = red;  // reuse: [G][2] before the PV reduction
+    // ---- per-head split max and p_t = exp(s_t - max) (one warp per head)
+    double *ml = red;  // [G][2] before the PV reduction reuses red
     for (int g = warp; g < G; g += ATT_WARPS) {
         float mx = -INFINITY;
         for (int t = lane; t < ntok; t += 32) mx = fmaxf(mx, ss[g * ST + t]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        float sum = 0.f;
+        double sum = 0.0;
         for (int t = lane; t < ST; t += 32) {
-            const float p = t < ntok ? expf(ss[g * ST + t] - mx) : 0.f;
-            ss[g * ST + t] = p;
-            sum += p;
+            const double p = t < ntok ? exp64(__dsub_rn((double)ss[g * ST + t], (double)mx)) : 0.0;
+            ps[g * ST + t] = p;
+            sum = __dadd_rn(sum, p);
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        sum = warp_sum64(sum);
         if (lane == 0) {
-            ml[2 * g] = mx;
+            ml[2 * g] = (double)mx;
             ml[2 * g + 1] = sum;
         }
     }
     __syncthreads();
-    float mls[G][2];
+    double mls[G][2];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         mls[g][0] = ml[2 * g];
@@ -207,11 +216,11 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
     }
     __syncthreads();
     // ---- o = sum_t p_t * v_t; warp w over tokens [32w, 32w+32), lane owns 4 dims
-    float o[G][4];
+    double o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) o[g][e] = 0.f;
+        for (int e = 0; e < 4; e++) o[g][e] = 0.0;
     if (tw0 < ntok) {
         waited_ok = mbar_wait_bounded(&bars[2 + tw0 / P], 0) && waited_ok;
         const int tend = min(tw0 + 32, ntok);
@@ -221,11 +230,11 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
             const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const float p = ss[g * ST + tok];
-                o[g][0] = fmaf(p, v01.x, o[g][0]);
-                o[g][1] = fmaf(p, v01.y, o[g][1]);
-                o[g][2] = fmaf(p, v23.x, o[g][2]);
-                o[g][3] = fmaf(p, v23.y, o[g][3]);
+                const double p = ps[g * ST + tok];
+                o[g][0] = __dadd_rn(o[g][0], __dmul_rn(p, (double)v01.x));
+                o[g][1] = __dadd_rn(o[g][1], __dmul_rn(p, (double)v01.y));
+                o[g][2] = __dadd_rn(o[g][2], __dmul_rn(p, (double)v23.x));
+                o[g][3] = __dadd_rn(o[g][3], __dmul_rn(p, (double)v23.y));
             }
         }
     }
@@ -233,7 +242,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
         atomicOr(A.err, ERRBIT_WAIT_TIMEOUT);
         // let any copy still in flight land before the CTA's shared memory
         // is released (bounded as well)
-        for (int j = 0; j < 4; j++) mbar_wait_bounded(&bars[j], 0);
+        for (int j = 0; j < npages; j++) {
+            mbar_wait_bounded(&bars[j], 0);
+            mbar_wait_bounded(&bars[2 + j], 0);
+        }
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
@@ -242,9 +254,9 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
     __syncthreads();
     for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) {
         const int g = i / ATT_HD, d = i % ATT_HD;
-        float s = 0.f;
+        double s = 0.0;
 #pragma unroll
-        for (int w = 0; w < ATT_WARPS; w++) s += red[(w * G + g) * ATT_HD + d];
+        for (int w = 0; w < ATT_WARPS; w++) s = __dadd_rn(s, red[(w * G + g) * ATT_HD + d]);
         const int64_t hrow = ((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * A.nsplit_max + split;
         A.part_o[hrow * ATT_HD + d] = s;
         if (d == 0) {
@@ -271,15 +283,15 @@ __global__ void __launch_bounds__(256) k_attn_combine(AttnArgs A, float *__restr
     const int i = blk * 256 + tid;  // value index in [n_heads * hd]
     const int h = i / ATT_HD, d = i % ATT_HD;
     const int64_t hbase = ((int64_t)b * A.n_heads + h) * A.nsplit_max;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, A.part_ml[2 * (hbase + s)]);
-    float L = 0.f, acc = 0.f;
+    double M = -INFINITY;
+    for (int s = 0; s < nsplit; s++) M = fmax(M, A.part_ml[2 * (hbase + s)]);
+    double L = 0.0, acc = 0.0;
     for (int s = 0; s < nsplit; s++) {
-        const float w = expf(A.part_ml[2 * (hbase + s)] - M);
-        L = fmaf(A.part_ml[2 * (hbase + s) + 1], w, L);
-        acc = fmaf(A.part_o[(hbase + s) * ATT_HD + d], w, acc);
+        const double w = exp64(__dsub_rn(A.part_ml[2 * (hbase + s)], M));
+        L = __dadd_rn(L, __dmul_rn(A.part_ml[2 * (hbase + s) + 1], w));
+        acc = __dadd_rn(acc, __dmul_rn(A.part_o[(hbase + s) * ATT_HD + d], w));
     }
-    const float val = acc / L;
+    const float val = __double2float_rn(__ddiv_rn(acc, L));
     if (out_f32) out_f32[(int64_t)b * A.n_heads * ATT_HD + i] = val;
     if (use_q8) {
         __shared__ float vals[256];
@@ -346,8 +358,8 @@ __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane
 
 size_t attn_smem_bytes(int G, int page_size) {
     const int ST = 2 * page_size;
-    return (size_t)2 * ST * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * ST * 4 +
-           (size_t)ATT_WARPS * G * ATT_HD * 4;
+    return (size_t)2 * ST * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * ST * 4 + (size_t)G * ST * 8 +
+           (size_t)ATT_WARPS * G * ATT_HD * 8;
 }
 
 template <typename K>

@@ -156,8 +156,8 @@ struct AttnArgs {
     const int32_t *block_table;  // [b, max_pages]
     const int32_t *seq_lens;     // [b] or null (then pos[b] + 1)
     const int32_t *pos;          // [b]
-    float *part_o;               // [b, n_heads, nsplit_max, hd]
-    float *part_ml;              // [b, n_heads, nsplit_max, 2]
+    double *part_o;              // [b, n_heads, nsplit_max, hd] unnormalised sum p*v
+    double *part_ml;             // [b, n_heads, nsplit_max, 2] (split max, sum p)
     int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
     float scale;
     uint32_t *err;

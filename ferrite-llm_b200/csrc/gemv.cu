@@ -14,7 +14,9 @@
 // (Q6_K) sub-block runs on the tensor pipe as mma.m16n8k32.s8 (16 weight rows
 // x 8 activation rows per instruction), which keeps the ALU budget per weight
 // byte flat from m = 1 to m = 16; integer partials are exact, so the
-// per-sub-block scales are applied in int32 exactly as the CPU path does.
+// per-sub-block scales are applied in int32 exactly as the CPU path does, and
+// the per-super-block float combine runs in binary64 with one rounding to f32
+// (bit-identical to the CPU oracle whatever the block summation order).
 // The device weight layouts (see fb_qtensor) put each MMA quad lane's bytes
 // contiguously, and the Q8_K activation layout (see Q8Act) matches the MMA B
 // fragment, so no shuffles or shared-memory staging are needed.
@@ -64,7 +66,7 @@ __device__ __forceinline__ float act_d(const Q8Act &a, int m, int col, int64_t b
 }
 
 template <int NT, bool DOTS>
-__device__ __forceinline__ void write_out(float (&acc)[NT][4], float *red, int warp, int gid, int tig, int64_t row0,
+__device__ __forceinline__ void write_out(double (&acc)[NT][4], double *red, int warp, int gid, int tig, int64_t row0,
                                           int64_t n, int m, float *y, int64_t ldy) {
     constexpr int C = 8 * NT;
     // red[w][r][c] with a padded row to keep the stores conflict-light
@@ -78,11 +80,11 @@ __device__ __forceinline__ void write_out(float (&acc)[NT][4], float *red, int w
     __syncthreads();
     for (int o = threadIdx.x; o < 16 * C; o += blockDim.x) {
         const int r = o / C, c = o % C;
-        float s = 0.f;
+        double s = 0.0;
 #pragma unroll
-        for (int w = 0; w < GEMV_WARPS; w++) s += red[(w * 16 + r) * (C + 1) + c];
+        for (int w = 0; w < GEMV_WARPS; w++) s = __dadd_rn(s, red[(w * 16 + r) * (C + 1) + c]);
         const int64_t row = row0 + r;
-        if (row < n && c < m) y[(int64_t)c * ldy + row] = s;
+        if (row < n && c < m) y[(int64_t)c * ldy + row] = __double2float_rn(s);
     }
 }
 
@@ -91,7 +93,7 @@ template <int NT, bool DOTS>
 __global__ void __launch_bounds__(256) k_gemv_q4k(const uint8_t *__restrict__ W, int64_t n, int nb, Q8Act a, int m,
                                                   float *__restrict__ y, int64_t ldy, int32_t *__restrict__ dots_sc,
                                                   int32_t *__restrict__ dots_min) {
-    __shared__ float red[GEMV_WARPS * 16 * (8 * NT + 1)];
+    __shared__ double red[GEMV_WARPS * 16 * (8 * NT + 1)];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t row0 = (int64_t)blockIdx.x * 16;
@@ -99,11 +101,11 @@ __global__ void __launch_bounds__(256) k_gemv_q4k(const uint8_t *__restrict__ W,
     const uint8_t *w0 = W + r0 * nb * 144;
     const uint8_t *w1 = W + r1 * nb * 144;
 
-    float acc[NT][4];
+    double acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
+        for (int i = 0; i < 4; i++) acc[nt][i] = 0.0;
 
     // Weights do not depend on the previous kernel: issue the first loads
     // before waiting on it.
@@ -194,11 +196,12 @@ __global__ void __launch_bounds__(256) k_gemv_q4k(const uint8_t *__restrict__ W,
                             dots_min[row * nb + b] = msum;
                         }
                     }
-                } else {
-                    const float dw = (i < 2) ? dw0 : dw1, dm = (i < 2) ? dm0 : dm1;
-                    const float yd = dy[nt][j];
-                    acc[nt][i] = fmaf(dw * yd, (float)isum[nt][i], acc[nt][i]);
-                    acc[nt][i] = fmaf(-(dm * yd), (float)msum, acc[nt][i]);
+                } else if (nt * 8 + 2 * tig + j < m) {
+                    // binary64 combine: ((d * dy) * isum) - ((dmin * dy) * msum)
+                    const double dw = (i < 2) ? dw0 : dw1, dm = (i < 2) ? dm0 : dm1;
+                    const double yd = dy[nt][j];
+                    acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, yd), (double)isum[nt][i]));
+                    acc[nt][i] = __dsub_rn(acc[nt][i], __dmul_rn(__dmul_rn(dm, yd), (double)msum));
                 }
             }
     }
@@ -214,7 +217,7 @@ template <int NT, bool DOTS>
 __global__ void __launch_bounds__(256) k_gemv_q6k(const uint8_t *__restrict__ W, const uint16_t *__restrict__ Wd,
                                                   int64_t n, int nb, Q8Act a, int m, float *__restrict__ y, int64_t ldy,
                                                   int32_t *__restrict__ dots_sc) {
-    __shared__ float red[GEMV_WARPS * 16 * (8 * NT + 1)];
+    __shared__ double red[GEMV_WARPS * 16 * (8 * NT + 1)];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
     const uint32_t mlo = tig < 2 ? 0xFFFFFFFFu : 0u;
@@ -225,11 +228,11 @@ __global__ void __launch_bounds__(256) k_gemv_q6k(const uint8_t *__restrict__ W,
     const uint16_t *d0p = Wd + r0 * nb;
     const uint16_t *d1p = Wd + r1 * nb;
 
-    float acc[NT][4];
+    double acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
+        for (int i = 0; i < 4; i++) acc[nt][i] = 0.0;
 
     int b = warp;
     uint4 x0[3], x1[3], sc0v, sc1v;
@@ -344,9 +347,9 @@ __global__ void __launch_bounds__(256) k_gemv_q6k(const uint8_t *__restrict__ W,
                         const int64_t row = row0 + gid + 8 * (i >> 1);
                         if (row < n) dots_sc[row * nb + b] = tot;
                     }
-                } else {
-                    const float dw = (i < 2) ? dw0 : dw1;
-                    acc[nt][i] = fmaf(dw * dy[nt][j], (float)tot, acc[nt][i]);
+                } else if (nt * 8 + 2 * tig + j < m) {
+                    const double dw = (i < 2) ? dw0 : dw1;
+                    acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, (double)dy[nt][j]), (double)tot));
                 }
             }
     }

@@ -85,7 +85,7 @@ struct fb_model {
     DevBuf kv;  // [L][K|V][num_pages][n_kv][page][hd] fp16
     DevBuf block_table, rope_cos, rope_sin;
     // step buffers
-    DevBuf x, y_qkv, q, y_o, y_gu, y_d, logits, part_o, part_ml;
+    DevBuf x, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml;
     DevBuf act_h, act_a, act_f;
     DevBuf tok, pos, next;
     int32_t *pinned = nullptr;  // host staging [3 * max_batch]
@@ -122,8 +122,8 @@ static void step(fb_model *m, int b) {
     A.block_table = m->block_table.as<int32_t>();
     A.seq_lens = nullptr;
     A.pos = m->pos.as<int32_t>();
-    A.part_o = m->part_o.as<float>();
-    A.part_ml = m->part_ml.as<float>();
+    A.part_o = m->part_o.as<double>();
+    A.part_ml = m->part_ml.as<double>();
     A.n_heads = c.n_heads;
     A.n_kv = c.n_kv_heads;
     A.page_size = kPage;
@@ -142,7 +142,7 @@ static void step(fb_model *m, int b) {
                           m->pages_per_seq, kPage, m->num_pages);
         A.kpool = m->kpool(l);
         A.vpool = m->vpool(l);
-        launch_attn_decode(ctx, A, b, c.max_ctx, nullptr, &aa);
+        launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), &aa);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         launch_residual_rmsnorm_q8k(ctx, x, m->y_o.as<float>(), L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
                                     nullptr, c.vocab);
@@ -236,12 +236,13 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         m->x.alloc((size_t)B * H * 4);
         m->y_qkv.alloc((size_t)B * (qd + 2 * kd) * 4);
         m->q.alloc((size_t)B * qd * 4);
+        m->attn.alloc((size_t)B * qd * 4);
         m->y_o.alloc((size_t)B * H * 4);
         m->y_gu.alloc((size_t)B * 2 * c.ffn * 4);
         m->y_d.alloc((size_t)B * H * 4);
         m->logits.alloc((size_t)B * c.vocab * 4);
-        m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 4);
-        m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 4);
+        m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 8);
+        m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 8);
         m->act_h.alloc(q8act_bytes(B, H));
         m->act_a.alloc(q8act_bytes(B, qd));
         m->act_f.alloc(q8act_bytes(B, c.ffn));
@@ -517,6 +518,31 @@ int fb_model_weight_bytes(const fb_model *m, int64_t *bytes) {
     });
 }
 
+int fb_model_read_activation(fb_model *m, const char *name, int row, float *out_host, int64_t count) {
+    return guarded([&] {
+        FB_REQUIRE(m && name && out_host, "null argument");
+        const fb_model_config &c = m->c;
+        FB_REQUIRE(row >= 0 && row < c.max_batch, "row out of range");
+        const int64_t qd = (int64_t)c.n_heads * c.head_dim, kd = (int64_t)c.n_kv_heads * c.head_dim;
+        const std::string n(name);
+        const DevBuf *buf = nullptr;
+        int64_t len = 0;
+        if (n == "x") buf = &m->x, len = c.hidden;
+        else if (n == "qkv") buf = &m->y_qkv, len = qd + 2 * kd;
+        else if (n == "q") buf = &m->q, len = qd;
+        else if (n == "attn") buf = &m->attn, len = qd;
+        else if (n == "o") buf = &m->y_o, len = c.hidden;
+        else if (n == "gate_up") buf = &m->y_gu, len = 2LL * c.ffn;
+        else if (n == "down") buf = &m->y_d, len = c.hidden;
+        else if (n == "logits") buf = &m->logits, len = c.vocab;
+        else fail(FB_ERR_INVALID, "unknown activation name: " + n);
+        FB_REQUIRE(count == len, "count must equal the row length (" + std::to_string(len) + ")");
+        FB_CUDA(cudaMemcpyAsync(out_host, buf->as<float>() + (size_t)row * len, (size_t)len * 4,
+                                cudaMemcpyDeviceToHost, m->ctx->stream));
+        FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
 // ---------------------------------------------------------------------------
 int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, const void *v_pages_dev,
                    const int32_t *block_table_dev, const int32_t *seq_lens_dev, float *out_dev, int batch,
@@ -531,7 +557,7 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
         const int nsplit = (max_seq_len + 2 * page_size - 1) / (2 * page_size);
-        void *base = ctx->ensure_scratch((size_t)batch * n_heads * nsplit * (head_dim + 2) * 4);
+        void *base = ctx->ensure_scratch((size_t)batch * n_heads * nsplit * (head_dim + 2) * 8);
         AttnArgs A{};
         A.q = q_dev;
         A.kpool = k_pages_dev;
@@ -539,8 +565,8 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         A.block_table = block_table_dev;
         A.seq_lens = seq_lens_dev;
         A.pos = nullptr;
-        A.part_o = (float *)base;
-        A.part_ml = (float *)base + (size_t)batch * n_heads * nsplit * head_dim;
+        A.part_o = (double *)base;
+        A.part_ml = (double *)base + (size_t)batch * n_heads * nsplit * head_dim;
         A.n_heads = n_heads;
         A.n_kv = n_kv_heads;
         A.page_size = page_size;

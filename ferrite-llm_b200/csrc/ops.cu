@@ -8,9 +8,10 @@
 //   rope_i    interleaved pairs (x[2i], x[2i+1])         (reduce.cu:275-292)
 //   rope      rotate-half pairs (x[i], x[i + d/2])       (reduce.cu:294-318)
 //   silu      v / (1 + exp(-v))                          (unary.cu:59)
-// Elementwise float steps use round-to-nearest intrinsics (no contraction)
-// so values match the CPU arithmetic bit for bit; only reductions differ in
-// summation order.
+// Elementwise float steps use round-to-nearest intrinsics (no contraction);
+// reductions and the SiLU exponential run in binary64 with one rounding to
+// f32, so values match the CPU oracle bit for bit regardless of summation
+// order.
 #include <math.h>
 
 #include "fb_internal.h"
@@ -69,18 +70,26 @@ __device__ __forceinline__ void q8k_store_warp(const float (&v)[8], int lane, co
     if (lane == 0) a.d[row * (k / QK) + blk] = d;
 }
 
+// Block sum in binary64 (RMSNorm sums of squares: each f32 square is exact
+// in binary64, so the result is independent of the summation order up to
+// binary64 rounding, and rounds to the same f32 as the oracle's).
 template <int NW>
-__device__ __forceinline__ float block_sum(float v, float *sh) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+__device__ __forceinline__ double block_sum64(double v, double *sh) {
+    v = warp_sum64(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __syncthreads();
     if (lane == 0) sh[warp] = v;
     __syncthreads();
-    float t = 0.f;
+    double t = 0.0;
 #pragma unroll
-    for (int w = 0; w < NW; w++) t += sh[w];
+    for (int w = 0; w < NW; w++) t = __dadd_rn(t, sh[w]);
     return t;
+}
+
+// 1 / rms from a binary64 sum of squares, as the oracle computes it:
+// m = sqrtf((float)(ss / dim) + eps).
+__device__ __forceinline__ float rms_of(double ss, int dim, float eps) {
+    return __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(ss, (double)dim)), eps));
 }
 
 // ------------------------------------------------------------------------
@@ -106,12 +115,12 @@ __global__ void __launch_bounds__(NORM_WARPS * 32)
     k_residual_rmsnorm_q8k(float *__restrict__ x, const float *__restrict__ add, const float *__restrict__ g,
                            int dim, float eps, Q8Act a, const uint8_t *__restrict__ emb_tab,
                            const int32_t *__restrict__ tokens, int vocab, uint32_t *err) {
-    __shared__ float sh[NORM_WARPS];
+    __shared__ double sh[NORM_WARPS];
     extern __shared__ float xs[];  // dim floats
     pdl_wait();
     const int64_t row = blockIdx.x;
     float *xr = x + row * dim;
-    float ss = 0.f;
+    double ss = 0.0;
     if (emb_tab) {
         int tok = tokens[row];
         if (tok < 0 || tok >= vocab) {
@@ -123,7 +132,7 @@ __global__ void __launch_bounds__(NORM_WARPS * 32)
             const float v = q4k_value(er + (i / QK) * 144, i % QK);
             xs[i] = v;
             xr[i] = v;
-            ss += v * v;
+            ss = __fma_rn((double)v, (double)v, ss);
         }
     } else {
         for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -133,11 +142,11 @@ __global__ void __launch_bounds__(NORM_WARPS * 32)
                 xr[i] = v;
             }
             xs[i] = v;
-            ss += v * v;
+            ss = __fma_rn((double)v, (double)v, ss);
         }
     }
-    ss = block_sum<NORM_WARPS>(ss, sh);
-    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    ss = block_sum64<NORM_WARPS>(ss, sh);
+    const float m = rms_of(ss, dim, eps);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int blk = warp; blk < dim / QK; blk += NORM_WARPS) {
         float v[8];
@@ -179,11 +188,10 @@ __global__ void __launch_bounds__(256)
     for (int e = 0; e < per; e++) v[e] = src[lane * per + e];
     const bool is_q = head < nq, is_k = !is_q && head < nq + nkv;
     if ((is_q || is_k) && qn) {
-        float ss = 0.f;
-        for (int e = 0; e < per; e++) ss += v[e] * v[e];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
+        double ss = 0.0;
+        for (int e = 0; e < per; e++) ss = __fma_rn((double)v[e], (double)v[e], ss);
+        ss = warp_sum64(ss);
+        const float m = rms_of(ss, hd, eps);
         const float *gw = is_q ? qn : kn;
         for (int e = 0; e < per; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), gw[lane * per + e]);
     }
@@ -242,9 +250,7 @@ __global__ void __launch_bounds__(256) k_swiglu_q8k(const float *__restrict__ y,
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            const float gv = gp[e];
-            const float sg = __fdiv_rn(gv, __fadd_rn(expf(-gv), 1.0f));
-            v[e] = __fmul_rn(sg, up[e]);
+            v[e] = __fmul_rn(silu64(gp[e]), up[e]);
         }
         q8k_store_warp(v, lane, a, row, blk);
     }
@@ -306,13 +312,13 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ logit
 // Standalone ops for the C ABI.
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ g, float *__restrict__ y, int64_t dim,
                           float eps) {
-    __shared__ float sh[8];
+    __shared__ double sh[8];
     const float *xr = x + (int64_t)blockIdx.x * dim;
     float *yr = y + (int64_t)blockIdx.x * dim;
-    float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
-    ss = block_sum<8>(ss, sh);
-    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    double ss = 0.0;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) ss = __fma_rn((double)xr[i], (double)xr[i], ss);
+    ss = block_sum64<8>(ss, sh);
+    const float m = rms_of(ss, (int)dim, eps);
     for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
 }
 
@@ -333,8 +339,7 @@ __global__ void k_rope(float *__restrict__ x, int64_t n_tok, int64_t n_heads, in
 __global__ void k_swiglu(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ o, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const float gv = g[i];
-    o[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(expf(-gv), 1.0f)), u[i]);
+    o[i] = __fmul_rn(silu64(g[i]), u[i]);
 }
 
 void launch_rmsnorm(fb_ctx *ctx, const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps) {

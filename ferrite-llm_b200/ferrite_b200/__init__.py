@@ -37,6 +37,7 @@ EXPORTED = (
     "fb_swiglu", "fb_attn_decode", "fb_model_create", "fb_model_destroy", "fb_model_set_tensor", "fb_model_synth",
     "fb_model_finalize", "fb_model_forward", "fb_model_decode_greedy", "fb_model_decode_dev", "fb_model_prefill",
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
+    "fb_model_read_activation",
 )
 
 
@@ -107,6 +108,7 @@ def _declare(L):
         "fb_model_synth_kv": (i32, [vp, u64, i32, f32]),
         "fb_model_read_kv": (i32, [vp, i32, i32, i32, vp]),
         "fb_model_weight_bytes": (i32, [vp, P(i64)]),
+        "fb_model_read_activation": (i32, [vp, C.c_char_p, i32, vp, i64]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -314,6 +316,15 @@ class Model:
     def read_kv(self, layer: int, which: int, pos: int) -> np.ndarray:
         out = np.zeros(self.cfg["n_kv_heads"] * self.cfg["head_dim"], dtype=np.float32)
         _check(lib().fb_model_read_kv(self.h, layer, which, pos, _np(out)))
+        return out
+
+    def read_activation(self, name: str, row: int = 0) -> np.ndarray:
+        c = self.cfg
+        qd, kd = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
+        n = {"x": c["hidden"], "qkv": qd + 2 * kd, "q": qd, "attn": qd, "o": c["hidden"], "gate_up": 2 * c["ffn"],
+             "down": c["hidden"], "logits": c["vocab"]}[name]
+        out = np.zeros(n, dtype=np.float32)
+        _check(lib().fb_model_read_activation(self.h, name.encode(), row, _np(out), n))
         return out
 
     def weight_bytes(self) -> int:

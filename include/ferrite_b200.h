@@ -194,6 +194,13 @@ int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale);
 int fb_model_read_kv(fb_model *m, int layer, int which, int pos,
                      float *out_host);
 int fb_model_weight_bytes(const fb_model *m, int64_t *bytes);
+/* Diagnostic read of the last decode step's f32 activations of batch row
+ * `row` (values of the last layer for per-layer buffers): "x" (residual
+ * stream, hidden), "qkv", "q" (after QK-norm + RoPE), "attn" (attention
+ * output, n_heads*head_dim), "o" (output projection), "gate_up" (2*ffn),
+ * "down", "logits".  count must equal the buffer's row length. */
+int fb_model_read_activation(fb_model *m, const char *name, int row,
+                             float *out_host, int64_t count);
 
 #ifdef __cplusplus
 }

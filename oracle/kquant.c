@@ -424,31 +424,33 @@ static void q6k_block_int(const or_block_q6k *x, const or_block_q8k *y,
     }
 }
 
+/* Per super-block the integer partials are exact; they are combined with the
+ * fp16 super-block scales in binary64 (one rounding to f32 at the end) so the
+ * result does not depend on the order in which blocks are summed.  candle
+ * combines in f32 (8 lane sums); the two differ in the last bits only. */
 float or_vec_dot(int dtype, int64_t n, const void *w, const void *a) {
     int64_t nb = n / OR_QK_K;
     const or_block_q8k *y = (const or_block_q8k *)a;
-    float sums[8] = {0};
-    float sumf = 0.f;
+    double acc = 0.0;
     for (int64_t b = 0; b < nb; b++) {
         int32_t lanes[8] = {0};
+        int32_t isum = 0;
         if (dtype == OR_Q4_K) {
             const or_block_q4k *x = (const or_block_q4k *)w + b;
             int32_t smin;
             q4k_block_int(x, y + b, lanes, &smin);
-            float d = or_f16_to_f32(x->d) * y[b].d;
-            for (int l = 0; l < 8; l++) sums[l] += d * (float)lanes[l];
-            float dmin = or_f16_to_f32(x->dmin) * y[b].d;
-            sumf -= dmin * (float)smin;
+            for (int l = 0; l < 8; l++) isum += lanes[l];
+            double dy = (double)y[b].d;
+            acc += (double)or_f16_to_f32(x->d) * dy * (double)isum;
+            acc -= (double)or_f16_to_f32(x->dmin) * dy * (double)smin;
         } else {
             const or_block_q6k *x = (const or_block_q6k *)w + b;
             q6k_block_int(x, y + b, lanes);
-            float d = or_f16_to_f32(x->d) * y[b].d;
-            for (int l = 0; l < 8; l++) sums[l] += d * (float)lanes[l];
+            for (int l = 0; l < 8; l++) isum += lanes[l];
+            acc += (double)or_f16_to_f32(x->d) * (double)y[b].d * (double)isum;
         }
     }
-    float tail = 0.f;
-    for (int l = 0; l < 8; l++) tail += sums[l];
-    return sumf + tail; /* Q6_K: sumf stays 0 */
+    return (float)acc;
 }
 
 void or_block_dots(int dtype, int64_t nrows, int64_t k, const void *w,

@@ -28,16 +28,36 @@
 #endif
 
 /* ----------------------------------------------------------- ops ------ */
+/* Reductions accumulate in binary64 (each f32 square / product is exact
+ * there), so the result does not depend on summation order; candle sums in
+ * f32 left to right, which differs from this in the last bits only. */
 void or_rmsnorm(const float *x, const float *g, float *y, int64_t rows,
                 int64_t dim, float eps) {
     for (int64_t r = 0; r < rows; r++) {
         const float *xr = x + r * dim;
         float *yr = y + r * dim;
-        float ss = 0.f;
-        for (int64_t i = 0; i < dim; i++) ss += xr[i] * xr[i];
-        float m = sqrtf(ss / (float)dim + eps);
+        double ss = 0.0;
+        for (int64_t i = 0; i < dim; i++) ss += (double)xr[i] * (double)xr[i];
+        float mean = (float)(ss / (double)dim);
+        float m = sqrtf(mean + eps);
         for (int64_t i = 0; i < dim; i++) yr[i] = xr[i] / m * g[i];
     }
+}
+
+double or_exp64(double x) {
+    static const double C[14] = {1.0, 1.0, 0.5, 0.16666666666666666, 0.041666666666666664,
+                                 0.008333333333333333, 0.001388888888888889, 0.0001984126984126984,
+                                 2.48015873015873e-05, 2.7557319223985893e-06, 2.755731922398589e-07,
+                                 2.505210838544172e-08, 2.08767569878681e-09, 1.6059043836821613e-10};
+    const double LOG2E = 1.4426950408889634, LN2_HI = 0.6931471803691238, LN2_LO = 1.9082149292705877e-10;
+    if (x != x) return x;
+    if (x > 709.5) return INFINITY;
+    if (x < -745.5) return 0.0;
+    double k = nearbyint(x * LOG2E);
+    double r = (x - k * LN2_HI) - k * LN2_LO;
+    double p = C[13];
+    for (int i = 12; i >= 0; i--) p = p * r + C[i];
+    return ldexp(p, (int)k);
 }
 
 static float rope_inv_freq(int i, int head_dim, float theta) {
@@ -72,7 +92,7 @@ void or_softmax(float *x, int64_t n) {
     for (int64_t i = 0; i < n; i++) x[i] /= s;
 }
 
-float or_silu(float v) { return v / (expf(-v) + 1.0f); }
+float or_silu(float v) { return (float)((double)v / (or_exp64(-(double)v) + 1.0)); }
 
 int or_argmax(const float *x, int64_t n) {
     int64_t best = 0;
@@ -302,23 +322,35 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
 #pragma omp parallel for num_threads(nt) collapse(2) schedule(dynamic, 1)
         for (int i = 0; i < n; i++)
             for (int hq = 0; hq < nq; hq++) {
+                /* softmax(q.k^T * scale) . v; dots, exponentials and sums
+                 * in binary64, one rounding to f32 at the end */
                 int T = pos + i + 1, hk = hq / grp;
                 const float *qh = q + (size_t)i * qd + (size_t)hq * hd;
                 float *sc = (float *)malloc(sizeof(float) * (size_t)T);
+                double *pr = (double *)malloc(sizeof(double) * (size_t)T);
+                double *acc = (double *)calloc((size_t)hd, sizeof(double));
+                float mx = -INFINITY;
                 for (int s = 0; s < T; s++) {
                     const float *ks = kl + (size_t)s * kd + (size_t)hk * hd;
-                    float acc = 0.f;
-                    for (int e = 0; e < hd; e++) acc += qh[e] * ks[e];
-                    sc[s] = acc * scale;
+                    double dot = 0.0;
+                    for (int e = 0; e < hd; e++) dot += (double)qh[e] * (double)ks[e];
+                    sc[s] = (float)dot * scale;
+                    mx = sc[s] > mx ? sc[s] : mx;
                 }
-                or_softmax(sc, T);
-                float *oh = o + (size_t)i * qd + (size_t)hq * hd;
-                for (int e = 0; e < hd; e++) oh[e] = 0.f;
+                double l = 0.0;
+                for (int s = 0; s < T; s++) {
+                    pr[s] = or_exp64((double)sc[s] - (double)mx);
+                    l += pr[s];
+                }
                 for (int s = 0; s < T; s++) {
                     const float *vs = vl + (size_t)s * kd + (size_t)hk * hd;
-                    for (int e = 0; e < hd; e++) oh[e] += sc[s] * vs[e];
+                    for (int e = 0; e < hd; e++) acc[e] += pr[s] * (double)vs[e];
                 }
+                float *oh = o + (size_t)i * qd + (size_t)hq * hd;
+                for (int e = 0; e < hd; e++) oh[e] = (float)(acc[e] / l);
                 free(sc);
+                free(pr);
+                free(acc);
             }
         linear(m, &L->wo, o, n, t, matmul_mode);
         for (size_t e = 0; e < (size_t)n * H; e++) x[e] = t[e] + x[e];

@@ -108,6 +108,11 @@ void or_rope(float *x, int64_t n_heads, int64_t head_dim, int64_t pos,
              float theta, int mode);
 void or_softmax(float *x, int64_t n);
 float or_silu(float x);
+/* exp in binary64: Cody-Waite reduction x = k ln2 + r, Taylor polynomial of
+ * degree 13 in r (|r| <= ln2/2, truncation < 5e-18), scaling by 2^k.  The
+ * device path evaluates the same operations, so both sides agree bit for
+ * bit. */
+double or_exp64(double x);
 
 /* -------------------------------------------------------------- model ---- */
 typedef struct {

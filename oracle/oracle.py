@@ -73,6 +73,10 @@ def _declare(L):
     L.or_rmsnorm.argtypes = [vp, vp, vp, i64, i64, f32]
     L.or_rope.argtypes = [vp, i64, i64, i64, f32, C.c_int]
     L.or_softmax.argtypes = [vp, i64]
+    L.or_silu.argtypes = [f32]
+    L.or_silu.restype = f32
+    L.or_exp64.argtypes = [C.c_double]
+    L.or_exp64.restype = C.c_double
     L.or_synth_q4k.argtypes = [u64, i64, f32, vp]
     L.or_synth_q6k.argtypes = [u64, i64, f32, vp]
     L.or_synth_f32.argtypes = [u64, i64, f32, f32, vp]
@@ -159,6 +163,20 @@ def qmatmul_f32(dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, nthrea
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
     y = np.zeros((x.shape[0], n), dtype=np.float32)
     lib().or_qmatmul_f32(dtype, _p(np.ascontiguousarray(w)), n, k, _p(x), x.shape[0], _p(y), nthreads)
+    return y
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    f = lib().or_silu
+    return np.array([f(float(v)) for v in np.asarray(x, dtype=np.float32).reshape(-1)],
+                    dtype=np.float32).reshape(np.shape(x))
+
+
+def rmsnorm(x: np.ndarray, g: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    y = np.zeros_like(x)
+    lib().or_rmsnorm(_p(x), _p(g), _p(y), x.size // x.shape[-1], x.shape[-1], eps)
     return y
 
 

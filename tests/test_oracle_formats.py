@@ -147,3 +147,15 @@ def test_qmatmul_f32_matches_dequantized_matmul():
     y = O.qmatmul_f32(O.Q6_K, w, 16, 512, x)
     wd = O.dequantize(O.Q6_K, w, 16 * 512).reshape(16, 512).astype(np.float64)
     np.testing.assert_allclose(y, x.astype(np.float64) @ wd.T, rtol=1e-6, atol=1e-6)
+
+
+def test_exp64_accuracy():
+    """The shared binary64 exp (Cody-Waite + Taylor) is within 2 ulp of
+    numpy's exp over the softmax / SiLU input range."""
+    xs = np.concatenate([np.linspace(-740, 700, 20001), np.random.default_rng(0).normal(0, 5, 20000),
+                         [0.0, -0.0, 1e-300, -1e-300, 0.5 * np.log(2), -0.5 * np.log(2)]])
+    got = np.array([O.lib().or_exp64(float(v)) for v in xs])
+    ref = np.exp(xs)
+    ok = np.abs(got - ref) <= 2 * np.spacing(ref)
+    assert ok.all(), xs[~ok][:5]
+    assert O.lib().or_exp64(-800.0) == 0.0 and O.lib().or_exp64(800.0) == np.inf
