@@ -1,0 +1,344 @@
+"""Decode benchmark: Qwen3-8B-architecture Q4_K_M decode tok/s on B200.
+
+Workload (one "step" = one greedy decode token per sequence): random-init
+Qwen3-8B architecture (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim
+128, QK-norm, RoPE theta 1e6, SwiGLU 12288, vocab 151936), Q4_K weights
+except ffn_down and output (Q6_K), fp16 paged KV cache holding 4096 tokens
+when decoding starts, batch 1 by default.
+
+  value  device-resident throughput: token ids fed back on the device, one
+         CUDA-graph replay per step, CUDA events over K timed steps.
+  e2e    the same metric through the public host API fb_model_decode_greedy
+         (token + position copied from pinned host memory, next token read
+         back every step).
+  roofline  the dominant kernel class (by measured time) from a live
+         per-kernel CUDA-event profile of the same workload.
+  cpu_baseline  the CPU oracle (C restatement of candle's CPU quantized path)
+         decoding the same random-init model on the host cores (rank 0, N=1).
+
+N > 1 (torchrun): every rank runs an independent replica on its own GPU
+(decode of independent sequences; no data-path collective); value is the
+total over ranks divided by the max-over-ranks elapsed time.
+--impl reference: the CPU oracle alone (the reference's path restated; the
+reference itself is Rust + candle and cannot be built here), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "ferrite-llm_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+MODELS = {
+    "qwen3-8b": dict(n_layers=36, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=12288, vocab=151936,
+                     rope_theta=1e6, eps=1e-6, qk_norm=1, rope_mode=1),
+    "llama3-70b": dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256,
+                       rope_theta=5e5, eps=1e-5, qk_norm=0, rope_mode=0),
+}
+METRIC = "Q4_K_M decode tok/s + GEMV HBM GB/s vs roofline (Qwen3-8B arch, 1-8 B200)"
+SEED = 1234
+
+
+def peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def step_bytes(cfg: dict, batch: int, ctx: int) -> dict:
+    """Algorithmic bytes per decode step by kernel class (weights once per
+    step, KV once per sequence, activations f32/Q8_K once)."""
+    H, F, V, L = cfg["hidden"], cfg["ffn"], cfg["vocab"], cfg["n_layers"]
+    qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    q4, q6 = 144 / 256, 210 / 256
+
+    def q8(k):  # Q8_K activation row: qs + d + bsums(16 and 32)
+        return k + 4 * k / 256 + 2 * k / 16 + 2 * k / 32
+
+    b = batch
+    per = {
+        "qkv": (qd + 2 * kd) * H * q4 + b * (q8(H) + 4 * (qd + 2 * kd)),
+        "o": H * qd * q4 + b * (q8(qd) + 4 * H),
+        "gate_up": 2 * F * H * q4 + b * (q8(H) + 8 * F),
+        "down": H * F * q6 + b * (q8(F) + 4 * H),
+        "attn": b * (2 * (ctx + 1) * kd * 2 + 4 * qd * 2),
+    }
+    tot = {k: v * L for k, v in per.items()}
+    tot["lm_head"] = V * H * q6 + b * (q8(H) + 4 * V)
+    tot["embed"] = b * H * q4
+    return {"per_launch": per | {"lm_head": tot["lm_head"]}, "per_step": tot, "total": sum(tot.values())}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict | None:
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_oracle_decode(cfg: dict, ctx: int, batch: int, budget_s: float, max_tokens: int, warmup: int = 1):
+    """Decode with the CPU oracle on all host threads; returns (tok/s,
+    tokens measured, threads)."""
+    from oracle import oracle as O
+
+    ocfg = dict(cfg, max_ctx=ctx + warmup + max_tokens + 2, kv_f16=1)
+    w = O.synth_model_weights(ocfg, SEED)
+    m = O.Model(ocfg, w, nthreads=0)
+    m.synth_kv(SEED + 7, ctx)
+    tok = int(O.synth_tokens(2, 1, cfg["vocab"])[0])
+    pos = ctx
+    for _ in range(warmup):
+        tok = int(O.np.argmax(m.forward([tok], pos)))
+        pos += 1
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens:
+        tok = int(O.np.argmax(m.forward([tok], pos)))
+        pos += 1
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    m.close()
+    return n / dt, n, os.cpu_count()
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    budget = min(150.0, 3.0 * (args.steps + args.warmup))
+    tps, n, cores = cpu_oracle_decode(cfg, args.ctx, 1, budget_s=budget, max_tokens=args.steps, warmup=1)
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 (Q4_K/Q6_K x Q8_K, CPU scalar)", "data": "synthetic",
+            "config": workload_config(args), "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                                     "d2h_bytes_per_step": 0},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} greedy decode tokens of the full model at ctx {args.ctx}, batch 1 "
+                                       f"(CPU oracle = C restatement of candle 0.8.4's CPU quantized path; "
+                                       f"the Rust reference cannot be built here)"}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {"workload": f"{args.model}-arch Q4_K_M random-init decode, batch {args.batch}, fp16 KV ctx {args.ctx}",
+            "model_arch": args.model, "batch": args.batch, "kv_ctx": args.ctx, "weights": "Q4_K (+Q6_K ffn_down, output)",
+            "parallelism": "replicas" if args.gpus > 1 else "single-gpu",
+            "l2": "not flushed: each step streams ~4.9 GB of weights, >> 126 MB L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="qwen3-8b", choices=sorted(MODELS))
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--profile-run", type=int, default=0,
+                    help="build the workload, run N untimed decode steps and exit (driver for ncu captures)")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = dict(MODELS[args.model])
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import numpy as np
+    import torch
+
+    import ferrite_b200 as fb
+
+    ws, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    pg = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        pg = dist
+    stream = torch.cuda.current_stream()
+    ctx = fb.Context(local, stream.cuda_stream)
+    B = args.batch
+    max_ctx = args.ctx + args.warmup + args.steps + args.e2e_steps + 16
+    mcfg = dict(cfg, max_ctx=max_ctx, max_batch=B)
+    model = fb.Model(ctx, mcfg)
+    model.synth(SEED)
+    model.finalize()
+    model.synth_kv(SEED + 7, args.ctx)
+    nsteps = args.warmup + args.steps
+    pos_all = torch.arange(args.ctx, args.ctx + nsteps + 8, dtype=torch.int32, device="cuda")
+    pos_all = pos_all.repeat_interleave(B).reshape(-1, B).contiguous()
+    tok = torch.randint(0, cfg["vocab"], (B,), dtype=torch.int32, device="cuda",
+                        generator=torch.Generator(device="cuda").manual_seed(2))
+
+    def dstep(i):
+        model.decode_dev(tok.data_ptr(), pos_all[i].data_ptr(), B, next_ptr=tok.data_ptr())
+
+    if args.profile_run:
+        for i in range(args.profile_run):
+            dstep(i)
+        torch.cuda.synchronize()
+        print("profile run ok", tok.cpu().tolist(), "error word", ctx.error_word())
+        return
+
+    for i in range(args.warmup):
+        dstep(i)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.warmup, nsteps):
+            dstep(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        pg.barrier()
+    torch.cuda.synchronize()
+    ms_per_step = ms / args.steps
+    value = ws * B * args.steps / (ms / 1e3)
+    err = ctx.error_word()
+
+    # ---- e2e through the public host API (pinned H2D + D2H every step)
+    toks_h = tok.cpu().numpy().astype(np.int32)
+    p0 = args.ctx + nsteps
+    for i in range(2):
+        toks_h = model.decode_greedy(toks_h, np.full(B, p0 + i, np.int32))
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        toks_h = model.decode_greedy(toks_h, np.full(B, p0 + 2 + i, np.int32))
+    e2e_s = time.perf_counter() - t0
+    if pg:
+        t = torch.tensor([e2e_s], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = ws * B * args.e2e_steps / e2e_s
+
+    # ---- live per-kernel profile (CUDA events per kernel class, serialised)
+    prof = model.profile(tok.data_ptr(), pos_all[0].data_ptr(), B, 3)
+    sb = step_bytes(cfg, B, args.ctx)
+    peak, peak_kind = peaks()
+    gemv_classes = ("qkv", "o", "gate_up", "down", "lm_head")
+    dom = max(gemv_classes, key=lambda k: prof[k][0])
+    dom_ms_per_launch = prof[dom][0] / 3 / max(1, prof[dom][1])
+    achieved = sb["per_launch"][dom] / (dom_ms_per_launch * 1e-3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", f"gemv_{dom}_{args.model}_b{B}.md")
+    if os.path.exists(tfile):
+        for ln in open(tfile):
+            if ln.startswith("dram_bytes_per_launch:"):
+                traffic = float(ln.split(":")[1].split()[0])
+    step_achieved = sb["total"] / (ms_per_step * 1e-3) / 1e9
+    prof_ms = {k: round(v[0] / 3, 4) for k, v in prof.items()}
+
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 (Q4_K/Q6_K weights x Q8_K activations, int8 MMA, f32/f64 combine)",
+            "data": "synthetic (random-init weights and KV, seeded)", "config": workload_config(args),
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": model.launches_per_step() * args.steps,
+            "roofline": {"bound": "hbm", "kernel": f"gemv_{dom}", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": sb["per_launch"][dom],
+                         "launch_ms": dom_ms_per_launch},
+            "step_roofline": {"achieved": step_achieved, "peak": peak, "unit": "GB/s",
+                              "frac": step_achieved / peak, "bytes_per_step": sb["total"],
+                              "roofline_tok_s": B * peak * 1e9 / sb["total"]},
+            "kernel_ms_per_step": prof_ms, "device_error_word": err}
+    clocks = clk.summary()
+    if clocks:
+        line["clocks"] = clocks
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        model.close()
+        torch.cuda.empty_cache()
+        tps, n, cores = cpu_oracle_decode(cfg, args.ctx, 1, budget_s=20.0, max_tokens=8)
+        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} greedy decode tokens of the same random-init model at ctx "
+                                          f"{args.ctx}, batch 1, CPU oracle (C restatement of candle's CPU "
+                                          f"quantized path) on all host threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -90,12 +90,7 @@ int fb_ctx_create(int device, void *stream, fb_ctx **out) {
         FB_CUDA(cudaSetDevice(device));
         auto c = std::make_unique<fb_ctx>();
         c->device = device;
-        if (stream) {
-            c->stream = (cudaStream_t)stream;
-        } else {
-            FB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
-            c->own_stream = true;
-        }
+        c->stream = (cudaStream_t)stream;  // NULL = CUDA default stream
         FB_CUDA(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device));
         FB_CUDA(cudaMalloc(&c->err_word, 64));
         FB_CUDA(cudaMemset(c->err_word, 0, 64));
@@ -117,7 +112,8 @@ int fb_ctx_destroy(fb_ctx *ctx) {
 
 int fb_ctx_set_stream(fb_ctx *ctx, void *stream) {
     return guarded([&] {
-        FB_REQUIRE(ctx && stream, "null argument");
+        FB_REQUIRE(ctx, "null ctx");
+        FB_CUDA(cudaStreamSynchronize(ctx->stream));
         if (ctx->own_stream) {
             FB_CUDA(cudaStreamSynchronize(ctx->stream));
             FB_CUDA(cudaStreamDestroy(ctx->stream));

@@ -89,8 +89,11 @@ struct fb_model {
     DevBuf act_h, act_a, act_f;
     DevBuf tok, pos, next;
     int32_t *pinned = nullptr;  // host staging [3 * max_batch]
+    cudaStream_t work = nullptr;        // private stream the step graph runs on
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
     int len0 = 0;  // tokens held by sequence slot 0 (forward / prefill API)
+    int launches_per_step = 0;
 
     size_t kv_half_layer() const { return (size_t)num_pages * c.n_kv_heads * kPage * c.head_dim; }
     __half *kpool(int l) const { return kv.as<__half>() + (size_t)l * 2 * kv_half_layer(); }
@@ -99,6 +102,9 @@ struct fb_model {
     ~fb_model() {
         for (auto &g : graphs) cudaGraphExecDestroy(g.second);
         if (pinned) cudaFreeHost(pinned);
+        if (work) cudaStreamDestroy(work);
+        if (ev_in) cudaEventDestroy(ev_in);
+        if (ev_out) cudaEventDestroy(ev_out);
     }
 };
 
@@ -107,8 +113,51 @@ static void upload_f32(fb_ctx *ctx, DevBuf &buf, const void *host, size_t n) {
     FB_CUDA(cudaMemcpyAsync(buf.ptr, host, n * 4, cudaMemcpyHostToDevice, ctx->stream));
 }
 
-static void step(fb_model *m, int b) {
+// Optional per-class timing of an eager step (fb_model_profile): one event
+// after every kernel class, elapsed times read after the step completes.
+struct StepProbe {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kinds;
+    float ms[FB_PROF_KINDS] = {0};
+    int launches[FB_PROF_KINDS] = {0};
+    cudaStream_t s = nullptr;
+    ~StepProbe() {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
+    cudaEvent_t next_event() {
+        cudaEvent_t e;
+        FB_CUDA(cudaEventCreate(&e));
+        ev.push_back(e);
+        return e;
+    }
+    void start() {
+        FB_CUDA(cudaEventRecord(next_event(), s));
+        kinds.push_back(-1);
+    }
+    void mark(int kind, int nlaunch) {
+        FB_CUDA(cudaEventRecord(next_event(), s));
+        kinds.push_back(kind);
+        launches[kind] += nlaunch;
+    }
+    void collect() {
+        FB_CUDA(cudaStreamSynchronize(s));
+        for (size_t i = 1; i < ev.size(); i++) {
+            if (kinds[i] < 0) continue;
+            float t = 0.f;
+            FB_CUDA(cudaEventElapsedTime(&t, ev[i - 1], ev[i]));
+            ms[kinds[i]] += t;
+        }
+    }
+};
+
+static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     fb_ctx *ctx = m->ctx;
+    int nl = 0;
+    auto mark = [&](int kind, int n) {
+        nl += n;
+        if (probe) probe->mark(kind, n);
+    };
+    if (probe) probe->start();
     const fb_model_config &c = m->c;
     const int H = c.hidden, qd = c.n_heads * c.head_dim, F = c.ffn;
     const Q8Act ah = q8act_view(m->act_h.ptr, b, H);
@@ -117,6 +166,7 @@ static void step(fb_model *m, int b) {
     float *x = m->x.as<float>();
     launch_residual_rmsnorm_q8k(ctx, x, nullptr, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
                                 m->tok_embd.t, m->tok.as<int32_t>(), c.vocab);
+    mark(FB_PROF_EMBED_NORM, 1);
     AttnArgs A{};
     A.q = m->q.as<float>();
     A.block_table = m->block_table.as<int32_t>();
@@ -135,31 +185,62 @@ static void step(fb_model *m, int b) {
     for (int l = 0; l < c.n_layers; l++) {
         Layer &L = *m->layers[l];
         launch_gemv(ctx, L.wqkv.t, ah, b, m->y_qkv.as<float>(), L.wqkv.t->n);
+        mark(FB_PROF_QKV, 1);
         launch_qk_rope_kv(ctx, m->y_qkv.as<float>(), b, c.n_heads, c.n_kv_heads, c.head_dim,
                           c.qk_norm ? L.q_norm.as<float>() : nullptr, c.qk_norm ? L.k_norm.as<float>() : nullptr,
                           c.eps, m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.rope_mode, m->pos.as<int32_t>(),
                           c.max_ctx, m->q.as<float>(), m->kpool(l), m->vpool(l), m->block_table.as<int32_t>(),
                           m->pages_per_seq, kPage, m->num_pages);
+        mark(FB_PROF_ROPE_KV, 1);
         A.kpool = m->kpool(l);
         A.vpool = m->vpool(l);
         launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), &aa);
+        mark(FB_PROF_ATTN, 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
+        mark(FB_PROF_O, 1);
         launch_residual_rmsnorm_q8k(ctx, x, m->y_o.as<float>(), L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
                                     nullptr, c.vocab);
+        mark(FB_PROF_NORM, 1);
         launch_gemv(ctx, L.wgu.t, ah, b, m->y_gu.as<float>(), 2 * F);
+        mark(FB_PROF_GATE_UP, 1);
         launch_swiglu_q8k(ctx, m->y_gu.as<float>(), F, b, af);
+        mark(FB_PROF_SWIGLU, 1);
         launch_gemv(ctx, L.wdown.t, af, b, m->y_d.as<float>(), H);
+        mark(FB_PROF_DOWN, 1);
         const float *gn = (l + 1 < c.n_layers) ? m->layers[l + 1]->attn_norm.as<float>() : m->out_norm.as<float>();
         launch_residual_rmsnorm_q8k(ctx, x, m->y_d.as<float>(), gn, b, H, c.eps, ah, nullptr, nullptr, c.vocab);
+        mark(FB_PROF_NORM, 1);
     }
     launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), c.vocab);
+    mark(FB_PROF_LM_HEAD, 1);
     launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>());
+    mark(FB_PROF_ARGMAX, 1);
+    m->launches_per_step = nl;
 }
 
 // Runs one step; the first call for a batch size runs eagerly and then
 // captures the chain into a CUDA graph for later replays.
+// The step's kernels are issued on the model's private stream (a captured
+// graph cannot live on the legacy default stream), ordered after everything
+// queued on the context stream and joined back to it.
+struct StreamSwap {
+    fb_model *m;
+    cudaStream_t user;
+    explicit StreamSwap(fb_model *mm) : m(mm), user(mm->ctx->stream) {
+        FB_CUDA(cudaEventRecord(m->ev_in, user));
+        FB_CUDA(cudaStreamWaitEvent(m->work, m->ev_in, 0));
+        m->ctx->stream = m->work;
+    }
+    ~StreamSwap() {
+        m->ctx->stream = user;
+        cudaEventRecord(m->ev_out, m->work);
+        cudaStreamWaitEvent(user, m->ev_out, 0);
+    }
+};
+
 static void run_step(fb_model *m, int b) {
     fb_ctx *ctx = m->ctx;
+    StreamSwap swap(m);
     auto it = m->graphs.find(b);
     if (it != m->graphs.end()) {
         FB_CUDA(cudaGraphLaunch(it->second, ctx->stream));
@@ -252,6 +333,9 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         FB_CUDA(cudaMemsetAsync(m->tok.ptr, 0, (size_t)B * 4, ctx->stream));
         FB_CUDA(cudaMemsetAsync(m->pos.ptr, 0, (size_t)B * 4, ctx->stream));
         FB_CUDA(cudaMallocHost(&m->pinned, (size_t)3 * B * 4));
+        FB_CUDA(cudaStreamCreateWithFlags(&m->work, cudaStreamNonBlocking));
+        FB_CUDA(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
+        FB_CUDA(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
         FB_CUDA(cudaStreamSynchronize(ctx->stream));
         *out = m.release();
     });
@@ -515,6 +599,45 @@ int fb_model_weight_bytes(const fb_model *m, int64_t *bytes) {
             add(L.wqkv), add(L.wgu);
         }
         *bytes = tot;
+    });
+}
+
+int fb_model_profile(fb_model *m, const int32_t *tokens_dev, const int32_t *pos_dev, int batch, int steps,
+                     float *ms_out, int *launches_out) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_dev && pos_dev && ms_out, "null argument");
+        require_ready(m);
+        FB_REQUIRE(batch >= 1 && batch <= m->c.max_batch && steps >= 1, "bad batch / steps");
+        cudaStream_t s = m->ctx->stream;
+        StepProbe probe;
+        probe.s = s;
+        const bool pdl = m->ctx->pdl;
+        m->ctx->pdl = false;
+        try {
+            for (int i = 0; i < steps; i++) {
+                FB_CUDA(cudaMemcpyAsync(m->tok.ptr, tokens_dev, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+                FB_CUDA(cudaMemcpyAsync(m->pos.ptr, pos_dev, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
+                step(m, batch, &probe);
+            }
+            probe.collect();
+        } catch (...) {
+            m->ctx->pdl = pdl;
+            throw;
+        }
+        m->ctx->pdl = pdl;
+        for (int k = 0; k < FB_PROF_KINDS; k++) {
+            ms_out[k] = probe.ms[k];
+            if (launches_out) launches_out[k] = probe.launches[k] / steps;
+        }
+    });
+}
+
+int fb_model_launches_per_step(const fb_model *m, int *launches) {
+    return guarded([&] {
+        FB_REQUIRE(m && launches, "null argument");
+        require_ready(m);
+        const int L = m->c.n_layers;
+        *launches = 1 + 10 * L + 2;  // matches step(): embed-norm, 10 per layer, lm_head, argmax
     });
 }
 

@@ -37,8 +37,10 @@ EXPORTED = (
     "fb_swiglu", "fb_attn_decode", "fb_model_create", "fb_model_destroy", "fb_model_set_tensor", "fb_model_synth",
     "fb_model_finalize", "fb_model_forward", "fb_model_decode_greedy", "fb_model_decode_dev", "fb_model_prefill",
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
-    "fb_model_read_activation",
+    "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step",
 )
+
+PROF_KINDS = ("embed_norm", "qkv", "rope_kv", "attn", "o", "norm", "gate_up", "swiglu", "down", "lm_head", "argmax")
 
 
 class FerriteError(RuntimeError):
@@ -109,6 +111,8 @@ def _declare(L):
         "fb_model_read_kv": (i32, [vp, i32, i32, i32, vp]),
         "fb_model_weight_bytes": (i32, [vp, P(i64)]),
         "fb_model_read_activation": (i32, [vp, C.c_char_p, i32, vp, i64]),
+        "fb_model_profile": (i32, [vp, vp, vp, i32, i32, vp, vp]),
+        "fb_model_launches_per_step": (i32, [vp, P(i32)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -326,6 +330,19 @@ class Model:
         out = np.zeros(n, dtype=np.float32)
         _check(lib().fb_model_read_activation(self.h, name.encode(), row, _np(out), n))
         return out
+
+    def profile(self, tok_ptr: int, pos_ptr: int, batch: int, steps: int) -> dict:
+        """Per-kernel-class milliseconds (summed over `steps` eager steps) and
+        launches per step."""
+        ms = np.zeros(len(PROF_KINDS), dtype=np.float32)
+        nl = np.zeros(len(PROF_KINDS), dtype=np.int32)
+        _check(lib().fb_model_profile(self.h, tok_ptr, pos_ptr, batch, steps, _np(ms), _np(nl)))
+        return {k: (float(ms[i]), int(nl[i])) for i, k in enumerate(PROF_KINDS)}
+
+    def launches_per_step(self) -> int:
+        v = C.c_int()
+        _check(lib().fb_model_launches_per_step(self.h, C.byref(v)))
+        return v.value
 
     def weight_bytes(self) -> int:
         v = C.c_int64()

@@ -70,7 +70,9 @@ typedef struct fb_model fb_model;
 /* ------------------------------------------------------------ context --- */
 const char *fb_last_error(void);
 int fb_abi_version(void);
-/* stream: a cudaStream_t (NULL = create a private non-blocking stream). */
+/* stream: the cudaStream_t all work of this context is ordered on, used as
+ * given (NULL = the CUDA default stream).  Model steps replay their CUDA
+ * graph on a private stream joined to this one by events. */
 int fb_ctx_create(int device, void *stream, fb_ctx **out);
 int fb_ctx_destroy(fb_ctx *ctx);
 int fb_ctx_set_stream(fb_ctx *ctx, void *stream);
@@ -194,6 +196,22 @@ int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale);
 int fb_model_read_kv(fb_model *m, int layer, int which, int pos,
                      float *out_host);
 int fb_model_weight_bytes(const fb_model *m, int64_t *bytes);
+/* Kernel classes of one decode step, for fb_model_profile. */
+enum fb_prof_kind {
+    FB_PROF_EMBED_NORM = 0, FB_PROF_QKV = 1, FB_PROF_ROPE_KV = 2, FB_PROF_ATTN = 3,
+    FB_PROF_O = 4, FB_PROF_NORM = 5, FB_PROF_GATE_UP = 6, FB_PROF_SWIGLU = 7,
+    FB_PROF_DOWN = 8, FB_PROF_LM_HEAD = 9, FB_PROF_ARGMAX = 10, FB_PROF_KINDS = 11
+};
+/* Runs `steps` eager decode steps (batch rows, device-resident inputs as in
+ * fb_model_decode_dev) with a CUDA event after every kernel class and writes
+ * the summed milliseconds per class into ms_out[FB_PROF_KINDS] and the
+ * launches per class into launches_out[FB_PROF_KINDS] (per step).  Kernels
+ * run serialised, without PDL overlap. */
+int fb_model_profile(fb_model *m, const int32_t *tokens_dev,
+                     const int32_t *pos_dev, int batch, int steps,
+                     float *ms_out, int *launches_out);
+/* Kernels one decode step launches (graph nodes of the captured step). */
+int fb_model_launches_per_step(const fb_model *m, int *launches);
 /* Diagnostic read of the last decode step's f32 activations of batch row
  * `row` (values of the last layer for per-layer buffers): "x" (residual
  * stream, hidden), "qkv", "q" (after QK-norm + RoPE), "attn" (attention

@@ -204,6 +204,47 @@ def synth_tokens(seed: int, n: int, vocab: int) -> np.ndarray:
     return out
 
 
+# Per-tensor seeds of a random-init model: the convention the product's
+# fb_model_synth uses (seed + 0x1000 * (layer + 1) + kind id, layer = -1 for
+# global tensors).
+KIND_ID = {"token_embd": 1, "output_norm": 2, "output": 3, "attn_norm": 10, "attn_q": 11, "attn_k": 12,
+           "attn_v": 13, "attn_output": 14, "attn_q_norm": 15, "attn_k_norm": 16, "ffn_norm": 17, "ffn_gate": 18,
+           "ffn_up": 19, "ffn_down": 20}
+
+
+def tensor_seed(seed: int, layer: int, name: str) -> int:
+    return (seed + 0x1000 * (layer + 1) + KIND_ID[name]) & 0xFFFFFFFFFFFFFFFF
+
+
+def synth_model_weights(cfg: dict, seed: int) -> dict:
+    """Oracle-side copy of the random-init model (Q4_K linear layers, Q6_K
+    ffn_down and output, f32 norms), generated with the restated generator."""
+    H, F, V = cfg["hidden"], cfg["ffn"], cfg["vocab"]
+    qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+
+    def q4(n, k, s):
+        return (Q4_K, n, k, synth_q4k(s, n * k // 256, 0.02))
+
+    def q6(n, k, s):
+        return (Q6_K, n, k, synth_q6k(s, n * k // 256, 0.02))
+
+    def v(n, s):
+        return (F32, 1, n, synth_f32(s, n, 1.0, 0.02))
+
+    layers = []
+    for l in range(cfg["n_layers"]):
+        def ts(name, l=l):
+            return tensor_seed(seed, l, name)
+        layers.append(dict(
+            attn_norm=v(H, ts("attn_norm")), wq=q4(qd, H, ts("attn_q")), wk=q4(kd, H, ts("attn_k")),
+            wv=q4(kd, H, ts("attn_v")), wo=q4(H, qd, ts("attn_output")), q_norm=v(cfg["head_dim"], ts("attn_q_norm")),
+            k_norm=v(cfg["head_dim"], ts("attn_k_norm")), ffn_norm=v(H, ts("ffn_norm")),
+            w_gate=q4(F, H, ts("ffn_gate")), w_up=q4(F, H, ts("ffn_up")), w_down=q6(H, F, ts("ffn_down"))))
+    return dict(tok_embd=q4(V, H, tensor_seed(seed, -1, "token_embd")),
+                out_norm=v(H, tensor_seed(seed, -1, "output_norm")),
+                output=q6(V, H, tensor_seed(seed, -1, "output")), layers=layers)
+
+
 # ------------------------------------------------------------------ model --
 class Model:
     """Oracle quantized Llama/Qwen3 model over caller-supplied weight arrays.

@@ -95,30 +95,7 @@ def load_into_device_model(model, weights: dict):
 
 def synth_weights(cfg: dict, seed: int) -> dict:
     """Oracle-side copy of fb_model_synth's random-init tensors."""
-    from ferrite_b200 import tensor_seed  # pure-python helper, no library load
-    H, F, V = cfg["hidden"], cfg["ffn"], cfg["vocab"]
-    qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
-
-    def q4(n, k, s):
-        return (O.Q4_K, n, k, O.synth_q4k(s, n * k // 256, 0.02))
-
-    def q6(n, k, s):
-        return (O.Q6_K, n, k, O.synth_q6k(s, n * k // 256, 0.02))
-
-    def v(n, s):
-        return (O.F32, 1, n, O.synth_f32(s, n, 1.0, 0.02))
-
-    layers = []
-    for l in range(cfg["n_layers"]):
-        ts = lambda name: tensor_seed(seed, l, name)  # noqa: E731
-        layers.append(dict(
-            attn_norm=v(H, ts("attn_norm")), wq=q4(qd, H, ts("attn_q")), wk=q4(kd, H, ts("attn_k")),
-            wv=q4(kd, H, ts("attn_v")), wo=q4(H, qd, ts("attn_output")), q_norm=v(cfg["head_dim"], ts("attn_q_norm")),
-            k_norm=v(cfg["head_dim"], ts("attn_k_norm")), ffn_norm=v(H, ts("ffn_norm")),
-            w_gate=q4(F, H, ts("ffn_gate")), w_up=q4(F, H, ts("ffn_up")), w_down=q6(H, F, ts("ffn_down"))))
-    return dict(tok_embd=q4(V, H, tensor_seed(seed, -1, "token_embd")),
-                out_norm=v(H, tensor_seed(seed, -1, "output_norm")),
-                output=q6(V, H, tensor_seed(seed, -1, "output")), layers=layers)
+    return O.synth_model_weights(cfg, seed)
 
 
 @pytest.fixture(scope="session")

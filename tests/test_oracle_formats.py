@@ -159,3 +159,12 @@ def test_exp64_accuracy():
     ok = np.abs(got - ref) <= 2 * np.spacing(ref)
     assert ok.all(), xs[~ok][:5]
     assert O.lib().or_exp64(-800.0) == 0.0 and O.lib().or_exp64(800.0) == np.inf
+
+
+def test_tensor_seed_convention_matches_product():
+    """The oracle's per-tensor seed convention equals the product's
+    (ferrite_b200.tensor_seed, used by fb_model_synth)."""
+    import ferrite_b200 as fb
+    for layer in (-1, 0, 5, 35):
+        for name in O.KIND_ID:
+            assert O.tensor_seed(99, layer, name) == fb.tensor_seed(99, layer, name)
