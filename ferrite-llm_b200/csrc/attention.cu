@@ -27,6 +27,8 @@
 // ERRBIT_WAIT_TIMEOUT in the context's error word and returns.
 #include <math.h>
 
+#include <mutex>
+
 #include "fb_internal.h"
 #include "kq_common.cuh"
 
@@ -417,4 +419,89 @@ void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A0, int batch, int max_seq_
     FB_CUDA(cudaLaunchKernelEx(&cfg, k_attn_combine, A, out_f32, q, aq ? 1 : 0));
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention (fb_attn_decode_noalloc).
+//
+// fb_attn_decode takes its split-K scratch (partial sums and maxima of every
+// split) from the context's workspace, which is grown with cudaMalloc and a
+// stream synchronisation on first use.  Some callers cannot allow that: code
+// running under a caching or pooled device allocator that forbids direct
+// cudaMalloc/cudaFree (ferrite-os routes device allocations through its own
+// TLSF pool), and latency-critical loops that must never take the implicit
+// device synchronisation cudaMalloc/cudaFree may cause.  For them this entry
+// point keeps the scratch in a fixed, file-scope device array instead.
+//
+// The array is a `static __device__` object: every GPU that loads the library
+// holds it until the process exits.  Host code cannot use the array's name as
+// a device address (it is a host-side stand-in), so its device address is
+// looked up per device with cudaGetSymbolAddress, with that device current,
+// the first time the entry point runs on it; that first call should therefore
+// come before any stream capture.  All calls on a device share the one array:
+// calls that overlap on the GPU (two streams, or two contexts of one device)
+// race on it.  Nothing in it must start at zero: every slot a call reads is
+// written by the same call first.
+constexpr size_t kAttnNoAllocScratchBytes = (size_t)4 << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kAttnNoAllocScratchBytes];
+
+static void *noalloc_scratch_address(int device) {
+    static std::mutex mu;
+    static void *addr[128] = {nullptr};
+    FB_REQUIRE(device >= 0 && device < 128, "attn_decode_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[device]) {
+        int cur = 0;
+        FB_CUDA(cudaGetDevice(&cur));
+        if (cur != device) FB_CUDA(cudaSetDevice(device));
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (cur != device) cudaSetDevice(cur);
+        FB_CUDA(e);
+        addr[device] = p;
+    }
+    return addr[device];
+}
+
 }  // namespace fb
+
+extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
+                                      const void *v_pages_dev, const int32_t *block_table_dev,
+                                      const int32_t *seq_lens_dev, float *out_dev, int batch, int n_heads,
+                                      int n_kv_heads, int head_dim, int page_size, int max_pages,
+                                      int max_seq_len, float scale) {
+    using namespace fb;
+    return guarded([&] {
+        FB_REQUIRE(ctx && q_dev && k_pages_dev && v_pages_dev && block_table_dev && seq_lens_dev && out_dev,
+                   "null argument");
+        FB_REQUIRE(head_dim == 128, "head_dim must be 128");
+        FB_REQUIRE(page_size == 32 || page_size == 64, "page_size must be 32 or 64");
+        FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
+                   "bad shape");
+        FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
+        const int nsplit = (max_seq_len + 2 * page_size - 1) / (2 * page_size);
+        const size_t need = (size_t)batch * n_heads * nsplit * (head_dim + 2) * sizeof(double);
+        if (need > kAttnNoAllocScratchBytes)
+            fail(FB_ERR_INVALID, "attn_decode_noalloc: batch * n_heads * ceil(max_seq_len / (2 * page_size)) * " +
+                                     std::to_string((head_dim + 2) * sizeof(double)) + " bytes = " +
+                                     std::to_string(need) + " exceeds the fixed " +
+                                     std::to_string(kAttnNoAllocScratchBytes) + "-byte scratch");
+        double *base = static_cast<double *>(noalloc_scratch_address(ctx->device));
+        AttnArgs A{};
+        A.q = q_dev;
+        A.kpool = k_pages_dev;
+        A.vpool = v_pages_dev;
+        A.block_table = block_table_dev;
+        A.seq_lens = seq_lens_dev;
+        A.pos = nullptr;
+        A.part_o = base;
+        A.part_ml = base + (size_t)batch * n_heads * nsplit * head_dim;
+        A.n_heads = n_heads;
+        A.n_kv = n_kv_heads;
+        A.page_size = page_size;
+        A.max_pages = max_pages;
+        A.num_pages = 0x7fffffff;
+        A.nsplit_max = nsplit;
+        A.scale = scale;
+        A.err = ctx->err_word;
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr);
+    });
+}

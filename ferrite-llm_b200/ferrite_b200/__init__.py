@@ -37,7 +37,7 @@ EXPORTED = (
     "fb_swiglu", "fb_attn_decode", "fb_model_create", "fb_model_destroy", "fb_model_set_tensor", "fb_model_synth",
     "fb_model_finalize", "fb_model_forward", "fb_model_decode_greedy", "fb_model_decode_dev", "fb_model_prefill",
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
-    "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step",
+    "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
 )
 
 PROF_KINDS = ("embed_norm", "qkv", "rope_kv", "attn", "o", "norm", "gate_up", "swiglu", "down", "lm_head", "argmax")
@@ -97,6 +97,7 @@ def _declare(L):
         "fb_rope": (i32, [vp, vp, i64, i64, i64, i64, f32, i32]),
         "fb_swiglu": (i32, [vp, vp, vp, vp, i64, i64]),
         "fb_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32]),
+        "fb_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32]),
         "fb_model_create": (i32, [vp, P(ModelConfig), P(vp)]),
         "fb_model_destroy": (i32, [vp]),
         "fb_model_set_tensor": (i32, [vp, C.c_char_p, i32, i32, i64, i64, vp]),
@@ -253,6 +254,14 @@ def attn_decode(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, ba
                 page_size, max_pages, max_seq_len, scale):
     _check(lib().fb_attn_decode(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
                                 head_dim, page_size, max_pages, max_seq_len, scale))
+
+
+def attn_decode_noalloc(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
+                        head_dim, page_size, max_pages, max_seq_len, scale):
+    """fb_attn_decode without any device allocation (fixed 4 MiB scratch in
+    the library's device image; see include/ferrite_b200.h)."""
+    _check(lib().fb_attn_decode_noalloc(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
+                                        head_dim, page_size, max_pages, max_seq_len, scale))
 
 
 # GGUF tensor names of one layer / of the whole model.

@@ -149,6 +149,27 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
                    int n_heads, int n_kv_heads, int head_dim, int page_size,
                    int max_pages, int max_seq_len, float scale);
 
+/* Same computation and arguments as fb_attn_decode, for callers that cannot
+ * allocate device memory: no reference counterpart (the reference's candle
+ * path allocates freely).  fb_attn_decode grows a workspace with cudaMalloc
+ * (plus a stream synchronisation) on first use; code that runs under a pooled
+ * or hooked device allocator that forbids direct cudaMalloc/cudaFree, or in a
+ * loop that must not take the synchronisation those calls can imply, uses
+ * this entry point instead.  It allocates nothing: its split-K scratch is a
+ * fixed 4 MiB array in the library's device image, so it accepts
+ * batch * n_heads * ceil(max_seq_len / (2 * page_size)) * (head_dim + 2) * 8
+ * bytes <= 4 MiB (e.g. 32 heads at 8192 tokens for batch 1) and returns
+ * FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
+ * device address (make that first call before any stream capture).  All calls
+ * on a device share the array, so calls that overlap on the GPU race. */
+int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,
+                           const void *k_pages_dev, const void *v_pages_dev,
+                           const int32_t *block_table_dev,
+                           const int32_t *seq_lens_dev, float *out_dev,
+                           int batch, int n_heads, int n_kv_heads,
+                           int head_dim, int page_size, int max_pages,
+                           int max_seq_len, float scale);
+
 /* -------------------------------------------------------------- model --- */
 typedef struct {
     int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
