@@ -34,42 +34,6 @@
 
 namespace fb {
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (~1 s of SM clock).  Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > 2000000000LL) return false;
-    }
-    return true;
-}
-
 constexpr int ATT_HD = 128;
 constexpr int ATT_WARPS = 4;
 
@@ -77,89 +41,103 @@ __device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
     return A.seq_lens ? A.seq_lens[b] : A.pos[b] + 1;
 }
 
-// Dynamic shared memory: K[2*page][hd] half, V[2*page][hd] half,
-// q[G][hd] f32, s[G][2*page] f32, p[G][2*page] f64, red[ATT_WARPS][G][hd] f64.
+__device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
+                                                   int64_t blk);
+
+// One CTA per (kv head, page of the sequence, sequence).  Dynamic shared
+// memory: K[page][hd] half, V[page][hd] half, q[G][hd] f32, s[G][page] f32,
+// p[G][page] f64, red[ATT_WARPS][G][hd] f64.  The last CTA of each (sequence,
+// kv head) to finish merges all pages' partials (fixed order) and writes the
+// G heads' output (f32 and/or Q8_K); the per-(sequence, kv head) counters
+// return to zero afterwards.
 //
 // Numerics (identical to the CPU oracle up to binary64 rounding):
 //   s_t = f32(sum_e q_e * k_te in binary64) * scale
-//   per split: m = max_t s_t, p_t = exp64(s_t - m), l = sum p_t,
+//   per page:  m = max_t s_t, p_t = exp64(s_t - m), l = sum p_t,
 //              o = sum p_t v_t              (binary64)
-//   combine:   M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
+//   merge:     M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
 template <int G>
-__global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
+__global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq,
+                                                                int use_q8, int *__restrict__ counters) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bars[4];  // K page 0, K page 1, V page 0, V page 1
+    __shared__ uint64_t bars[2];  // K page, V page
+    __shared__ int s_last;
+    __shared__ double s_M[G], s_L[G];
     const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int P = A.page_size, ST = 2 * P;
-    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int P = A.page_size;
+    // sequence lengths are inputs of the whole step (written before it began)
     const int len = seq_len_of(A, b);
-    const int t0 = split * ST;
+    const int t0 = split * P;
     if (t0 >= len) {
         pdl_launch();
         return;
     }
-    const int ntok = min(ST, len - t0);
+    const int nsplit = (len + P - 1) / P;
+    const int ntok = min(P, len - t0);
     __half *Ks = reinterpret_cast<__half *>(smem);
-    __half *Vs = Ks + (size_t)ST * ATT_HD;
-    float *qs = reinterpret_cast<float *>(Vs + (size_t)ST * ATT_HD);
+    __half *Vs = Ks + (size_t)P * ATT_HD;
+    float *qs = reinterpret_cast<float *>(Vs + (size_t)P * ATT_HD);
     float *ss = qs + G * ATT_HD;
-    double *ps = reinterpret_cast<double *>(ss + G * ST);
-    double *red = ps + G * ST;
+    double *ps = reinterpret_cast<double *>(ss + G * P);
+    double *red = ps + G * P;
     const uint32_t page_bytes = (uint32_t)P * ATT_HD * 2;
-    const int npages = (ntok + P - 1) / P;  // 1 or 2
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < 4; i++) mbar_init(&bars[i], 1);
+    // the page holding the newest position is written by the preceding kernel
+    const bool fresh = t0 + P >= len;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int j = 0; j < npages; j++) {
-            const int lp = t0 / P + j;
-            int page = lp < A.max_pages ? A.block_table[(int64_t)b * A.max_pages + lp] : -1;
-            if (page < 0 || page >= A.num_pages) {
-                atomicOr(A.err, ERRBIT_BAD_PAGE);
-                page = -1;
-            }
-            if (page >= 0) {
-                const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
-                mbar_expect_tx(&bars[j], page_bytes);
-                bulk_g2s(Ks + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes,
-                         &bars[j]);
-                mbar_expect_tx(&bars[2 + j], page_bytes);
-                bulk_g2s(Vs + (size_t)j * P * ATT_HD, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes,
-                         &bars[2 + j]);
-            } else {
-                // complete the phases without data (the error word is set)
-                mbar_expect_tx(&bars[j], 0);
-                mbar_expect_tx(&bars[2 + j], 0);
-            }
+    int page = -1;
+    if (tid == 0) {
+        page = split < A.max_pages ? A.block_table[(int64_t)b * A.max_pages + split] : -1;
+        if (page < 0 || page >= A.num_pages) {
+            atomicOr(A.err, ERRBIT_BAD_PAGE);
+            page = -1;
         }
     }
-    // q of the G heads of this kv head (already RoPE'd)
+    auto issue = [&]() {
+        if (page >= 0) {
+            const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
+            mbar_expect_tx(&bars[0], page_bytes);
+            bulk_g2s(Ks, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes, &bars[0]);
+            mbar_expect_tx(&bars[1], page_bytes);
+            bulk_g2s(Vs, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes, &bars[1]);
+        } else {
+            // complete the phases without data (the error word is set)
+            mbar_expect_tx(&bars[0], 0);
+            mbar_expect_tx(&bars[1], 0);
+        }
+    };
+    if (tid == 0 && !fresh) issue();  // older pages stream in before the wait
+    pdl_wait();
+    if (tid == 0 && fresh) issue();
     const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
-    for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) qs[i] = qg[i];
+    for (int i = tid; i < G * ATT_HD; i += blockDim.x) qs[i] = qg[i];
     __syncthreads();
 
-    // ---- scores: warp w handles tokens [32w, 32w+32) of the split
+    // ---- scores: warp w handles tokens [WT*w, WT*w + WT) of the page
     constexpr int TCH = 32 / G;  // tokens per reduce-scatter chunk
-    const int tw0 = warp * 32;
+    const int WT = P / ATT_WARPS;
+    const int tw0 = warp * WT;
     bool waited_ok = true;
     if (tw0 < ntok) {
-        waited_ok = mbar_wait_bounded(&bars[tw0 / P], 0);
+        waited_ok = mbar_wait_bounded(&bars[0], 0);
         float qv[G][4];
 #pragma unroll
         for (int g = 0; g < G; g++)
 #pragma unroll
             for (int e = 0; e < 4; e++) qv[g][e] = qs[g * ATT_HD + 4 * lane + e];
+        const int nch = WT > TCH ? WT / TCH : 1;
 #pragma unroll 1
-        for (int c = 0; c < G; c++) {
+        for (int c = 0; c < nch; c++) {
             const int tc0 = tw0 + c * TCH;
             double v[32];
 #pragma unroll
             for (int t = 0; t < TCH; t++) {
-                const int tok = tc0 + t;
+                const int tok = tc0 + t;  // rows past the page are masked below
                 const uint2 kr = *reinterpret_cast<const uint2 *>(Ks + (size_t)tok * ATT_HD + 4 * lane);
                 const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
                 const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
@@ -185,23 +163,23 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
                 }
             }
             const int t = lane / G, g = lane % G;
-            const int tok = tc0 + t;
-            ss[g * ST + tok] = tok < ntok ? __fmul_rn(__double2float_rn(v[0]), A.scale) : -INFINITY;
+            const int tl = c * TCH + t, tok = tw0 + tl;
+            if (tl < WT) ss[g * P + tok] = tok < ntok ? __fmul_rn(__double2float_rn(v[0]), A.scale) : -INFINITY;
         }
     }
     __syncthreads();
-    // ---- per-head split max and p_t = exp(s_t - max) (one warp per head)
-    double *ml = red;  // [G][2] before the PV reduction reuses red
+    // ---- per-head page max and p_t = exp(s_t - max) (warps take heads)
+    double *ml = red;  // [G][2] before the P.V reduction reuses red
     for (int g = warp; g < G; g += ATT_WARPS) {
         float mx = -INFINITY;
-        for (int t = lane; t < ntok; t += 32) mx = fmaxf(mx, ss[g * ST + t]);
+        for (int t = lane; t < ntok; t += 32) mx = fmaxf(mx, ss[g * P + t]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         double sum = 0.0;
-        for (int t = lane; t < ST; t += 32) {
-            const double p = t < ntok ? exp64(__dsub_rn((double)ss[g * ST + t], (double)mx)) : 0.0;
-            ps[g * ST + t] = p;
-            sum = __dadd_rn(sum, p);
+        for (int t = lane; t < P; t += 32) {
+            const double pv = t < ntok ? exp64(__dsub_rn((double)ss[g * P + t], (double)mx)) : 0.0;
+            ps[g * P + t] = pv;
+            sum = __dadd_rn(sum, pv);
         }
         sum = warp_sum64(sum);
         if (lane == 0) {
@@ -217,93 +195,128 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(AttnArgs A) {
         mls[g][1] = ml[2 * g + 1];
     }
     __syncthreads();
-    // ---- o = sum_t p_t * v_t; warp w over tokens [32w, 32w+32), lane owns 4 dims
+    // ---- o = sum_t p_t * v_t; warp w over its tokens, lane owns 4 dims
     double o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) o[g][e] = 0.0;
     if (tw0 < ntok) {
-        waited_ok = mbar_wait_bounded(&bars[2 + tw0 / P], 0) && waited_ok;
-        const int tend = min(tw0 + 32, ntok);
+        waited_ok = mbar_wait_bounded(&bars[1], 0) && waited_ok;
+        const int tend = min(tw0 + WT, ntok);
         for (int tok = tw0; tok < tend; tok++) {
             const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)tok * ATT_HD + 4 * lane);
             const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
             const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const double p = ps[g * ST + tok];
-                o[g][0] = __dadd_rn(o[g][0], __dmul_rn(p, (double)v01.x));
-                o[g][1] = __dadd_rn(o[g][1], __dmul_rn(p, (double)v01.y));
-                o[g][2] = __dadd_rn(o[g][2], __dmul_rn(p, (double)v23.x));
-                o[g][3] = __dadd_rn(o[g][3], __dmul_rn(p, (double)v23.y));
+                const double pg = ps[g * P + tok];
+                o[g][0] = __dadd_rn(o[g][0], __dmul_rn(pg, (double)v01.x));
+                o[g][1] = __dadd_rn(o[g][1], __dmul_rn(pg, (double)v01.y));
+                o[g][2] = __dadd_rn(o[g][2], __dmul_rn(pg, (double)v23.x));
+                o[g][3] = __dadd_rn(o[g][3], __dmul_rn(pg, (double)v23.y));
             }
         }
     }
     if (!waited_ok) {
         atomicOr(A.err, ERRBIT_WAIT_TIMEOUT);
-        // let any copy still in flight land before the CTA's shared memory
-        // is released (bounded as well)
-        for (int j = 0; j < npages; j++) {
-            mbar_wait_bounded(&bars[j], 0);
-            mbar_wait_bounded(&bars[2 + j], 0);
-        }
+        // let any copy still in flight land before shared memory is released
+        mbar_wait_bounded(&bars[0], 0);
+        mbar_wait_bounded(&bars[1], 0);
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
     __syncthreads();
-    for (int i = threadIdx.x; i < G * ATT_HD; i += blockDim.x) {
+    for (int i = tid; i < G * ATT_HD; i += blockDim.x) {
         const int g = i / ATT_HD, d = i % ATT_HD;
-        double s = 0.0;
+        double sum = 0.0;
 #pragma unroll
-        for (int w = 0; w < ATT_WARPS; w++) s = __dadd_rn(s, red[(w * G + g) * ATT_HD + d]);
+        for (int w = 0; w < ATT_WARPS; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
         const int64_t hrow = ((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * A.nsplit_max + split;
-        A.part_o[hrow * ATT_HD + d] = s;
+        A.part_o[hrow * ATT_HD + d] = sum;
         if (d == 0) {
             A.part_ml[2 * hrow] = mls[g][0];
             A.part_ml[2 * hrow + 1] = mls[g][1];
         }
     }
-    pdl_launch();
-}
-
-// Merge the splits of each head.  One CTA per (256-value block of the
-// [n_heads * hd] output row, sequence); out_q8 != null quantizes the block to
-// Q8_K (input of the output projection), out_f32 != null stores f32.
-__device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
-                                                   int64_t blk);
-
-__global__ void __launch_bounds__(256) k_attn_combine(AttnArgs A, float *__restrict__ out_f32, Q8Act aq,
-                                                      int use_q8) {
-    pdl_wait();
-    const int blk = blockIdx.x, b = blockIdx.y;
-    const int len = seq_len_of(A, b);
-    const int nsplit = (len + 2 * A.page_size - 1) / (2 * A.page_size);
-    const int tid = threadIdx.x;
-    const int i = blk * 256 + tid;  // value index in [n_heads * hd]
-    const int h = i / ATT_HD, d = i % ATT_HD;
-    const int64_t hbase = ((int64_t)b * A.n_heads + h) * A.nsplit_max;
-    double M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmax(M, A.part_ml[2 * (hbase + s)]);
-    double L = 0.0, acc = 0.0;
-    for (int s = 0; s < nsplit; s++) {
-        const double w = exp64(__dsub_rn(A.part_ml[2 * (hbase + s)], M));
-        L = __dadd_rn(L, __dmul_rn(A.part_ml[2 * (hbase + s) + 1], w));
-        acc = __dadd_rn(acc, __dmul_rn(A.part_o[(hbase + s) * ATT_HD + d], w));
+    // ---- the last page CTA of this (sequence, kv head) merges all pages
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        int *cnt = counters + (int64_t)b * A.n_kv + kvh;
+        const int prev = atomicAdd(cnt, 1);
+        s_last = prev == nsplit - 1;
+        if (s_last) *cnt = 0;  // ready for the next step
     }
-    const float val = __double2float_rn(__ddiv_rn(acc, L));
-    if (out_f32) out_f32[(int64_t)b * A.n_heads * ATT_HD + i] = val;
+    __syncthreads();
+    if (!s_last) {
+        pdl_launch();
+        return;
+    }
+    __threadfence();
+    const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * A.nsplit_max;
+    double *wts = reinterpret_cast<double *>(smem);  // [G][nsplit], reuses the K/V area
+    for (int g = warp; g < G; g += ATT_WARPS) {
+        const int64_t hb = hb0 + (int64_t)g * A.nsplit_max;
+        double M = -INFINITY;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmax(M, __ldcg(&A.part_ml[2 * (hb + s2)]));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(0xffffffffu, M, off));
+        double L = 0.0;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) {
+            const double w = exp64(__dsub_rn(__ldcg(&A.part_ml[2 * (hb + s2)]), M));
+            wts[g * nsplit + s2] = w;
+            L = __dadd_rn(L, __dmul_rn(__ldcg(&A.part_ml[2 * (hb + s2) + 1]), w));
+        }
+        L = warp_sum64(L);
+        if (lane == 0) {
+            s_M[g] = M;
+            s_L[g] = L;
+        }
+    }
+    __syncthreads();
+    float *vals = qs;  // [G][hd] outputs, reuses the q area
+    // each thread owns G outputs (one per head: index tid + 128 g when hd =
+    // 128 = blockDim); 16 pages of all G heads are loaded per batch so the L2
+    // round trips overlap
+    {
+        const int d = tid;  // blockDim.x == ATT_HD
+        double acc[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[g] = 0.0;
+        constexpr int UB = G >= 8 ? 8 : 16;
+        for (int s0 = 0; s0 < nsplit; s0 += UB) {
+            double v[G][UB];
+#pragma unroll
+            for (int g = 0; g < G; g++)
+#pragma unroll
+                for (int u = 0; u < UB; u++)
+                    v[g][u] = s0 + u < nsplit
+                                  ? __ldcg(&A.part_o[(hb0 + (int64_t)g * A.nsplit_max + s0 + u) * ATT_HD + d])
+                                  : 0.0;
+#pragma unroll
+            for (int g = 0; g < G; g++)
+#pragma unroll
+                for (int u = 0; u < UB; u++)
+                    if (s0 + u < nsplit) acc[g] = __dadd_rn(acc[g], __dmul_rn(v[g][u], wts[g * nsplit + s0 + u]));
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float val = __double2float_rn(__ddiv_rn(acc[g], s_L[g]));
+            vals[g * ATT_HD + d] = val;
+            if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
+        }
+    }
     if (use_q8) {
-        __shared__ float vals[256];
-        vals[tid] = val;
         __syncthreads();
-        if (tid < 32) {
+        // G*hd values = G/2 Q8_K blocks of the [n_heads*hd] row
+        for (int blk = warp; blk < G / 2; blk += ATT_WARPS) {
             float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = vals[8 * tid + e];
-            q8k_store_warp_ext(v, tid, aq, b, blk);
+            for (int e = 0; e < 8; e++) v[e] = vals[blk * 256 + 8 * lane + e];
+            q8k_store_warp_ext(v, lane, aq, b, (int64_t)kvh * G / 2 + blk);
         }
     }
     pdl_launch();
@@ -359,43 +372,44 @@ __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane
 }
 
 size_t attn_smem_bytes(int G, int page_size) {
-    const int ST = 2 * page_size;
-    return (size_t)2 * ST * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * ST * 4 + (size_t)G * ST * 8 +
+    const size_t P = (size_t)page_size;
+    return 2 * P * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * P * 4 + (size_t)G * P * 8 +
            (size_t)ATT_WARPS * G * ATT_HD * 8;
 }
 
-template <typename K>
-static void launch_ex(fb_ctx *ctx, K kernel, dim3 grid, dim3 block, size_t smem, AttnArgs A) {
+// Paged decode attention with the page merge fused in.  `counters` holds
+// batch * n_kv int32 that are zero on entry and zero again on exit.  out_f32
+// and/or (aq != null, needs an even GQA group) receive the result.
+void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32, const Q8Act *aq,
+                        int *counters, bool pdl) {
+    const int G = A.n_heads / A.n_kv;
+    FB_REQUIRE(A.n_heads % A.n_kv == 0, "attn: n_heads must be a multiple of n_kv_heads");
+    FB_REQUIRE(A.page_size == 32 || A.page_size == 64, "attn: page_size must be 32 or 64");
+    FB_REQUIRE(!aq || G % 2 == 0, "attn: fused Q8_K output needs an even GQA group");
+    const int nsplit = (max_seq_len + A.page_size - 1) / A.page_size;
+    FB_REQUIRE(nsplit <= A.nsplit_max, "attn: max_seq_len exceeds the split scratch");
+    const size_t smem = attn_smem_bytes(G, A.page_size);
+    FB_REQUIRE((size_t)G * nsplit * 8 <= (size_t)2 * A.page_size * ATT_HD * 2,
+               "attn: max_seq_len too long for the in-kernel page merge");
+    dim3 grid(A.n_kv, nsplit, batch);
+    Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    // older KV pages are read before griddepcontrol.wait: only valid when the
+    // preceding kernel is one of this library's (the model's decode step)
+    attr[0].val.programmaticStreamSerializationAllowed = (ctx->pdl && pdl) ? 1 : 0;
     cfg.gridDim = grid;
-    cfg.blockDim = block;
+    cfg.blockDim = dim3(ATT_WARPS * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, A));
-}
-
-// Split pass + combine.  out_f32 and/or (use_q8, aq) receive the result.
-void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A0, int batch, int max_seq_len, float *out_f32,
-                        const Q8Act *aq) {
-    AttnArgs A = A0;
-    const int G = A.n_heads / A.n_kv;
-    FB_REQUIRE(A.n_heads % A.n_kv == 0, "attn: n_heads must be a multiple of n_kv_heads");
-    FB_REQUIRE(A.page_size >= 16 && A.page_size <= 64 && A.page_size % 16 == 0,
-               "attn: page_size must be 16, 32, 48 or 64");
-    const int nsplit = (max_seq_len + 2 * A.page_size - 1) / (2 * A.page_size);
-    FB_REQUIRE(nsplit <= A.nsplit_max, "attn: max_seq_len exceeds the split scratch");
-    const size_t smem = attn_smem_bytes(G, A.page_size);
-    dim3 grid(A.n_kv, nsplit, batch);
     switch (G) {
-#define FB_ATT_CASE(GG)                                                                                     \
-    case GG:                                                                                                \
-        FB_CUDA(cudaFuncSetAttribute(k_attn_split<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-        launch_ex(ctx, k_attn_split<GG>, grid, dim3(ATT_WARPS * 32), smem, A);                              \
+#define FB_ATT_CASE(GG)                                                                                           \
+    case GG:                                                                                                      \
+        FB_CUDA(cudaFuncSetAttribute(k_attn_decode<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        FB_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<GG>, A, out_f32, q, aq ? 1 : 0, counters));              \
         break;
         FB_ATT_CASE(1)
         FB_ATT_CASE(2)
@@ -405,18 +419,6 @@ void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A0, int batch, int max_seq_
     default:
         fail(FB_ERR_INVALID, "attn: GQA group size must be 1, 2, 4 or 8");
     }
-    FB_REQUIRE((A.n_heads * ATT_HD) % 256 == 0, "attn: n_heads * head_dim must be a multiple of 256");
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
-    cfg.gridDim = dim3((A.n_heads * ATT_HD) / 256, batch);
-    cfg.blockDim = dim3(256);
-    cfg.stream = ctx->stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
-    FB_CUDA(cudaLaunchKernelEx(&cfg, k_attn_combine, A, out_f32, q, aq ? 1 : 0));
 }
 
 // ---------------------------------------------------------------------------
@@ -438,8 +440,9 @@ void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A0, int batch, int max_seq_
 // the first time the entry point runs on it; that first call should therefore
 // come before any stream capture.  All calls on a device share the one array:
 // calls that overlap on the GPU (two streams, or two contexts of one device)
-// race on it.  Nothing in it must start at zero: every slot a call reads is
-// written by the same call first.
+// race on it.  The partial sums need no clearing (every slot a call reads is
+// written by the same call first); the page-merge counters at its start must
+// be zero, so each call clears them (cudaMemsetAsync, no allocation).
 constexpr size_t kAttnNoAllocScratchBytes = (size_t)4 << 20;  // 4 MiB
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kAttnNoAllocScratchBytes];
 
@@ -477,14 +480,19 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
-        const int nsplit = (max_seq_len + 2 * page_size - 1) / (2 * page_size);
-        const size_t need = (size_t)batch * n_heads * nsplit * (head_dim + 2) * sizeof(double);
+        const int nsplit = (max_seq_len + page_size - 1) / page_size;
+        const size_t cnt_bytes = ((size_t)batch * n_kv_heads * sizeof(int) + 255) & ~(size_t)255;
+        const size_t need = (size_t)batch * n_heads * nsplit * (head_dim + 2) * sizeof(double) + cnt_bytes;
         if (need > kAttnNoAllocScratchBytes)
-            fail(FB_ERR_INVALID, "attn_decode_noalloc: batch * n_heads * ceil(max_seq_len / (2 * page_size)) * " +
+            fail(FB_ERR_INVALID, "attn_decode_noalloc: batch * n_heads * ceil(max_seq_len / page_size) * " +
                                      std::to_string((head_dim + 2) * sizeof(double)) + " bytes = " +
-                                     std::to_string(need) + " exceeds the fixed " +
+                                     std::to_string(need) + " (with the merge counters) exceeds the fixed " +
                                      std::to_string(kAttnNoAllocScratchBytes) + "-byte scratch");
-        double *base = static_cast<double *>(noalloc_scratch_address(ctx->device));
+        uint8_t *raw = static_cast<uint8_t *>(noalloc_scratch_address(ctx->device));
+        int *counters = reinterpret_cast<int *>(raw);
+        // the merge counters must start at zero; the partials need no clearing
+        FB_CUDA(cudaMemsetAsync(counters, 0, cnt_bytes, ctx->stream));
+        double *base = reinterpret_cast<double *>(raw + cnt_bytes);
         AttnArgs A{};
         A.q = q_dev;
         A.kpool = k_pages_dev;
@@ -502,6 +510,6 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         A.nsplit_max = nsplit;
         A.scale = scale;
         A.err = ctx->err_word;
-        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr);
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false);
     });
 }

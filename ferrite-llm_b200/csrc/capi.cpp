@@ -50,10 +50,10 @@ void *fb_ctx::ensure_scratch(size_t n) {
 }
 
 size_t fb_qtensor::device_bytes(int dtype, int64_t n, int64_t k) {
-    const int64_t nb = k / 256;
+    const int64_t nb = k / 256, np = (n + 15) / 16 * 16;  // tile-major, rows padded to 16
     switch (dtype) {
-    case FB_Q4_K: return (size_t)(n * nb) * 144;
-    case FB_Q6_K: return (size_t)(n * nb) * 210;  // 208-byte blocks + fp16 d array
+    case FB_Q4_K: return (size_t)(np * nb) * 144;
+    case FB_Q6_K: return (size_t)(np * nb) * 210;
     case FB_F32: return (size_t)(n * k) * 4;
     default: return 0;
     }
@@ -163,6 +163,7 @@ static fb_qtensor *new_qtensor(fb_ctx *ctx, int dtype, int64_t n, int64_t k, con
     } else {
         DevBuf staging;
         const void *gsrc = src;
+        if (t->n_pad() != n) FB_CUDA(cudaMemsetAsync(t->buf.ptr, 0, bytes, ctx->stream));  // zero pad rows
         if (kind == cudaMemcpyHostToDevice) {
             staging.alloc(gguf_bytes(dtype, n, k));
             FB_CUDA(cudaMemcpyAsync(staging.ptr, src, staging.bytes, kind, ctx->stream));
@@ -213,29 +214,23 @@ int fb_qtensor_concat_rows(fb_ctx *ctx, const fb_qtensor *const *parts, int npar
             FB_REQUIRE(parts[i] && parts[i]->dtype == dtype && parts[i]->k == k, "concat: dtype and k must match");
             n += parts[i]->n;
         }
+        for (int i = 0; i + 1 < nparts; i++)
+            FB_REQUIRE(dtype == FB_F32 || parts[i]->n % 16 == 0,
+                       "concat: all parts but the last need a multiple of 16 rows");
         auto t = std::make_unique<fb_qtensor>();
         t->dtype = dtype;
         t->n = n;
         t->k = k;
         t->buf.alloc(fb_qtensor::device_bytes(dtype, n, k));
-        const int64_t nb = k / 256;
-        size_t off_main = 0, off_d = 0;
+        if (t->buf.bytes) FB_CUDA(cudaMemsetAsync(t->buf.ptr, 0, t->buf.bytes, ctx->stream));
+        size_t off = 0;
         for (int i = 0; i < nparts; i++) {
             const fb_qtensor *p = parts[i];
-            if (dtype == FB_Q6_K) {
-                const size_t mb = (size_t)(p->n * nb) * 208, db = (size_t)(p->n * nb) * 2;
-                FB_CUDA(cudaMemcpyAsync(t->buf.as<uint8_t>() + off_main, p->main(), mb, cudaMemcpyDeviceToDevice,
-                                        ctx->stream));
-                FB_CUDA(cudaMemcpyAsync(const_cast<uint16_t *>(t->q6_d()) + off_d / 2, p->q6_d(), db,
-                                        cudaMemcpyDeviceToDevice, ctx->stream));
-                off_main += mb;
-                off_d += db;
-            } else {
-                const size_t bytes = fb_qtensor::device_bytes(dtype, p->n, k);
-                FB_CUDA(cudaMemcpyAsync(t->buf.as<uint8_t>() + off_main, p->main(), bytes, cudaMemcpyDeviceToDevice,
-                                        ctx->stream));
-                off_main += bytes;
-            }
+            // tile-major records of whole 16-row tiles concatenate as bytes
+            const size_t bytes = fb_qtensor::device_bytes(dtype, p->n, k);
+            FB_CUDA(cudaMemcpyAsync(t->buf.as<uint8_t>() + off, p->main(), bytes, cudaMemcpyDeviceToDevice,
+                                    ctx->stream));
+            off += bytes;
         }
         FB_CUDA(cudaStreamSynchronize(ctx->stream));
         *out = t.release();

@@ -79,28 +79,46 @@ struct fb_ctx {
     void *ensure_scratch(size_t bytes);
 };
 
-// Device layouts (all 16-byte aligned):
-//  Q4_K: n*nb blocks of 144 B in row order; each block keeps the GGUF
-//        header (d, dmin, scales[12]) in bytes 0..15 and stores the 128
-//        quant bytes permuted so that MMA quad lane t reads bytes
-//        [16+32t, 48+32t): for g = 0..3, GGUF qs[32g + 8t .. 32g + 8t + 7].
-//  Q6_K: "main" n*nb blocks of 208 B: bytes [48t, 48t+48) for quad lane t
-//        hold 8 ql words (h, j, x) = GGUF ql[64h + 32j + 8t + 4x .. +3] and
-//        4 qh words (h, x) = GGUF qh[32h + 8t + 4x .. +3]; bytes 192..207 are
-//        the 16 int8 scales.  The fp16 super-block scales d live in a
-//        separate [n, nb] array after the main area.
+// Device layouts of k-quant weights W[n, k] (nb = k/256 super-blocks per
+// row): tile-major, 16 rows per tile (n padded to a multiple of 16 with zero
+// rows).  The 16 rows' super-block b of tile T form one contiguous record,
+// records ordered (T, b), so the GEMV streams (tile, block) records with one
+// bulk copy each.
+//  Q4_K record = 16 x 144 B: row slot r at +144r holds the GGUF header (d,
+//        dmin, scales[12]) in bytes 0..15 and the 128 quant bytes permuted so
+//        MMA quad lane t reads bytes [16+32t, 48+32t): for g = 0..3, GGUF
+//        qs[32g + 8t .. 32g + 8t + 7].
+//  Q6_K record = 16 x 208 B + 16 x 2 B: row slot r at +208r: bytes [48t,
+//        48t+48) for quad lane t hold 8 ql words (h, j, x) = GGUF
+//        ql[64h + 32j + 8t + 4x .. +3] and 4 qh words (h, x) = GGUF
+//        qh[32h + 8t + 4x .. +3]; bytes 192..207 the 16 int8 scales.  The
+//        fp16 super-block scale d of row slot r is at +3328 + 2r.
 struct fb_qtensor {
     int dtype = 0;
     int64_t n = 0, k = 0;
     fb::DevBuf buf;
     int64_t nb() const { return k / 256; }
+    int64_t n_pad() const { return (n + 15) / 16 * 16; }
+    int64_t n_tiles() const { return (n + 15) / 16; }
     const uint8_t *main() const { return buf.as<uint8_t>(); }
-    // Q6_K: fp16 d array after the 208-byte blocks.
-    const uint16_t *q6_d() const {
-        return reinterpret_cast<const uint16_t *>(buf.as<uint8_t>() + (size_t)n * nb() * 208);
-    }
     static size_t device_bytes(int dtype, int64_t n, int64_t k);
 };
+
+namespace fb {
+constexpr int Q4K_REC = 16 * 144;  // 2304
+constexpr int Q6K_REC = 16 * 210;  // 3360
+// Byte offset of row `row`, super-block `b` (nb per row) in the tile-major
+// layout: the row's 144-byte Q4_K block / the row's 208-byte Q6_K part.
+__host__ __device__ inline size_t q4k_offset(int64_t row, int64_t b, int64_t nb) {
+    return (size_t)(((row >> 4) * nb + b) * Q4K_REC) + (size_t)(row & 15) * 144;
+}
+__host__ __device__ inline size_t q6k_offset(int64_t row, int64_t b, int64_t nb) {
+    return (size_t)(((row >> 4) * nb + b) * Q6K_REC) + (size_t)(row & 15) * 208;
+}
+__host__ __device__ inline size_t q6k_d_offset(int64_t row, int64_t b, int64_t nb) {
+    return (size_t)(((row >> 4) * nb + b) * Q6K_REC) + 3328 + (size_t)(row & 15) * 2;
+}
+}  // namespace fb
 
 namespace fb {
 
@@ -156,14 +174,14 @@ struct AttnArgs {
     const int32_t *block_table;  // [b, max_pages]
     const int32_t *seq_lens;     // [b] or null (then pos[b] + 1)
     const int32_t *pos;          // [b]
-    double *part_o;              // [b, n_heads, nsplit_max, hd] unnormalised sum p*v
-    double *part_ml;             // [b, n_heads, nsplit_max, 2] (split max, sum p)
+    double *part_o;              // [b, n_heads, nsplit_max, hd] per-page unnormalised sum p*v
+    double *part_ml;             // [b, n_heads, nsplit_max, 2] (page max, sum p)
     int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
     float scale;
     uint32_t *err;
 };
 void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
-                        const Q8Act *aq);
+                        const Q8Act *aq, int *counters, bool pdl);
 
 // RoPE tables [max_pos][hd/2] computed on the host exactly as the oracle does
 // (candle precompute_freqs_cis: angle = pos * theta^(-2i/hd) in f32).

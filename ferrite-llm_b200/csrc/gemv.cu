@@ -4,33 +4,47 @@
 // Arithmetic = candle-core 0.8.4 CPU QMatMul (crates/ferrite-wasm-host/src/
 // adapter.rs:61-70 -> QMatMul::forward): activations quantized to Q8_K, then
 // per super-block the integer sums  sum_j sc_j * (q_w . q_x)_j  (and for Q4_K
-// sum_j m_j * bsum_j) combined in f32 with the fp16 super-block scales.  The
+// sum_j m_j * bsum_j) combined with the fp16 super-block scales.  The
 // reference's GPU kernels for the same op are the dp4a MMVQ kernels
 // mul_mat_vec_q{4,6}_K_q8_1 (ptx-kernels/kernels/candle/quantized.cu:2627-3344).
 //
 // B200 design: the op is HBM-bound (0.5625 / 0.8203 weight bytes per MAC at
-// m = 1), so every weight byte is read exactly once with 16-byte streaming
-// loads that bypass L1.  The integer dot of each 32-value (Q4_K) or 16-value
-// (Q6_K) sub-block runs on the tensor pipe as mma.m16n8k32.s8 (16 weight rows
-// x 8 activation rows per instruction), which keeps the ALU budget per weight
-// byte flat from m = 1 to m = 16; integer partials are exact, so the
-// per-sub-block scales are applied in int32 exactly as the CPU path does, and
-// the per-super-block float combine runs in binary64 with one rounding to f32
-// (bit-identical to the CPU oracle whatever the block summation order).
-// The device weight layouts (see fb_qtensor) put each MMA quad lane's bytes
-// contiguously, and the Q8_K activation layout (see Q8Act) matches the MMA B
-// fragment, so no shuffles or shared-memory staging are needed.
-//
-// CTA = 8 warps on one 16-row tile; warp w takes super-blocks w, w+8, ...;
-// partial sums are reduced across warps through shared memory (fixed order,
-// deterministic).  Thread (gid = lane/4, tig = lane%4) owns weight rows gid
-// and gid+8 and output columns 2*tig, 2*tig+1 of each 8-wide n-tile.
+// m = 1), so the kernel's job is to keep enough weight bytes in flight.
+//  * Persistent CTAs of KS warps loop over 16-row tiles; warp w owns a fixed
+//    slice of the super-blocks of every tile.  Each warp streams its (tile,
+//    super-block) records -- one contiguous record per 16 rows in the
+//    tile-major device layout -- through its own DEPTH-stage shared-memory
+//    ring with cp.async.bulk (TMA, no multicast) and per-stage mbarriers;
+//    lane 0 refills a stage as soon as the warp has consumed it, so each SM
+//    keeps ~150 KB of weights in flight without spending registers on them.
+//  * The first DEPTH stages are issued before griddepcontrol.wait: weights do
+//    not depend on the previous kernel, so they stream in while it finishes.
+//  * The integer dot of each 32-value sub-block runs on the tensor pipe as
+//    mma.m16n8k32.s8 (16 weight rows x 8 activation rows per instruction,
+//    exact int32); per-sub-block scales are applied in int32 exactly as the
+//    CPU path does, and the per-super-block combine runs in binary64 with one
+//    rounding to f32 (bit-identical to the CPU oracle whatever the order).
+//  * Q6_K: each 32-value part spans two 16-value scale groups; lanes with
+//    tig < 2 hold the first group's values and tig >= 2 the second's, so two
+//    MMAs with the B fragment masked by lane group separate them.
+// Thread (gid = lane/4, tig = lane%4) owns weight rows gid and gid+8 of the
+// tile and output columns 2*tig, 2*tig+1 of each 8-wide n-tile; the KS warps'
+// partial sums of a tile are reduced through shared memory in fixed order.
+// mbarrier waits are bounded; on timeout the kernel raises
+// ERRBIT_WAIT_TIMEOUT, drains its outstanding copies (bounded) and exits.
 #include "fb_internal.h"
 #include "kq_common.cuh"
 
+#include <algorithm>
+
 namespace fb {
 
-constexpr int GEMV_WARPS = 8;
+constexpr int KS = 4;     // warps per CTA (super-block slices of a tile)
+constexpr int DEPTH = 6;  // TMA ring stages per warp
+
+template <int DT> struct QRec;
+template <> struct QRec<4> { static constexpr int bytes = Q4K_REC; };
+template <> struct QRec<6> { static constexpr int bytes = Q6K_REC; };
 
 template <int NT>
 struct ActBlock {
@@ -48,7 +62,7 @@ __device__ __forceinline__ void load_act(const Q8Act &a, int m, int64_t blk, int
             const int8_t *p = a.qs + (int64_t)col * a.k + blk * QK + 64 * tig;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                uint4 v = ld_act16(p + 16 * i);
+                const uint4 v = ld_act16(p + 16 * i);
                 ab.b[nt][4 * i + 0] = v.x;
                 ab.b[nt][4 * i + 1] = v.y;
                 ab.b[nt][4 * i + 2] = v.z;
@@ -61,349 +75,493 @@ __device__ __forceinline__ void load_act(const Q8Act &a, int m, int64_t blk, int
     }
 }
 
-__device__ __forceinline__ float act_d(const Q8Act &a, int m, int col, int64_t blk, int64_t nbk) {
-    return col < m ? a.d[(int64_t)col * nbk + blk] : 0.f;
-}
-
+// ---------------------------------------------------------- Q4_K block ---
+// One (tile, super-block) record in shared memory; accumulates the rows
+// gid / gid+8 x columns (2tig, 2tig+1) of every n-tile into acc (binary64),
+// or (DOTS) writes the integer partials of column 0.
 template <int NT, bool DOTS>
-__device__ __forceinline__ void write_out(double (&acc)[NT][4], double *red, int warp, int gid, int tig, int64_t row0,
-                                          int64_t n, int m, float *y, int64_t ldy) {
-    constexpr int C = 8 * NT;
-    // red[w][r][c] with a padded row to keep the stores conflict-light
+__device__ __forceinline__ void q4k_block(const uint8_t *rec, const Q8Act &a, int m, int b, int nb, int gid, int tig,
+                                          int64_t row0, int64_t n, double (&acc)[NT][4], int32_t *dots_sc,
+                                          int32_t *dots_min) {
+    const uint8_t *r0 = rec + gid * 144, *r1 = rec + (gid + 8) * 144;
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(r0), h1 = *reinterpret_cast<const uint4 *>(r1);
+    const uint4 q0a = *reinterpret_cast<const uint4 *>(r0 + 16 + 32 * tig);
+    const uint4 q0b = *reinterpret_cast<const uint4 *>(r0 + 32 + 32 * tig);
+    const uint4 q1a = *reinterpret_cast<const uint4 *>(r1 + 16 + 32 * tig);
+    const uint4 q1b = *reinterpret_cast<const uint4 *>(r1 + 32 + 32 * tig);
+    ActBlock<NT> ab;
+    load_act<NT>(a, m, b, gid, tig, ab);
+    uint4 bs[NT][2];
+    float dy[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int col = nt * 8 + 2 * tig + j;
+            const bool v = col < m;
+            bs[nt][j] = v ? ld_act16(a.bs32 + (int64_t)col * (a.k / 32) + (int64_t)b * 8) : make_uint4(0, 0, 0, 0);
+            dy[nt][j] = v ? a.d[(int64_t)col * nb + b] : 0.f;
+        }
+    const Q4Scales s0 = q4k_unpack_scales(h0.y, h0.z, h0.w);
+    const Q4Scales s1 = q4k_unpack_scales(h1.y, h1.z, h1.w);
+    const uint32_t W0[8] = {q0a.x, q0a.y, q0a.z, q0a.w, q0b.x, q0b.y, q0b.z, q0b.w};
+    const uint32_t W1[8] = {q1a.x, q1a.y, q1a.z, q1a.w, q1b.x, q1b.y, q1b.z, q1b.w};
+    int isum[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) isum[nt][i] = 0;
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        const int g = s >> 1, sh = 4 * (s & 1);
+        const uint32_t a0 = (W0[2 * g] >> sh) & 0x0F0F0F0Fu;
+        const uint32_t a2 = (W0[2 * g + 1] >> sh) & 0x0F0F0F0Fu;
+        const uint32_t a1 = (W1[2 * g] >> sh) & 0x0F0F0F0Fu;
+        const uint32_t a3 = (W1[2 * g + 1] >> sh) & 0x0F0F0F0Fu;
+        const int sc0 = byte_of(s < 4 ? s0.sc_lo : s0.sc_hi, s & 3);
+        const int sc1 = byte_of(s < 4 ? s1.sc_lo : s1.sc_hi, s & 3);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            int c[4] = {0, 0, 0, 0};
+            mma_k32(c, a0, a1, a2, a3, ab.b[nt][2 * s], ab.b[nt][2 * s + 1]);
+            isum[nt][0] += sc0 * c[0];
+            isum[nt][1] += sc0 * c[1];
+            isum[nt][2] += sc1 * c[2];
+            isum[nt][3] += sc1 * c[3];
+        }
+    }
+    const double dw0 = h2f(h0.x & 0xFFFF), dm0 = h2f(h0.x >> 16);
+    const double dw1 = h2f(h1.x & 0xFFFF), dm1 = h2f(h1.x >> 16);
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const int r = gid + 8 * (i >> 1), c = nt * 8 + 2 * tig + (i & 1);
-            red[(warp * 16 + r) * (C + 1) + c] = acc[nt][i];
+            const int j = i & 1;
+            if (nt * 8 + 2 * tig + j >= m) continue;
+            const Q4Scales &sr = (i < 2) ? s0 : s1;
+            const uint4 q = bs[nt][j];
+            int msum = __dp2a_lo((int)q.x, (int)sr.mn_lo, 0);
+            msum = __dp2a_hi((int)q.y, (int)sr.mn_lo, msum);
+            msum = __dp2a_lo((int)q.z, (int)sr.mn_hi, msum);
+            msum = __dp2a_hi((int)q.w, (int)sr.mn_hi, msum);
+            if (DOTS) {
+                const int64_t row = row0 + gid + 8 * (i >> 1);
+                if (nt == 0 && j == 0 && row < n) {
+                    dots_sc[row * nb + b] = isum[nt][i];
+                    dots_min[row * nb + b] = msum;
+                }
+            } else {
+                // binary64 combine: ((d * dy) * isum) - ((dmin * dy) * msum)
+                const double dw = (i < 2) ? dw0 : dw1, dm = (i < 2) ? dm0 : dm1;
+                const double yd = dy[nt][j];
+                acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, yd), (double)isum[nt][i]));
+                acc[nt][i] = __dsub_rn(acc[nt][i], __dmul_rn(__dmul_rn(dm, yd), (double)msum));
+            }
         }
-    __syncthreads();
-    for (int o = threadIdx.x; o < 16 * C; o += blockDim.x) {
-        const int r = o / C, c = o % C;
-        double s = 0.0;
-#pragma unroll
-        for (int w = 0; w < GEMV_WARPS; w++) s = __dadd_rn(s, red[(w * 16 + r) * (C + 1) + c]);
-        const int64_t row = row0 + r;
-        if (row < n && c < m) y[(int64_t)c * ldy + row] = __double2float_rn(s);
-    }
 }
 
-// ---------------------------------------------------------------- Q4_K ---
+// ---------------------------------------------------------- Q6_K block ---
 template <int NT, bool DOTS>
-__global__ void __launch_bounds__(256) k_gemv_q4k(const uint8_t *__restrict__ W, int64_t n, int nb, Q8Act a, int m,
-                                                  float *__restrict__ y, int64_t ldy, int32_t *__restrict__ dots_sc,
-                                                  int32_t *__restrict__ dots_min) {
-    __shared__ double red[GEMV_WARPS * 16 * (8 * NT + 1)];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gid = lane >> 2, tig = lane & 3;
-    const int64_t row0 = (int64_t)blockIdx.x * 16;
-    const int64_t r0 = min(row0 + gid, n - 1), r1 = min(row0 + gid + 8, n - 1);
-    const uint8_t *w0 = W + r0 * nb * 144;
-    const uint8_t *w1 = W + r1 * nb * 144;
-
-    double acc[NT][4];
+__device__ __forceinline__ void q6k_block(const uint8_t *rec, const Q8Act &a, int m, int b, int nb, int gid, int tig,
+                                          int64_t row0, int64_t n, double (&acc)[NT][4], int32_t *dots_sc) {
+    const uint32_t mlo = tig < 2 ? 0xFFFFFFFFu : 0u;
+    const uint8_t *r0 = rec + gid * 208, *r1 = rec + (gid + 8) * 208;
+    uint32_t Q0[12], Q1[12];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(r0 + 48 * tig + 16 * i);
+        const uint4 v1 = *reinterpret_cast<const uint4 *>(r1 + 48 * tig + 16 * i);
+        Q0[4 * i] = v0.x, Q0[4 * i + 1] = v0.y, Q0[4 * i + 2] = v0.z, Q0[4 * i + 3] = v0.w;
+        Q1[4 * i] = v1.x, Q1[4 * i + 1] = v1.y, Q1[4 * i + 2] = v1.z, Q1[4 * i + 3] = v1.w;
+    }
+    const uint4 sc0v = *reinterpret_cast<const uint4 *>(r0 + 192);
+    const uint4 sc1v = *reinterpret_cast<const uint4 *>(r1 + 192);
+    const uint32_t S0[4] = {sc0v.x, sc0v.y, sc0v.z, sc0v.w};
+    const uint32_t S1[4] = {sc1v.x, sc1v.y, sc1v.z, sc1v.w};
+    const double dw0 = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * gid));
+    const double dw1 = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * (gid + 8)));
+    ActBlock<NT> ab;
+    load_act<NT>(a, m, b, gid, tig, ab);
+    uint4 bsa[NT][2], bsb[NT][2];  // bs16 of the two columns: groups 0..7, 8..15
+    float dy[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[nt][i] = 0.0;
-
-    // Weights do not depend on the previous kernel: issue the first loads
-    // before waiting on it.
-    int b = warp;
-    uint4 h0, h1, q0a, q0b, q1a, q1b;
-    if (b < nb) {
-        h0 = ld_stream16(w0 + b * 144);
-        h1 = ld_stream16(w1 + b * 144);
-        q0a = ld_stream16(w0 + b * 144 + 16 + 32 * tig);
-        q0b = ld_stream16(w0 + b * 144 + 32 + 32 * tig);
-        q1a = ld_stream16(w1 + b * 144 + 16 + 32 * tig);
-        q1b = ld_stream16(w1 + b * 144 + 32 + 32 * tig);
-    }
-    pdl_wait();
-    const int64_t nbk = nb;
-    for (; b < nb; b += GEMV_WARPS) {
-        ActBlock<NT> ab;
-        load_act<NT>(a, m, b, gid, tig, ab);
-        uint4 bs[NT][2];
-        float dy[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int col = nt * 8 + 2 * tig + j;
-                bs[nt][j] = col < m ? ld_act16(a.bs32 + (int64_t)col * (a.k / 32) + b * 8) : make_uint4(0, 0, 0, 0);
-                dy[nt][j] = act_d(a, m, col, b, nbk);
+        for (int j = 0; j < 2; j++) {
+            const int col = nt * 8 + 2 * tig + j;
+            if (col < m) {
+                const int16_t *p = a.bs16 + (int64_t)col * (a.k / 16) + (int64_t)b * 16;
+                bsa[nt][j] = ld_act16(p);
+                bsb[nt][j] = ld_act16(p + 8);
+                dy[nt][j] = a.d[(int64_t)col * nb + b];
+            } else {
+                bsa[nt][j] = make_uint4(0, 0, 0, 0);
+                bsb[nt][j] = make_uint4(0, 0, 0, 0);
+                dy[nt][j] = 0.f;
             }
-        const Q4Scales s0 = q4k_unpack_scales(h0.y, h0.z, h0.w);
-        const Q4Scales s1 = q4k_unpack_scales(h1.y, h1.z, h1.w);
-        const float dw0 = h2f(h0.x & 0xFFFF), dm0 = h2f(h0.x >> 16);
-        const float dw1 = h2f(h1.x & 0xFFFF), dm1 = h2f(h1.x >> 16);
-        const uint32_t W0[8] = {q0a.x, q0a.y, q0a.z, q0a.w, q0b.x, q0b.y, q0b.z, q0b.w};
-        const uint32_t W1[8] = {q1a.x, q1a.y, q1a.z, q1a.w, q1b.x, q1b.y, q1b.z, q1b.w};
-
-        // prefetch the next super-block of this warp
-        const int bn = b + GEMV_WARPS;
-        if (bn < nb) {
-            h0 = ld_stream16(w0 + bn * 144);
-            h1 = ld_stream16(w1 + bn * 144);
-            q0a = ld_stream16(w0 + bn * 144 + 16 + 32 * tig);
-            q0b = ld_stream16(w0 + bn * 144 + 32 + 32 * tig);
-            q1a = ld_stream16(w1 + bn * 144 + 16 + 32 * tig);
-            q1b = ld_stream16(w1 + bn * 144 + 32 + 32 * tig);
         }
-
-        int isum[NT][4];
+    int isum[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-            for (int i = 0; i < 4; i++) isum[nt][i] = 0;
+        for (int i = 0; i < 4; i++) isum[nt][i] = 0;
 #pragma unroll
-        for (int s = 0; s < 8; s++) {
-            const int g = s >> 1, sh = 4 * (s & 1);
-            const uint32_t a0 = (W0[2 * g] >> sh) & 0x0F0F0F0Fu;
-            const uint32_t a2 = (W0[2 * g + 1] >> sh) & 0x0F0F0F0Fu;
-            const uint32_t a1 = (W1[2 * g] >> sh) & 0x0F0F0F0Fu;
-            const uint32_t a3 = (W1[2 * g + 1] >> sh) & 0x0F0F0F0Fu;
-            const int sc0 = byte_of(s < 4 ? s0.sc_lo : s0.sc_hi, s & 3);
-            const int sc1 = byte_of(s < 4 ? s1.sc_lo : s1.sc_hi, s & 3);
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int s = 4 * h + p;
+            const int lw = 4 * h + 2 * (p & 1), ls = 4 * (p >> 1);
+            const int hw = 8 + 2 * h;
+            // 6-bit quants (0..63) of values 8*tig + 4x + e of the part
+            auto q6 = [&](const uint32_t *Q, int x) -> uint32_t {
+                const uint32_t lo = (Q[lw + x] >> ls) & 0x0F0F0F0Fu;
+                const uint32_t hi = (2 * p <= 4) ? ((Q[hw + x] << (4 - 2 * p)) & 0x30303030u)
+                                                 : ((Q[hw + x] >> (2 * p - 4)) & 0x30303030u);
+                return lo | hi;
+            };
+            const uint32_t a0 = q6(Q0, 0), a2 = q6(Q0, 1), a1 = q6(Q1, 0), a3 = q6(Q1, 1);
+            const int G = 8 * h + 2 * p;  // groups G (tig < 2) and G + 1
+            const int s0a = sbyte_of(S0[G >> 2], G & 3), s0b = sbyte_of(S0[G >> 2], (G & 3) + 1);
+            const int s1a = sbyte_of(S1[G >> 2], G & 3), s1b = sbyte_of(S1[G >> 2], (G & 3) + 1);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                int c[4] = {0, 0, 0, 0};
-                mma_k32(c, a0, a1, a2, a3, ab.b[nt][2 * s], ab.b[nt][2 * s + 1]);
-                isum[nt][0] += sc0 * c[0];
-                isum[nt][1] += sc0 * c[1];
-                isum[nt][2] += sc1 * c[2];
-                isum[nt][3] += sc1 * c[3];
+                const uint32_t b0 = ab.b[nt][2 * s], b1 = ab.b[nt][2 * s + 1];
+                int ca[4] = {0, 0, 0, 0}, cb[4] = {0, 0, 0, 0};
+                mma_k32(ca, a0, a1, a2, a3, b0 & mlo, b1 & mlo);
+                mma_k32(cb, a0, a1, a2, a3, b0 & ~mlo, b1 & ~mlo);
+                isum[nt][0] += s0a * ca[0] + s0b * cb[0];
+                isum[nt][1] += s0a * ca[1] + s0b * cb[1];
+                isum[nt][2] += s1a * ca[2] + s1b * cb[2];
+                isum[nt][3] += s1a * ca[3] + s1b * cb[3];
             }
         }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int j = i & 1;
-                const Q4Scales &sr = (i < 2) ? s0 : s1;
-                const uint4 q = bs[nt][j];
-                int msum = __dp2a_lo((int)q.x, (int)sr.mn_lo, 0);
-                msum = __dp2a_hi((int)q.y, (int)sr.mn_lo, msum);
-                msum = __dp2a_lo((int)q.z, (int)sr.mn_hi, msum);
-                msum = __dp2a_hi((int)q.w, (int)sr.mn_hi, msum);
-                if (DOTS) {
-                    // integer partials for column 0 only
-                    if (nt == 0 && tig == 0 && j == 0) {
-                        const int64_t row = row0 + gid + 8 * (i >> 1);
-                        if (row < n) {
-                            dots_sc[row * nb + b] = isum[nt][i];
-                            dots_min[row * nb + b] = msum;
-                        }
-                    }
-                } else if (nt * 8 + 2 * tig + j < m) {
-                    // binary64 combine: ((d * dy) * isum) - ((dmin * dy) * msum)
-                    const double dw = (i < 2) ? dw0 : dw1, dm = (i < 2) ? dm0 : dm1;
-                    const double yd = dy[nt][j];
-                    acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, yd), (double)isum[nt][i]));
-                    acc[nt][i] = __dsub_rn(acc[nt][i], __dmul_rn(__dmul_rn(dm, yd), (double)msum));
-                }
-            }
-    }
-    pdl_launch();
-    if (!DOTS) write_out<NT, DOTS>(acc, red, warp, gid, tig, row0, n, m, y, ldy);
-}
-
-// ---------------------------------------------------------------- Q6_K ---
-// Each 32-value part (half h, part p) spans two 16-value scale groups; lanes
-// with tig < 2 hold the first group's values and tig >= 2 the second's, so
-// two MMAs with the B fragment masked by lane group separate them.
-template <int NT, bool DOTS>
-__global__ void __launch_bounds__(256) k_gemv_q6k(const uint8_t *__restrict__ W, const uint16_t *__restrict__ Wd,
-                                                  int64_t n, int nb, Q8Act a, int m, float *__restrict__ y, int64_t ldy,
-                                                  int32_t *__restrict__ dots_sc) {
-    __shared__ double red[GEMV_WARPS * 16 * (8 * NT + 1)];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gid = lane >> 2, tig = lane & 3;
-    const uint32_t mlo = tig < 2 ? 0xFFFFFFFFu : 0u;
-    const int64_t row0 = (int64_t)blockIdx.x * 16;
-    const int64_t r0 = min(row0 + gid, n - 1), r1 = min(row0 + gid + 8, n - 1);
-    const uint8_t *w0 = W + r0 * nb * 208;
-    const uint8_t *w1 = W + r1 * nb * 208;
-    const uint16_t *d0p = Wd + r0 * nb;
-    const uint16_t *d1p = Wd + r1 * nb;
-
-    double acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[nt][i] = 0.0;
-
-    int b = warp;
-    uint4 x0[3], x1[3], sc0v, sc1v;
-    uint16_t dd0 = 0, dd1 = 0;
-    if (b < nb) {
-#pragma unroll
-        for (int i = 0; i < 3; i++) {
-            x0[i] = ld_stream16(w0 + b * 208 + 48 * tig + 16 * i);
-            x1[i] = ld_stream16(w1 + b * 208 + 48 * tig + 16 * i);
+        for (int i = 0; i < 4; i++) {
+            const int j = i & 1;
+            if (nt * 8 + 2 * tig + j >= m) continue;
+            const uint32_t *S = (i < 2) ? S0 : S1;
+            // sum_G sc_G * bsum16_G (quants are offset by +32)
+            const uint4 qa = bsa[nt][j], qb = bsb[nt][j];
+            int cs = __dp2a_lo((int)qa.x, (int)S[0], 0);
+            cs = __dp2a_hi((int)qa.y, (int)S[0], cs);
+            cs = __dp2a_lo((int)qa.z, (int)S[1], cs);
+            cs = __dp2a_hi((int)qa.w, (int)S[1], cs);
+            cs = __dp2a_lo((int)qb.x, (int)S[2], cs);
+            cs = __dp2a_hi((int)qb.y, (int)S[2], cs);
+            cs = __dp2a_lo((int)qb.z, (int)S[3], cs);
+            cs = __dp2a_hi((int)qb.w, (int)S[3], cs);
+            const int tot = isum[nt][i] - 32 * cs;
+            if (DOTS) {
+                const int64_t row = row0 + gid + 8 * (i >> 1);
+                if (nt == 0 && j == 0 && row < n) dots_sc[row * nb + b] = tot;
+            } else {
+                const double dw = (i < 2) ? dw0 : dw1;
+                acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, (double)dy[nt][j]), (double)tot));
+            }
         }
-        sc0v = ld_stream16(w0 + b * 208 + 192);
-        sc1v = ld_stream16(w1 + b * 208 + 192);
-        dd0 = ld_stream_u16(d0p + b);
-        dd1 = ld_stream_u16(d1p + b);
-    }
-    pdl_wait();
-    for (; b < nb; b += GEMV_WARPS) {
-        ActBlock<NT> ab;
-        load_act<NT>(a, m, b, gid, tig, ab);
-        uint4 bsa[NT][2], bsb[NT][2];  // bs16 of the two columns: groups 0..7, 8..15
-        float dy[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int col = nt * 8 + 2 * tig + j;
-                if (col < m) {
-                    const int16_t *p = a.bs16 + (int64_t)col * (a.k / 16) + b * 16;
-                    bsa[nt][j] = ld_act16(p);
-                    bsb[nt][j] = ld_act16(p + 8);
-                } else {
-                    bsa[nt][j] = make_uint4(0, 0, 0, 0);
-                    bsb[nt][j] = make_uint4(0, 0, 0, 0);
-                }
-                dy[nt][j] = act_d(a, m, col, b, nb);
-            }
-        const uint32_t Q0[12] = {x0[0].x, x0[0].y, x0[0].z, x0[0].w, x0[1].x, x0[1].y,
-                                 x0[1].z, x0[1].w, x0[2].x, x0[2].y, x0[2].z, x0[2].w};
-        const uint32_t Q1[12] = {x1[0].x, x1[0].y, x1[0].z, x1[0].w, x1[1].x, x1[1].y,
-                                 x1[1].z, x1[1].w, x1[2].x, x1[2].y, x1[2].z, x1[2].w};
-        const uint32_t S0[4] = {sc0v.x, sc0v.y, sc0v.z, sc0v.w};
-        const uint32_t S1[4] = {sc1v.x, sc1v.y, sc1v.z, sc1v.w};
-        const float dw0 = h2f(dd0), dw1 = h2f(dd1);
-
-        const int bn = b + GEMV_WARPS;
-        if (bn < nb) {
-#pragma unroll
-            for (int i = 0; i < 3; i++) {
-                x0[i] = ld_stream16(w0 + bn * 208 + 48 * tig + 16 * i);
-                x1[i] = ld_stream16(w1 + bn * 208 + 48 * tig + 16 * i);
-            }
-            sc0v = ld_stream16(w0 + bn * 208 + 192);
-            sc1v = ld_stream16(w1 + bn * 208 + 192);
-            dd0 = ld_stream_u16(d0p + bn);
-            dd1 = ld_stream_u16(d1p + bn);
-        }
-
-        int isum[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) isum[nt][i] = 0;
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-#pragma unroll
-            for (int p = 0; p < 4; p++) {
-                const int s = 4 * h + p;
-                const int lw = 4 * h + 2 * (p & 1), ls = 4 * (p >> 1);
-                const int hw = 8 + 2 * h;
-                // 6-bit quants (0..63) of values 8*tig + 4x + e of the part
-                auto q6 = [&](const uint32_t *Q, int x) -> uint32_t {
-                    const uint32_t lo = (Q[lw + x] >> ls) & 0x0F0F0F0Fu;
-                    const uint32_t hi = (2 * p <= 4) ? ((Q[hw + x] << (4 - 2 * p)) & 0x30303030u)
-                                                     : ((Q[hw + x] >> (2 * p - 4)) & 0x30303030u);
-                    return lo | hi;
-                };
-                const uint32_t a0 = q6(Q0, 0), a2 = q6(Q0, 1), a1 = q6(Q1, 0), a3 = q6(Q1, 1);
-                const int G = 8 * h + 2 * p;  // groups G (tig < 2) and G + 1
-                const int s0a = sbyte_of(S0[G >> 2], G & 3), s0b = sbyte_of(S0[G >> 2], (G & 3) + 1);
-                const int s1a = sbyte_of(S1[G >> 2], G & 3), s1b = sbyte_of(S1[G >> 2], (G & 3) + 1);
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    const uint32_t b0 = ab.b[nt][2 * s], b1 = ab.b[nt][2 * s + 1];
-                    int ca[4] = {0, 0, 0, 0}, cb[4] = {0, 0, 0, 0};
-                    mma_k32(ca, a0, a1, a2, a3, b0 & mlo, b1 & mlo);
-                    mma_k32(cb, a0, a1, a2, a3, b0 & ~mlo, b1 & ~mlo);
-                    isum[nt][0] += s0a * ca[0] + s0b * cb[0];
-                    isum[nt][1] += s0a * ca[1] + s0b * cb[1];
-                    isum[nt][2] += s1a * ca[2] + s1b * cb[2];
-                    isum[nt][3] += s1a * ca[3] + s1b * cb[3];
-                }
-            }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int j = i & 1;
-                const uint32_t *S = (i < 2) ? S0 : S1;
-                // sum_G sc_G * bsum16_G (quants are offset by +32)
-                const uint4 qa = bsa[nt][j], qb = bsb[nt][j];
-                int cs = __dp2a_lo((int)qa.x, (int)S[0], 0);
-                cs = __dp2a_hi((int)qa.y, (int)S[0], cs);
-                cs = __dp2a_lo((int)qa.z, (int)S[1], cs);
-                cs = __dp2a_hi((int)qa.w, (int)S[1], cs);
-                cs = __dp2a_lo((int)qb.x, (int)S[2], cs);
-                cs = __dp2a_hi((int)qb.y, (int)S[2], cs);
-                cs = __dp2a_lo((int)qb.z, (int)S[3], cs);
-                cs = __dp2a_hi((int)qb.w, (int)S[3], cs);
-                const int tot = isum[nt][i] - 32 * cs;
-                if (DOTS) {
-                    if (nt == 0 && tig == 0 && j == 0) {
-                        const int64_t row = row0 + gid + 8 * (i >> 1);
-                        if (row < n) dots_sc[row * nb + b] = tot;
-                    }
-                } else if (nt * 8 + 2 * tig + j < m) {
-                    const double dw = (i < 2) ? dw0 : dw1;
-                    acc[nt][i] = __dadd_rn(acc[nt][i], __dmul_rn(__dmul_rn(dw, (double)dy[nt][j]), (double)tot));
-                }
-            }
-    }
-    pdl_launch();
-    if (!DOTS) write_out<NT, DOTS>(acc, red, warp, gid, tig, row0, n, m, y, ldy);
 }
 
-template <typename K, typename... Args>
-static void launch_pdl(fb_ctx *ctx, K kernel, unsigned grid, Args... args) {
+// ------------------------------------------------ dp4a consumers (m <= 4) ---
+// For a handful of activation rows the 16x8 MMA tile is mostly padding, so
+// small batches use CUDA-core dp4a instead: lane (r = lane & 15, h = lane >> 4)
+// takes row r of the record and half h of the super-block (four 32-value
+// sub-blocks), which keeps every lane busy and the shared-memory reads
+// bank-conflict-free.  Both halves' integer partials are added with one
+// shuffle before the binary64 combine.
+__device__ __forceinline__ int dp4(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+template <int M, bool DOTS>
+__device__ __forceinline__ void q4k_block_dp4a(const uint8_t *rec, const Q8Act &a, int b, int nb, int lane,
+                                               int64_t row0, int64_t n, double (&acc)[M], int32_t *dots_sc,
+                                               int32_t *dots_min) {
+    const int r = lane & 15, h = lane >> 4;
+    const uint8_t *rp = rec + r * 144;
+    const uint4 hd = *reinterpret_cast<const uint4 *>(rp);
+    uint4 wq[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) wq[t] = *reinterpret_cast<const uint4 *>(rp + 16 + 32 * t + 16 * h);
+    const Q4Scales sc = q4k_unpack_scales(hd.y, hd.z, hd.w);
+    // this half's sub-blocks 4h..4h+3: scales / mins are bytes of the lo or hi word
+    const uint32_t scw = h ? sc.sc_hi : sc.sc_lo, mnw = h ? sc.mn_hi : sc.mn_lo;
+    const double dw = h2f(hd.x & 0xFFFF), dm = h2f(hd.x >> 16);
+#pragma unroll
+    for (int c = 0; c < M; c++) {
+        const int8_t *qa = a.qs + (int64_t)c * a.k + (int64_t)b * QK + 32 * h;
+        int dot[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint4 a0 = ld_act16(qa + 64 * t), a1 = ld_act16(qa + 64 * t + 16);
+            const uint4 w = wq[t];
+            dot[0] = dp4(w.x & 0x0F0F0F0Fu, a0.x, dot[0]);
+            dot[0] = dp4(w.y & 0x0F0F0F0Fu, a0.y, dot[0]);
+            dot[1] = dp4((w.x >> 4) & 0x0F0F0F0Fu, a0.z, dot[1]);
+            dot[1] = dp4((w.y >> 4) & 0x0F0F0F0Fu, a0.w, dot[1]);
+            dot[2] = dp4(w.z & 0x0F0F0F0Fu, a1.x, dot[2]);
+            dot[2] = dp4(w.w & 0x0F0F0F0Fu, a1.y, dot[2]);
+            dot[3] = dp4((w.z >> 4) & 0x0F0F0F0Fu, a1.z, dot[3]);
+            dot[3] = dp4((w.w >> 4) & 0x0F0F0F0Fu, a1.w, dot[3]);
+        }
+        int isum = byte_of(scw, 0) * dot[0] + byte_of(scw, 1) * dot[1] + byte_of(scw, 2) * dot[2] +
+                   byte_of(scw, 3) * dot[3];
+        // mins: bs32 of sub-blocks 4h..4h+3 (two int16 pairs)
+        const int32_t *bsp = reinterpret_cast<const int32_t *>(a.bs32 + (int64_t)c * (a.k / 32) + (int64_t)b * 8 + 4 * h);
+        int msum = __dp2a_lo(bsp[0], (int)mnw, 0);
+        msum = __dp2a_hi(bsp[1], (int)mnw, msum);
+        isum += __shfl_xor_sync(0xffffffffu, isum, 16);
+        msum += __shfl_xor_sync(0xffffffffu, msum, 16);
+        if (h == 0) {
+            if (DOTS) {
+                const int64_t row = row0 + r;
+                if (c == 0 && row < n) {
+                    dots_sc[row * nb + b] = isum;
+                    dots_min[row * nb + b] = msum;
+                }
+            } else {
+                const double yd = a.d[(int64_t)c * nb + b];
+                acc[c] = __dadd_rn(acc[c], __dmul_rn(__dmul_rn(dw, yd), (double)isum));
+                acc[c] = __dsub_rn(acc[c], __dmul_rn(__dmul_rn(dm, yd), (double)msum));
+            }
+        }
+    }
+}
+
+template <int M, bool DOTS>
+__device__ __forceinline__ void q6k_block_dp4a(const uint8_t *rec, const Q8Act &a, int b, int nb, int lane,
+                                               int64_t row0, int64_t n, double (&acc)[M], int32_t *dots_sc) {
+    const int r = lane & 15, h = lane >> 4;
+    const uint8_t *rp = rec + r * 208;
+    uint4 ql[4];
+    uint2 qh[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        ql[t] = *reinterpret_cast<const uint4 *>(rp + 48 * t + 16 * h);
+        qh[t] = *reinterpret_cast<const uint2 *>(rp + 48 * t + 32 + 8 * h);
+    }
+    const uint2 scv = *reinterpret_cast<const uint2 *>(rp + 192 + 8 * h);  // scales of groups 8h..8h+7
+    const double dw = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * r));
+#pragma unroll
+    for (int c = 0; c < M; c++) {
+        const int8_t *qa = a.qs + (int64_t)c * a.k + (int64_t)b * QK + 32 * h;
+        int dg[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};  // [part p][t >> 1]: group 8h + 2p + (t >> 1)
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint4 a0 = ld_act16(qa + 64 * t), a1 = ld_act16(qa + 64 * t + 16);
+            const uint32_t av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const uint32_t qlw[4] = {ql[t].x, ql[t].y, ql[t].z, ql[t].w};  // index 2j + x
+            const uint32_t qhw[2] = {qh[t].x, qh[t].y};                        // index x
+#pragma unroll
+            for (int p = 0; p < 4; p++)
+#pragma unroll
+                for (int x = 0; x < 2; x++) {
+                    const uint32_t lo = (qlw[2 * (p & 1) + x] >> (4 * (p >> 1))) & 0x0F0F0F0Fu;
+                    const uint32_t hi = (2 * p <= 4) ? ((qhw[x] << (4 - 2 * p)) & 0x30303030u)
+                                                     : ((qhw[x] >> (2 * p - 4)) & 0x30303030u);
+                    dg[p][t >> 1] = dp4(lo | hi, av[2 * p + x], dg[p][t >> 1]);
+                }
+        }
+        int isum = 0;
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int G = 2 * p + u;  // group within this half
+                isum += sbyte_of(G < 4 ? scv.x : scv.y, G & 3) * dg[p][u];
+            }
+        // -32 offset of the 6-bit quants: sum_G sc_G * bsum16_G over the half's 8 groups
+        const int32_t *bsp = reinterpret_cast<const int32_t *>(a.bs16 + (int64_t)c * (a.k / 16) + (int64_t)b * 16 + 8 * h);
+        int cs = __dp2a_lo(bsp[0], (int)scv.x, 0);
+        cs = __dp2a_hi(bsp[1], (int)scv.x, cs);
+        cs = __dp2a_lo(bsp[2], (int)scv.y, cs);
+        cs = __dp2a_hi(bsp[3], (int)scv.y, cs);
+        int tot = isum - 32 * cs;
+        tot += __shfl_xor_sync(0xffffffffu, tot, 16);
+        if (h == 0) {
+            if (DOTS) {
+                const int64_t row = row0 + r;
+                if (c == 0 && row < n) dots_sc[row * nb + b] = tot;
+            } else {
+                const double yd = a.d[(int64_t)c * nb + b];
+                acc[c] = __dadd_rn(acc[c], __dmul_rn(__dmul_rn(dw, yd), (double)tot));
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------- pipeline ---
+// NT > 0: MMA consumer with NT 8-wide n-tiles (m <= 8*NT); NT < 0: dp4a
+// consumer for exactly M = -NT activation rows.
+template <int DT, int NT, bool DOTS>
+__global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W, int64_t n, int nb, int n_tiles,
+                                                  Q8Act a, int m, float *__restrict__ y, int64_t ldy,
+                                                  int32_t *__restrict__ dots_sc, int32_t *__restrict__ dots_min,
+                                                  uint32_t *err) {
+    constexpr int REC = QRec<DT>::bytes;
+    constexpr bool DP4A = NT < 0;
+    constexpr int M = DP4A ? -NT : 1;
+    constexpr int C = DP4A ? M : 8 * NT;
+    constexpr int NTA = DP4A ? 1 : NT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[KS * DEPTH];
+    __shared__ double red[KS * 16 * (C + 1)];
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int bpw = (nb + KS - 1) / KS;
+    const int bbeg = min(nb, warp * bpw), nmine = min(nb, bbeg + bpw) - bbeg;
+    const int ntl = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = ntl * nmine;  // records this warp streams
+    uint8_t *ring = smem + (size_t)warp * DEPTH * REC;
+    uint64_t *wbar = bars + warp * DEPTH;
+    if (lane == 0) {
+        for (int i = 0; i < DEPTH; i++) mbar_init(&wbar[i], 1);
+        mbar_fence_init();
+    }
+    if (threadIdx.x == 0) s_abort = 0;
+    __syncthreads();
+    int issued = 0;
+    auto issue = [&](int c) {
+        const int ti = c / nmine, bl = c - ti * nmine;
+        const int64_t T = (int64_t)blockIdx.x + (int64_t)ti * gridDim.x;
+        const int slot = c % DEPTH;
+        mbar_expect_tx(&wbar[slot], REC);
+        bulk_g2s(ring + (size_t)slot * REC, W + ((size_t)T * nb + bbeg + bl) * REC, REC, &wbar[slot]);
+    };
+    // weights do not depend on the previous kernel: start streaming them now
+    if (lane == 0)
+        for (; issued < DEPTH && issued < total; issued++) issue(issued);
+    pdl_wait();
+    bool ok = true;
+    int c = 0;
+    for (int ti = 0; ti < ntl; ti++) {
+        const int64_t row0 = ((int64_t)blockIdx.x + (int64_t)ti * gridDim.x) * 16;
+        double acc[NTA][4];
+        double accd[M];
+#pragma unroll
+        for (int nt = 0; nt < NTA; nt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[nt][i] = 0.0;
+#pragma unroll
+        for (int c2 = 0; c2 < M; c2++) accd[c2] = 0.0;
+        for (int bl = 0; bl < nmine; bl++, c++) {
+            const int slot = c % DEPTH;
+            if (ok) ok = mbar_wait_bounded(&wbar[slot], (uint32_t)(c / DEPTH) & 1u);
+            if (ok) {
+                const uint8_t *rec = ring + (size_t)slot * REC;
+                if constexpr (DP4A) {
+                    if constexpr (DT == 4)
+                        q4k_block_dp4a<M, DOTS>(rec, a, bbeg + bl, nb, lane, row0, n, accd, dots_sc, dots_min);
+                    else
+                        q6k_block_dp4a<M, DOTS>(rec, a, bbeg + bl, nb, lane, row0, n, accd, dots_sc);
+                } else {
+                    if constexpr (DT == 4)
+                        q4k_block<NTA, DOTS>(rec, a, m, bbeg + bl, nb, gid, tig, row0, n, acc, dots_sc, dots_min);
+                    else
+                        q6k_block<NTA, DOTS>(rec, a, m, bbeg + bl, nb, gid, tig, row0, n, acc, dots_sc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && ok && issued < total) {
+                fence_proxy_async_smem();  // our reads of this stage precede the refill
+                issue(issued++);
+            }
+        }
+        if (!ok && lane == 0) {
+            s_abort = 1;
+            atomicOr(err, ERRBIT_WAIT_TIMEOUT);
+        }
+        if (!DOTS) {
+            if constexpr (DP4A) {
+                if (lane < 16)
+#pragma unroll
+                    for (int c2 = 0; c2 < M; c2++) red[(warp * 16 + lane) * (C + 1) + c2] = accd[c2];
+            } else {
+#pragma unroll
+                for (int nt = 0; nt < NTA; nt++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int r = gid + 8 * (i >> 1), col = nt * 8 + 2 * tig + (i & 1);
+                        red[(warp * 16 + r) * (C + 1) + col] = acc[nt][i];
+                    }
+            }
+        }
+        __syncthreads();
+        if (!DOTS && !s_abort) {
+            for (int o = threadIdx.x; o < 16 * C; o += blockDim.x) {
+                const int r = o / C, col = o % C;
+                double sum = 0.0;
+#pragma unroll
+                for (int w = 0; w < KS; w++) sum = __dadd_rn(sum, red[(w * 16 + r) * (C + 1) + col]);
+                const int64_t row = row0 + r;
+                if (row < n && col < m) y[(int64_t)col * ldy + row] = __double2float_rn(sum);
+            }
+        }
+        __syncthreads();
+        if (s_abort) break;
+    }
+    if (!ok && lane == 0) {
+        // let the copies still in flight land before shared memory is released
+        for (int k = c; k < issued; k++) mbar_wait_bounded(&wbar[k % DEPTH], (uint32_t)(k / DEPTH) & 1u);
+    }
+    pdl_launch();
+}
+
+template <int DT, int NT, bool DOTS>
+static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
+                          int32_t *dsc, int32_t *dmn) {
+    constexpr int REC = QRec<DT>::bytes;
+    const size_t smem = (size_t)KS * DEPTH * REC;
+    auto kernel = k_gemv<DT, NT, DOTS>;
+    static int occ = 0;  // resident CTAs per SM (per instantiation)
+    FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (occ == 0) {
+        int o = 0;
+        FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kernel, KS * 32, smem));
+        occ = o > 0 ? o : 1;
+    }
+    const int n_tiles = (int)w->n_tiles();
+    const int grid = std::min(n_tiles, occ * ctx->num_sms);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(GEMV_WARPS * 32);
+    cfg.blockDim = dim3(KS * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
+    FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, w->main(), w->n, (int)w->nb(), n_tiles, a, m, y, ldy, dsc, dmn,
+                               ctx->err_word));
+}
+
+template <int DT>
+static void launch_gemv_dt(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy) {
+    switch (m) {
+    case 1: launch_gemv_t<DT, -1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
+    case 2: launch_gemv_t<DT, -2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
+    case 3: launch_gemv_t<DT, -3, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
+    case 4: launch_gemv_t<DT, -4, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
+    default:
+        if (m <= 8) launch_gemv_t<DT, 1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr);
+        else launch_gemv_t<DT, 2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr);
+    }
 }
 
 void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy) {
     FB_REQUIRE(m >= 1 && m <= 16, "gemv: m must be in 1..16");
-    const unsigned grid = (unsigned)((w->n + 15) / 16);
-    const int nb = (int)w->nb();
-    if (w->dtype == FB_Q4_K) {
-        if (m <= 8)
-            launch_pdl(ctx, k_gemv_q4k<1, false>, grid, w->main(), w->n, nb, a, m, y, ldy, (int32_t *)nullptr,
-                       (int32_t *)nullptr);
-        else
-            launch_pdl(ctx, k_gemv_q4k<2, false>, grid, w->main(), w->n, nb, a, m, y, ldy, (int32_t *)nullptr,
-                       (int32_t *)nullptr);
-    } else if (w->dtype == FB_Q6_K) {
-        if (m <= 8)
-            launch_pdl(ctx, k_gemv_q6k<1, false>, grid, w->main(), w->q6_d(), w->n, nb, a, m, y, ldy,
-                       (int32_t *)nullptr);
-        else
-            launch_pdl(ctx, k_gemv_q6k<2, false>, grid, w->main(), w->q6_d(), w->n, nb, a, m, y, ldy,
-                       (int32_t *)nullptr);
-    } else {
-        fail(FB_ERR_INVALID, "gemv: weight dtype must be Q4_K or Q6_K");
-    }
+    if (w->dtype == FB_Q4_K) launch_gemv_dt<4>(ctx, w, a, m, y, ldy);
+    else if (w->dtype == FB_Q6_K) launch_gemv_dt<6>(ctx, w, a, m, y, ldy);
+    else fail(FB_ERR_INVALID, "gemv: weight dtype must be Q4_K or Q6_K");
 }
 
 void launch_block_dots(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int32_t *out_sc, int32_t *out_min) {
-    const unsigned grid = (unsigned)((w->n + 15) / 16);
-    const int nb = (int)w->nb();
     if (w->dtype == FB_Q4_K) {
-        launch_pdl(ctx, k_gemv_q4k<1, true>, grid, w->main(), w->n, nb, a, 1, (float *)nullptr, (int64_t)0, out_sc,
-                   out_min);
+        launch_gemv_t<4, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, out_min);
     } else if (w->dtype == FB_Q6_K) {
-        FB_CUDA(cudaMemsetAsync(out_min, 0, (size_t)(w->n * nb) * 4, ctx->stream));
-        launch_pdl(ctx, k_gemv_q6k<1, true>, grid, w->main(), w->q6_d(), w->n, nb, a, 1, (float *)nullptr, (int64_t)0,
-                   out_sc);
+        FB_CUDA(cudaMemsetAsync(out_min, 0, (size_t)(w->n * w->nb()) * 4, ctx->stream));
+        launch_gemv_t<6, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, nullptr);
     } else {
         fail(FB_ERR_INVALID, "block_dots: weight dtype must be Q4_K or Q6_K");
     }

@@ -85,7 +85,7 @@ struct fb_model {
     DevBuf kv;  // [L][K|V][num_pages][n_kv][page][hd] fp16
     DevBuf block_table, rope_cos, rope_sin;
     // step buffers
-    DevBuf x, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml;
+    DevBuf x, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml, att_cnt;
     DevBuf act_h, act_a, act_f;
     DevBuf tok, pos, next;
     int32_t *pinned = nullptr;  // host staging [3 * max_batch]
@@ -194,7 +194,10 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         mark(FB_PROF_ROPE_KV, 1);
         A.kpool = m->kpool(l);
         A.vpool = m->vpool(l);
-        launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), &aa);
+        const bool q8_fused = (c.n_heads / c.n_kv_heads) % 2 == 0;
+        launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), q8_fused ? &aa : nullptr,
+                           m->att_cnt.as<int>(), true);
+        if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
         mark(FB_PROF_ATTN, 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         mark(FB_PROF_O, 1);
@@ -301,7 +304,7 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
         m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
         m->num_pages = m->pages_per_seq * c.max_batch;
-        m->nsplit_max = (m->pages_per_seq + 1) / 2;
+        m->nsplit_max = m->pages_per_seq;
         m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
         FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
         std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);
@@ -324,6 +327,8 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         m->logits.alloc((size_t)B * c.vocab * 4);
         m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 8);
         m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 8);
+        m->att_cnt.alloc((size_t)B * c.n_kv_heads * 4);
+        FB_CUDA(cudaMemsetAsync(m->att_cnt.ptr, 0, m->att_cnt.bytes, ctx->stream));
         m->act_h.alloc(q8act_bytes(B, H));
         m->act_a.alloc(q8act_bytes(B, qd));
         m->act_f.alloc(q8act_bytes(B, c.ffn));
@@ -679,8 +684,13 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
-        const int nsplit = (max_seq_len + 2 * page_size - 1) / (2 * page_size);
-        void *base = ctx->ensure_scratch((size_t)batch * n_heads * nsplit * (head_dim + 2) * 8);
+        const int nsplit = (max_seq_len + page_size - 1) / page_size;
+        const size_t cnt_bytes = ((size_t)batch * n_kv_heads * 4 + 255) & ~(size_t)255;
+        uint8_t *raw = static_cast<uint8_t *>(
+            ctx->ensure_scratch(cnt_bytes + (size_t)batch * n_heads * nsplit * (head_dim + 2) * 8));
+        int *counters = reinterpret_cast<int *>(raw);
+        FB_CUDA(cudaMemsetAsync(counters, 0, cnt_bytes, ctx->stream));
+        void *base = raw + cnt_bytes;
         AttnArgs A{};
         A.q = q_dev;
         A.kpool = k_pages_dev;
@@ -698,7 +708,7 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         A.nsplit_max = nsplit;
         A.scale = scale;
         A.err = ctx->err_word;
-        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr);
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false);
     });
 }
 

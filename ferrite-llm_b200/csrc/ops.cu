@@ -127,9 +127,9 @@ __global__ void __launch_bounds__(NORM_WARPS * 32)
             if (threadIdx.x == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
             tok = 0;
         }
-        const uint8_t *er = emb_tab + (int64_t)tok * (dim / QK) * 144;
+        const int64_t nbe = dim / QK;
         for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-            const float v = q4k_value(er + (i / QK) * 144, i % QK);
+            const float v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
             xs[i] = v;
             xr[i] = v;
             ss = __fma_rn((double)v, (double)v, ss);

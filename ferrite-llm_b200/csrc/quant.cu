@@ -163,14 +163,14 @@ void launch_quantize_q8k_gguf(fb_ctx *ctx, const float *x, int64_t m, int64_t k,
 }
 
 // ------------------------------------------------------------------------
-// GGUF <-> device re-layout, one thread per super-block.
-__global__ void k_repack_q4k(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst, int64_t nblocks) {
-    int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    const uint32_t *s = src + b * 36;
-    uint32_t *d = dst + b * 36;
+// GGUF <-> device re-layout, one thread per (row, super-block).
+__global__ void k_repack_q4k(const uint32_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t nblocks, int64_t nb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const uint32_t *s = src + i * 36;
+    uint32_t *d = reinterpret_cast<uint32_t *>(dst + q4k_offset(i / nb, i % nb, nb));
 #pragma unroll
-    for (int i = 0; i < 4; i++) d[i] = s[i];
+    for (int w = 0; w < 4; w++) d[w] = s[w];
     // device word 4 + 8t + 2g + x  <-  GGUF qs word 8g + 2t + x
 #pragma unroll
     for (int t = 0; t < 4; t++)
@@ -180,13 +180,13 @@ __global__ void k_repack_q4k(const uint32_t *__restrict__ src, uint32_t *__restr
             for (int x = 0; x < 2; x++) d[4 + 8 * t + 2 * g + x] = s[4 + 8 * g + 2 * t + x];
 }
 
-__global__ void k_unpack_q4k(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst, int64_t nblocks) {
-    int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    const uint32_t *s = src + b * 36;
-    uint32_t *d = dst + b * 36;
+__global__ void k_unpack_q4k(const uint8_t *__restrict__ src, uint32_t *__restrict__ dst, int64_t nblocks, int64_t nb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const uint32_t *s = reinterpret_cast<const uint32_t *>(src + q4k_offset(i / nb, i % nb, nb));
+    uint32_t *d = dst + i * 36;
 #pragma unroll
-    for (int i = 0; i < 4; i++) d[i] = s[i];
+    for (int w = 0; w < 4; w++) d[w] = s[w];
 #pragma unroll
     for (int t = 0; t < 4; t++)
 #pragma unroll
@@ -206,53 +206,55 @@ __device__ __forceinline__ int q6k_src_off(int t, int w) {
     return 128 + 32 * h + 8 * t + 4 * x;
 }
 
-__global__ void k_repack_q6k(const uint8_t *__restrict__ src, uint8_t *__restrict__ main,
-                             uint16_t *__restrict__ darr, int64_t nblocks) {
-    int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    const uint8_t *s = src + b * 210;
-    uint32_t *d = reinterpret_cast<uint32_t *>(main + b * 208);
+__global__ void k_repack_q6k(const uint8_t *__restrict__ src, uint8_t *__restrict__ dev, int64_t nblocks,
+                             int64_t nb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const int64_t row = i / nb, b = i % nb;
+    const uint8_t *s = src + i * 210;
+    uint32_t *d = reinterpret_cast<uint32_t *>(dev + q6k_offset(row, b, nb));
     for (int t = 0; t < 4; t++)
         for (int w = 0; w < 12; w++) {
             const uint8_t *p = s + q6k_src_off(t, w);
             d[12 * t + w] = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
         }
-    for (int i = 0; i < 4; i++) {
-        const uint8_t *p = s + 192 + 4 * i;
-        d[48 + i] = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+    for (int w = 0; w < 4; w++) {
+        const uint8_t *p = s + 192 + 4 * w;
+        d[48 + w] = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
     }
-    darr[b] = (uint16_t)(s[208] | (s[209] << 8));
+    *reinterpret_cast<uint16_t *>(dev + q6k_d_offset(row, b, nb)) = (uint16_t)(s[208] | (s[209] << 8));
 }
 
-__global__ void k_unpack_q6k(const uint8_t *__restrict__ main, const uint16_t *__restrict__ darr,
-                             uint8_t *__restrict__ dst, int64_t nblocks) {
-    int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    uint8_t *o = dst + b * 210;
-    const uint32_t *s = reinterpret_cast<const uint32_t *>(main + b * 208);
+__global__ void k_unpack_q6k(const uint8_t *__restrict__ dev, uint8_t *__restrict__ dst, int64_t nblocks,
+                             int64_t nb) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const int64_t row = i / nb, b = i % nb;
+    uint8_t *o = dst + i * 210;
+    const uint32_t *s = reinterpret_cast<const uint32_t *>(dev + q6k_offset(row, b, nb));
     for (int t = 0; t < 4; t++)
         for (int w = 0; w < 12; w++) {
             uint32_t v = s[12 * t + w];
             uint8_t *p = o + q6k_src_off(t, w);
             p[0] = v & 0xFF; p[1] = (v >> 8) & 0xFF; p[2] = (v >> 16) & 0xFF; p[3] = v >> 24;
         }
-    for (int i = 0; i < 4; i++) {
-        uint32_t v = s[48 + i];
-        uint8_t *p = o + 192 + 4 * i;
+    for (int w = 0; w < 4; w++) {
+        uint32_t v = s[48 + w];
+        uint8_t *p = o + 192 + 4 * w;
         p[0] = v & 0xFF; p[1] = (v >> 8) & 0xFF; p[2] = (v >> 16) & 0xFF; p[3] = v >> 24;
     }
-    o[208] = darr[b] & 0xFF;
-    o[209] = darr[b] >> 8;
+    const uint16_t d = *reinterpret_cast<const uint16_t *>(dev + q6k_d_offset(row, b, nb));
+    o[208] = d & 0xFF;
+    o[209] = d >> 8;
 }
 
 void launch_repack(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *gguf, void *dev) {
-    int64_t nbl = n * (k / QK);
+    const int64_t nb = k / QK, nbl = n * nb;
     unsigned grid = (unsigned)((nbl + 255) / 256);
     if (dtype == FB_Q4_K) {
-        k_repack_q4k<<<grid, 256, 0, ctx->stream>>>((const uint32_t *)gguf, (uint32_t *)dev, nbl);
+        k_repack_q4k<<<grid, 256, 0, ctx->stream>>>((const uint32_t *)gguf, (uint8_t *)dev, nbl, nb);
     } else if (dtype == FB_Q6_K) {
-        k_repack_q6k<<<grid, 256, 0, ctx->stream>>>((const uint8_t *)gguf, (uint8_t *)dev,
-                                                     (uint16_t *)((uint8_t *)dev + (size_t)nbl * 208), nbl);
+        k_repack_q6k<<<grid, 256, 0, ctx->stream>>>((const uint8_t *)gguf, (uint8_t *)dev, nbl, nb);
     } else {
         fail(FB_ERR_INVALID, "repack: unsupported dtype");
     }
@@ -260,13 +262,12 @@ void launch_repack(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *ggu
 }
 
 void launch_unpack(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *dev, void *gguf) {
-    int64_t nbl = n * (k / QK);
+    const int64_t nb = k / QK, nbl = n * nb;
     unsigned grid = (unsigned)((nbl + 255) / 256);
     if (dtype == FB_Q4_K) {
-        k_unpack_q4k<<<grid, 256, 0, ctx->stream>>>((const uint32_t *)dev, (uint32_t *)gguf, nbl);
+        k_unpack_q4k<<<grid, 256, 0, ctx->stream>>>((const uint8_t *)dev, (uint32_t *)gguf, nbl, nb);
     } else if (dtype == FB_Q6_K) {
-        k_unpack_q6k<<<grid, 256, 0, ctx->stream>>>(
-            (const uint8_t *)dev, (const uint16_t *)((const uint8_t *)dev + (size_t)nbl * 208), (uint8_t *)gguf, nbl);
+        k_unpack_q6k<<<grid, 256, 0, ctx->stream>>>((const uint8_t *)dev, (uint8_t *)gguf, nbl, nb);
     } else {
         fail(FB_ERR_INVALID, "unpack: unsupported dtype");
     }
@@ -381,11 +382,12 @@ template <> __device__ __forceinline__ __half cvt_out<__half>(float v) { return 
 template <> __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
 template <typename T>
-__global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__ w, int64_t nblocks, T *__restrict__ y) {
+__global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
+                                                     T *__restrict__ y) {
     const int lane = threadIdx.x & 31;
     const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (b >= nblocks) return;
-    const uint8_t *blk = w + b * 144;
+    const uint8_t *blk = w + q4k_offset(b / nb, b % nb, nb);
     const uint32_t *hw = reinterpret_cast<const uint32_t *>(blk);
     Q4Scales s = q4k_unpack_scales(hw[1], hw[2], hw[3]);
     const float d = h2f((uint16_t)(hw[0] & 0xFFFF)), dmin = h2f((uint16_t)(hw[0] >> 16));
@@ -407,13 +409,13 @@ __global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__ w, const uint16_t *__restrict__ dar,
-                                                     int64_t nblocks, T *__restrict__ y) {
+__global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
+                                                     T *__restrict__ y) {
     const int lane = threadIdx.x & 31;
     const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (b >= nblocks) return;
-    const uint32_t *blk = reinterpret_cast<const uint32_t *>(w + b * 208);
-    const float d = h2f(dar[b]);
+    const uint32_t *blk = reinterpret_cast<const uint32_t *>(w + q6k_offset(b / nb, b % nb, nb));
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(w + q6k_d_offset(b / nb, b % nb, nb)));
     T *out = y + b * QK + 8 * lane;
 #pragma unroll
     for (int e = 0; e < 8; e++) {
@@ -430,21 +432,20 @@ __global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__
 }
 
 void launch_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out, int out_dtype) {
-    int64_t nbl = t->n * t->nb();
+    const int64_t nb = t->nb(), nbl = t->n * nb;
     unsigned grid = (unsigned)((nbl + 7) / 8);
     cudaStream_t s = ctx->stream;
     if (t->dtype == FB_Q4_K) {
-        if (out_dtype == FB_F32) k_dequant_q4k<float><<<grid, 256, 0, s>>>(t->main(), nbl, (float *)out);
-        else if (out_dtype == FB_F16) k_dequant_q4k<__half><<<grid, 256, 0, s>>>(t->main(), nbl, (__half *)out);
+        if (out_dtype == FB_F32) k_dequant_q4k<float><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (float *)out);
+        else if (out_dtype == FB_F16) k_dequant_q4k<__half><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (__half *)out);
         else if (out_dtype == FB_BF16)
-            k_dequant_q4k<__nv_bfloat16><<<grid, 256, 0, s>>>(t->main(), nbl, (__nv_bfloat16 *)out);
+            k_dequant_q4k<__nv_bfloat16><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (__nv_bfloat16 *)out);
         else fail(FB_ERR_INVALID, "dequantize: out_dtype must be F32, F16 or BF16");
     } else if (t->dtype == FB_Q6_K) {
-        if (out_dtype == FB_F32) k_dequant_q6k<float><<<grid, 256, 0, s>>>(t->main(), t->q6_d(), nbl, (float *)out);
-        else if (out_dtype == FB_F16)
-            k_dequant_q6k<__half><<<grid, 256, 0, s>>>(t->main(), t->q6_d(), nbl, (__half *)out);
+        if (out_dtype == FB_F32) k_dequant_q6k<float><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (float *)out);
+        else if (out_dtype == FB_F16) k_dequant_q6k<__half><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (__half *)out);
         else if (out_dtype == FB_BF16)
-            k_dequant_q6k<__nv_bfloat16><<<grid, 256, 0, s>>>(t->main(), t->q6_d(), nbl, (__nv_bfloat16 *)out);
+            k_dequant_q6k<__nv_bfloat16><<<grid, 256, 0, s>>>(t->main(), nbl, nb, (__nv_bfloat16 *)out);
         else fail(FB_ERR_INVALID, "dequantize: out_dtype must be F32, F16 or BF16");
     } else if (t->dtype == FB_F32) {
         FB_REQUIRE(out_dtype == FB_F32, "dequantize: F32 tensor only to F32");

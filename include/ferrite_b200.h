@@ -157,9 +157,9 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
  * loop that must not take the synchronisation those calls can imply, uses
  * this entry point instead.  It allocates nothing: its split-K scratch is a
  * fixed 4 MiB array in the library's device image, so it accepts
- * batch * n_heads * ceil(max_seq_len / (2 * page_size)) * (head_dim + 2) * 8
- * bytes <= 4 MiB (e.g. 32 heads at 8192 tokens for batch 1) and returns
- * FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
+ * batch * n_heads * ceil(max_seq_len / page_size) * (head_dim + 2) * 8 bytes
+ * (plus 256 bytes of merge counters) <= 4 MiB (e.g. 32 heads at 4096 tokens
+ * with 64-token pages for batch 1) and returns FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
  * device address (make that first call before any stream capture).  All calls
  * on a device share the array, so calls that overlap on the GPU race. */
 int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,
