@@ -155,8 +155,10 @@ void launch_rope(fb_ctx *ctx, float *x, int64_t n_tok, int64_t n_heads, int64_t 
 void launch_swiglu(fb_ctx *ctx, const float *g, const float *u, float *out, int64_t m, int64_t f);
 
 // Fused decode-step kernels (ops.cu).
-void launch_residual_rmsnorm_q8k(fb_ctx *ctx, float *x, const float *add, const float *g, int rows, int dim, float eps,
-                                 const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab);
+// Reads the residual x (+ add), writes it to x_out (must not alias x).
+void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, float *x_out, const float *g, int rows,
+                                 int dim, float eps, const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens,
+                                 int vocab);
 void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
                        const float *kn, float eps, const float *cos_t, const float *sin_t, int mode,
                        const int32_t *pos, int max_ctx, float *q_out, void *kpool, void *vpool,

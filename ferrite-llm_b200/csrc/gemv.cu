@@ -39,8 +39,7 @@
 
 namespace fb {
 
-constexpr int KS = 4;     // warps per CTA (super-block slices of a tile)
-constexpr int DEPTH = 6;  // TMA ring stages per warp
+constexpr int KS_MAX = 8;  // warps per CTA (super-block slices of a tile): 4 or 8
 
 template <int DT> struct QRec;
 template <> struct QRec<4> { static constexpr int bytes = Q4K_REC; };
@@ -292,7 +291,8 @@ __device__ __forceinline__ void q4k_block_dp4a(const uint8_t *rec, const Q8Act &
         int dot[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int t = 0; t < 4; t++) {
-            const uint4 a0 = ld_act16(qa + 64 * t), a1 = ld_act16(qa + 64 * t + 16);
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(qa + 64 * t);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(qa + 64 * t + 16);
             const uint4 w = wq[t];
             dot[0] = dp4(w.x & 0x0F0F0F0Fu, a0.x, dot[0]);
             dot[0] = dp4(w.y & 0x0F0F0F0Fu, a0.y, dot[0]);
@@ -347,7 +347,8 @@ __device__ __forceinline__ void q6k_block_dp4a(const uint8_t *rec, const Q8Act &
         int dg[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};  // [part p][t >> 1]: group 8h + 2p + (t >> 1)
 #pragma unroll
         for (int t = 0; t < 4; t++) {
-            const uint4 a0 = ld_act16(qa + 64 * t), a1 = ld_act16(qa + 64 * t + 16);
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(qa + 64 * t);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(qa + 64 * t + 16);
             const uint32_t av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const uint32_t qlw[4] = {ql[t].x, ql[t].y, ql[t].z, ql[t].w};  // index 2j + x
             const uint32_t qhw[2] = {qh[t].x, qh[t].y};                        // index x
@@ -390,20 +391,30 @@ __device__ __forceinline__ void q6k_block_dp4a(const uint8_t *rec, const Q8Act &
 }
 
 // ----------------------------------------------------------- pipeline ---
+// Bytes of the shared-memory copy of M activation rows of length k (dp4a
+// path): qs [M][k] | d [M][k/256] f32 | bs16 [M][k/16] | bs32 [M][k/32].
+__host__ __device__ inline size_t r16(size_t x) { return (x + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t act_smem_bytes(int M, int64_t k) {
+    return r16((size_t)M * k) + r16((size_t)M * (k / 256) * 4) + r16((size_t)M * (k / 16) * 2) +
+           r16((size_t)M * (k / 32) * 2);
+}
+
 // NT > 0: MMA consumer with NT 8-wide n-tiles (m <= 8*NT); NT < 0: dp4a
-// consumer for exactly M = -NT activation rows.
-template <int DT, int NT, bool DOTS>
+// consumer for exactly M = -NT activation rows, whose Q8_K rows are first
+// copied to shared memory.  KS warps per CTA, `depth` ring stages per warp.
+template <int DT, int NT, bool DOTS, int KS>
 __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W, int64_t n, int nb, int n_tiles,
                                                   Q8Act a, int m, float *__restrict__ y, int64_t ldy,
                                                   int32_t *__restrict__ dots_sc, int32_t *__restrict__ dots_min,
-                                                  uint32_t *err) {
+                                                  uint32_t *err, int depth) {
     constexpr int REC = QRec<DT>::bytes;
+    const int DEPTH = depth;
     constexpr bool DP4A = NT < 0;
     constexpr int M = DP4A ? -NT : 1;
     constexpr int C = DP4A ? M : 8 * NT;
     constexpr int NTA = DP4A ? 1 : NT;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bars[KS * DEPTH];
+    __shared__ uint64_t bars[KS * 8];
     __shared__ double red[KS * 16 * (C + 1)];
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -412,8 +423,9 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     const int bbeg = min(nb, warp * bpw), nmine = min(nb, bbeg + bpw) - bbeg;
     const int ntl = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int total = ntl * nmine;  // records this warp streams
-    uint8_t *ring = smem + (size_t)warp * DEPTH * REC;
-    uint64_t *wbar = bars + warp * DEPTH;
+    const size_t act_bytes = DP4A ? (act_smem_bytes(M, a.k) + 127) & ~(size_t)127 : 0;
+    uint8_t *ring = smem + act_bytes + (size_t)warp * DEPTH * REC;
+    uint64_t *wbar = bars + warp * 8;
     if (lane == 0) {
         for (int i = 0; i < DEPTH; i++) mbar_init(&wbar[i], 1);
         mbar_fence_init();
@@ -432,6 +444,31 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     if (lane == 0)
         for (; issued < DEPTH && issued < total; issued++) issue(issued);
     pdl_wait();
+    pdl_launch();  // let the next kernel start streaming its weights
+    Q8Act act = a;
+    if constexpr (DP4A) {
+        // the activation rows are read by every record: keep them in shared memory
+        const int64_t k = a.k;
+        // regions rounded up to 16 bytes; the global arrays are padded to 256
+        // bytes (q8act_view), so the rounded copies stay inside them
+        const size_t bq = r16((size_t)M * k), bd = r16((size_t)M * (k / 256) * 4), b16 = r16((size_t)M * (k / 16) * 2),
+                     b32 = r16((size_t)M * (k / 32) * 2);
+        uint8_t *sq = smem;
+        float *sd = reinterpret_cast<float *>(smem + bq);
+        int16_t *s16 = reinterpret_cast<int16_t *>(smem + bq + bd);
+        int16_t *s32 = reinterpret_cast<int16_t *>(smem + bq + bd + b16);
+        const int64_t nq = (int64_t)(bq / 16), nd = (int64_t)(bd / 16), n16 = (int64_t)(b16 / 16), n32 = (int64_t)(b32 / 16);
+        for (int64_t i = threadIdx.x; i < nq; i += blockDim.x)
+            reinterpret_cast<uint4 *>(sq)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.qs) + i);
+        for (int64_t i = threadIdx.x; i < nd; i += blockDim.x)
+            reinterpret_cast<uint4 *>(sd)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.d) + i);
+        for (int64_t i = threadIdx.x; i < n16; i += blockDim.x)
+            reinterpret_cast<uint4 *>(s16)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.bs16) + i);
+        for (int64_t i = threadIdx.x; i < n32; i += blockDim.x)
+            reinterpret_cast<uint4 *>(s32)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.bs32) + i);
+        act = Q8Act{reinterpret_cast<int8_t *>(sq), sd, s16, s32, k};
+        __syncthreads();
+    }
     bool ok = true;
     int c = 0;
     for (int ti = 0; ti < ntl; ti++) {
@@ -451,9 +488,9 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
                 const uint8_t *rec = ring + (size_t)slot * REC;
                 if constexpr (DP4A) {
                     if constexpr (DT == 4)
-                        q4k_block_dp4a<M, DOTS>(rec, a, bbeg + bl, nb, lane, row0, n, accd, dots_sc, dots_min);
+                        q4k_block_dp4a<M, DOTS>(rec, act, bbeg + bl, nb, lane, row0, n, accd, dots_sc, dots_min);
                     else
-                        q6k_block_dp4a<M, DOTS>(rec, a, bbeg + bl, nb, lane, row0, n, accd, dots_sc);
+                        q6k_block_dp4a<M, DOTS>(rec, act, bbeg + bl, nb, lane, row0, n, accd, dots_sc);
                 } else {
                     if constexpr (DT == 4)
                         q4k_block<NTA, DOTS>(rec, a, m, bbeg + bl, nb, gid, tig, row0, n, acc, dots_sc, dots_min);
@@ -507,19 +544,23 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     pdl_launch();
 }
 
-template <int DT, int NT, bool DOTS>
-static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
+template <int DT, int NT, bool DOTS, int KS>
+static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
                           int32_t *dsc, int32_t *dmn) {
     constexpr int REC = QRec<DT>::bytes;
-    const size_t smem = (size_t)KS * DEPTH * REC;
-    auto kernel = k_gemv<DT, NT, DOTS>;
-    static int occ = 0;  // resident CTAs per SM (per instantiation)
+    constexpr int M = NT < 0 ? -NT : 0;
+    const size_t act = M ? (act_smem_bytes(M, w->k) + 127) & ~(size_t)127 : 0;
+    // ring depth: as deep as fits next to the staged activations while keeping
+    // 16 warps per SM (4 CTAs of 4 warps or 2 of 8), 3..8 stages per warp
+    const size_t budget = (size_t)(KS == 4 ? 56 : 112) * 1024;
+    int depth = (int)std::min<size_t>(8, (budget - std::min(act, budget / 2)) / ((size_t)KS * REC));
+    depth = std::max(depth, 3);
+    const size_t smem = act + (size_t)KS * depth * REC;
+    auto kernel = k_gemv<DT, NT, DOTS, KS>;
     FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (occ == 0) {
-        int o = 0;
-        FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kernel, KS * 32, smem));
-        occ = o > 0 ? o : 1;
-    }
+    int occ = 0;
+    FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, KS * 32, smem));
+    FB_REQUIRE(occ > 0, "gemv: configuration does not fit on an SM");
     const int n_tiles = (int)w->n_tiles();
     const int grid = std::min(n_tiles, occ * ctx->num_sms);
     cudaLaunchConfig_t cfg = {};
@@ -533,7 +574,18 @@ static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, w->main(), w->n, (int)w->nb(), n_tiles, a, m, y, ldy, dsc, dmn,
-                               ctx->err_word));
+                               ctx->err_word, depth));
+}
+
+// Few tiles (fewer than two per SM): 8-warp CTAs so each SM still runs
+// enough warps; otherwise 4-warp CTAs.
+template <int DT, int NT, bool DOTS>
+static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
+                          int32_t *dsc, int32_t *dmn) {
+    if (w->n_tiles() < 2 * ctx->num_sms && w->nb() >= 16)
+        launch_gemv_k<DT, NT, DOTS, 8>(ctx, w, a, m, y, ldy, dsc, dmn);
+    else
+        launch_gemv_k<DT, NT, DOTS, 4>(ctx, w, a, m, y, ldy, dsc, dmn);
 }
 
 template <int DT>

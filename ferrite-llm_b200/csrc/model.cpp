@@ -85,7 +85,8 @@ struct fb_model {
     DevBuf kv;  // [L][K|V][num_pages][n_kv][page][hd] fp16
     DevBuf block_table, rope_cos, rope_sin;
     // step buffers
-    DevBuf x, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml, att_cnt;
+    DevBuf x, x2, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml, att_cnt;
+    float *x_last = nullptr;  // residual buffer holding the last step's final value
     DevBuf act_h, act_a, act_f;
     DevBuf tok, pos, next;
     int32_t *pinned = nullptr;  // host staging [3 * max_batch]
@@ -163,8 +164,10 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     const Q8Act ah = q8act_view(m->act_h.ptr, b, H);
     const Q8Act aa = q8act_view(m->act_a.ptr, b, qd);
     const Q8Act af = q8act_view(m->act_f.ptr, b, F);
-    float *x = m->x.as<float>();
-    launch_residual_rmsnorm_q8k(ctx, x, nullptr, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
+    // residual stream ping-pongs between two buffers (the norm kernels read
+    // one row while writing the updated row)
+    float *xa = m->x.as<float>(), *xb = m->x2.as<float>();
+    launch_residual_rmsnorm_q8k(ctx, nullptr, nullptr, xa, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
                                 m->tok_embd.t, m->tok.as<int32_t>(), c.vocab);
     mark(FB_PROF_EMBED_NORM, 1);
     AttnArgs A{};
@@ -201,8 +204,9 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         mark(FB_PROF_ATTN, 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         mark(FB_PROF_O, 1);
-        launch_residual_rmsnorm_q8k(ctx, x, m->y_o.as<float>(), L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
+        launch_residual_rmsnorm_q8k(ctx, xa, m->y_o.as<float>(), xb, L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
                                     nullptr, c.vocab);
+        std::swap(xa, xb);
         mark(FB_PROF_NORM, 1);
         launch_gemv(ctx, L.wgu.t, ah, b, m->y_gu.as<float>(), 2 * F);
         mark(FB_PROF_GATE_UP, 1);
@@ -211,9 +215,11 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         launch_gemv(ctx, L.wdown.t, af, b, m->y_d.as<float>(), H);
         mark(FB_PROF_DOWN, 1);
         const float *gn = (l + 1 < c.n_layers) ? m->layers[l + 1]->attn_norm.as<float>() : m->out_norm.as<float>();
-        launch_residual_rmsnorm_q8k(ctx, x, m->y_d.as<float>(), gn, b, H, c.eps, ah, nullptr, nullptr, c.vocab);
+        launch_residual_rmsnorm_q8k(ctx, xa, m->y_d.as<float>(), xb, gn, b, H, c.eps, ah, nullptr, nullptr, c.vocab);
+        std::swap(xa, xb);
         mark(FB_PROF_NORM, 1);
     }
+    m->x_last = xa;
     launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), c.vocab);
     mark(FB_PROF_LM_HEAD, 1);
     launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>());
@@ -318,6 +324,7 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         const int B = c.max_batch, H = c.hidden, qd = c.n_heads * c.head_dim;
         const int kd = c.n_kv_heads * c.head_dim;
         m->x.alloc((size_t)B * H * 4);
+        m->x2.alloc((size_t)B * H * 4);
         m->y_qkv.alloc((size_t)B * (qd + 2 * kd) * 4);
         m->q.alloc((size_t)B * qd * 4);
         m->attn.alloc((size_t)B * qd * 4);
@@ -655,8 +662,14 @@ int fb_model_read_activation(fb_model *m, const char *name, int row, float *out_
         const std::string n(name);
         const DevBuf *buf = nullptr;
         int64_t len = 0;
-        if (n == "x") buf = &m->x, len = c.hidden;
-        else if (n == "qkv") buf = &m->y_qkv, len = qd + 2 * kd;
+        if (n == "x") {
+            FB_REQUIRE(m->x_last, "no decode step has run yet");
+            len = c.hidden;
+            FB_CUDA(cudaMemcpyAsync(out_host, m->x_last + (size_t)row * len, (size_t)len * 4, cudaMemcpyDeviceToHost,
+                                    m->ctx->stream));
+            FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+            return;
+        } else if (n == "qkv") buf = &m->y_qkv, len = qd + 2 * kd;
         else if (n == "q") buf = &m->q, len = qd;
         else if (n == "attn") buf = &m->attn, len = qd;
         else if (n == "o") buf = &m->y_o, len = c.hidden;

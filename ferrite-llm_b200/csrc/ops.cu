@@ -93,10 +93,14 @@ __device__ __forceinline__ float rms_of(double ss, int dim, float eps) {
 }
 
 // ------------------------------------------------------------------------
-// Residual add + RMSNorm + Q8_K, one CTA (NW warps) per row of width dim.
-// x[row] (+= add[row] when add != null) is written back when x_out != null;
-// emb_tab != null replaces x by the dequantized embedding row of token[row].
-constexpr int NORM_WARPS = 16;
+// Residual add + RMSNorm + Q8_K.  One CTA per (256-value block, row): every
+// CTA sums the squares of the whole row itself (binary64; the row is a few
+// KB in L2) and then normalizes and quantizes only its own block, so the row
+// is processed by dim/256 CTAs in parallel.  x[row] (+= add[row] when add !=
+// null) is written to x_out block by block (a different buffer: other CTAs
+// are still reading x); emb_tab != null takes the dequantized embedding row
+// of token[row] instead of x.
+constexpr int NORM_THREADS = 256;
 
 __device__ __forceinline__ float q4k_value(const uint8_t *blk, int i) {
     const uint32_t *hw = reinterpret_cast<const uint32_t *>(blk);
@@ -111,53 +115,48 @@ __device__ __forceinline__ float q4k_value(const uint8_t *blk, int i) {
     return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)nib), __fmul_rn(dmin, (float)mn));
 }
 
-__global__ void __launch_bounds__(NORM_WARPS * 32)
-    k_residual_rmsnorm_q8k(float *__restrict__ x, const float *__restrict__ add, const float *__restrict__ g,
-                           int dim, float eps, Q8Act a, const uint8_t *__restrict__ emb_tab,
-                           const int32_t *__restrict__ tokens, int vocab, uint32_t *err) {
-    __shared__ double sh[NORM_WARPS];
-    extern __shared__ float xs[];  // dim floats
+__global__ void __launch_bounds__(NORM_THREADS)
+    k_residual_rmsnorm_q8k(const float *__restrict__ x, const float *__restrict__ add, float *__restrict__ x_out,
+                           const float *__restrict__ g, int dim, float eps, Q8Act a,
+                           const uint8_t *__restrict__ emb_tab, const int32_t *__restrict__ tokens, int vocab,
+                           uint32_t *err) {
+    __shared__ double sh[NORM_THREADS / 32];
+    __shared__ float xb[QK];
+    const int blk = blockIdx.x;
+    const int64_t row = blockIdx.y;
     pdl_wait();
-    const int64_t row = blockIdx.x;
-    float *xr = x + row * dim;
-    double ss = 0.0;
+    pdl_launch();
+    const float *xr = x ? x + row * dim : nullptr;
+    const int nbe = dim / QK;
+    int tok = 0;
     if (emb_tab) {
-        int tok = tokens[row];
+        tok = tokens[row];
         if (tok < 0 || tok >= vocab) {
-            if (threadIdx.x == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
+            if (threadIdx.x == 0 && blk == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
             tok = 0;
         }
-        const int64_t nbe = dim / QK;
-        for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-            const float v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
-            xs[i] = v;
-            xr[i] = v;
-            ss = __fma_rn((double)v, (double)v, ss);
-        }
-    } else {
-        for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-            float v = xr[i];
-            if (add) {
-                v = __fadd_rn(add[row * dim + i], v);
-                xr[i] = v;
-            }
-            xs[i] = v;
-            ss = __fma_rn((double)v, (double)v, ss);
-        }
     }
-    ss = block_sum64<NORM_WARPS>(ss, sh);
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < dim; i += NORM_THREADS) {
+        float v;
+        if (emb_tab) v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
+        else v = add ? __fadd_rn(add[row * dim + i], xr[i]) : xr[i];
+        ss = __fma_rn((double)v, (double)v, ss);
+        if (i / QK == blk) xb[i % QK] = v;
+    }
+    ss = block_sum64<NORM_THREADS / 32>(ss, sh);  // (has a __syncthreads before the shared reads)
     const float m = rms_of(ss, dim, eps);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int blk = warp; blk < dim / QK; blk += NORM_WARPS) {
+    if (x_out) x_out[row * dim + blk * QK + threadIdx.x] = xb[threadIdx.x];
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
             const int i = blk * QK + 8 * lane + e;
-            v[e] = __fmul_rn(__fdiv_rn(xs[i], m), g[i]);
+            v[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), g[i]);
         }
         q8k_store_warp(v, lane, a, row, blk);
     }
-    pdl_launch();
 }
 
 // ------------------------------------------------------------------------
@@ -172,6 +171,7 @@ __global__ void __launch_bounds__(256)
                  const int32_t *__restrict__ block_table, int max_pages, int page_size, int num_pages,
                  uint32_t *err) {
     pdl_wait();
+    pdl_launch();
     const int row = blockIdx.y;
     const int head = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(256)
 // SwiGLU + Q8_K: y[row] = [gate (f) | up (f)] -> act = Q8K(silu(gate) * up).
 __global__ void __launch_bounds__(256) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
     pdl_wait();
+    pdl_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nbk = f / QK;
     const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -377,19 +378,18 @@ static void launch_k(fb_ctx *ctx, K kernel, dim3 grid, dim3 block, size_t smem, 
     FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
 }
 
-void launch_residual_rmsnorm_q8k(fb_ctx *ctx, float *x, const float *add, const float *g, int rows, int dim, float eps,
-                                 const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab) {
+void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, float *x_out, const float *g, int rows,
+                                 int dim, float eps, const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens,
+                                 int vocab) {
     FB_REQUIRE(dim % QK == 0, "rmsnorm_q8k: dim must be a multiple of 256");
-    const size_t smem = (size_t)dim * 4;
-    if (smem > 48 * 1024)
-        FB_CUDA(cudaFuncSetAttribute(k_residual_rmsnorm_q8k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const uint8_t *tab = nullptr;
     if (emb) {
         FB_REQUIRE(emb->dtype == FB_Q4_K && emb->k == dim, "embedding table must be Q4_K [vocab, hidden]");
         tab = emb->main();
     }
-    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(rows), dim3(NORM_WARPS * 32), smem, x, add, g, dim, eps, a, tab,
-             tokens, vocab, ctx->err_word);
+    FB_REQUIRE(x_out != x, "rmsnorm_q8k: x_out must not alias x");
+    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g, dim, eps, a,
+             tab, tokens, vocab, ctx->err_word);
 }
 
 void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
