@@ -7,35 +7,57 @@
 // crates/ferrite-core/kernels/flash_attention.cu:166-225 (f32, hd <= 64,
 // never launched).
 //
+// KV layout (per layer): K pages are dim-major, [page][kv head][hd][page
+// tokens], V pages token-major, [page][kv head][page tokens][hd], fp16.
+//
 // B200 design (HBM-bound: 2 * ctx * n_kv * hd * 2 bytes per layer and token):
-//  * split-K: CTA (kv head, split of 2 pages, sequence); every CTA of the
-//    grid issues its K and V page copies at once with cp.async.bulk (TMA,
-//    one 16 KB copy per page, no multicast) onto per-page mbarriers, so each
-//    SM keeps >64 KB in flight;
-//  * the G = n_heads / n_kv query heads of the kv head share each K/V row
-//    read from shared memory;
-//  * scores: lane owns 4 dims of hd, a 32-value butterfly reduce-scatter
-//    turns (32/G tokens x G heads) per-lane partials into one full dot per
-//    lane (31 shuffles per 32 dots);
-//  * partial (max, sum, o) per split go to a scratch buffer; a combine kernel
-//    merges the splits (log-sum-exp) and, fused into the model path,
-//    quantizes the result to Q8_K for the output projection;
-//  * dots, exponentials and sums run in binary64 with one rounding to f32
-//    at the end, so the result equals the CPU oracle's single-pass softmax
-//    bit for bit whatever the split layout.
-// All mbarrier waits are bounded: on timeout the kernel raises
-// ERRBIT_WAIT_TIMEOUT in the context's error word and returns.
+//  * one thread-block cluster of ATT_SPLITS CTAs per (kv head, sequence); the
+//    sequence's 64-token chunks are split evenly over the cluster at run time
+//    (from the sequence length on the device), so the grid does not depend on
+//    the context length;
+//  * each CTA streams its chunks through a ring of `depth` shared-memory
+//    stages with cp.async.bulk (TMA, no multicast) on per-stage mbarriers;
+//  * scores: warp w owns 16 of the 128 dims, lane owns two adjacent tokens;
+//    dim-major K rows are read conflict-free and the G query heads (held as
+//    binary64 in shared memory) are broadcast, so each K element is
+//    converted once and feeds 2G DFMAs; the eight per-warp partial dots are
+//    summed in a fixed order;
+//  * online softmax over the chunks (running max per head, rescale factor
+//    exp(m_old - m_new)); P.V with the lane owning 4 dims of V rows;
+//  * the cluster merges its 16 partial (max, sum, o) sets through
+//    distributed shared memory: CTA r writes dims [8r, 8r+8) of every head,
+//    then (model path) the first G/2 CTAs quantize the result to Q8_K for
+//    the output projection.  No global scratch, counters or atomics.
+//  * a variant without clusters (for the allocation-free entry point, or a
+//    GPU partition that cannot hold a 16-CTA cluster) writes the partials to
+//    global scratch and lets the last CTA of each (kv head, sequence) merge.
+// Dots, exponentials and sums run in binary64 with one rounding to f32 at the
+// end, so the result equals the CPU oracle's single-pass softmax bit for bit
+// whatever the split layout.  All mbarrier waits are bounded: on timeout the
+// kernel raises ERRBIT_WAIT_TIMEOUT in the context's error word.
 #include <math.h>
 
+#include <algorithm>
+#include <cooperative_groups.h>
+#include <map>
 #include <mutex>
 
 #include "fb_internal.h"
 #include "kq_common.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace fb {
 
 constexpr int ATT_HD = 128;
-constexpr int ATT_WARPS = 4;
+constexpr int ATT_CHUNK = 64;  // tokens per pipeline stage (one or two pages)
+constexpr int ATT_WARPS = 8;
+constexpr int ATT_THREADS = 32 * ATT_WARPS;
+constexpr int ATT_DPR = ATT_HD / ATT_SPLITS;  // output dims merged per cluster rank
+constexpr int ATT_MAX_DEPTH = 4;
+constexpr int ATT_KPAD = 64;  // bytes between the two K pages of a 32-token-page chunk (bank shift)
+constexpr uint32_t ATT_STAGE_K = ATT_CHUNK * ATT_HD * 2 + ATT_KPAD;  // K^T region of a stage
+constexpr uint32_t ATT_STAGE = ATT_STAGE_K + ATT_CHUNK * ATT_HD * 2;  // + V region
 
 __device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
     return A.seq_lens ? A.seq_lens[b] : A.pos[b] + 1;
@@ -44,279 +66,394 @@ __device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
 __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
                                                    int64_t blk);
 
-// One CTA per (kv head, page of the sequence, sequence).  Dynamic shared
-// memory: K[page][hd] half, V[page][hd] half, q[G][hd] f32, s[G][page] f32,
-// p[G][page] f64, red[ATT_WARPS][G][hd] f64.  The last CTA of each (sequence,
-// kv head) to finish merges all pages' partials (fixed order) and writes the
-// G heads' output (f32 and/or Q8_K); the per-(sequence, kv head) counters
-// return to zero afterwards.
+// Dynamic shared memory of one CTA (byte offsets).
+struct AttnLayout {
+    size_t q, part, p, misc, inbox, q8in, bt, total;
+};
+__host__ __device__ inline AttnLayout attn_layout(int G, int depth, int bt_cap) {
+    AttnLayout L;
+    size_t off = (size_t)depth * ATT_STAGE;
+    off = (off + 127) & ~(size_t)127;
+    L.q = off;  // q[hd][G] f32; merged outputs (f32) at the end
+    off += (size_t)ATT_HD * G * 4;
+    L.part = off;  // part[warp][G][chunk] f32 slice dots; CTA partial o[G][hd] f64 at the end
+    const size_t part_bytes = (size_t)ATT_WARPS * G * ATT_CHUNK * 4, o_bytes = (size_t)G * ATT_HD * 8;
+    off += part_bytes > o_bytes ? part_bytes : o_bytes;
+    L.p = off;  // p[chunk][G] f64
+    off += (size_t)ATT_CHUNK * G * 8;
+    L.misc = off;  // alpha[G] M[G] L[G] ls[warps] wts[G][S] wl[G][S] f64
+    off += (size_t)(3 * G + ATT_WARPS + 2 * G * ATT_SPLITS) * 8;
+    L.inbox = off;  // cluster merge: [src rank][G][ATT_DPR + 2] f64 pushed by the peers
+    off += (size_t)ATT_SPLITS * G * (ATT_DPR + 2) * 8;
+    L.q8in = off;  // cluster merge: [2][hd] f32 outputs of one Q8_K block
+    off += (size_t)2 * ATT_HD * 4;
+    L.bt = off;  // block-table entries of the CTA's pages
+    off += (size_t)bt_cap * 4;
+    L.total = (off + 127) & ~(size_t)127;
+    return L;
+}
+
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// grid (ATT_SPLITS, n_kv, batch); CLUSTER: cluster dims (ATT_SPLITS, 1, 1).
 //
-// Numerics (identical to the CPU oracle up to binary64 rounding):
-//   s_t = f32(sum_e q_e * k_te in binary64) * scale
-//   per page:  m = max_t s_t, p_t = exp64(s_t - m), l = sum p_t,
-//              o = sum p_t v_t              (binary64)
-//   merge:     M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
-template <int G>
-__global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq,
-                                                                int use_q8, int *__restrict__ counters) {
+// Numerics (identical to the CPU oracle, or_attn_dot / or_exp64):
+//   s_t = f32 dot of q and k_t in eight 16-dim fused-multiply-add slices,
+//         summed in slice order, times scale
+//   per CTA:  running max m, p_t = exp64(s_t - m), l = sum p_t,
+//             o = sum p_t v_t, rescaled by exp64(m_old - m_new)  (binary64)
+//   merge:    M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
+// The binary64 stages make the result independent of how the tokens are
+// split (up to binary64 rounding, far below the final f32 rounding).
+template <int G, bool CLUSTER>
+__global__ void __launch_bounds__(ATT_THREADS, 2)
+    k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq, int use_q8, int *__restrict__ counters,
+                  int depth, int bt_cap) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bars[2];  // K page, V page
-    __shared__ int s_last;
-    __shared__ double s_M[G], s_L[G];
-    const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+    __shared__ uint64_t full[ATT_MAX_DEPTH];
+    __shared__ int s_len, s_first, s_mine, s_last;
+    constexpr int S = ATT_SPLITS;
+    constexpr int TPW = ATT_CHUNK * G / ATT_WARPS;  // tokens per warp in the softmax phase
+    constexpr int TPC = ATT_CHUNK / ATT_WARPS;      // tokens per warp in the P.V phase
+    constexpr int IB = ATT_DPR + 2;                 // inbox doubles per (source rank, head)
+    // peers may push into this CTA's shared memory once every CTA of the
+    // cluster has started: arrive now, wait just before the first push
+    if constexpr (CLUSTER) cluster_arrive_relaxed();
+    const int rank = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int P = A.page_size;
-    // sequence lengths are inputs of the whole step (written before it began)
-    const int len = seq_len_of(A, b);
-    const int t0 = split * P;
-    if (t0 >= len) {
-        pdl_launch();
-        return;
-    }
-    const int nsplit = (len + P - 1) / P;
-    const int ntok = min(P, len - t0);
-    __half *Ks = reinterpret_cast<__half *>(smem);
-    __half *Vs = Ks + (size_t)P * ATT_HD;
-    float *qs = reinterpret_cast<float *>(Vs + (size_t)P * ATT_HD);
-    float *ss = qs + G * ATT_HD;
-    double *ps = reinterpret_cast<double *>(ss + G * P);
-    double *red = ps + G * P;
-    const uint32_t page_bytes = (uint32_t)P * ATT_HD * 2;
-    // the page holding the newest position is written by the preceding kernel
-    const bool fresh = t0 + P >= len;
+    const int P = A.page_size, PPC = ATT_CHUNK / P;  // pages per chunk
+    const AttnLayout Ly = attn_layout(G, depth, bt_cap);
+    uint8_t *ring = smem;
+    float *q_s = reinterpret_cast<float *>(smem + Ly.q);
+    float *part = reinterpret_cast<float *>(smem + Ly.part);
+    double *p_s = reinterpret_cast<double *>(smem + Ly.p);
+    double *alpha_s = reinterpret_cast<double *>(smem + Ly.misc);
+    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + ATT_WARPS, *wl = wts + G * S;
+    double *inbox = reinterpret_cast<double *>(smem + Ly.inbox);
+    float *q8in = reinterpret_cast<float *>(smem + Ly.q8in);
+    int *bt_s = reinterpret_cast<int *>(smem + Ly.bt);
+    double *O_s = reinterpret_cast<double *>(part);  // [G][hd] CTA partial at the end
+    double *red = reinterpret_cast<double *>(ring);  // [warps][G][hd] at the end
+    float *fin = q_s;                                // merged outputs at the end
+
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < depth; i++) mbar_init(&full[i], 1);
         mbar_fence_init();
+        // sequence lengths are inputs of the whole step (written before it began)
+        int len = seq_len_of(A, b);
+        const int cap = A.max_pages * P;
+        if (len < 1 || len > cap) {
+            atomicOr(A.err, ERRBIT_BAD_POS);
+            len = len < 1 ? 0 : cap;
+        }
+        const int nch = (len + ATT_CHUNK - 1) / ATT_CHUNK;
+        const int cpr = (nch + S - 1) / S;  // chunks per rank
+        const int first = min(rank * cpr, nch);
+        s_len = len;
+        s_first = first;
+        s_mine = min(cpr, nch - first);
     }
     __syncthreads();
-    int page = -1;
-    if (tid == 0) {
-        page = split < A.max_pages ? A.block_table[(int64_t)b * A.max_pages + split] : -1;
-        if (page < 0 || page >= A.num_pages) {
-            atomicOr(A.err, ERRBIT_BAD_PAGE);
-            page = -1;
+    const int len = s_len, first = s_first, mine = s_mine;
+    // block-table entries of this CTA's pages (-1: past the sequence end)
+    for (int i = tid; i < mine * PPC; i += ATT_THREADS) {
+        const int lp = first * PPC + i;
+        int page = -1;
+        if (lp * P < len) {
+            page = lp < A.max_pages ? A.block_table[(int64_t)b * A.max_pages + lp] : -1;
+            if (page < 0 || page >= A.num_pages) {
+                atomicOr(A.err, ERRBIT_BAD_PAGE);
+                page = -1;
+            }
         }
+        bt_s[i] = page;
     }
-    auto issue = [&]() {
-        if (page >= 0) {
+    __syncthreads();
+    const uint32_t pbytes = (uint32_t)P * ATT_HD * 2;  // one K (or V) page
+    auto issue = [&](int j) {                          // chunk j of this CTA into stage j % depth
+        const int st = j % depth;
+        uint8_t *kd = ring + (size_t)st * ATT_STAGE;
+        uint8_t *vd = kd + ATT_STAGE_K;
+        uint32_t bytes = 0;
+        for (int i = 0; i < PPC; i++)
+            if (bt_s[j * PPC + i] >= 0) bytes += 2 * pbytes;
+        mbar_expect_tx(&full[st], bytes);  // zero bytes: the phase completes without data
+        for (int i = 0; i < PPC; i++) {
+            const int page = bt_s[j * PPC + i];
+            if (page < 0) continue;
             const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
-            mbar_expect_tx(&bars[0], page_bytes);
-            bulk_g2s(Ks, reinterpret_cast<const __half *>(A.kpool) + off, page_bytes, &bars[0]);
-            mbar_expect_tx(&bars[1], page_bytes);
-            bulk_g2s(Vs, reinterpret_cast<const __half *>(A.vpool) + off, page_bytes, &bars[1]);
-        } else {
-            // complete the phases without data (the error word is set)
-            mbar_expect_tx(&bars[0], 0);
-            mbar_expect_tx(&bars[1], 0);
+            bulk_g2s(kd + i * (pbytes + ATT_KPAD), reinterpret_cast<const __half *>(A.kpool) + off, pbytes,
+                     &full[st]);
+            bulk_g2s(vd + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes, &full[st]);
         }
     };
-    if (tid == 0 && !fresh) issue();  // older pages stream in before the wait
+    // the chunk holding the newest position is written by the preceding
+    // kernel; older chunks stream in before the wait
+    const int jf = len > 0 ? (len - 1) / ATT_CHUNK - first : -1;
+    const int pre = min(mine, depth);
+    if (tid == 0)
+        for (int j = 0; j < pre; j++)
+            if (j != jf) issue(j);
     pdl_wait();
-    if (tid == 0 && fresh) issue();
-    const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
-    for (int i = tid; i < G * ATT_HD; i += blockDim.x) qs[i] = qg[i];
-    __syncthreads();
+    if (tid == 0 && jf >= 0 && jf < pre) issue(jf);
+    {
+        const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
+        for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) q_s[(i % ATT_HD) * G + i / ATT_HD] = qg[i];
+    }
 
-    // ---- scores: warp w handles tokens [WT*w, WT*w + WT) of the page
-    constexpr int TCH = 32 / G;  // tokens per reduce-scatter chunk
-    const int WT = P / ATT_WARPS;
-    const int tw0 = warp * WT;
-    bool waited_ok = true;
-    if (tw0 < ntok) {
-        waited_ok = mbar_wait_bounded(&bars[0], 0);
-        float qv[G][4];
-#pragma unroll
-        for (int g = 0; g < G; g++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) qv[g][e] = qs[g * ATT_HD + 4 * lane + e];
-        const int nch = WT > TCH ? WT / TCH : 1;
-#pragma unroll 1
-        for (int c = 0; c < nch; c++) {
-            const int tc0 = tw0 + c * TCH;
-            double v[32];
-#pragma unroll
-            for (int t = 0; t < TCH; t++) {
-                const int tok = tc0 + t;  // rows past the page are masked below
-                const uint2 kr = *reinterpret_cast<const uint2 *>(Ks + (size_t)tok * ATT_HD + 4 * lane);
-                const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
-                const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
-#pragma unroll
-                for (int g = 0; g < G; g++) {
-                    // f32 x fp16 products are exact in binary64
-                    double acc = __dmul_rn((double)qv[g][0], (double)k01.x);
-                    acc = __fma_rn((double)qv[g][1], (double)k01.y, acc);
-                    acc = __fma_rn((double)qv[g][2], (double)k23.x, acc);
-                    acc = __fma_rn((double)qv[g][3], (double)k23.y, acc);
-                    v[t * G + g] = acc;
-                }
-            }
-            // butterfly reduce-scatter: lane l ends with the sum of index l
-#pragma unroll
-            for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
-                const bool up = (lane & o) != 0;
-#pragma unroll
-                for (int i = 0; i < n / 2; i++) {
-                    const double send = up ? v[i] : v[i + n / 2];
-                    const double keep = up ? v[i + n / 2] : v[i];
-                    v[i] = __dadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
-                }
-            }
-            const int t = lane / G, g = lane % G;
-            const int tl = c * TCH + t, tok = tw0 + tl;
-            if (tl < WT) ss[g * P + tok] = tok < ntok ? __fmul_rn(__double2float_rn(v[0]), A.scale) : -INFINITY;
-        }
-    }
-    __syncthreads();
-    // ---- per-head page max and p_t = exp(s_t - max) (warps take heads)
-    double *ml = red;  // [G][2] before the P.V reduction reuses red
-    for (int g = warp; g < G; g += ATT_WARPS) {
-        float mx = -INFINITY;
-        for (int t = lane; t < ntok; t += 32) mx = fmaxf(mx, ss[g * P + t]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        double sum = 0.0;
-        for (int t = lane; t < P; t += 32) {
-            const double pv = t < ntok ? exp64(__dsub_rn((double)ss[g * P + t], (double)mx)) : 0.0;
-            ps[g * P + t] = pv;
-            sum = __dadd_rn(sum, pv);
-        }
-        sum = warp_sum64(sum);
-        if (lane == 0) {
-            ml[2 * g] = (double)mx;
-            ml[2 * g + 1] = sum;
-        }
-    }
-    __syncthreads();
-    double mls[G][2];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        mls[g][0] = ml[2 * g];
-        mls[g][1] = ml[2 * g + 1];
-    }
-    __syncthreads();
-    // ---- o = sum_t p_t * v_t; warp w over its tokens, lane owns 4 dims
+    const int hg = warp % G, kb = warp / G;  // softmax phase: head and token block of this warp
+    float m_run = -INFINITY;
+    double l_lane = 0.0;
     double o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) o[g][e] = 0.0;
-    if (tw0 < ntok) {
-        waited_ok = mbar_wait_bounded(&bars[1], 0) && waited_ok;
-        const int tend = min(tw0 + WT, ntok);
-        for (int tok = tw0; tok < tend; tok++) {
-            const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)tok * ATT_HD + 4 * lane);
-            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
-            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+    bool ok = true;
+    // this lane's token pair (2 lane, 2 lane + 1) inside a stage's K^T region
+    const int tk = 2 * lane;
+    const uint32_t k_lane = (uint32_t)((tk / P) * (pbytes + ATT_KPAD) + (tk % P) * 2);
+    const uint32_t k_row = 2u * P;  // bytes between consecutive dims
+
+    for (int j = 0; j < mine; j++) {
+        // every warp is done with chunk j-1 (and q is staged): its stage takes chunk j-1+depth
+        __syncthreads();
+        if (tid == 0 && j >= 1 && j - 1 + depth < mine) {
+            fence_proxy_async_smem();
+            issue(j - 1 + depth);
+        }
+        const int st = j % depth;
+        const uint8_t *kst = ring + (size_t)st * ATT_STAGE;
+        const __half *Vs = reinterpret_cast<const __half *>(kst + ATT_STAGE_K);
+        const int ntok = min(ATT_CHUNK, len - (first + j) * ATT_CHUNK);
+        ok = mbar_wait_bounded(&full[st], (uint32_t)(j / depth) & 1u) && ok;
+        // ---- scores: f32 slice dot over this warp's 16 dims for tokens tk, tk+1
+        {
+            float acc[2][G];
+#pragma unroll
+            for (int g = 0; g < G; g++) acc[0][g] = acc[1][g] = 0.f;
+            const uint8_t *kp = kst + k_lane + (size_t)(warp * 16) * k_row;
+            const float *qw = q_s + warp * 16 * G;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(kp + e * k_row));
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float qv = qw[e * G + g];
+                    acc[0][g] = __fmaf_rn(qv, kf.x, acc[0][g]);
+                    acc[1][g] = __fmaf_rn(qv, kf.y, acc[1][g]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++)
+                *reinterpret_cast<float2 *>(&part[(warp * G + g) * ATT_CHUNK + tk]) =
+                    make_float2(acc[0][g], acc[1][g]);
+        }
+        __syncthreads();
+        // ---- softmax: warp (hg, kb) scores all 64 tokens of head hg (for the
+        // chunk max) and exponentiates its block of TPW tokens
+        {
+            float sc[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int t = lane + 32 * h;
+                float sum = part[hg * ATT_CHUNK + t];
+#pragma unroll
+                for (int w = 1; w < ATT_WARPS; w++) sum = __fadd_rn(sum, part[(w * G + hg) * ATT_CHUNK + t]);
+                sc[h] = t < ntok ? __fmul_rn(sum, A.scale) : -INFINITY;
+            }
+            float mp = fmaxf(sc[0], sc[1]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, off));
+            const float m_new = fmaxf(m_run, mp);  // finite: the chunk holds at least one token
+            const double alpha = m_run == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run, (double)m_new));
+            m_run = m_new;
+            double psum = 0.0;
+#pragma unroll
+            for (int i = 0; i < (TPW + 31) / 32; i++) {
+                const int tl = lane + 32 * i;
+                const int t = kb * TPW + (tl < TPW ? tl : 0);
+                const float s0 = __shfl_sync(0xffffffffu, sc[0], t & 31);
+                const float s1 = __shfl_sync(0xffffffffu, sc[1], t & 31);
+                if (tl < TPW) {
+                    const double p = t < ntok ? exp64(__dsub_rn((double)((t >> 5) ? s1 : s0), (double)m_new)) : 0.0;
+                    p_s[t * G + hg] = p;
+                    psum = __dadd_rn(psum, p);
+                }
+            }
+            l_lane = __dadd_rn(__dmul_rn(l_lane, alpha), psum);
+            if (kb == 0 && lane == 0) alpha_s[hg] = alpha;
+        }
+        __syncthreads();
+        // ---- o = alpha * o + sum_t p_t v_t over this warp's TPC tokens; lane owns 4 dims
+        {
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const double pg = ps[g * P + tok];
-                o[g][0] = __dadd_rn(o[g][0], __dmul_rn(pg, (double)v01.x));
-                o[g][1] = __dadd_rn(o[g][1], __dmul_rn(pg, (double)v01.y));
-                o[g][2] = __dadd_rn(o[g][2], __dmul_rn(pg, (double)v23.x));
-                o[g][3] = __dadd_rn(o[g][3], __dmul_rn(pg, (double)v23.y));
+                const double al = alpha_s[g];
+#pragma unroll
+                for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al);
+            }
+            const int t0 = warp * TPC, t1 = min(t0 + TPC, ntok);
+            for (int t = t0; t < t1; t++) {
+                const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)t * ATT_HD + 4 * lane);
+                const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
+                const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+                const double vd[4] = {(double)v01.x, (double)v01.y, (double)v23.x, (double)v23.y};
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const double pg = p_s[t * G + g];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) o[g][e] = __fma_rn(pg, vd[e], o[g][e]);
+                }
             }
         }
     }
-    if (!waited_ok) {
-        atomicOr(A.err, ERRBIT_WAIT_TIMEOUT);
-        // let any copy still in flight land before shared memory is released
-        mbar_wait_bounded(&bars[0], 0);
-        mbar_wait_bounded(&bars[1], 0);
+    // every warp is done with the ring; on a timed-out wait let the copies in
+    // flight land before the ring is reused
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+            atomicOr(A.err, ERRBIT_WAIT_TIMEOUT);
+            for (int st = 0; st < min(depth, mine); st++) {
+                const int jl = st + ((mine - 1 - st) / depth) * depth;
+                mbar_wait_bounded(&full[st], (uint32_t)(jl / depth) & 1u);
+            }
+        }
+        __syncthreads();
+    }
+    // ---- CTA partial: o summed over warps (fixed order), l, running max
+    {
+        const double lw = warp_sum64(l_lane);
+        if (lane == 0) ls[warp] = lw;
+        if (lane == 0 && warp < G) M_s[warp] = (double)m_run;  // warp g < G owns head g
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
     __syncthreads();
-    for (int i = tid; i < G * ATT_HD; i += blockDim.x) {
+    for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
         const int g = i / ATT_HD, d = i % ATT_HD;
-        double sum = 0.0;
+        double sum = red[g * ATT_HD + d];
 #pragma unroll
-        for (int w = 0; w < ATT_WARPS; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
-        const int64_t hrow = ((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * A.nsplit_max + split;
-        A.part_o[hrow * ATT_HD + d] = sum;
-        if (d == 0) {
-            A.part_ml[2 * hrow] = mls[g][0];
-            A.part_ml[2 * hrow + 1] = mls[g][1];
-        }
+        for (int w = 1; w < ATT_WARPS; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
+        O_s[i] = sum;
     }
-    // ---- the last page CTA of this (sequence, kv head) merges all pages
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        int *cnt = counters + (int64_t)b * A.n_kv + kvh;
-        const int prev = atomicAdd(cnt, 1);
-        s_last = prev == nsplit - 1;
-        if (s_last) *cnt = 0;  // ready for the next step
+    if (tid < G) {
+        double l = 0.0;
+        for (int w = tid; w < ATT_WARPS; w += G) l = __dadd_rn(l, ls[w]);
+        L_s[tid] = l;
     }
-    __syncthreads();
-    if (!s_last) {
-        pdl_launch();
-        return;
-    }
-    __threadfence();
-    const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * A.nsplit_max;
-    double *wts = reinterpret_cast<double *>(smem);  // [G][nsplit], reuses the K/V area
-    for (int g = warp; g < G; g += ATT_WARPS) {
-        const int64_t hb = hb0 + (int64_t)g * A.nsplit_max;
-        double M = -INFINITY;
-        for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmax(M, __ldcg(&A.part_ml[2 * (hb + s2)]));
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(0xffffffffu, M, off));
-        double L = 0.0;
-        for (int s2 = lane; s2 < nsplit; s2 += 32) {
-            const double w = exp64(__dsub_rn(__ldcg(&A.part_ml[2 * (hb + s2)]), M));
-            wts[g * nsplit + s2] = w;
-            L = __dadd_rn(L, __dmul_rn(__ldcg(&A.part_ml[2 * (hb + s2) + 1]), w));
-        }
-        L = warp_sum64(L);
-        if (lane == 0) {
-            s_M[g] = M;
-            s_L[g] = L;
-        }
-    }
-    __syncthreads();
-    float *vals = qs;  // [G][hd] outputs, reuses the q area
-    // each thread owns G outputs (one per head: index tid + 128 g when hd =
-    // 128 = blockDim); 16 pages of all G heads are loaded per batch so the L2
-    // round trips overlap
-    {
-        const int d = tid;  // blockDim.x == ATT_HD
-        double acc[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) acc[g] = 0.0;
-        constexpr int UB = G >= 8 ? 8 : 16;
-        for (int s0 = 0; s0 < nsplit; s0 += UB) {
-            double v[G][UB];
-#pragma unroll
-            for (int g = 0; g < G; g++)
-#pragma unroll
-                for (int u = 0; u < UB; u++)
-                    v[g][u] = s0 + u < nsplit
-                                  ? __ldcg(&A.part_o[(hb0 + (int64_t)g * A.nsplit_max + s0 + u) * ATT_HD + d])
-                                  : 0.0;
-#pragma unroll
-            for (int g = 0; g < G; g++)
-#pragma unroll
-                for (int u = 0; u < UB; u++)
-                    if (s0 + u < nsplit) acc[g] = __dadd_rn(acc[g], __dmul_rn(v[g][u], wts[g * nsplit + s0 + u]));
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float val = __double2float_rn(__ddiv_rn(acc[g], s_L[g]));
-            vals[g * ATT_HD + d] = val;
-            if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
-        }
-    }
-    if (use_q8) {
+    constexpr unsigned wmask = G * S >= 32 ? 0xffffffffu : (1u << (G * S)) - 1u;
+    if constexpr (CLUSTER) {
+        cg::cluster_group cl = cg::this_cluster();
         __syncthreads();
-        // G*hd values = G/2 Q8_K blocks of the [n_heads*hd] row
-        for (int blk = warp; blk < G / 2; blk += ATT_WARPS) {
-            float v[8];
+        cluster_wait();  // every CTA of the cluster has started
+        // push: rank r receives dims [r*DPR, (r+1)*DPR) of each head plus (max, sum)
+        for (int i = tid; i < S * G * IB; i += ATT_THREADS) {
+            const int r = i / (G * IB), g = (i / IB) % G, k = i % IB;
+            const double v = k < ATT_DPR ? O_s[g * ATT_HD + r * ATT_DPR + k] : (k == ATT_DPR ? M_s[g] : L_s[g]);
+            *cl.map_shared_rank(&inbox[(rank * G + g) * IB + k], r) = v;
+        }
+        cluster_sync_all();  // every push has landed
+        if (tid < G * S) {
+            const int g = tid / S, r = tid % S;
+            const double Mr = inbox[(r * G + g) * IB + ATT_DPR];
+            const double Lr = inbox[(r * G + g) * IB + ATT_DPR + 1];
+            double M = Mr;
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = vals[blk * 256 + 8 * lane + e];
-            q8k_store_warp_ext(v, lane, aq, b, (int64_t)kvh * G / 2 + blk);
+            for (int off = S / 2; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(wmask, M, off));
+            const double w = Mr == -INFINITY ? 0.0 : exp64(__dsub_rn(Mr, M));
+            wts[tid] = w;
+            wl[tid] = __dmul_rn(w, Lr);
+        }
+        __syncthreads();
+        if (tid < G * ATT_DPR) {
+            const int g = tid / ATT_DPR, dd = tid % ATT_DPR, d = rank * ATT_DPR + dd;
+            double L = 0.0, O = 0.0;
+#pragma unroll
+            for (int r = 0; r < S; r++) {
+                L = __dadd_rn(L, wl[g * S + r]);
+                O = __dadd_rn(O, __dmul_rn(wts[g * S + r], inbox[(r * G + g) * IB + dd]));
+            }
+            const float val = L > 0.0 ? __double2float_rn(__ddiv_rn(O, L)) : 0.f;
+            if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
+            // Q8_K block g/2 (heads g & ~1, g | 1) is quantized by rank g/2
+            if (use_q8) *cl.map_shared_rank(&q8in[(g & 1) * ATT_HD + d], g >> 1) = val;
+        }
+        if (use_q8) {
+            cluster_sync_all();  // the block's 256 values have landed
+            if (rank < G / 2 && warp == 0) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = q8in[8 * lane + e];
+                q8k_store_warp_ext(v, lane, aq, b, (int64_t)kvh * G / 2 + rank);
+            }
+        }
+    } else {
+        const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * S;
+        __syncthreads();
+        for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
+            const int g = i / ATT_HD, d = i % ATT_HD;
+            A.part_o[(hb0 + (int64_t)g * S + rank) * ATT_HD + d] = O_s[i];
+        }
+        if (tid < G) {
+            A.part_ml[2 * (hb0 + (int64_t)tid * S + rank)] = M_s[tid];
+            A.part_ml[2 * (hb0 + (int64_t)tid * S + rank) + 1] = L_s[tid];
+        }
+        // the last CTA of this (kv head, sequence) merges
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            int *cnt = counters + (int64_t)b * A.n_kv + kvh;
+            const int prev = atomicAdd(cnt, 1);
+            s_last = prev == S - 1;
+            if (s_last) *cnt = 0;  // ready for the next call
+        }
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            if (tid < G * S) {
+                const int g = tid / S, r = tid % S;
+                const double Mr = __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * S + r)]);
+                const double Lr = __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * S + r) + 1]);
+                double M = Mr;
+#pragma unroll
+                for (int off = S / 2; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(wmask, M, off));
+                const double w = Mr == -INFINITY ? 0.0 : exp64(__dsub_rn(Mr, M));
+                wts[tid] = w;
+                wl[tid] = __dmul_rn(w, Lr);
+            }
+            __syncthreads();
+            for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
+                const int g = i / ATT_HD, d = i % ATT_HD;
+                double Or[S];
+#pragma unroll
+                for (int r = 0; r < S; r++) Or[r] = __ldcg(&A.part_o[(hb0 + (int64_t)g * S + r) * ATT_HD + d]);
+                double L = 0.0, O = 0.0;
+#pragma unroll
+                for (int r = 0; r < S; r++) {
+                    L = __dadd_rn(L, wl[g * S + r]);
+                    O = __dadd_rn(O, __dmul_rn(wts[g * S + r], Or[r]));
+                }
+                const float val = L > 0.0 ? __double2float_rn(__ddiv_rn(O, L)) : 0.f;
+                if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
+                fin[i] = val;
+            }
+            if (use_q8) {
+                __syncthreads();
+                for (int blk = warp; blk < G / 2; blk += ATT_WARPS) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = fin[blk * 256 + 8 * lane + e];
+                    q8k_store_warp_ext(v, lane, aq, b, (int64_t)kvh * G / 2 + blk);
+                }
+            }
         }
     }
     pdl_launch();
@@ -371,67 +508,139 @@ __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane
     if (lane == 0) a.d[row * (k / QK) + blk] = d;
 }
 
-size_t attn_smem_bytes(int G, int page_size) {
-    const size_t P = (size_t)page_size;
-    return 2 * P * ATT_HD * 2 + (size_t)G * ATT_HD * 4 + (size_t)G * P * 4 + (size_t)G * P * 8 +
-           (size_t)ATT_WARPS * G * ATT_HD * 8;
+
+static int attn_bt_cap(int max_pages, int page_size) {
+    const int nch = (int)(((int64_t)max_pages * page_size + ATT_CHUNK - 1) / ATT_CHUNK);
+    return (nch + ATT_SPLITS - 1) / ATT_SPLITS * (ATT_CHUNK / page_size);
 }
 
-// Paged decode attention with the page merge fused in.  `counters` holds
-// batch * n_kv int32 that are zero on entry and zero again on exit.  out_f32
-// and/or (aq != null, needs an even GQA group) receive the result.
+// Whether a cluster of ATT_SPLITS CTAs with this shared-memory footprint can
+// be resident on the device (cached per device and size).
+template <int G>
+static bool attn_cluster_fits(int device, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, bool> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(device, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    auto kern = k_attn_decode<G, true>;
+    bool fits = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
+                cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    if (fits) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = ATT_SPLITS;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(ATT_SPLITS, 1, 1);
+        cfg.blockDim = dim3(ATT_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        fits = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1;
+    }
+    cudaGetLastError();  // a refused query leaves no sticky error
+    cache[key] = fits;
+    return fits;
+}
+
+template <int G>
+static bool attn_plan(fb_ctx *ctx, const AttnArgs &A, int batch, bool want_cluster, int *depth, int *bt_cap,
+                      size_t *smem) {
+    *bt_cap = attn_bt_cap(A.max_pages, A.page_size);
+    // two stages keep a CTA under half of an SM's shared memory, so a
+    // 16-CTA cluster fits a GPC even where other work holds some SMs
+    (void)batch;
+    *depth = 2;
+    *smem = attn_layout(G, *depth, *bt_cap).total;
+    return want_cluster && attn_cluster_fits<G>(ctx->device, *smem);
+}
+
+bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch) {
+    int depth, cap;
+    size_t smem;
+    switch (A.n_heads / A.n_kv) {
+        case 1: return attn_plan<1>(ctx, A, batch, true, &depth, &cap, &smem);
+        case 2: return attn_plan<2>(ctx, A, batch, true, &depth, &cap, &smem);
+        case 4: return attn_plan<4>(ctx, A, batch, true, &depth, &cap, &smem);
+        case 8: return attn_plan<8>(ctx, A, batch, true, &depth, &cap, &smem);
+        default: return false;
+    }
+}
+
+template <int G>
+static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, float *out_f32, const Q8Act *aq,
+                          int *counters, bool pdl, bool want_cluster) {
+    int depth, bt_cap;
+    size_t smem;
+    const bool cluster = attn_plan<G>(ctx, A, batch, want_cluster, &depth, &bt_cap, &smem);
+    FB_REQUIRE(cluster || (counters && A.part_o && A.part_ml), "attn: the cluster-free merge needs scratch");
+    Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    // older KV chunks are read before griddepcontrol.wait: only valid when the
+    // preceding kernel is one of this library's (the model's decode step)
+    attr[0].val.programmaticStreamSerializationAllowed = (ctx->pdl && pdl) ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = ATT_SPLITS;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(ATT_SPLITS, A.n_kv, batch);
+    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = cluster ? 2 : 1;
+    if (cluster) {
+        auto kern = k_attn_decode<G, true>;
+        FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, depth, bt_cap));
+    } else {
+        auto kern = k_attn_decode<G, false>;
+        FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, depth, bt_cap));
+    }
+}
+
+// Paged decode attention.  out_f32 and/or (aq != null, needs an even GQA
+// group) receive the result.  With want_cluster the 16 splits of each (kv
+// head, sequence) merge through distributed shared memory when the device can
+// hold such a cluster; otherwise A.part_o / A.part_ml (ATT_SPLITS splits) and
+// `counters` (batch * n_kv int32, zero on entry and again on exit) are used.
 void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32, const Q8Act *aq,
-                        int *counters, bool pdl) {
+                        int *counters, bool pdl, bool want_cluster) {
     const int G = A.n_heads / A.n_kv;
     FB_REQUIRE(A.n_heads % A.n_kv == 0, "attn: n_heads must be a multiple of n_kv_heads");
     FB_REQUIRE(A.page_size == 32 || A.page_size == 64, "attn: page_size must be 32 or 64");
     FB_REQUIRE(!aq || G % 2 == 0, "attn: fused Q8_K output needs an even GQA group");
-    const int nsplit = (max_seq_len + A.page_size - 1) / A.page_size;
-    FB_REQUIRE(nsplit <= A.nsplit_max, "attn: max_seq_len exceeds the split scratch");
-    const size_t smem = attn_smem_bytes(G, A.page_size);
-    FB_REQUIRE((size_t)G * nsplit * 8 <= (size_t)2 * A.page_size * ATT_HD * 2,
-               "attn: max_seq_len too long for the in-kernel page merge");
-    dim3 grid(A.n_kv, nsplit, batch);
-    Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    // older KV pages are read before griddepcontrol.wait: only valid when the
-    // preceding kernel is one of this library's (the model's decode step)
-    attr[0].val.programmaticStreamSerializationAllowed = (ctx->pdl && pdl) ? 1 : 0;
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(ATT_WARPS * 32);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = ctx->stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    FB_REQUIRE(max_seq_len >= 1 && max_seq_len <= A.max_pages * A.page_size, "attn: max_seq_len exceeds the block table");
     switch (G) {
-#define FB_ATT_CASE(GG)                                                                                           \
-    case GG:                                                                                                      \
-        FB_CUDA(cudaFuncSetAttribute(k_attn_decode<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-        FB_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<GG>, A, out_f32, q, aq ? 1 : 0, counters));              \
-        break;
-        FB_ATT_CASE(1)
-        FB_ATT_CASE(2)
-        FB_ATT_CASE(4)
-        FB_ATT_CASE(8)
-#undef FB_ATT_CASE
-    default:
-        fail(FB_ERR_INVALID, "attn: GQA group size must be 1, 2, 4 or 8");
+        case 1: launch_attn_g<1>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
+        case 2: launch_attn_g<2>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
+        case 4: launch_attn_g<4>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
+        case 8: launch_attn_g<8>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
+        default: fail(FB_ERR_INVALID, "attn: GQA group size must be 1, 2, 4 or 8");
     }
 }
 
 // ---------------------------------------------------------------------------
 // Allocation-free decode attention (fb_attn_decode_noalloc).
 //
-// fb_attn_decode takes its split-K scratch (partial sums and maxima of every
-// split) from the context's workspace, which is grown with cudaMalloc and a
-// stream synchronisation on first use.  Some callers cannot allow that: code
-// running under a caching or pooled device allocator that forbids direct
+// fb_attn_decode merges its 16 splits through distributed shared memory when
+// the GPU can hold a 16-CTA cluster, and otherwise takes global split scratch
+// from the context's workspace, which is grown with cudaMalloc and a stream
+// synchronisation on first use.  Some callers cannot allow that: code running
+// under a caching or pooled device allocator that forbids direct
 // cudaMalloc/cudaFree (ferrite-os routes device allocations through its own
 // TLSF pool), and latency-critical loops that must never take the implicit
 // device synchronisation cudaMalloc/cudaFree may cause.  For them this entry
-// point keeps the scratch in a fixed, file-scope device array instead.
+// point always runs the cluster-free merge and keeps its scratch in a fixed,
+// file-scope device array instead.
 //
 // The array is a `static __device__` object: every GPU that loads the library
 // holds it until the process exits.  Host code cannot use the array's name as
@@ -441,8 +650,8 @@ void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_l
 // come before any stream capture.  All calls on a device share the one array:
 // calls that overlap on the GPU (two streams, or two contexts of one device)
 // race on it.  The partial sums need no clearing (every slot a call reads is
-// written by the same call first); the page-merge counters at its start must
-// be zero, so each call clears them (cudaMemsetAsync, no allocation).
+// written by the same call first); the merge counters at its start must be
+// zero, so each call clears them (cudaMemsetAsync, no allocation).
 constexpr size_t kAttnNoAllocScratchBytes = (size_t)4 << 20;  // 4 MiB
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kAttnNoAllocScratchBytes];
 
@@ -480,11 +689,11 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
-        const int nsplit = (max_seq_len + page_size - 1) / page_size;
+        const int nsplit = ATT_SPLITS;
         const size_t cnt_bytes = ((size_t)batch * n_kv_heads * sizeof(int) + 255) & ~(size_t)255;
         const size_t need = (size_t)batch * n_heads * nsplit * (head_dim + 2) * sizeof(double) + cnt_bytes;
         if (need > kAttnNoAllocScratchBytes)
-            fail(FB_ERR_INVALID, "attn_decode_noalloc: batch * n_heads * ceil(max_seq_len / page_size) * " +
+            fail(FB_ERR_INVALID, "attn_decode_noalloc: batch * n_heads * " + std::to_string(nsplit) + " splits * " +
                                      std::to_string((head_dim + 2) * sizeof(double)) + " bytes = " +
                                      std::to_string(need) + " (with the merge counters) exceeds the fixed " +
                                      std::to_string(kAttnNoAllocScratchBytes) + "-byte scratch");
@@ -510,6 +719,6 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         A.nsplit_max = nsplit;
         A.scale = scale;
         A.err = ctx->err_word;
-        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false);
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false, false);
     });
 }

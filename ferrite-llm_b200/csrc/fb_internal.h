@@ -169,21 +169,23 @@ void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, in
                      const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale);
 
 // Paged flash-decode attention (attention.cu).
+constexpr int ATT_SPLITS = 16;  // attention splits (cluster CTAs) per (kv head, sequence)
 struct AttnArgs {
     const float *q;              // [b, n_heads, hd]
-    const void *kpool;           // fp16 [num_pages, n_kv, page, hd]
-    const void *vpool;
+    const void *kpool;           // fp16 [num_pages, n_kv, hd, page] (dim-major pages)
+    const void *vpool;           // fp16 [num_pages, n_kv, page, hd]
     const int32_t *block_table;  // [b, max_pages]
     const int32_t *seq_lens;     // [b] or null (then pos[b] + 1)
     const int32_t *pos;          // [b]
-    double *part_o;              // [b, n_heads, nsplit_max, hd] per-page unnormalised sum p*v
-    double *part_ml;             // [b, n_heads, nsplit_max, 2] (page max, sum p)
+    double *part_o;              // cluster-free merge: [b, n_heads, ATT_SPLITS, hd] unnormalised sum p*v
+    double *part_ml;             // cluster-free merge: [b, n_heads, ATT_SPLITS, 2] (running max, sum p)
     int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
     float scale;
     uint32_t *err;
 };
 void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
-                        const Q8Act *aq, int *counters, bool pdl);
+                        const Q8Act *aq, int *counters, bool pdl, bool want_cluster);
+bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch);
 
 // RoPE tables [max_pos][hd/2] computed on the host exactly as the oracle does
 // (candle precompute_freqs_cis: angle = pos * theta^(-2i/hd) in f32).

@@ -110,33 +110,37 @@ __device__ __forceinline__ Q4Scales q4k_unpack_scales(uint32_t s0, uint32_t s1, 
 __device__ __forceinline__ int byte_of(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); }
 __device__ __forceinline__ int sbyte_of(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xFFu); }
 
-// exp in binary64 by Cody-Waite reduction x = k*ln2 + r (ln2 split into a
-// 32-bit head and a binary64 tail of the exact remainder, so k*LN2_HI is
-// exact), a degree-13 Taylor
-// polynomial in r (|r| <= ln2/2, truncation below 5e-18) and scaling by 2^k.
-// Every step is an explicitly rounded binary64 operation, so the CPU oracle
-// (which evaluates the same sequence) produces the same bits.
+// exp(x) in binary64: Cody-Waite reduction x = k ln2 + r (ln2 split into a
+// 32-bit head and a tail), the degree-13 Taylor polynomial of e^r evaluated
+// by Horner's rule with fused multiply-adds, and the scaling by 2^k done with
+// one rounding (as C's ldexp).  The CPU oracle evaluates the same sequence.
+__device__ __forceinline__ double exp64_pow2(int n) {  // 2^n, -1022 <= n <= 1023
+    return __longlong_as_double((long long)(n + 1023) << 52);
+}
 __device__ __forceinline__ double exp64(double x) {
     if (x != x) return x;
     if (x > 709.5) return __longlong_as_double(0x7FF0000000000000LL);
     if (x < -745.5) return 0.0;
     const double k = rint(__dmul_rn(x, 1.4426950408889634));
     const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(k, 0.6931471803691238)), __dmul_rn(k, 1.9082149292705877e-10));
-    double p = 1.6059043836821613e-10;
-    p = __dadd_rn(__dmul_rn(p, r), 2.08767569878681e-09);
-    p = __dadd_rn(__dmul_rn(p, r), 2.505210838544172e-08);
-    p = __dadd_rn(__dmul_rn(p, r), 2.755731922398589e-07);
-    p = __dadd_rn(__dmul_rn(p, r), 2.7557319223985893e-06);
-    p = __dadd_rn(__dmul_rn(p, r), 2.48015873015873e-05);
-    p = __dadd_rn(__dmul_rn(p, r), 0.0001984126984126984);
-    p = __dadd_rn(__dmul_rn(p, r), 0.001388888888888889);
-    p = __dadd_rn(__dmul_rn(p, r), 0.008333333333333333);
-    p = __dadd_rn(__dmul_rn(p, r), 0.041666666666666664);
-    p = __dadd_rn(__dmul_rn(p, r), 0.16666666666666666);
-    p = __dadd_rn(__dmul_rn(p, r), 0.5);
-    p = __dadd_rn(__dmul_rn(p, r), 1.0);
-    p = __dadd_rn(__dmul_rn(p, r), 1.0);
-    return ldexp(p, (int)k);
+    double p = 1.6059043836821613e-10;  // 1/13!
+    p = __fma_rn(p, r, 2.08767569878681e-09);
+    p = __fma_rn(p, r, 2.505210838544172e-08);
+    p = __fma_rn(p, r, 2.755731922398589e-07);
+    p = __fma_rn(p, r, 2.7557319223985893e-06);
+    p = __fma_rn(p, r, 2.48015873015873e-05);
+    p = __fma_rn(p, r, 0.0001984126984126984);
+    p = __fma_rn(p, r, 0.001388888888888889);
+    p = __fma_rn(p, r, 0.008333333333333333);
+    p = __fma_rn(p, r, 0.041666666666666664);
+    p = __fma_rn(p, r, 0.16666666666666666);
+    p = __fma_rn(p, r, 0.5);
+    p = __fma_rn(p, r, 1.0);
+    p = __fma_rn(p, r, 1.0);
+    const int ki = (int)k;
+    if (ki >= -1022 && ki <= 1023) return __dmul_rn(p, exp64_pow2(ki));
+    if (ki > 1023) return __dmul_rn(__dmul_rn(p, 2.0), exp64_pow2(ki - 1));
+    return __dmul_rn(__dmul_rn(p, exp64_pow2(ki + 64)), 5.421010862427522e-20);  // subnormal: * 2^-64 rounds once
 }
 
 // silu(v) = v / (1 + exp(-v)), evaluated in binary64 and rounded once.

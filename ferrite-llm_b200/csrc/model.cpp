@@ -199,7 +199,7 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         A.vpool = m->vpool(l);
         const bool q8_fused = (c.n_heads / c.n_kv_heads) % 2 == 0;
         launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), q8_fused ? &aa : nullptr,
-                           m->att_cnt.as<int>(), true);
+                           m->att_cnt.as<int>(), true, true);
         if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
         mark(FB_PROF_ATTN, 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
@@ -310,7 +310,7 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
         m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
         m->num_pages = m->pages_per_seq * c.max_batch;
-        m->nsplit_max = m->pages_per_seq;
+        m->nsplit_max = ATT_SPLITS;  // cluster-free attention merge (fallback) scratch
         m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
         FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
         std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);
@@ -588,8 +588,15 @@ int fb_model_read_kv(fb_model *m, int layer, int which, int pos, float *out_host
         const int page = pos / kPage;  // slot 0 uses pages [0, pages_per_seq)
         std::vector<__half> tmp((size_t)c.head_dim);
         for (int h = 0; h < c.n_kv_heads; h++) {
-            const __half *src = pool + (((size_t)page * c.n_kv_heads + h) * kPage + (pos % kPage)) * c.head_dim;
-            FB_CUDA(cudaMemcpyAsync(tmp.data(), src, (size_t)c.head_dim * 2, cudaMemcpyDeviceToHost, m->ctx->stream));
+            if (which == 0) {  // K pages are dim-major: gather one column
+                const __half *src = pool + ((size_t)page * c.n_kv_heads + h) * c.head_dim * kPage + (pos % kPage);
+                FB_CUDA(cudaMemcpy2DAsync(tmp.data(), 2, src, (size_t)kPage * 2, 2, (size_t)c.head_dim,
+                                          cudaMemcpyDeviceToHost, m->ctx->stream));
+            } else {
+                const __half *src = pool + (((size_t)page * c.n_kv_heads + h) * kPage + (pos % kPage)) * c.head_dim;
+                FB_CUDA(cudaMemcpyAsync(tmp.data(), src, (size_t)c.head_dim * 2, cudaMemcpyDeviceToHost,
+                                        m->ctx->stream));
+            }
             FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
             for (int d = 0; d < c.head_dim; d++) out_host[h * c.head_dim + d] = __half2float(tmp[d]);
         }
@@ -697,13 +704,6 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
-        const int nsplit = (max_seq_len + page_size - 1) / page_size;
-        const size_t cnt_bytes = ((size_t)batch * n_kv_heads * 4 + 255) & ~(size_t)255;
-        uint8_t *raw = static_cast<uint8_t *>(
-            ctx->ensure_scratch(cnt_bytes + (size_t)batch * n_heads * nsplit * (head_dim + 2) * 8));
-        int *counters = reinterpret_cast<int *>(raw);
-        FB_CUDA(cudaMemsetAsync(counters, 0, cnt_bytes, ctx->stream));
-        void *base = raw + cnt_bytes;
         AttnArgs A{};
         A.q = q_dev;
         A.kpool = k_pages_dev;
@@ -711,17 +711,26 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         A.block_table = block_table_dev;
         A.seq_lens = seq_lens_dev;
         A.pos = nullptr;
-        A.part_o = (double *)base;
-        A.part_ml = (double *)base + (size_t)batch * n_heads * nsplit * head_dim;
         A.n_heads = n_heads;
         A.n_kv = n_kv_heads;
         A.page_size = page_size;
         A.max_pages = max_pages;
         A.num_pages = 0x7fffffff;  // caller-owned pool: ids are trusted up to int range
-        A.nsplit_max = nsplit;
+        A.nsplit_max = ATT_SPLITS;
         A.scale = scale;
         A.err = ctx->err_word;
-        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false);
+        int *counters = nullptr;
+        if (n_heads % n_kv_heads == 0 && !attn_uses_cluster(ctx, A, batch)) {
+            // cluster-free merge: split partials and merge counters in the workspace
+            const size_t cnt_bytes = ((size_t)batch * n_kv_heads * 4 + 255) & ~(size_t)255;
+            uint8_t *raw = static_cast<uint8_t *>(
+                ctx->ensure_scratch(cnt_bytes + (size_t)batch * n_heads * ATT_SPLITS * (head_dim + 2) * 8));
+            counters = reinterpret_cast<int *>(raw);
+            FB_CUDA(cudaMemsetAsync(counters, 0, cnt_bytes, ctx->stream));
+            A.part_o = reinterpret_cast<double *>(raw + cnt_bytes);
+            A.part_ml = A.part_o + (size_t)batch * n_heads * ATT_SPLITS * head_dim;
+        }
+        launch_attn_decode(ctx, A, batch, max_seq_len, out_dev, nullptr, counters, false, true);
     });
 }
 

@@ -229,9 +229,13 @@ __global__ void __launch_bounds__(256)
             if (lane == 0) atomicOr(err, ERRBIT_BAD_PAGE);
             return;
         }
-        __half *pool = is_k ? kpool : vpool;
-        __half *dst = pool + (((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + lane * per;
-        for (int e = 0; e < per; e++) dst[e] = __float2half_rn(v[e]);
+        if (is_k) {  // K pages are dim-major: [page][kv head][hd][page tokens]
+            __half *dst = kpool + ((int64_t)page * nkv + kvh) * hd * page_size + (p % page_size);
+            for (int e = 0; e < per; e++) dst[(int64_t)(lane * per + e) * page_size] = __float2half_rn(v[e]);
+        } else {  // V pages are token-major: [page][kv head][page tokens][hd]
+            __half *dst = vpool + (((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + lane * per;
+            for (int e = 0; e < per; e++) dst[e] = __float2half_rn(v[e]);
+        }
     }
     pdl_launch();
 }
@@ -465,7 +469,10 @@ __global__ void k_synth_kv(__half *__restrict__ pool, int layer, int which, int 
     const int kvh = e / hd, d = e % hd;
     for (int s = 0; s < slots; s++) {
         const int page = block_table[(int64_t)s * max_pages + p / page_size];
-        pool[(((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + d] = v;
+        if (which == 0)  // K: dim-major pages
+            pool[(((int64_t)page * nkv + kvh) * hd + d) * page_size + (p % page_size)] = v;
+        else
+            pool[(((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + d] = v;
     }
 }
 

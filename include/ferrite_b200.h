@@ -139,10 +139,15 @@ int fb_rope(fb_ctx *ctx, float *x_dev, int64_t n_tok, int64_t n_heads,
 int fb_swiglu(fb_ctx *ctx, const float *gate_dev, const float *up_dev,
               float *out_dev, int64_t m, int64_t f);
 /* GQA decode attention of one query token per sequence over a paged fp16 KV
- * cache.  q[b, n_heads, head_dim] f32; k/v pages fp16
+ * cache.  q[b, n_heads, head_dim] f32; K pages fp16 dim-major
+ * [num_pages, n_kv_heads, head_dim, page_size]; V pages fp16
  * [num_pages, n_kv_heads, page_size, head_dim]; block_table[b, max_pages]
  * int32 physical page ids; seq_lens[b] int32 (tokens to attend, including
- * the current one); out[b, n_heads, head_dim] f32.  scale = 1/sqrt(hd). */
+ * the current one); out[b, n_heads, head_dim] f32.  scale = 1/sqrt(hd).
+ * head_dim 128, page_size 32 or 64, n_heads / n_kv_heads in {1, 2, 4, 8}.
+ * Allocates nothing when the GPU can hold a 16-CTA thread-block cluster
+ * (the split merge runs in distributed shared memory); otherwise grows a
+ * workspace once (cudaMalloc plus a stream synchronisation). */
 int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
                    const void *v_pages_dev, const int32_t *block_table_dev,
                    const int32_t *seq_lens_dev, float *out_dev, int batch,
@@ -151,15 +156,16 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
 
 /* Same computation and arguments as fb_attn_decode, for callers that cannot
  * allocate device memory: no reference counterpart (the reference's candle
- * path allocates freely).  fb_attn_decode grows a workspace with cudaMalloc
- * (plus a stream synchronisation) on first use; code that runs under a pooled
- * or hooked device allocator that forbids direct cudaMalloc/cudaFree, or in a
- * loop that must not take the synchronisation those calls can imply, uses
- * this entry point instead.  It allocates nothing: its split-K scratch is a
- * fixed 4 MiB array in the library's device image, so it accepts
- * batch * n_heads * ceil(max_seq_len / page_size) * (head_dim + 2) * 8 bytes
- * (plus 256 bytes of merge counters) <= 4 MiB (e.g. 32 heads at 4096 tokens
- * with 64-token pages for batch 1) and returns FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
+ * path allocates freely).  fb_attn_decode may grow a workspace with
+ * cudaMalloc (plus a stream synchronisation) on first use; code that runs
+ * under a pooled or hooked device allocator that forbids direct
+ * cudaMalloc/cudaFree, or in a loop that must not take the synchronisation
+ * those calls can imply, uses this entry point instead.  It allocates
+ * nothing: its split scratch (16 splits per kv head and sequence) is a fixed
+ * 4 MiB array in the library's device image, so it accepts
+ * batch * n_heads * 16 * (head_dim + 2) * 8 bytes (plus 256 bytes of merge
+ * counters) <= 4 MiB (e.g. batch 7 with 32 heads, any context length) and
+ * returns FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
  * device address (make that first call before any stream capture).  All calls
  * on a device share the array, so calls that overlap on the GPU race. */
 int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,

@@ -44,6 +44,20 @@ void or_rmsnorm(const float *x, const float *g, float *y, int64_t rows,
     }
 }
 
+/* Attention score q.k in f32 with a fixed evaluation order: eight slices of
+ * hd/8 consecutive dims, each a fused multiply-add chain from zero in
+ * increasing dim order, then the slice sums added left to right. */
+float or_attn_dot(const float *q, const float *k, int hd) {
+    const int sl = hd / 8;
+    float dot = 0.f;
+    for (int w = 0; w < 8; w++) {
+        float pw = 0.f;
+        for (int e = w * sl; e < (w + 1) * sl; e++) pw = fmaf(q[e], k[e], pw);
+        dot = w == 0 ? pw : dot + pw;
+    }
+    return dot;
+}
+
 double or_exp64(double x) {
     static const double C[14] = {1.0, 1.0, 0.5, 0.16666666666666666, 0.041666666666666664,
                                  0.008333333333333333, 0.001388888888888889, 0.0001984126984126984,
@@ -56,7 +70,7 @@ double or_exp64(double x) {
     double k = nearbyint(x * LOG2E);
     double r = (x - k * LN2_HI) - k * LN2_LO;
     double p = C[13];
-    for (int i = 12; i >= 0; i--) p = p * r + C[i];
+    for (int i = 12; i >= 0; i--) p = fma(p, r, C[i]);
     return ldexp(p, (int)k);
 }
 
@@ -322,8 +336,9 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
 #pragma omp parallel for num_threads(nt) collapse(2) schedule(dynamic, 1)
         for (int i = 0; i < n; i++)
             for (int hq = 0; hq < nq; hq++) {
-                /* softmax(q.k^T * scale) . v; dots, exponentials and sums
-                 * in binary64, one rounding to f32 at the end */
+                /* softmax(q.k^T * scale) . v; the score dots in f32 in the
+                 * fixed order of or_attn_dot, exponentials and sums in
+                 * binary64 with one rounding to f32 at the end */
                 int T = pos + i + 1, hk = hq / grp;
                 const float *qh = q + (size_t)i * qd + (size_t)hq * hd;
                 float *sc = (float *)malloc(sizeof(float) * (size_t)T);
@@ -332,9 +347,7 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
                 float mx = -INFINITY;
                 for (int s = 0; s < T; s++) {
                     const float *ks = kl + (size_t)s * kd + (size_t)hk * hd;
-                    double dot = 0.0;
-                    for (int e = 0; e < hd; e++) dot += (double)qh[e] * (double)ks[e];
-                    sc[s] = (float)dot * scale;
+                    sc[s] = or_attn_dot(qh, ks, hd) * scale;
                     mx = sc[s] > mx ? sc[s] : mx;
                 }
                 double l = 0.0;

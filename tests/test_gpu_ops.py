@@ -80,7 +80,8 @@ def test_attn_decode_paged(fbctx, torch_cuda, nh, nkv, page):
     vp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
     q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
-    qd, kd, vd, btd, ld = t(q), t(kp), t(vp), t(perm), t(lens)
+    # K pages are dim-major on the device: [page][kv head][hd][page tokens]
+    qd, kd, vd, btd, ld = t(q), t(kp.transpose(0, 1, 3, 2)), t(vp), t(perm), t(lens)
     out = torch.zeros((b, nh, hd), dtype=torch.float32, device="cuda")
     fb.attn_decode(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(),
                    out.data_ptr(), b, nh, nkv, hd, page, max_pages, int(lens.max()), 1.0 / math.sqrt(hd))

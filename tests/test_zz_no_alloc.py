@@ -29,7 +29,8 @@ def make_inputs(torch, seed, b, nh, nkv, page, lens):
     vp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
     q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
-    return dict(q=t(q), k=t(kp), v=t(vp), bt=t(bt), lens=t(np.asarray(lens, np.int32)), b=b, nh=nh, nkv=nkv,
+    # K pages are dim-major on the device: [page][kv head][hd][page tokens]
+    return dict(q=t(q), k=t(kp.transpose(0, 1, 3, 2)), v=t(vp), bt=t(bt), lens=t(np.asarray(lens, np.int32)), b=b, nh=nh, nkv=nkv,
                 page=page, max_pages=max_pages, max_len=int(max(lens)))
 
 
@@ -58,7 +59,7 @@ def test_noalloc_matches_allocating_entry_point_two_calls(fbctx, torch_cuda):
 def test_noalloc_rejects_oversized_request(fbctx, torch_cuda):
     torch = torch_cuda
     d = make_inputs(torch, 3, b=1, nh=8, nkv=8, page=64, lens=[64])
-    # 16 sequences x 64 heads x 8192 tokens needs 64 splits x 1040 B x 1024 rows: > 4 MiB
+    # 16 sequences x 64 heads x 16 splits x 1040 B = 17 MB: > 4 MiB
     with pytest.raises(fb.FerriteError, match="exceeds the fixed"):
         fb.attn_decode_noalloc(fbctx, d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["bt"].data_ptr(),
                                d["lens"].data_ptr(), d["q"].data_ptr(), 16, 64, 8, 128, 64, 128, 8192, 0.088)
