@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[ATT_MAX_DEPTH];
     __shared__ int s_len, s_first, s_mine, s_last;
+    __shared__ __half s_newkv[2 * ATT_HD];  // fused prologue: the new token's k and v (fp16)
     constexpr int S = ATT_SPLITS;
     constexpr int TPW = ATT_CHUNK * G / ATT_WARPS;  // tokens per warp in the softmax phase
     constexpr int TPC = ATT_CHUNK / ATT_WARPS;      // tokens per warp in the P.V phase
@@ -147,10 +148,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         mbar_fence_init();
         // sequence lengths are inputs of the whole step (written before it began)
         int len = seq_len_of(A, b);
-        const int cap = A.max_pages * P;
+        const int cap = A.qkv ? min(A.max_pages * P, A.rope_rows) : A.max_pages * P;
         if (len < 1 || len > cap) {
             atomicOr(A.err, ERRBIT_BAD_POS);
-            len = len < 1 ? 0 : cap;
+            len = 0;  // no work: the output of this sequence is zero
         }
         const int nch = (len + ATT_CHUNK - 1) / ATT_CHUNK;
         const int cpr = (nch + S - 1) / S;  // chunks per rank
@@ -193,16 +194,59 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             bulk_g2s(vd + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes, &full[st]);
         }
     };
-    // the chunk holding the newest position is written by the preceding
-    // kernel; older chunks stream in before the wait
+    // the chunk holding the newest position: without the fused prologue its
+    // newest token is written by the preceding kernel, so it is copied after
+    // griddepcontrol.wait; every other copy streams in before the wait
     const int jf = len > 0 ? (len - 1) / ATT_CHUNK - first : -1;
+    const bool owner = jf >= 0 && jf < mine;
     const int pre = min(mine, depth);
     if (tid == 0)
         for (int j = 0; j < pre; j++)
-            if (j != jf) issue(j);
+            if (j != jf || A.qkv) issue(j);
     pdl_wait();
-    if (tid == 0 && jf >= 0 && jf < pre) issue(jf);
-    {
+    pdl_launch();  // the next kernel may start streaming its weights
+    if (tid == 0 && !A.qkv && jf >= 0 && jf < pre) issue(jf);
+    if (A.qkv) {
+        // q of the G heads (every CTA), k and v of the new token (owner only)
+        const int p = len - 1;
+        const float *yrow = A.qkv + (int64_t)b * A.qkv_ld;
+        const float *ct = A.rope_cos + (int64_t)p * (ATT_HD / 2), *st = A.rope_sin + (int64_t)p * (ATT_HD / 2);
+        const int nwork = len > 0 ? G + (owner ? 2 : 0) : 0;
+        for (int hh = warp; hh < nwork; hh += ATT_WARPS) {
+            const bool is_q = hh < G, is_k = hh == G;
+            const int64_t off = is_q ? (int64_t)(kvh * G + hh) * ATT_HD
+                                     : ((int64_t)A.n_heads + (is_k ? kvh : A.n_kv + kvh)) * ATT_HD;
+            const float4 x = *reinterpret_cast<const float4 *>(yrow + off + 4 * lane);
+            float v[4] = {x.x, x.y, x.z, x.w};
+            if (is_q || is_k)
+                qk_head_transform(v, lane, A.q_norm ? (is_q ? A.q_norm : A.k_norm) : nullptr, A.eps, ct, st,
+                                  A.rope_mode);
+            if (is_q) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) q_s[(4 * lane + e) * G + hh] = v[e];
+                if (rank == 0 && A.q_out)
+                    *reinterpret_cast<float4 *>(A.q_out + ((int64_t)b * A.n_heads + kvh * G + hh) * ATT_HD +
+                                                4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                // into the KV pool (for later steps) and, below, into the staged chunk
+                const int tc = p % ATT_CHUNK, page = bt_s[jf * PPC + tc / P], slot = p % P;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int d = 4 * lane + e;
+                    const __half h = __float2half_rn(v[e]);
+                    s_newkv[(is_k ? 0 : ATT_HD) + d] = h;
+                    if (page >= 0) {
+                        if (is_k)
+                            reinterpret_cast<__half *>(const_cast<void *>(A.kpool))
+                                [(((size_t)page * A.n_kv + kvh) * ATT_HD + d) * P + slot] = h;
+                        else
+                            reinterpret_cast<__half *>(const_cast<void *>(A.vpool))
+                                [(((size_t)page * A.n_kv + kvh) * P + slot) * ATT_HD + d] = h;
+                    }
+                }
+            }
+        }
+    } else {
         const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
         for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) q_s[(i % ATT_HD) * G + i / ATT_HD] = qg[i];
     }
@@ -233,6 +277,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         const __half *Vs = reinterpret_cast<const __half *>(kst + ATT_STAGE_K);
         const int ntok = min(ATT_CHUNK, len - (first + j) * ATT_CHUNK);
         ok = mbar_wait_bounded(&full[st], (uint32_t)(j / depth) & 1u) && ok;
+        if (A.qkv && j == jf) {
+            // the staged copy of the newest chunk predates this step's token: patch it in
+            if (tid < ATT_HD) {
+                const int tc = (len - 1) % ATT_CHUNK;
+                *reinterpret_cast<__half *>(const_cast<uint8_t *>(kst) + (tc / P) * (pbytes + ATT_KPAD) +
+                                            tid * k_row + (tc % P) * 2) = s_newkv[tid];
+                const_cast<__half *>(Vs)[(size_t)tc * ATT_HD + tid] = s_newkv[ATT_HD + tid];
+            }
+            __syncthreads();
+        }
         // ---- scores: f32 slice dot over this warp's 16 dims for tokens tk, tk+1
         {
             float acc[2][G];
@@ -456,7 +510,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             }
         }
     }
-    pdl_launch();
 }
 
 // (same arithmetic as the Q8_K store in ops.cu)

@@ -159,10 +159,6 @@ void launch_swiglu(fb_ctx *ctx, const float *g, const float *u, float *out, int6
 void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, float *x_out, const float *g, int rows,
                                  int dim, float eps, const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens,
                                  int vocab);
-void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
-                       const float *kn, float eps, const float *cos_t, const float *sin_t, int mode,
-                       const int32_t *pos, int max_ctx, float *q_out, void *kpool, void *vpool,
-                       const int32_t *block_table, int max_pages, int page_size, int num_pages);
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a);
 void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out);
 void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
@@ -182,6 +178,18 @@ struct AttnArgs {
     int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
     float scale;
     uint32_t *err;
+    // fused prologue (model path): when qkv != null the kernel takes q, k, v
+    // of the new token from the projection output [b][qkv_ld] = (q | k | v),
+    // applies the optional QK RMSNorm (q_norm / k_norm gains) and RoPE at
+    // position seq_len - 1, writes k / v into the pools and (q_out != null) a
+    // copy of the transformed q [b][n_heads][hd]
+    const float *qkv;
+    int64_t qkv_ld;
+    const float *q_norm, *k_norm;
+    float eps;
+    const float *rope_cos, *rope_sin;  // [rope_rows][hd / 2]
+    int rope_rows, rope_mode;
+    float *q_out;
 };
 void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
                         const Q8Act *aq, int *counters, bool pdl, bool want_cluster);

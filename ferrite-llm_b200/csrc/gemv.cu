@@ -39,7 +39,6 @@
 
 namespace fb {
 
-constexpr int KS_MAX = 8;  // warps per CTA (super-block slices of a tile): 4 or 8
 
 template <int DT> struct QRec;
 template <> struct QRec<4> { static constexpr int bytes = Q4K_REC; };

@@ -148,11 +148,52 @@ __device__ __forceinline__ float silu64(float v) {
     return __double2float_rn(__ddiv_rn((double)v, __dadd_rn(exp64(-(double)v), 1.0)));
 }
 
+// 1 / RMS factor of a row: sqrt(mean(x^2) + eps) from a binary64 sum of squares.
+__device__ __forceinline__ float rms_of(double ss, int dim, float eps) {
+    return __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(ss, (double)dim)), eps));
+}
+
 // Warp sum in binary64.
 __device__ __forceinline__ double warp_sum64(double v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
     return v;
+}
+
+// One 128-dim attention head held by a warp (lane owns dims 4 lane .. 4 lane
+// + 3): optional per-head RMSNorm with gain `gw` (Qwen3 QK-norm), then RoPE
+// with the position's cos / sin rows (64 entries): mode 0 rotates adjacent
+// pairs (2i, 2i+1), mode 1 rotates (i, i + 64) (partner in lane ^ 16).
+__device__ __forceinline__ void qk_head_transform(float (&v)[4], int lane, const float *gw, float eps,
+                                                  const float *ct, const float *st, int mode) {
+    if (gw) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 4; e++) ss = __fma_rn((double)v[e], (double)v[e], ss);
+        ss = warp_sum64(ss);
+        const float m = rms_of(ss, 128, eps);
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), gw[lane * 4 + e]);
+    }
+    if (mode == 0) {
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+            const int i = (lane * 4 + e) >> 1;
+            const float c = ct[i], s = st[i], x0 = v[e], x1 = v[e + 1];
+            v[e] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            v[e + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            const int d = lane * 4 + e;
+            const int i = d < 64 ? d : d - 64;
+            const float c = ct[i], s = st[i];
+            if (d < 64) v[e] = __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s));
+            else v[e] = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
+        }
+    }
 }
 
 }  // namespace fb

@@ -185,23 +185,28 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     A.nsplit_max = m->nsplit_max;
     A.scale = (float)(1.0 / sqrt((double)c.head_dim));
     A.err = ctx->err_word;
+    // QK-norm, RoPE and the KV-cache write run in the attention prologue
+    A.qkv = m->y_qkv.as<float>();
+    A.qkv_ld = (int64_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    A.eps = c.eps;
+    A.rope_cos = m->rope_cos.as<float>();
+    A.rope_sin = m->rope_sin.as<float>();
+    A.rope_rows = c.max_ctx;
+    A.rope_mode = c.rope_mode;
+    A.q_out = m->q.as<float>();
     for (int l = 0; l < c.n_layers; l++) {
         Layer &L = *m->layers[l];
         launch_gemv(ctx, L.wqkv.t, ah, b, m->y_qkv.as<float>(), L.wqkv.t->n);
         mark(FB_PROF_QKV, 1);
-        launch_qk_rope_kv(ctx, m->y_qkv.as<float>(), b, c.n_heads, c.n_kv_heads, c.head_dim,
-                          c.qk_norm ? L.q_norm.as<float>() : nullptr, c.qk_norm ? L.k_norm.as<float>() : nullptr,
-                          c.eps, m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.rope_mode, m->pos.as<int32_t>(),
-                          c.max_ctx, m->q.as<float>(), m->kpool(l), m->vpool(l), m->block_table.as<int32_t>(),
-                          m->pages_per_seq, kPage, m->num_pages);
-        mark(FB_PROF_ROPE_KV, 1);
         A.kpool = m->kpool(l);
         A.vpool = m->vpool(l);
+        A.q_norm = c.qk_norm ? L.q_norm.as<float>() : nullptr;
+        A.k_norm = c.qk_norm ? L.k_norm.as<float>() : nullptr;
         const bool q8_fused = (c.n_heads / c.n_kv_heads) % 2 == 0;
         launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), q8_fused ? &aa : nullptr,
                            m->att_cnt.as<int>(), true, true);
         if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
-        mark(FB_PROF_ATTN, 2);
+        mark(FB_PROF_ATTN, q8_fused ? 1 : 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         mark(FB_PROF_O, 1);
         launch_residual_rmsnorm_q8k(ctx, xa, m->y_o.as<float>(), xb, L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
@@ -656,7 +661,10 @@ int fb_model_launches_per_step(const fb_model *m, int *launches) {
         FB_REQUIRE(m && launches, "null argument");
         require_ready(m);
         const int L = m->c.n_layers;
-        *launches = 1 + 10 * L + 2;  // matches step(): embed-norm, 10 per layer, lm_head, argmax
+        const bool q8_fused = (m->c.n_heads / m->c.n_kv_heads) % 2 == 0;
+        // matches step(): embed-norm; per layer qkv, attention (+ Q8_K quantize
+        // for odd GQA groups), o, norm, gate_up, swiglu, down, norm; lm_head, argmax
+        *launches = 1 + (q8_fused ? 8 : 9) * L + 2;
     });
 }
 

@@ -88,9 +88,6 @@ __device__ __forceinline__ double block_sum64(double v, double *sh) {
 
 // 1 / rms from a binary64 sum of squares, as the oracle computes it:
 // m = sqrtf((float)(ss / dim) + eps).
-__device__ __forceinline__ float rms_of(double ss, int dim, float eps) {
-    return __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(ss, (double)dim)), eps));
-}
 
 // ------------------------------------------------------------------------
 // Residual add + RMSNorm + Q8_K.  One CTA per (256-value block, row): every
@@ -157,87 +154,6 @@ __global__ void __launch_bounds__(NORM_THREADS)
         }
         q8k_store_warp(v, lane, a, row, blk);
     }
-}
-
-// ------------------------------------------------------------------------
-// After the fused QKV GEMV: y[row] = [q (nq*hd) | k (nkv*hd) | v (nkv*hd)].
-// Per head (one warp): optional QK RMSNorm, RoPE at pos[row]; q -> q_out
-// (f32), k/v -> fp16 KV pages of sequence `row` at position pos[row].
-__global__ void __launch_bounds__(256)
-    k_qk_rope_kv(const float *__restrict__ y, int nq, int nkv, int hd, const float *__restrict__ qn,
-                 const float *__restrict__ kn, float eps, const float *__restrict__ cos_t,
-                 const float *__restrict__ sin_t, int mode, const int32_t *__restrict__ pos, int max_ctx,
-                 float *__restrict__ q_out, __half *__restrict__ kpool, __half *__restrict__ vpool,
-                 const int32_t *__restrict__ block_table, int max_pages, int page_size, int num_pages,
-                 uint32_t *err) {
-    pdl_wait();
-    pdl_launch();
-    const int row = blockIdx.y;
-    const int head = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int nh = nq + 2 * nkv;
-    if (head >= nh) return;
-    int p = pos[row];
-    if (p < 0 || p >= max_ctx) {
-        if (lane == 0) atomicOr(err, ERRBIT_BAD_POS);
-        return;
-    }
-    const float *src = y + (int64_t)row * nh * hd + (int64_t)head * hd;
-    const int per = hd / 32;  // values per lane (4 for hd = 128)
-    float v[8];
-    for (int e = 0; e < per; e++) v[e] = src[lane * per + e];
-    const bool is_q = head < nq, is_k = !is_q && head < nq + nkv;
-    if ((is_q || is_k) && qn) {
-        double ss = 0.0;
-        for (int e = 0; e < per; e++) ss = __fma_rn((double)v[e], (double)v[e], ss);
-        ss = warp_sum64(ss);
-        const float m = rms_of(ss, hd, eps);
-        const float *gw = is_q ? qn : kn;
-        for (int e = 0; e < per; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), gw[lane * per + e]);
-    }
-    if (is_q || is_k) {
-        const int half = hd / 2;
-        const float *ct = cos_t + (int64_t)p * half, *st = sin_t + (int64_t)p * half;
-        if (mode == 0) {
-            // interleaved: lane owns pairs (2i, 2i+1) inside its own values
-            for (int e = 0; e < per; e += 2) {
-                const int i = (lane * per + e) >> 1;
-                const float c = ct[i], s = st[i], x0 = v[e], x1 = v[e + 1];
-                v[e] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-                v[e + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-            }
-        } else {
-            // rotate-half: partner value lives in lane ^ 16 (same e)
-            for (int e = 0; e < per; e++) {
-                const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-                const int d = lane * per + e;
-                const int i = d < half ? d : d - half;
-                const float c = ct[i], s = st[i];
-                if (d < half) v[e] = __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s));
-                else v[e] = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
-            }
-        }
-    }
-    if (is_q) {
-        float *dst = q_out + ((int64_t)row * nq + head) * hd + lane * per;
-        for (int e = 0; e < per; e++) dst[e] = v[e];
-    } else {
-        const int kvh = is_k ? head - nq : head - nq - nkv;
-        const int lp = p / page_size;
-        const int page = lp < max_pages ? block_table[(int64_t)row * max_pages + lp] : -1;
-        if (page < 0 || page >= num_pages) {
-            if (lane == 0) atomicOr(err, ERRBIT_BAD_PAGE);
-            return;
-        }
-        if (is_k) {  // K pages are dim-major: [page][kv head][hd][page tokens]
-            __half *dst = kpool + ((int64_t)page * nkv + kvh) * hd * page_size + (p % page_size);
-            for (int e = 0; e < per; e++) dst[(int64_t)(lane * per + e) * page_size] = __float2half_rn(v[e]);
-        } else {  // V pages are token-major: [page][kv head][page tokens][hd]
-            __half *dst = vpool + (((int64_t)page * nkv + kvh) * page_size + (p % page_size)) * hd + lane * per;
-            for (int e = 0; e < per; e++) dst[e] = __float2half_rn(v[e]);
-        }
-    }
-    pdl_launch();
 }
 
 // ------------------------------------------------------------------------
@@ -394,17 +310,6 @@ void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, 
     FB_REQUIRE(x_out != x, "rmsnorm_q8k: x_out must not alias x");
     launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g, dim, eps, a,
              tab, tokens, vocab, ctx->err_word);
-}
-
-void launch_qk_rope_kv(fb_ctx *ctx, const float *y, int rows, int nq, int nkv, int hd, const float *qn,
-                       const float *kn, float eps, const float *cos_t, const float *sin_t, int mode,
-                       const int32_t *pos, int max_ctx, float *q_out, void *kpool, void *vpool,
-                       const int32_t *block_table, int max_pages, int page_size, int num_pages) {
-    FB_REQUIRE(hd == 64 || hd == 128, "qk_rope_kv: head_dim must be 64 or 128");
-    const int nh = nq + 2 * nkv;
-    launch_k(ctx, k_qk_rope_kv, dim3((nh + 7) / 8, rows), dim3(256), 0, y, nq, nkv, hd, qn, kn, eps, cos_t, sin_t,
-             mode, pos, max_ctx, q_out, (__half *)kpool, (__half *)vpool, block_table, max_pages, page_size,
-             num_pages, ctx->err_word);
 }
 
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a) {

@@ -223,7 +223,8 @@ int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale);
 int fb_model_read_kv(fb_model *m, int layer, int which, int pos,
                      float *out_host);
 int fb_model_weight_bytes(const fb_model *m, int64_t *bytes);
-/* Kernel classes of one decode step, for fb_model_profile. */
+/* Kernel classes of one decode step, for fb_model_profile (QK-norm, RoPE
+ * and the KV write run inside the attention kernel: FB_PROF_ROPE_KV stays 0). */
 enum fb_prof_kind {
     FB_PROF_EMBED_NORM = 0, FB_PROF_QKV = 1, FB_PROF_ROPE_KV = 2, FB_PROF_ATTN = 3,
     FB_PROF_O = 4, FB_PROF_NORM = 5, FB_PROF_GATE_UP = 6, FB_PROF_SWIGLU = 7,
