@@ -160,7 +160,9 @@ void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, 
                                  int dim, float eps, const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens,
                                  int vocab);
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a);
-void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out);
+// ws: argmax_ws_bytes(rows) bytes, zeroed once before first use.
+size_t argmax_ws_bytes(int rows);
+void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out, void *ws);
 void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
                      const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale);
 

@@ -85,7 +85,7 @@ struct fb_model {
     DevBuf kv;  // [L][K|V][num_pages][n_kv][page][hd] fp16
     DevBuf block_table, rope_cos, rope_sin;
     // step buffers
-    DevBuf x, x2, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml, att_cnt;
+    DevBuf x, x2, y_qkv, q, attn, y_o, y_gu, y_d, logits, part_o, part_ml, att_cnt, argmax_ws;
     float *x_last = nullptr;  // residual buffer holding the last step's final value
     DevBuf act_h, act_a, act_f;
     DevBuf tok, pos, next;
@@ -227,7 +227,7 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     m->x_last = xa;
     launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), c.vocab);
     mark(FB_PROF_LM_HEAD, 1);
-    launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>());
+    launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
     mark(FB_PROF_ARGMAX, 1);
     m->launches_per_step = nl;
 }
@@ -337,6 +337,8 @@ int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
         m->y_gu.alloc((size_t)B * 2 * c.ffn * 4);
         m->y_d.alloc((size_t)B * H * 4);
         m->logits.alloc((size_t)B * c.vocab * 4);
+        m->argmax_ws.alloc(argmax_ws_bytes(B));
+        FB_CUDA(cudaMemsetAsync(m->argmax_ws.ptr, 0, m->argmax_ws.bytes, ctx->stream));
         m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 8);
         m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 8);
         m->att_cnt.alloc((size_t)B * c.n_kv_heads * 4);

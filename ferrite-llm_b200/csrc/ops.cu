@@ -14,6 +14,8 @@
 // order.
 #include <math.h>
 
+#include <algorithm>
+
 #include "fb_internal.h"
 #include "kq_common.cuh"
 
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
                            const uint8_t *__restrict__ emb_tab, const int32_t *__restrict__ tokens, int vocab,
                            uint32_t *err) {
     __shared__ double sh[NORM_THREADS / 32];
-    __shared__ float xb[QK];
+    __shared__ __align__(16) float xb[QK];
     const int blk = blockIdx.x;
     const int64_t row = blockIdx.y;
     pdl_wait();
@@ -134,12 +136,60 @@ __global__ void __launch_bounds__(NORM_THREADS)
         }
     }
     double ss = 0.0;
-    for (int i = threadIdx.x; i < dim; i += NORM_THREADS) {
-        float v;
-        if (emb_tab) v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
-        else v = add ? __fadd_rn(add[row * dim + i], xr[i]) : xr[i];
-        ss = __fma_rn((double)v, (double)v, ss);
-        if (i / QK == blk) xb[i % QK] = v;
+    if (emb_tab) {
+        for (int i = threadIdx.x; i < dim; i += NORM_THREADS) {
+            const float v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
+            ss = __fma_rn((double)v, (double)v, ss);
+            if (i / QK == blk) xb[i % QK] = v;
+        }
+    } else {
+        // 4 consecutive values per thread and pass, every load of the row
+        // issued before the first use (the kernel is latency-bound)
+        constexpr int MAXP = 8;  // passes held in registers: dim <= 8192
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        const float4 *a4 = add ? reinterpret_cast<const float4 *>(add + row * dim) : nullptr;
+        const int nv = dim / 4;
+        float4 v[MAXP];
+#pragma unroll
+        for (int p = 0; p < MAXP; p++) {
+            const int i = threadIdx.x + p * NORM_THREADS;
+            v[p] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (a4) {
+            float4 d[MAXP];
+#pragma unroll
+            for (int p = 0; p < MAXP; p++) {
+                const int i = threadIdx.x + p * NORM_THREADS;
+                d[p] = i < nv ? a4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int p = 0; p < MAXP; p++)
+                v[p] = make_float4(__fadd_rn(d[p].x, v[p].x), __fadd_rn(d[p].y, v[p].y), __fadd_rn(d[p].z, v[p].z),
+                                   __fadd_rn(d[p].w, v[p].w));
+        }
+#pragma unroll
+        for (int p = 0; p < MAXP; p++) {
+            const int i = threadIdx.x + p * NORM_THREADS;
+            if (i < nv) {
+                ss = __fma_rn((double)v[p].x, (double)v[p].x, ss);
+                ss = __fma_rn((double)v[p].y, (double)v[p].y, ss);
+                ss = __fma_rn((double)v[p].z, (double)v[p].z, ss);
+                ss = __fma_rn((double)v[p].w, (double)v[p].w, ss);
+                if ((4 * i) / QK == blk) *reinterpret_cast<float4 *>(&xb[(4 * i) % QK]) = v[p];
+            }
+        }
+        for (int i = threadIdx.x + MAXP * NORM_THREADS; i < nv; i += NORM_THREADS) {  // dim > 8192
+            float4 w = x4[i];
+            if (a4) {
+                const float4 dd = a4[i];
+                w = make_float4(__fadd_rn(dd.x, w.x), __fadd_rn(dd.y, w.y), __fadd_rn(dd.z, w.z), __fadd_rn(dd.w, w.w));
+            }
+            ss = __fma_rn((double)w.x, (double)w.x, ss);
+            ss = __fma_rn((double)w.y, (double)w.y, ss);
+            ss = __fma_rn((double)w.z, (double)w.z, ss);
+            ss = __fma_rn((double)w.w, (double)w.w, ss);
+            if ((4 * i) / QK == blk) *reinterpret_cast<float4 *>(&xb[(4 * i) % QK]) = w;
+        }
     }
     ss = block_sum64<NORM_THREADS / 32>(ss, sh);  // (has a __syncthreads before the shared reads)
     const float m = rms_of(ss, dim, eps);
@@ -158,73 +208,92 @@ __global__ void __launch_bounds__(NORM_THREADS)
 
 // ------------------------------------------------------------------------
 // SwiGLU + Q8_K: y[row] = [gate (f) | up (f)] -> act = Q8K(silu(gate) * up).
-__global__ void __launch_bounds__(256) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
+// One warp per (row, 256-value block), two warps per CTA; the eight
+// exponentials of a lane are independent and overlap.
+constexpr int SWIGLU_WARPS = 2;
+__global__ void __launch_bounds__(32 * SWIGLU_WARPS) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows,
+                                                                  Q8Act a) {
     pdl_wait();
     pdl_launch();
     const int lane = threadIdx.x & 31;
     const int64_t nbk = f / QK;
-    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int64_t wid = (int64_t)blockIdx.x * SWIGLU_WARPS + (threadIdx.x >> 5);
     if (wid < rows * nbk) {
         const int64_t row = wid / nbk, blk = wid % nbk;
-        const float *gp = y + row * 2 * f + blk * QK + 8 * lane;
-        const float *up = gp + f;
+        const float4 *gp = reinterpret_cast<const float4 *>(y + row * 2 * f + blk * QK + 8 * lane);
+        const float4 *up = reinterpret_cast<const float4 *>(y + row * 2 * f + f + blk * QK + 8 * lane);
+        const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
         float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            v[e] = __fmul_rn(silu64(gp[e]), up[e]);
-        }
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(silu64(g[e]), u[e]);
         q8k_store_warp(v, lane, a, row, blk);
     }
-    pdl_launch();
 }
 
 // ------------------------------------------------------------------------
 // Greedy argmax over each logits row (first index of the maximum, like the
-// CPU oracle); one CTA per row.
-__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ logits, int64_t vocab,
-                                                 int32_t *__restrict__ out) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    pdl_wait();
-    const float *r = logits + (int64_t)blockIdx.x * vocab;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-        const float v = r[i];
-        if (v > best) {
-            best = v;
-            bi = (int)i;
-        }
+// CPU oracle).  grid (chunks, rows): every CTA reduces one chunk of the row
+// to (max, first index); the last CTA of a row (counter) reduces the chunk
+// results.  ws: rows * ARGMAX_CHUNKS (value, index) pairs + rows counters
+// (zero between launches).
+constexpr int ARGMAX_CHUNKS = 128;
+__device__ __forceinline__ void argmax_merge(float &best, int &bi, float ov, int oi) {
+    if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
     }
+}
+__device__ __forceinline__ void argmax_block(float &best, int &bi, float *sv, int *si) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > best || (ov == best && oi < bi)) {
-            best = ov;
-            bi = oi;
-        }
-    }
+    for (int off = 16; off > 0; off >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, off), __shfl_xor_sync(0xffffffffu, bi, off));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
         sv[warp] = best;
         si[warp] = bi;
     }
     __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        best = lane < nw ? sv[lane] : -INFINITY;
-        bi = lane < nw ? si[lane] : 0x7fffffff;
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (ov > best || (ov == best && oi < bi)) {
-                best = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    for (int off = 16; off > 0; off >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, off), __shfl_xor_sync(0xffffffffu, bi, off));
+}
+__global__ void __launch_bounds__(256) k_argmax(const float *__restrict__ logits, int64_t vocab,
+                                                int32_t *__restrict__ out, float *__restrict__ ws_v,
+                                                int *__restrict__ ws_i, int *__restrict__ counters) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    __shared__ int s_last;
+    pdl_wait();
+    const int64_t row = blockIdx.y, chunk = (vocab + gridDim.x - 1) / gridDim.x;
+    const int64_t i0 = blockIdx.x * chunk, i1 = min(vocab, i0 + chunk);
+    const float *r = logits + row * vocab;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) argmax_merge(best, bi, r[i], (int)i);
+    argmax_block(best, bi, sv, si);
+    if (threadIdx.x == 0) {
+        ws_v[row * gridDim.x + blockIdx.x] = best;
+        ws_i[row * gridDim.x + blockIdx.x] = bi;
+        __threadfence();
+        const int prev = atomicAdd(&counters[row], 1);
+        s_last = prev == (int)gridDim.x - 1;
+        if (s_last) counters[row] = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        best = -INFINITY;
+        bi = 0x7fffffff;
+        for (int c = threadIdx.x; c < (int)gridDim.x; c += blockDim.x)
+            argmax_merge(best, bi, __ldcg(&ws_v[row * gridDim.x + c]), __ldcg(&ws_i[row * gridDim.x + c]));
+        __syncthreads();  // sv / si are reused
+        argmax_block(best, bi, sv, si);
+        if (threadIdx.x == 0) out[row] = bi == 0x7fffffff ? 0 : bi;
     }
     pdl_launch();
 }
@@ -313,13 +382,20 @@ void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, 
 }
 
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a) {
-    FB_REQUIRE(f % QK == 0, "swiglu_q8k: ffn must be a multiple of 256");
     const int64_t warps = (int64_t)rows * (f / QK);
-    launch_k(ctx, k_swiglu_q8k, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, y, f, (int64_t)rows, a);
+    launch_k(ctx, k_swiglu_q8k, dim3((unsigned)((warps + SWIGLU_WARPS - 1) / SWIGLU_WARPS)), dim3(32 * SWIGLU_WARPS), 0,
+             y, f, (int64_t)rows, a);
 }
 
-void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out) {
-    launch_k(ctx, k_argmax, dim3(rows), dim3(1024), 0, logits, vocab, out);
+size_t argmax_ws_bytes(int rows) { return (size_t)rows * ARGMAX_CHUNKS * 8 + (size_t)rows * 4; }
+
+void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out, void *ws) {
+    // ws: values, indices, counters (zero on first use, zero again after each launch)
+    float *wv = static_cast<float *>(ws);
+    int *wi = reinterpret_cast<int *>(wv + (size_t)rows * ARGMAX_CHUNKS);
+    int *cnt = wi + (size_t)rows * ARGMAX_CHUNKS;
+    const int chunks = (int)std::min<int64_t>(ARGMAX_CHUNKS, (vocab + 1023) / 1024);
+    launch_k(ctx, k_argmax, dim3(chunks, rows), dim3(256), 0, logits, vocab, out, wv, wi, cnt);
 }
 
 void rope_tables(int max_pos, int head_dim, float theta, std::vector<float> &cos_t, std::vector<float> &sin_t) {
