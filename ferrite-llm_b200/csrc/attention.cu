@@ -604,10 +604,12 @@ template <int G>
 static bool attn_plan(fb_ctx *ctx, const AttnArgs &A, int batch, bool want_cluster, int *depth, int *bt_cap,
                       size_t *smem) {
     *bt_cap = attn_bt_cap(A.max_pages, A.page_size);
-    // two stages keep a CTA under half of an SM's shared memory, so a
-    // 16-CTA cluster fits a GPC even where other work holds some SMs
+    // clusters: two stages keep a CTA under half of an SM's shared memory, so
+    // a 16-CTA cluster fits a GPC even where other work holds some SMs.
+    // Without clusters: three stages (over half of the shared memory, so one
+    // CTA per SM: the scheduler spreads the grid over all SMs).
     (void)batch;
-    *depth = 2;
+    *depth = want_cluster ? 2 : 3;
     *smem = attn_layout(G, *depth, *bt_cap).total;
     return want_cluster && attn_cluster_fits<G>(ctx->device, *smem);
 }

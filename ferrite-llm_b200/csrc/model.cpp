@@ -203,8 +203,10 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         A.q_norm = c.qk_norm ? L.q_norm.as<float>() : nullptr;
         A.k_norm = c.qk_norm ? L.k_norm.as<float>() : nullptr;
         const bool q8_fused = (c.n_heads / c.n_kv_heads) % 2 == 0;
+        // cluster-free merge: inside the step the 16-CTA clusters would be
+        // packed two per SM next to the still-running projection
         launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), q8_fused ? &aa : nullptr,
-                           m->att_cnt.as<int>(), true, true);
+                           m->att_cnt.as<int>(), true, false);
         if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
         mark(FB_PROF_ATTN, q8_fused ? 1 : 2);
         launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
