@@ -51,8 +51,10 @@ namespace fb {
 
 constexpr int ATT_HD = 128;
 constexpr int ATT_CHUNK = 64;  // tokens per pipeline stage (one or two pages)
-constexpr int ATT_WARPS = 8;
-constexpr int ATT_THREADS = 32 * ATT_WARPS;
+constexpr int ATT_SLICES = 8;  // 16-dim slices of the f32 score dot (fixed: the oracle's order)
+// warps per CTA: 16 for GQA groups up to 4, 8 for groups of 8 (whose per-warp
+// P.V partials would not fit the ring)
+__host__ __device__ constexpr int att_warps(int G) { return G <= 4 ? 16 : 8; }
 constexpr int ATT_DPR = ATT_HD / ATT_SPLITS;  // output dims merged per cluster rank
 constexpr int ATT_MAX_DEPTH = 4;
 constexpr int ATT_KPAD = 64;  // bytes between the two K pages of a 32-token-page chunk (bank shift)
@@ -77,12 +79,12 @@ __host__ __device__ inline AttnLayout attn_layout(int G, int depth, int bt_cap) 
     L.q = off;  // q[hd][G] f32; merged outputs (f32) at the end
     off += (size_t)ATT_HD * G * 4;
     L.part = off;  // part[warp][G][chunk] f32 slice dots; CTA partial o[G][hd] f64 at the end
-    const size_t part_bytes = (size_t)ATT_WARPS * G * ATT_CHUNK * 4, o_bytes = (size_t)G * ATT_HD * 8;
+    const size_t part_bytes = (size_t)ATT_SLICES * G * ATT_CHUNK * 4, o_bytes = (size_t)G * ATT_HD * 8;
     off += part_bytes > o_bytes ? part_bytes : o_bytes;
     L.p = off;  // p[chunk][G] f64
     off += (size_t)ATT_CHUNK * G * 8;
     L.misc = off;  // alpha[G] M[G] L[G] ls[warps] wts[G][S] wl[G][S] f64
-    off += (size_t)(3 * G + ATT_WARPS + 2 * G * ATT_SPLITS) * 8;
+    off += (size_t)(3 * G + att_warps(G) + 2 * G * ATT_SPLITS) * 8;
     L.inbox = off;  // cluster merge: [src rank][G][ATT_DPR + 2] f64 pushed by the peers
     off += (size_t)ATT_SPLITS * G * (ATT_DPR + 2) * 8;
     L.q8in = off;  // cluster merge: [2][hd] f32 outputs of one Q8_K block
@@ -112,7 +114,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 // The binary64 stages make the result independent of how the tokens are
 // split (up to binary64 rounding, far below the final f32 rounding).
 template <int G, bool CLUSTER>
-__global__ void __launch_bounds__(ATT_THREADS, 2)
+__global__ void __launch_bounds__(32 * att_warps(G), 1)
     k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq, int use_q8, int *__restrict__ counters,
                   int depth, int bt_cap) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -120,8 +122,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     __shared__ int s_len, s_first, s_mine, s_last;
     __shared__ __half s_newkv[2 * ATT_HD];  // fused prologue: the new token's k and v (fp16)
     constexpr int S = ATT_SPLITS;
-    constexpr int TPW = ATT_CHUNK * G / ATT_WARPS;  // tokens per warp in the softmax phase
-    constexpr int TPC = ATT_CHUNK / ATT_WARPS;      // tokens per warp in the P.V phase
+    constexpr int NW = att_warps(G), NT = 32 * NW;
+    constexpr int TPC = ATT_CHUNK / NW;          // tokens per warp in the P.V phase
+    constexpr int TPL = ATT_CHUNK * ATT_SLICES / NT;  // tokens per lane in the score phase (2 or 1)
+    constexpr int NWB = 2 * G < NW ? 2 * G : NW;      // softmax warps: one lane per (token, head)
+    constexpr int TPB = ATT_CHUNK * G / NWB;          // tokens per softmax warp (32 or 64)
     constexpr int IB = ATT_DPR + 2;                 // inbox doubles per (source rank, head)
     // peers may push into this CTA's shared memory once every CTA of the
     // cluster has started: arrive now, wait just before the first push
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     float *part = reinterpret_cast<float *>(smem + Ly.part);
     double *p_s = reinterpret_cast<double *>(smem + Ly.p);
     double *alpha_s = reinterpret_cast<double *>(smem + Ly.misc);
-    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + ATT_WARPS, *wl = wts + G * S;
+    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + NW, *wl = wts + G * S;
     double *inbox = reinterpret_cast<double *>(smem + Ly.inbox);
     float *q8in = reinterpret_cast<float *>(smem + Ly.q8in);
     int *bt_s = reinterpret_cast<int *>(smem + Ly.bt);
@@ -163,7 +168,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     __syncthreads();
     const int len = s_len, first = s_first, mine = s_mine;
     // block-table entries of this CTA's pages (-1: past the sequence end)
-    for (int i = tid; i < mine * PPC; i += ATT_THREADS) {
+    for (int i = tid; i < mine * PPC; i += NT) {
         const int lp = first * PPC + i;
         int page = -1;
         if (lp * P < len) {
@@ -203,6 +208,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     if (tid == 0)
         for (int j = 0; j < pre; j++)
             if (j != jf || A.qkv) issue(j);
+    // fused prologue: warp hh < G transforms q head hh, warps G and G + 1 (the
+    // newest chunk's owner) the new k and v; their gains and RoPE factors
+    // depend only on weights and the position, so they are loaded before the wait
+    const int nwork = A.qkv && len > 0 ? G + (owner ? 2 : 0) : 0;
+    QkHead qh{};
+    if (warp < nwork && warp <= G)
+        qh = qk_head_load(lane, A.q_norm ? (warp < G ? A.q_norm : A.k_norm) : nullptr,
+                          A.rope_cos + (int64_t)(len - 1) * (ATT_HD / 2), A.rope_sin + (int64_t)(len - 1) * (ATT_HD / 2),
+                          A.rope_mode);
     pdl_wait();
     pdl_launch();  // the next kernel may start streaming its weights
     if (tid == 0 && !A.qkv && jf >= 0 && jf < pre) issue(jf);
@@ -210,17 +224,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         // q of the G heads (every CTA), k and v of the new token (owner only)
         const int p = len - 1;
         const float *yrow = A.qkv + (int64_t)b * A.qkv_ld;
-        const float *ct = A.rope_cos + (int64_t)p * (ATT_HD / 2), *st = A.rope_sin + (int64_t)p * (ATT_HD / 2);
-        const int nwork = len > 0 ? G + (owner ? 2 : 0) : 0;
-        for (int hh = warp; hh < nwork; hh += ATT_WARPS) {
+        for (int hh = warp; hh < nwork; hh += NW) {
+            if (hh != warp && hh <= G)  // a second head on this warp (GQA group 8): load its factors now
+                qh = qk_head_load(lane, A.q_norm ? (hh < G ? A.q_norm : A.k_norm) : nullptr,
+                                  A.rope_cos + (int64_t)p * (ATT_HD / 2), A.rope_sin + (int64_t)p * (ATT_HD / 2),
+                                  A.rope_mode);
             const bool is_q = hh < G, is_k = hh == G;
             const int64_t off = is_q ? (int64_t)(kvh * G + hh) * ATT_HD
                                      : ((int64_t)A.n_heads + (is_k ? kvh : A.n_kv + kvh)) * ATT_HD;
             const float4 x = *reinterpret_cast<const float4 *>(yrow + off + 4 * lane);
             float v[4] = {x.x, x.y, x.z, x.w};
-            if (is_q || is_k)
-                qk_head_transform(v, lane, A.q_norm ? (is_q ? A.q_norm : A.k_norm) : nullptr, A.eps, ct, st,
-                                  A.rope_mode);
+            if (is_q || is_k) qk_head_apply(v, lane, qh, A.eps, A.rope_mode);
             if (is_q) {
 #pragma unroll
                 for (int e = 0; e < 4; e++) q_s[(4 * lane + e) * G + hh] = v[e];
@@ -248,20 +262,22 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         }
     } else {
         const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
-        for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) q_s[(i % ATT_HD) * G + i / ATT_HD] = qg[i];
+        for (int i = tid; i < G * ATT_HD; i += NT) q_s[(i % ATT_HD) * G + i / ATT_HD] = qg[i];
     }
 
     const int hg = warp % G, kb = warp / G;  // softmax phase: head and token block of this warp
     float m_run = -INFINITY;
-    double l_lane = 0.0;
+    double l_lane = 0.0, psum = 0.0;
     double o[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) o[g][e] = 0.0;
     bool ok = true;
-    // this lane's token pair (2 lane, 2 lane + 1) inside a stage's K^T region
-    const int tk = 2 * lane;
+    // score phase: warp = (slice sl, token group); the lane's TPL adjacent
+    // tokens start at tk inside a stage's K^T region
+    const int sl = warp % ATT_SLICES;
+    const int tk = TPL * lane + 32 * TPL * (warp / ATT_SLICES);
     const uint32_t k_lane = (uint32_t)((tk / P) * (pbytes + ATT_KPAD) + (tk % P) * 2);
     const uint32_t k_row = 2u * P;  // bytes between consecutive dims
 
@@ -287,62 +303,72 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             }
             __syncthreads();
         }
-        // ---- scores: f32 slice dot over this warp's 16 dims for tokens tk, tk+1
+        // ---- scores: f32 dot over slice sl (16 dims) for this lane's tokens
         {
-            float acc[2][G];
+            float acc[TPL][G];
 #pragma unroll
-            for (int g = 0; g < G; g++) acc[0][g] = acc[1][g] = 0.f;
-            const uint8_t *kp = kst + k_lane + (size_t)(warp * 16) * k_row;
-            const float *qw = q_s + warp * 16 * G;
+            for (int u = 0; u < TPL; u++)
+#pragma unroll
+                for (int g = 0; g < G; g++) acc[u][g] = 0.f;
+            const uint8_t *kp = kst + k_lane + (size_t)(sl * 16) * k_row;
+            const float *qw = q_s + sl * 16 * G;
 #pragma unroll
             for (int e = 0; e < 16; e++) {
-                const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(kp + e * k_row));
+                float kf[TPL];
+                if constexpr (TPL == 2) {
+                    const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(kp + e * k_row));
+                    kf[0] = k2.x;
+                    kf[TPL - 1] = k2.y;
+                } else {
+                    kf[0] = __half2float(*reinterpret_cast<const __half *>(kp + e * k_row));
+                }
 #pragma unroll
                 for (int g = 0; g < G; g++) {
                     const float qv = qw[e * G + g];
-                    acc[0][g] = __fmaf_rn(qv, kf.x, acc[0][g]);
-                    acc[1][g] = __fmaf_rn(qv, kf.y, acc[1][g]);
+#pragma unroll
+                    for (int u = 0; u < TPL; u++) acc[u][g] = __fmaf_rn(qv, kf[u], acc[u][g]);
                 }
             }
 #pragma unroll
-            for (int g = 0; g < G; g++)
-                *reinterpret_cast<float2 *>(&part[(warp * G + g) * ATT_CHUNK + tk]) =
-                    make_float2(acc[0][g], acc[1][g]);
+            for (int g = 0; g < G; g++) {
+                if constexpr (TPL == 2)
+                    *reinterpret_cast<float2 *>(&part[(sl * G + g) * ATT_CHUNK + tk]) = make_float2(acc[0][g], acc[TPL - 1][g]);
+                else
+                    part[(sl * G + g) * ATT_CHUNK + tk] = acc[0][g];
+            }
         }
         __syncthreads();
-        // ---- softmax: warp (hg, kb) scores all 64 tokens of head hg (for the
-        // chunk max) and exponentiates its block of TPW tokens
-        {
+        // ---- softmax on the first NWB warps, each with full lanes: warp
+        // (hg, kb) sums the slice dots of all 64 tokens of head hg (for the
+        // chunk max) and exponentiates its block of TPB tokens; the rescale
+        // factor exp(m_old - m_new) is computed once per head (kb == 0)
+        if (warp < NWB) {
             float sc[2];
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const int t = lane + 32 * h;
                 float sum = part[hg * ATT_CHUNK + t];
 #pragma unroll
-                for (int w = 1; w < ATT_WARPS; w++) sum = __fadd_rn(sum, part[(w * G + hg) * ATT_CHUNK + t]);
+                for (int w = 1; w < ATT_SLICES; w++) sum = __fadd_rn(sum, part[(w * G + hg) * ATT_CHUNK + t]);
                 sc[h] = t < ntok ? __fmul_rn(sum, A.scale) : -INFINITY;
             }
             float mp = fmaxf(sc[0], sc[1]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, off));
             const float m_new = fmaxf(m_run, mp);  // finite: the chunk holds at least one token
-            const double alpha = m_run == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run, (double)m_new));
+            if (kb == 0 && lane == 0)
+                alpha_s[hg] = m_run == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run, (double)m_new));
             m_run = m_new;
-            double psum = 0.0;
+            psum = 0.0;
 #pragma unroll
-            for (int i = 0; i < (TPW + 31) / 32; i++) {
-                const int tl = lane + 32 * i;
-                const int t = kb * TPW + (tl < TPW ? tl : 0);
-                const float s0 = __shfl_sync(0xffffffffu, sc[0], t & 31);
-                const float s1 = __shfl_sync(0xffffffffu, sc[1], t & 31);
-                if (tl < TPW) {
-                    const double p = t < ntok ? exp64(__dsub_rn((double)((t >> 5) ? s1 : s0), (double)m_new)) : 0.0;
+            for (int h = 0; h < 2; h++) {
+                const int t = lane + 32 * h;
+                if (t / TPB == kb) {  // warp-uniform
+                    const double p = t < ntok ? exp64(__dsub_rn((double)sc[h], (double)m_new)) : 0.0;
                     p_s[t * G + hg] = p;
                     psum = __dadd_rn(psum, p);
                 }
             }
-            l_lane = __dadd_rn(__dmul_rn(l_lane, alpha), psum);
-            if (kb == 0 && lane == 0) alpha_s[hg] = alpha;
         }
         __syncthreads();
         // ---- o = alpha * o + sum_t p_t v_t over this warp's TPC tokens; lane owns 4 dims
@@ -350,9 +376,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 const double al = alpha_s[g];
+                if (al != 1.0)  // the running max moved (uniform across the CTA)
 #pragma unroll
-                for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al);
+                    for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al);
             }
+            if (warp < NWB) l_lane = __dadd_rn(__dmul_rn(l_lane, alpha_s[hg]), psum);
             const int t0 = warp * TPC, t1 = min(t0 + TPC, ntok);
             for (int t = t0; t < t1; t++) {
                 const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)t * ATT_HD + 4 * lane);
@@ -382,7 +410,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     }
     // ---- CTA partial: o summed over warps (fixed order), l, running max
     {
-        const double lw = warp_sum64(l_lane);
+        const double lw = warp_sum64(l_lane);  // zero outside the softmax warps
         if (lane == 0) ls[warp] = lw;
         if (lane == 0 && warp < G) M_s[warp] = (double)m_run;  // warp g < G owns head g
     }
@@ -391,16 +419,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 #pragma unroll
         for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
     __syncthreads();
-    for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
+    for (int i = tid; i < G * ATT_HD; i += NT) {
         const int g = i / ATT_HD, d = i % ATT_HD;
         double sum = red[g * ATT_HD + d];
 #pragma unroll
-        for (int w = 1; w < ATT_WARPS; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
+        for (int w = 1; w < NW; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
         O_s[i] = sum;
     }
     if (tid < G) {
         double l = 0.0;
-        for (int w = tid; w < ATT_WARPS; w += G) l = __dadd_rn(l, ls[w]);
+        for (int w = tid; w < NW; w += G) l = __dadd_rn(l, ls[w]);
         L_s[tid] = l;
     }
     constexpr unsigned wmask = G * S >= 32 ? 0xffffffffu : (1u << (G * S)) - 1u;
@@ -409,7 +437,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         __syncthreads();
         cluster_wait();  // every CTA of the cluster has started
         // push: rank r receives dims [r*DPR, (r+1)*DPR) of each head plus (max, sum)
-        for (int i = tid; i < S * G * IB; i += ATT_THREADS) {
+        for (int i = tid; i < S * G * IB; i += NT) {
             const int r = i / (G * IB), g = (i / IB) % G, k = i % IB;
             const double v = k < ATT_DPR ? O_s[g * ATT_HD + r * ATT_DPR + k] : (k == ATT_DPR ? M_s[g] : L_s[g]);
             *cl.map_shared_rank(&inbox[(rank * G + g) * IB + k], r) = v;
@@ -452,7 +480,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     } else {
         const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * S;
         __syncthreads();
-        for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
+        for (int i = tid; i < G * ATT_HD; i += NT) {
             const int g = i / ATT_HD, d = i % ATT_HD;
             A.part_o[(hb0 + (int64_t)g * S + rank) * ATT_HD + d] = O_s[i];
         }
@@ -484,7 +512,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                 wl[tid] = __dmul_rn(w, Lr);
             }
             __syncthreads();
-            for (int i = tid; i < G * ATT_HD; i += ATT_THREADS) {
+            for (int i = tid; i < G * ATT_HD; i += NT) {
                 const int g = i / ATT_HD, d = i % ATT_HD;
                 double Or[S];
 #pragma unroll
@@ -501,7 +529,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             }
             if (use_q8) {
                 __syncthreads();
-                for (int blk = warp; blk < G / 2; blk += ATT_WARPS) {
+                for (int blk = warp; blk < G / 2; blk += NW) {
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = fin[blk * 256 + 8 * lane + e];
@@ -588,7 +616,7 @@ static bool attn_cluster_fits(int device, size_t smem) {
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(ATT_SPLITS, 1, 1);
-        cfg.blockDim = dim3(ATT_THREADS);
+        cfg.blockDim = dim3(32 * att_warps(G));
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
@@ -645,7 +673,7 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, float *out_
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.gridDim = dim3(ATT_SPLITS, A.n_kv, batch);
-    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.blockDim = dim3(32 * att_warps(G));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
     cfg.attrs = attr;

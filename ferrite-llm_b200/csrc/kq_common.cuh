@@ -164,22 +164,40 @@ __device__ __forceinline__ double warp_sum64(double v) {
 // + 3): optional per-head RMSNorm with gain `gw` (Qwen3 QK-norm), then RoPE
 // with the position's cos / sin rows (64 entries): mode 0 rotates adjacent
 // pairs (2i, 2i+1), mode 1 rotates (i, i + 64) (partner in lane ^ 16).
-__device__ __forceinline__ void qk_head_transform(float (&v)[4], int lane, const float *gw, float eps,
-                                                  const float *ct, const float *st, int mode) {
-    if (gw) {
+// QkHead holds this lane's gains and rotation factors; it depends only on
+// weights and the position, so it can be loaded before the grid-dependency
+// wait.
+struct QkHead {
+    float g[4], c[4], s[4];
+    bool norm;
+};
+__device__ __forceinline__ QkHead qk_head_load(int lane, const float *gw, const float *ct, const float *st, int mode) {
+    QkHead h;
+    h.norm = gw != nullptr;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        h.g[e] = gw ? gw[lane * 4 + e] : 1.f;
+        const int d = lane * 4 + e;
+        const int i = mode == 0 ? d >> 1 : (d < 64 ? d : d - 64);
+        h.c[e] = ct[i];
+        h.s[e] = st[i];
+    }
+    return h;
+}
+__device__ __forceinline__ void qk_head_apply(float (&v)[4], int lane, const QkHead &h, float eps, int mode) {
+    if (h.norm) {
         double ss = 0.0;
 #pragma unroll
         for (int e = 0; e < 4; e++) ss = __fma_rn((double)v[e], (double)v[e], ss);
         ss = warp_sum64(ss);
         const float m = rms_of(ss, 128, eps);
 #pragma unroll
-        for (int e = 0; e < 4; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), gw[lane * 4 + e]);
+        for (int e = 0; e < 4; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], m), h.g[e]);
     }
     if (mode == 0) {
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-            const int i = (lane * 4 + e) >> 1;
-            const float c = ct[i], s = st[i], x0 = v[e], x1 = v[e + 1];
+            const float c = h.c[e], s = h.s[e], x0 = v[e], x1 = v[e + 1];
             v[e] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
             v[e + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
         }
@@ -188,8 +206,7 @@ __device__ __forceinline__ void qk_head_transform(float (&v)[4], int lane, const
         for (int e = 0; e < 4; e++) {
             const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
             const int d = lane * 4 + e;
-            const int i = d < 64 ? d : d - 64;
-            const float c = ct[i], s = st[i];
+            const float c = h.c[e], s = h.s[e];
             if (d < 64) v[e] = __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s));
             else v[e] = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
         }

@@ -123,9 +123,32 @@ __global__ void __launch_bounds__(NORM_THREADS)
     __shared__ __align__(16) float xb[QK];
     const int blk = blockIdx.x;
     const int64_t row = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    // Loads that do not depend on the preceding kernel come first: the gains
+    // of this block (weights; usually evicted from L2 by the weight stream)
+    // and the residual row x, written two or more launches earlier.  Only
+    // `add` (the preceding projection's output) is read after the wait.
+    float gv[8];
+    if (threadIdx.x < 32) {
+        const float4 g0 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane);
+        const float4 g1 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane + 4);
+        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+    }
+    constexpr int MAXP = 8;  // passes held in registers: dim <= 8192
+    const float *xr = x ? x + row * dim : nullptr;
+    const int nv = dim / 4;
+    float4 v[MAXP];
+    if (!emb_tab) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+#pragma unroll
+        for (int p = 0; p < MAXP; p++) {
+            const int i = threadIdx.x + p * NORM_THREADS;
+            v[p] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     pdl_wait();
     pdl_launch();
-    const float *xr = x ? x + row * dim : nullptr;
     const int nbe = dim / QK;
     int tok = 0;
     if (emb_tab) {
@@ -138,23 +161,12 @@ __global__ void __launch_bounds__(NORM_THREADS)
     double ss = 0.0;
     if (emb_tab) {
         for (int i = threadIdx.x; i < dim; i += NORM_THREADS) {
-            const float v = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
-            ss = __fma_rn((double)v, (double)v, ss);
-            if (i / QK == blk) xb[i % QK] = v;
+            const float e = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
+            ss = __fma_rn((double)e, (double)e, ss);
+            if (i / QK == blk) xb[i % QK] = e;
         }
     } else {
-        // 4 consecutive values per thread and pass, every load of the row
-        // issued before the first use (the kernel is latency-bound)
-        constexpr int MAXP = 8;  // passes held in registers: dim <= 8192
-        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
         const float4 *a4 = add ? reinterpret_cast<const float4 *>(add + row * dim) : nullptr;
-        const int nv = dim / 4;
-        float4 v[MAXP];
-#pragma unroll
-        for (int p = 0; p < MAXP; p++) {
-            const int i = threadIdx.x + p * NORM_THREADS;
-            v[p] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
         if (a4) {
             float4 d[MAXP];
 #pragma unroll
@@ -178,6 +190,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
                 if ((4 * i) / QK == blk) *reinterpret_cast<float4 *>(&xb[(4 * i) % QK]) = v[p];
             }
         }
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
         for (int i = threadIdx.x + MAXP * NORM_THREADS; i < nv; i += NORM_THREADS) {  // dim > 8192
             float4 w = x4[i];
             if (a4) {
@@ -195,14 +208,10 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const float m = rms_of(ss, dim, eps);
     if (x_out) x_out[row * dim + blk * QK + threadIdx.x] = xb[threadIdx.x];
     if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        float v[8];
+        float q[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const int i = blk * QK + 8 * lane + e;
-            v[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), g[i]);
-        }
-        q8k_store_warp(v, lane, a, row, blk);
+        for (int e = 0; e < 8; e++) q[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), gv[e]);
+        q8k_store_warp(q, lane, a, row, blk);
     }
 }
 
