@@ -148,6 +148,10 @@ void launch_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out, int out_dtyp
 void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy);
 // m > 16 QMatMul (prefill form).
 void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m);
+// Tensor-core prefill QMatMul (fp16 operands, f32 accumulation): m >= 17 rows,
+// n a multiple of 128.
+bool prefill_gemm_supported(const fb_qtensor *w, int64_t m);
+void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m);
 void launch_block_dots(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int32_t *out_sc, int32_t *out_min);
 void launch_rmsnorm(fb_ctx *ctx, const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps);
 void launch_rope(fb_ctx *ctx, float *x, int64_t n_tok, int64_t n_heads, int64_t hd, int64_t pos0,

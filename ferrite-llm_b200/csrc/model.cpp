@@ -749,9 +749,13 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
 }  // extern "C"
 
 namespace fb {
-// Until the tensor-core prefill GEMM is in place, m > 16 runs the Q8_K
-// integer path in chunks of 16 rows.
+// m > 16: the tensor-core GEMM when the shape allows (n a multiple of 128),
+// else the Q8_K integer path in chunks of 16 rows.
 void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
+    if (prefill_gemm_supported(w, m)) {
+        prefill_gemm(ctx, w, x, y, m);
+        return;
+    }
     const int rc = fb_qmatmul_q8k(ctx, w, x, y, m);
     if (rc != FB_OK) fail(rc, fb_last_error());
 }

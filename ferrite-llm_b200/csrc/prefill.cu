@@ -1,0 +1,402 @@
+// Prefill QMatMul on the 5th-generation tensor cores:
+//   Y[T, N] = X[T, K] . dequant(W)[N, K]^T     (T >= 17 rows, Q4_K / Q6_K W)
+//
+// Replaces candle's large-m QMatMul (quantized_llama's prompt forward; the
+// reference's CUDA build runs MMQ `mul_mat_q4_K` at ferrite-os/crates/
+// internal/ptx-kernels/kernels/candle/quantized.cu:4297 or dequantize + GEMM).
+// Arithmetic: W is dequantized exactly as candle's `to_float` (f32, the
+// dequant kernels' formulas) and rounded to fp16; X is scaled per row by an
+// exact power of two that keeps |x| below 32768 and rounded to fp16; the
+// products accumulate in f32 in tensor memory; the row scale is applied in
+// the epilogue.
+//
+// B200 design (tensor-bound: 2 T N K flops):
+//  * one CTA per 128 x 128 output tile (cta_group::1, M = 128 tokens, N = 128
+//    weight rows), 6 warps: warp 0 feeds the pipeline (TMA tensor loads of
+//    fp16 X tiles with 128-byte swizzle; cp.async.bulk of the tile-major
+//    weight records, one contiguous 16-row x 256-column record per copy),
+//    warp 1 allocates tensor memory and issues tcgen05.mma from one thread,
+//    warps 2..5 dequantize each 64-column slice of the weight records into
+//    the K-major, 128-byte-swizzled fp16 B operand and then drain the f32
+//    accumulator with tcgen05.ld;
+//  * 4 smem stages of (A 16 KB + B 16 KB) plus two record buffers;
+//    mbarriers between the roles, every wait bounded (a timeout raises
+//    ERRBIT_WAIT_TIMEOUT and all roles stop).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "fb_internal.h"
+#include "kq_common.cuh"
+
+namespace fb {
+
+constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;  // tile; K step = one 128-byte swizzle row of fp16
+constexpr int PF_STAGES = 4;
+constexpr int PF_THREADS = 192;
+constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2, PF_B_BYTES = PF_BN * PF_BK * 2;  // 16 KB each
+constexpr int PF_TILES_N = PF_BN / 16;                                              // weight row tiles per CTA
+
+template <int DT> struct PfRec;
+template <> struct PfRec<4> { static constexpr int bytes = Q4K_REC; };
+template <> struct PfRec<6> { static constexpr int bytes = Q6K_REC; };
+
+template <int DT>
+constexpr size_t pf_smem_bytes() {
+    return 1024 /* alignment slack */ + (size_t)PF_STAGES * (PF_A_BYTES + PF_B_BYTES) +
+           2 * (size_t)PF_TILES_N * PfRec<DT>::bytes;
+}
+
+// ---- tcgen05 / TMA helpers -------------------------------------------------
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    // K-major, 128-byte swizzle: 8-row groups 1024 bytes apart (SBO = 64 x 16 B),
+    // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B)
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)64 << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// kind::f16 instruction descriptor: A = B = fp16, D = f32, both K-major,
+// M = 128, N = 128
+constexpr uint32_t PF_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(PF_BN >> 3) << 17) |
+                              ((uint32_t)(PF_BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(PF_IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Dequantizes the 64-column slice c (0..3) of super-block records for one
+// weight row (row r of the 16-row tile record `rec`) into 8 chunks of 8 fp16
+// values (uint4 each, k = 8q .. 8q+7 of the slice).  Same formulas as the
+// dequantization kernels (candle `to_float`), rounded to fp16.
+__device__ __forceinline__ void dequant_slice_q4k(const uint8_t *rec, int r, int c, uint4 (&out)[8]) {
+    const uint8_t *blk = rec + r * 144;
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const Q4Scales s = q4k_unpack_scales(hd.y, hd.z, hd.w);
+    const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
+    // group g = c: sub-block 2c (low nibbles, chunks 0..3) and 2c + 1 (high nibbles, chunks 4..7)
+    float d1[2], m1[2];
+#pragma unroll
+    for (int hi = 0; hi < 2; hi++) {
+        const int j = 2 * c + hi;
+        const int sc = byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
+        const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
+        d1[hi] = __fmul_rn(d, (float)sc);
+        m1[hi] = __fmul_rn(dmin, (float)mn);
+    }
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * c);
+#pragma unroll
+        for (int hi = 0; hi < 2; hi++) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const uint32_t word = e < 4 ? q.x : q.y;
+                const int nib = (int)((word >> (8 * (e & 3) + 4 * hi)) & 0xF);
+                v[e] = __fsub_rn(__fmul_rn(d1[hi], (float)nib), m1[hi]);
+            }
+            out[4 * hi + t] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
+                                         pack_h2(v[6], v[7]));
+        }
+    }
+}
+
+__device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int c, uint4 (&out)[8]) {
+    const uint32_t *blk = reinterpret_cast<const uint32_t *>(rec + r * 208);
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * r));
+    const int h = c >> 1;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int p = 2 * (c & 1) + (q >> 2), t = q & 3;
+        const int sc = sbyte_of(blk[48 + c], q >> 1);
+        const float ds = __fmul_rn(d, (float)sc);
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int x = e >> 2, e4 = e & 3;
+            const uint32_t qlw = blk[12 * t + 4 * h + 2 * (p & 1) + x];
+            const uint32_t qhw = blk[12 * t + 8 + 2 * h + x];
+            const int lo = (int)((qlw >> (8 * e4 + 4 * (p >> 1))) & 0xF);
+            const int hi2 = (int)((qhw >> (8 * e4 + 2 * p)) & 0x3);
+            v[e] = __fmul_rn(ds, (float)((lo | (hi2 << 4)) - 32));
+        }
+        out[q] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+    }
+}
+
+// grid (N / 128, ceil(T / 128)), 192 threads.
+template <int DT>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+    k_prefill_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t nb, int T,
+                   int64_t N, const float *__restrict__ rowscale, float *__restrict__ Y, uint32_t *err) {
+    constexpr int REC = PfRec<DT>::bytes;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t a_full[PF_STAGES], b_full[PF_STAGES], empty[PF_STAGES], rec_full[2], rec_empty[2], acc_full;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort_raw;
+    volatile int &s_abort = s_abort_raw;  // set by any role that gives up; polled by the others
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem, *sB = smem + PF_STAGES * PF_A_BYTES;
+    uint8_t *sRec = sB + PF_STAGES * PF_B_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tile = blockIdx.x, m0 = blockIdx.y * PF_BM;
+    const int ksteps = (int)nb * 4;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PF_STAGES; i++) {
+            mbar_init(&a_full[i], 1);
+            mbar_init(&b_full[i], 4);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&rec_full[i], 1);
+            mbar_init(&rec_empty[i], 4);
+        }
+        mbar_init(&acc_full, 1);
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    if (warp == 1) {
+        // 128 f32 accumulator columns (one per output column) x 128 lanes (rows)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(PF_BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint8_t *wtiles = W + (size_t)n_tile * PF_TILES_N * nb * REC;
+            for (int s = 0; s < ksteps && !s_abort; s++) {
+                const int st = s % PF_STAGES;
+                if (s >= PF_STAGES && !mbar_wait_bounded(&empty[st], (uint32_t)((s / PF_STAGES) - 1) & 1u)) {
+                    s_abort = 1;
+                    break;
+                }
+                mbar_expect_tx(&a_full[st], PF_A_BYTES);
+                tma_load_2d(sA + st * PF_A_BYTES, &xmap, s * PF_BK, m0, &a_full[st]);
+                if (s % 4 == 0) {
+                    const int sb = s / 4, rb = sb & 1;
+                    if (sb >= 2 && !mbar_wait_bounded(&rec_empty[rb], (uint32_t)((sb >> 1) - 1) & 1u)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&rec_full[rb], PF_TILES_N * REC);
+                    for (int tt = 0; tt < PF_TILES_N; tt++)
+                        bulk_g2s(sRec + ((size_t)rb * PF_TILES_N + tt) * REC,
+                                 wtiles + ((size_t)tt * nb + sb) * REC, REC, &rec_full[rb]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+            for (int s = 0; s < ksteps && !s_abort; s++) {
+                const int st = s % PF_STAGES;
+                const uint32_t par = (uint32_t)(s / PF_STAGES) & 1u;
+                if (!mbar_wait_bounded(&a_full[st], par) || !mbar_wait_bounded(&b_full[st], par)) {
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < PF_BK / 16; kk++) {
+                    const uint64_t da = umma_desc_sw128(aBase + st * PF_A_BYTES + kk * 32);
+                    const uint64_t db = umma_desc_sw128(bBase + st * PF_B_BYTES + kk * 32);
+                    umma_f16(tmem, da, db, (s > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty[st]);  // frees the stage once these MMAs have read it
+            }
+            umma_commit(&acc_full);
+        }
+    } else {
+        // warps 2..5: dequantize, then drain the accumulator
+        const int tid = threadIdx.x - 64;  // 0..127: weight row of the tile
+        const int tt = tid >> 4, r = tid & 15;
+        for (int s = 0; s < ksteps && !s_abort; s++) {
+            const int st = s % PF_STAGES, sb = s >> 2, rb = sb & 1, c = s & 3;
+            if (c == 0 && !mbar_wait_bounded(&rec_full[rb], (uint32_t)(sb >> 1) & 1u)) {
+                s_abort = 1;
+                break;
+            }
+            if (s >= PF_STAGES && !mbar_wait_bounded(&empty[st], (uint32_t)((s / PF_STAGES) - 1) & 1u)) {
+                s_abort = 1;
+                break;
+            }
+            uint4 ch[8];
+            const uint8_t *rec = sRec + ((size_t)rb * PF_TILES_N + tt) * REC;
+            if constexpr (DT == 4) dequant_slice_q4k(rec, r, c, ch);
+            else dequant_slice_q6k(rec, r, c, ch);
+            uint8_t *brow = sB + st * PF_B_BYTES + tid * 128;
+#pragma unroll
+            for (int q = 0; q < 8; q++) *reinterpret_cast<uint4 *>(brow + ((q ^ (tid & 7)) << 4)) = ch[q];
+            fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor cores
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&b_full[st]);
+                if (c == 3) mbar_arrive(&rec_empty[rb]);
+            }
+        }
+        if (!s_abort && mbar_wait_bounded(&acc_full, 0)) {
+            tc_fence_after();
+            const int q = warp & 3;  // TMEM lane quarter of this warp
+            const int row = m0 + 32 * q + lane;
+            const float sc = row < T ? rowscale[row] : 0.f;
+#pragma unroll 1
+            for (int cc = 0; cc < PF_BN / 32; cc++) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
+                if (row < T) {
+                    float *dst = Y + (int64_t)row * N + (int64_t)n_tile * PF_BN + 32 * cc;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(dst + i) =
+                            make_float4(__fmul_rn(__uint_as_float(v[i]), sc), __fmul_rn(__uint_as_float(v[i + 1]), sc),
+                                        __fmul_rn(__uint_as_float(v[i + 2]), sc),
+                                        __fmul_rn(__uint_as_float(v[i + 3]), sc));
+                }
+            }
+        } else {
+            s_abort = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (s_abort && threadIdx.x == 0) atomicOr(err, ERRBIT_WAIT_TIMEOUT);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_BN) : "memory");
+    }
+    pdl_launch();
+}
+
+// X [T, K] f32 -> fp16 with a per-row power-of-two scale s (|x / s| <= 32768):
+// one warp per row.
+__global__ void __launch_bounds__(256) k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh,
+                                                  float *__restrict__ rowscale, int T, int64_t K) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float *xr = x + (int64_t)row * K;
+    float amax = 0.f;
+    for (int64_t i = 4 * lane; i < K; i += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + i);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    int e = 0;  // smallest e >= 0 with amax / 2^e <= 32768
+    while (e < 120 && amax > ldexpf(32768.f, e)) e++;
+    const float inv = ldexpf(1.f, -e);
+    if (lane == 0) rowscale[row] = ldexpf(1.f, e);
+    __half *hr = xh + (int64_t)row * K;
+    for (int64_t i = 4 * lane; i < K; i += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + i);
+        const __half2 a = __floats2half2_rn(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv));
+        const __half2 b = __floats2half2_rn(__fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+        *reinterpret_cast<uint2 *>(hr + i) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool prefill_gemm_supported(const fb_qtensor *w, int64_t m) {
+    return (w->dtype == FB_Q4_K || w->dtype == FB_Q6_K) && m >= 17 && w->n % PF_BN == 0 && w->k % QK == 0 &&
+           m <= 0x7fffffff;
+}
+
+template <int DT>
+static void launch_prefill_dt(fb_ctx *ctx, const fb_qtensor *w, const CUtensorMap &map, const float *rowscale,
+                              float *y, int T) {
+    const size_t smem = pf_smem_bytes<DT>();
+    FB_CUDA(cudaFuncSetAttribute(k_prefill_gemm<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)(w->n / PF_BN), (unsigned)((T + PF_BM - 1) / PF_BM));
+    k_prefill_gemm<DT><<<grid, PF_THREADS, smem, ctx->stream>>>(map, w->main(), w->nb(), T, w->n, rowscale, y,
+                                                                 ctx->err_word);
+    FB_CUDA(cudaGetLastError());
+}
+
+// Y[m, n] = X[m, k] . W^T on the tensor cores (prefill_gemm_supported(w, m)).
+void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
+    FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
+    auto encode = tensor_map_encoder();
+    FB_REQUIRE(encode != nullptr, "prefill gemm: cuTensorMapEncodeTiled is unavailable");
+    const int64_t K = w->k;
+    const size_t xh_bytes = ((size_t)m * K * 2 + 255) & ~(size_t)255;
+    uint8_t *scratch = static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + (size_t)m * 4));
+    __half *xh = reinterpret_cast<__half *>(scratch);
+    float *rowscale = reinterpret_cast<float *>(scratch + xh_bytes);
+    k_x_to_f16<<<(unsigned)((m + 7) / 8), 256, 0, ctx->stream>>>(x, xh, rowscale, (int)m, K);
+    FB_CUDA(cudaGetLastError());
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {PF_BK, PF_BM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FB_REQUIRE(cr == CUDA_SUCCESS, "prefill gemm: tensor map encoding failed");
+    if (w->dtype == FB_Q4_K) launch_prefill_dt<4>(ctx, w, map, rowscale, y, (int)m);
+    else launch_prefill_dt<6>(ctx, w, map, rowscale, y, (int)m);
+}
+
+}  // namespace fb
