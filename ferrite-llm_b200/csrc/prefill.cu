@@ -16,9 +16,9 @@
 //    fp16 X tiles with 128-byte swizzle; cp.async.bulk of the tile-major
 //    weight records, one contiguous 16-row x 256-column record per copy),
 //    warp 1 allocates tensor memory and issues tcgen05.mma from one thread,
-//    warps 2..5 dequantize each 64-column slice of the weight records into
-//    the K-major, 128-byte-swizzled fp16 B operand and then drain the f32
-//    accumulator with tcgen05.ld;
+//    warps 2..9 (two threads per weight row) dequantize each 64-column
+//    slice of the weight records into the K-major, 128-byte-swizzled fp16 B
+//    operand and then drain the f32 accumulator with tcgen05.ld;
 //  * 4 smem stages of (A 16 KB + B 16 KB) plus two record buffers;
 //    mbarriers between the roles, every wait bounded (a timeout raises
 //    ERRBIT_WAIT_TIMEOUT and all roles stop).
@@ -35,7 +35,8 @@ namespace fb {
 
 constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;  // tile; K step = one 128-byte swizzle row of fp16
 constexpr int PF_STAGES = 4;
-constexpr int PF_THREADS = 192;
+constexpr int PF_DQ_WARPS = 8;                        // dequant / epilogue warps (two per weight row)
+constexpr int PF_THREADS = 64 + 32 * PF_DQ_WARPS;
 constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2, PF_B_BYTES = PF_BN * PF_BK * 2;  // 16 KB each
 constexpr int PF_TILES_N = PF_BN / 16;                                              // weight row tiles per CTA
 
@@ -101,54 +102,53 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// (float)v for 0 <= v < 2^22 without the conversion pipe: 2^23 + v as float
+// bits, minus 2^23 (exact).
+__device__ __forceinline__ float small_int_to_float(uint32_t v) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f);
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Dequantizes the 64-column slice c (0..3) of super-block records for one
-// weight row (row r of the 16-row tile record `rec`) into 8 chunks of 8 fp16
-// values (uint4 each, k = 8q .. 8q+7 of the slice).  Same formulas as the
-// dequantization kernels (candle `to_float`), rounded to fp16.
-__device__ __forceinline__ void dequant_slice_q4k(const uint8_t *rec, int r, int c, uint4 (&out)[8]) {
+// Dequantizes half hf (0, 1) of the 64-column slice c (0..3) of one weight
+// row's super-block (row r of the 16-row tile record `rec`) into 4 chunks of
+// 8 fp16 values (uint4 each): chunks 4 hf .. 4 hf + 3, k = 8q .. 8q+7 of the
+// slice.  Same formulas as the dequantization kernels (candle `to_float`),
+// rounded to fp16.
+__device__ __forceinline__ void dequant_slice_q4k(const uint8_t *rec, int r, int c, int hf, uint4 (&out)[4]) {
     const uint8_t *blk = rec + r * 144;
     const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
     const Q4Scales s = q4k_unpack_scales(hd.y, hd.z, hd.w);
     const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
-    // group g = c: sub-block 2c (low nibbles, chunks 0..3) and 2c + 1 (high nibbles, chunks 4..7)
-    float d1[2], m1[2];
-#pragma unroll
-    for (int hi = 0; hi < 2; hi++) {
-        const int j = 2 * c + hi;
-        const int sc = byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
-        const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
-        d1[hi] = __fmul_rn(d, (float)sc);
-        m1[hi] = __fmul_rn(dmin, (float)mn);
-    }
+    // group g = c: sub-block 2c (low nibbles, chunks 0..3) or 2c + 1 (high nibbles, chunks 4..7)
+    const int j = 2 * c + hf;
+    const int sc = byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
+    const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
+    const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
 #pragma unroll
     for (int t = 0; t < 4; t++) {
         const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * c);
+        float v[8];
 #pragma unroll
-        for (int hi = 0; hi < 2; hi++) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const uint32_t word = e < 4 ? q.x : q.y;
-                const int nib = (int)((word >> (8 * (e & 3) + 4 * hi)) & 0xF);
-                v[e] = __fsub_rn(__fmul_rn(d1[hi], (float)nib), m1[hi]);
-            }
-            out[4 * hi + t] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
-                                         pack_h2(v[6], v[7]));
+        for (int e = 0; e < 8; e++) {
+            const uint32_t word = e < 4 ? q.x : q.y;
+            const uint32_t nib = (word >> (8 * (e & 3) + 4 * hf)) & 0xFu;
+            v[e] = __fsub_rn(__fmul_rn(d1, small_int_to_float(nib)), m1);
         }
+        out[t] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
     }
 }
 
-__device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int c, uint4 (&out)[8]) {
+__device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int c, int hf, uint4 (&out)[4]) {
     const uint32_t *blk = reinterpret_cast<const uint32_t *>(rec + r * 208);
     const float d = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * r));
     const int h = c >> 1;
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
+    for (int qq = 0; qq < 4; qq++) {
+        const int q = 4 * hf + qq;
         const int p = 2 * (c & 1) + (q >> 2), t = q & 3;
         const int sc = sbyte_of(blk[48 + c], q >> 1);
         const float ds = __fmul_rn(d, (float)sc);
@@ -158,15 +158,16 @@ __device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int
             const int x = e >> 2, e4 = e & 3;
             const uint32_t qlw = blk[12 * t + 4 * h + 2 * (p & 1) + x];
             const uint32_t qhw = blk[12 * t + 8 + 2 * h + x];
-            const int lo = (int)((qlw >> (8 * e4 + 4 * (p >> 1))) & 0xF);
-            const int hi2 = (int)((qhw >> (8 * e4 + 2 * p)) & 0x3);
-            v[e] = __fmul_rn(ds, (float)((lo | (hi2 << 4)) - 32));
+            const uint32_t lo = (qlw >> (8 * e4 + 4 * (p >> 1))) & 0xFu;
+            const uint32_t hi2 = (qhw >> (8 * e4 + 2 * p)) & 0x3u;
+            // (q6 - 32) exactly: 2^23 + q6 as float bits minus (2^23 + 32)
+            v[e] = __fmul_rn(ds, __fsub_rn(__uint_as_float(0x4B000000u | lo | (hi2 << 4)), 8388640.f));
         }
-        out[q] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+        out[qq] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
     }
 }
 
-// grid (N / 128, ceil(T / 128)), 192 threads.
+// grid (N / 128, ceil(T / 128)), PF_THREADS threads.
 template <int DT>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t nb, int T,
@@ -187,12 +188,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < PF_STAGES; i++) {
             mbar_init(&a_full[i], 1);
-            mbar_init(&b_full[i], 4);
+            mbar_init(&b_full[i], PF_DQ_WARPS);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&rec_full[i], 1);
-            mbar_init(&rec_empty[i], 4);
+            mbar_init(&rec_empty[i], PF_DQ_WARPS);
         }
         mbar_init(&acc_full, 1);
         mbar_fence_init();
@@ -257,9 +258,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             umma_commit(&acc_full);
         }
     } else {
-        // warps 2..5: dequantize, then drain the accumulator
-        const int tid = threadIdx.x - 64;  // 0..127: weight row of the tile
-        const int tt = tid >> 4, r = tid & 15;
+        // warps 2..9: dequantize (thread = weight row x half slice), then
+        // drain the accumulator (warp quarter x column half)
+        const int tid = threadIdx.x - 64;        // 0..255
+        const int row = tid & 127, hf = tid >> 7;  // weight row of the tile, half of the slice
+        const int tt = row >> 4, r = row & 15;
         for (int s = 0; s < ksteps && !s_abort; s++) {
             const int st = s % PF_STAGES, sb = s >> 2, rb = sb & 1, c = s & 3;
             if (c == 0 && !mbar_wait_bounded(&rec_full[rb], (uint32_t)(sb >> 1) & 1u)) {
@@ -270,13 +273,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 s_abort = 1;
                 break;
             }
-            uint4 ch[8];
+            uint4 ch[4];
             const uint8_t *rec = sRec + ((size_t)rb * PF_TILES_N + tt) * REC;
-            if constexpr (DT == 4) dequant_slice_q4k(rec, r, c, ch);
-            else dequant_slice_q6k(rec, r, c, ch);
-            uint8_t *brow = sB + st * PF_B_BYTES + tid * 128;
+            if constexpr (DT == 4) dequant_slice_q4k(rec, r, c, hf, ch);
+            else dequant_slice_q6k(rec, r, c, hf, ch);
+            uint8_t *brow = sB + st * PF_B_BYTES + row * 128;
 #pragma unroll
-            for (int q = 0; q < 8; q++) *reinterpret_cast<uint4 *>(brow + ((q ^ (tid & 7)) << 4)) = ch[q];
+            for (int qq = 0; qq < 4; qq++) {
+                const int q = 4 * hf + qq;
+                *reinterpret_cast<uint4 *>(brow + ((q ^ (row & 7)) << 4)) = ch[qq];
+            }
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor cores
             __syncwarp();
             if (lane == 0) {
@@ -286,15 +292,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
         if (!s_abort && mbar_wait_bounded(&acc_full, 0)) {
             tc_fence_after();
-            const int q = warp & 3;  // TMEM lane quarter of this warp
-            const int row = m0 + 32 * q + lane;
-            const float sc = row < T ? rowscale[row] : 0.f;
+            const int q = warp & 3;                  // TMEM lane quarter of this warp
+            const int ch0 = (warp - 2) >> 2;         // column half: warps 2..5 -> 0, 6..9 -> 1
+            const int orow = m0 + 32 * q + lane;
+            const float sc = orow < T ? rowscale[orow] : 0.f;
 #pragma unroll 1
-            for (int cc = 0; cc < PF_BN / 32; cc++) {
+            for (int cc = 2 * ch0; cc < 2 * ch0 + 2; cc++) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
-                if (row < T) {
-                    float *dst = Y + (int64_t)row * N + (int64_t)n_tile * PF_BN + 32 * cc;
+                if (orow < T) {
+                    float *dst = Y + (int64_t)orow * N + (int64_t)n_tile * PF_BN + 32 * cc;
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
                         *reinterpret_cast<float4 *>(dst + i) =
