@@ -4,11 +4,11 @@
 // Replaces candle's large-m QMatMul (quantized_llama's prompt forward; the
 // reference's CUDA build runs MMQ `mul_mat_q4_K` at ferrite-os/crates/
 // internal/ptx-kernels/kernels/candle/quantized.cu:4297 or dequantize + GEMM).
-// Arithmetic: W is dequantized exactly as candle's `to_float` (f32, the
-// dequant kernels' formulas) and rounded to fp16; X is scaled per row by an
-// exact power of two that keeps |x| below 32768 and rounded to fp16; the
-// products accumulate in f32 in tensor memory; the row scale is applied in
-// the epilogue.
+// Arithmetic: W is dequantized in fp16 with candle's `to_float` factors
+// (w = fp16(fp16(d*sc) * q - fp16(dmin*m)), see dequant_slice_*); X is
+// scaled per row by an exact power of two that keeps |x| below 32768 and
+// rounded to fp16; the products accumulate in f32 in tensor memory; the row
+// scale is applied in the epilogue.
 //
 // B200 design (tensor-bound: 2 T N K flops):
 //  * one CTA per 128 x 128 output tile (cta_group::1, M = 128 tokens, N = 128
@@ -102,68 +102,73 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// (float)v for 0 <= v < 2^22 without the conversion pipe: 2^23 + v as float
-// bits, minus 2^23 (exact).
-__device__ __forceinline__ float small_int_to_float(uint32_t v) {
-    return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f);
+// Packed fp16 dequantization (two weights per instruction).  A weight's
+// integer code q goes into an fp16 exactly as 1024 + q (bits 0x6400 | q) and
+// 1024 is subtracted; the factors are fp16 roundings of the exact f32
+// products d * sc (and dmin * m):  w = fp16(fp16(d*sc) * q - fp16(dmin*m))
+// for Q4_K (one fused multiply-add, one rounding) and
+// w = fp16(fp16(d*sc) * (q - 32)) for Q6_K.
+__device__ __forceinline__ __half2 h2_bits(uint32_t v) { return *reinterpret_cast<const __half2 *>(&v); }
+__device__ __forceinline__ uint32_t bits_h2(__half2 v) { return *reinterpret_cast<const uint32_t *>(&v); }
+__device__ __forceinline__ __half half_of_small_uint(uint32_t v) {  // 0 <= v < 1024, exact
+    return __hsub(__ushort_as_half((unsigned short)(0x6400u | v)), __ushort_as_half((unsigned short)0x6400u));
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
-
-// Dequantizes half hf (0, 1) of the 64-column slice c (0..3) of one weight
-// row's super-block (row r of the 16-row tile record `rec`) into 4 chunks of
-// 8 fp16 values (uint4 each): chunks 4 hf .. 4 hf + 3, k = 8q .. 8q+7 of the
-// slice.  Same formulas as the dequantization kernels (candle `to_float`),
-// rounded to fp16.
+// Half hf (0, 1) of the 64-column slice c (0..3) of one weight row's
+// super-block (row r of the 16-row tile record `rec`) -> 4 chunks of 8 fp16
+// weights (uint4 each): chunks 4 hf .. 4 hf + 3 (k = 8q .. 8q+7 of the slice).
 __device__ __forceinline__ void dequant_slice_q4k(const uint8_t *rec, int r, int c, int hf, uint4 (&out)[4]) {
     const uint8_t *blk = rec + r * 144;
     const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
     const Q4Scales s = q4k_unpack_scales(hd.y, hd.z, hd.w);
-    const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
     // group g = c: sub-block 2c (low nibbles, chunks 0..3) or 2c + 1 (high nibbles, chunks 4..7)
     const int j = 2 * c + hf;
-    const int sc = byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
-    const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
-    const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+    const uint32_t sc = (uint32_t)byte_of(j < 4 ? s.sc_lo : s.sc_hi, j & 3);
+    const uint32_t mn = (uint32_t)byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
+    const __half d1 = __hmul(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)), half_of_small_uint(sc));
+    const __half m1 = __hmul(__ushort_as_half((unsigned short)(hd.x >> 16)), half_of_small_uint(mn));
+    const __half2 d12 = __halves2half2(d1, d1), nm12 = __halves2half2(__hneg(m1), __hneg(m1));
+    const __half2 k1024 = h2_bits(0x64006400u);
 #pragma unroll
     for (int t = 0; t < 4; t++) {
         const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * c);
-        float v[8];
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const uint32_t word = e < 4 ? q.x : q.y;
-            const uint32_t nib = (word >> (8 * (e & 3) + 4 * hf)) & 0xFu;
-            v[e] = __fsub_rn(__fmul_rn(d1, small_int_to_float(nib)), m1);
+        for (int pr = 0; pr < 4; pr++) {  // bytes (2pr, 2pr + 1) of the 8
+            const uint32_t word = pr < 2 ? q.x : q.y;
+            uint32_t p = __byte_perm(word, 0u, (pr & 1) ? 0x4342u : 0x4140u);  // byte pair -> halves
+            if (hf) p >>= 4;
+            const __half2 nib = __hsub2(h2_bits((p & 0x000F000Fu) | 0x64006400u), k1024);
+            w[pr] = bits_h2(__hfma2(d12, nib, nm12));
         }
-        out[t] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+        out[t] = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
 __device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int c, int hf, uint4 (&out)[4]) {
     const uint32_t *blk = reinterpret_cast<const uint32_t *>(rec + r * 208);
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * r));
+    const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * r));
     const int h = c >> 1;
+    const __half2 k1056 = h2_bits(0x64206420u);  // 1024 + 32
 #pragma unroll
     for (int qq = 0; qq < 4; qq++) {
         const int q = 4 * hf + qq;
         const int p = 2 * (c & 1) + (q >> 2), t = q & 3;
-        const int sc = sbyte_of(blk[48 + c], q >> 1);
-        const float ds = __fmul_rn(d, (float)sc);
-        float v[8];
+        const int sc = sbyte_of(blk[48 + c], q >> 1);  // int8
+        const __half ds = __hmul(d, __hsub(half_of_small_uint((uint32_t)(sc + 128)),
+                                           __ushort_as_half((unsigned short)0x5800u)));  // sc exactly (128 = 0x5800)
+        const __half2 ds2 = __halves2half2(ds, ds);
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const int x = e >> 2, e4 = e & 3;
-            const uint32_t qlw = blk[12 * t + 4 * h + 2 * (p & 1) + x];
-            const uint32_t qhw = blk[12 * t + 8 + 2 * h + x];
-            const uint32_t lo = (qlw >> (8 * e4 + 4 * (p >> 1))) & 0xFu;
-            const uint32_t hi2 = (qhw >> (8 * e4 + 2 * p)) & 0x3u;
-            // (q6 - 32) exactly: 2^23 + q6 as float bits minus (2^23 + 32)
-            v[e] = __fmul_rn(ds, __fsub_rn(__uint_as_float(0x4B000000u | lo | (hi2 << 4)), 8388640.f));
+        for (int pr = 0; pr < 4; pr++) {  // weights (2pr, 2pr + 1) of the chunk
+            const int x = pr >> 1;
+            const uint32_t sel = (pr & 1) ? 0x4342u : 0x4140u;
+            const uint32_t lo = (__byte_perm(blk[12 * t + 4 * h + 2 * (p & 1) + x], 0u, sel) >> (4 * (p >> 1))) & 0x000F000Fu;
+            const uint32_t hi = (__byte_perm(blk[12 * t + 8 + 2 * h + x], 0u, sel) >> (2 * p)) & 0x00030003u;
+            const __half2 qc = __hsub2(h2_bits(lo | (hi << 4) | 0x64006400u), k1056);  // q6 - 32, exact
+            w[pr] = bits_h2(__hmul2(ds2, qc));
         }
-        out[qq] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+        out[qq] = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 

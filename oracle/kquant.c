@@ -374,6 +374,40 @@ static void dequant_q6k_block(const or_block_q6k *b, float *y) {
         y[i] = d * (float)b->scales[i >> 4] * (float)q6k_quant(b, i);
 }
 
+/* The factors of each weight's dequantization, w = scale * q - offset, with
+ * scale = d * sc (Q4_K, Q6_K) and offset = dmin * m (Q4_K; 0 for Q6_K): both
+ * products are exact in f32 (an fp16 times a 6- or 8-bit integer), q is the
+ * integer code (0..15, or -32..31 for Q6_K).  Lets a test restate other
+ * rounding orders of the same dequantization exactly. */
+void or_dequant_parts(int dtype, const void *blocks, int64_t n, float *scale, float *offset, int8_t *q) {
+    int64_t nb = n / OR_QK_K;
+    if (dtype == OR_Q4_K) {
+        const or_block_q4k *b = (const or_block_q4k *)blocks;
+        for (int64_t i = 0; i < nb; i++) {
+            float d = or_f16_to_f32(b[i].d), dm = or_f16_to_f32(b[i].dmin);
+            for (int j = 0; j < OR_QK_K; j++) {
+                int g = j / 64, hi = (j % 64) >= 32, l = j % 32, sc, m;
+                q4k_scale_min(2 * g + hi, b[i].scales, &sc, &m);
+                int64_t o = i * OR_QK_K + j;
+                scale[o] = d * (float)sc;
+                offset[o] = dm * (float)m;
+                q[o] = (int8_t)(hi ? (b[i].qs[32 * g + l] >> 4) : (b[i].qs[32 * g + l] & 0xF));
+            }
+        }
+    } else if (dtype == OR_Q6_K) {
+        const or_block_q6k *b = (const or_block_q6k *)blocks;
+        for (int64_t i = 0; i < nb; i++) {
+            float d = or_f16_to_f32(b[i].d);
+            for (int j = 0; j < OR_QK_K; j++) {
+                int64_t o = i * OR_QK_K + j;
+                scale[o] = d * (float)b[i].scales[j >> 4];
+                offset[o] = 0.0f;
+                q[o] = (int8_t)q6k_quant(b + i, j);
+            }
+        }
+    }
+}
+
 void or_dequantize(int dtype, const void *blocks, int64_t n, float *y) {
     int64_t nb = n / OR_QK_K;
     if (dtype == OR_Q4_K) {

@@ -113,6 +113,8 @@ float or_silu(float x);
  * device path evaluates the same operations, so both sides agree bit for
  * bit. */
 double or_exp64(double x);
+/* per-weight dequantization factors (w = scale * q - offset, exact f32 products) */
+void or_dequant_parts(int dtype, const void *blocks, int64_t n, float *scale, float *offset, int8_t *q);
 /* attention score dot in f32: 8 slices of hd/8 dims (fmaf chains), summed in order */
 float or_attn_dot(const float *q, const float *k, int hd);
 

@@ -61,6 +61,7 @@ def _declare(L):
     L.or_quantize_q6k.argtypes = [vp, i64, vp]
     L.or_quantize_q8k.argtypes = [vp, i64, vp, C.c_int]
     L.or_dequantize.argtypes = [C.c_int, vp, i64, vp]
+    L.or_dequant_parts.argtypes = [C.c_int, vp, i64, vp, vp, vp]
     L.or_vec_dot.argtypes = [C.c_int, i64, vp, vp]
     L.or_vec_dot.restype = f32
     L.or_block_dots.argtypes = [C.c_int, i64, i64, vp, vp, vp, vp]
@@ -137,6 +138,16 @@ def dequantize(dtype: int, blocks: np.ndarray, n: int) -> np.ndarray:
     y = np.zeros(n, dtype=np.float32)
     lib().or_dequantize(dtype, _p(blocks), n, _p(y))
     return y
+
+
+def dequant_parts(dtype: int, blocks: np.ndarray, n: int):
+    """Per-weight (scale, offset, integer code) with w = scale * q - offset."""
+    blocks = np.ascontiguousarray(blocks)
+    sc = np.zeros(n, dtype=np.float32)
+    off = np.zeros(n, dtype=np.float32)
+    q = np.zeros(n, dtype=np.int8)
+    lib().or_dequant_parts(dtype, _p(blocks), n, _p(sc), _p(off), _p(q))
+    return sc, off, q
 
 
 def vec_dot(dtype: int, k: int, w_row: np.ndarray, a_q8k: np.ndarray) -> float:

@@ -1,13 +1,14 @@
 """Prefill QMatMul (m > 16 rows) on the tensor cores.
 
 Two checks per case, on identical seeded inputs:
-* kernel arithmetic: against an f64 emulation of the kernel's operands
-  (W dequantized exactly by the oracle and rounded to fp16; X scaled by the
-  kernel's power-of-two row scale and rounded to fp16) -- only the f32
-  accumulation order differs, so the bound is tight;
+* kernel arithmetic: against an exact f64 restatement of the kernel's
+  operands -- weights w = fp16(fp16(d*sc) * q - fp16(dmin*m)) (Q4_K) or
+  fp16(fp16(d*sc) * (q - 32)) (Q6_K) from the oracle's exact per-weight
+  factors, X scaled by the kernel's power-of-two row scale and rounded to
+  fp16 -- only the f32 accumulation order differs, so the bound is tight;
 * parity with the oracle's float QMatMul (f32 dequantized W times f32 X,
-  binary64 accumulation): the fp16 rounding of the operands is the only
-  difference; tolerance 1e-3 relative / 1e-2 absolute per element.
+  binary64 accumulation): the fp16 operands are the only difference;
+  tolerance 1e-3 relative / 1e-2 absolute per element.
 """
 import numpy as np
 import pytest
@@ -29,8 +30,15 @@ def run(fbctx, torch, dtype, n, k, w, x):
     return y.cpu().numpy()
 
 
+def fp16_weights(dtype, w, n, k):
+    sc, off, q = O.dequant_parts(dtype, w, n * k)
+    s16 = sc.astype(np.float16).astype(np.float64)
+    o16 = off.astype(np.float16).astype(np.float64)
+    return (s16 * q.astype(np.float64) - o16).astype(np.float16).reshape(n, k)
+
+
 def emulate(dtype, w, n, k, x):
-    wf = O.dequantize(dtype, w, n * k).reshape(n, k).astype(np.float16).astype(np.float64)
+    wf = fp16_weights(dtype, w, n, k).astype(np.float64)
     amax = np.abs(x).max(axis=1)
     e = np.zeros(x.shape[0], dtype=np.int64)
     while True:  # smallest e >= 0 with amax / 2^e <= 32768
