@@ -181,6 +181,70 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_SHAPES = {  # (class, dtype name, n = output rows, k) per layer
+    "qwen3-8b": [("qkv", "Q4_K", 6144, 4096), ("o", "Q4_K", 4096, 4096), ("gate_up", "Q4_K", 24576, 4096),
+                 ("down", "Q6_K", 4096, 12288)],
+    "llama3-70b": [("qkv", "Q4_K", 10240, 8192), ("o", "Q4_K", 8192, 8192), ("gate_up", "Q4_K", 57344, 8192),
+                   ("down", "Q6_K", 8192, 28672)],
+}
+
+
+def run_prefill_gemm(args):
+    """Prefill QMatMul (tcgen05 dequant-GEMM) on one layer's projections at
+    T = args.prefill_gemm activation rows; TFLOP/s per class against the
+    measured bf16 tensor peak.  Inputs: f32 activations T x k (re-used; the
+    weights of one class are 13-130 MB, the outputs T x n f32 up to 200 MB)."""
+    import torch
+
+    import ferrite_b200 as fb
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    ctx = fb.Context(0, stream.cuda_stream)
+    T = args.prefill_gemm
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peak, kind = float(pk["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    res, tot_fl, tot_ms = {}, 0.0, 0.0
+    with ClockSampler(0) as clk:
+        for name, dts, n, k in PREFILL_SHAPES[args.model]:
+            w = fb.QTensor.synth(ctx, getattr(fb, dts), n, k, seed=n + k)
+            x = torch.randn(T, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(k))
+            y = torch.empty(T, n, device="cuda")
+            mm = fb.QMatMul(w)
+            for _ in range(args.warmup):
+                mm.forward(x.data_ptr(), y.data_ptr(), T)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                mm.forward(x.data_ptr(), y.data_ptr(), T)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            fl = 2.0 * T * n * k
+            res[name] = {"n": n, "k": k, "dtype": dts, "ms": ms, "tflops": fl / ms / 1e9}
+            tot_fl, tot_ms = tot_fl + fl, tot_ms + ms
+            del w, x, y, mm
+            torch.cuda.empty_cache()
+    achieved = tot_fl / tot_ms / 1e9
+    line = {"metric": "prefill QMatMul TFLOP/s (Q4_K/Q6_K dequant-GEMM, fp16 tcgen05, f32 accumulate)",
+            "value": achieved, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 x fp16 -> f32", "data": "synthetic (seeded weights and activations)",
+            "config": {"workload": f"{args.model}-arch one layer's projections at {T} prefill rows", "rows": T},
+            "per_class": res, "error_word": ctx.error_word(),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": kind}}
+    clocks = clk.summary()
+    if clocks:
+        line["clocks"] = clocks
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args) -> dict:
     return {"workload": f"{args.model}-arch Q4_K_M random-init decode, batch {args.batch}, fp16 KV ctx {args.ctx}",
             "model_arch": args.model, "batch": args.batch, "kv_ctx": args.ctx, "weights": "Q4_K (+Q6_K ffn_down, output)",
@@ -202,6 +266,8 @@ def main():
     ap.add_argument("--profile-run", type=int, default=0,
                     help="build the workload, run N untimed decode steps and exit (driver for ncu captures)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
+    ap.add_argument("--prefill-gemm", type=int, default=0, metavar="T",
+                    help="instead of decode: time one layer's prefill QMatMuls at T rows (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = dict(MODELS[args.model])
@@ -209,6 +275,8 @@ def main():
         cfg["n_layers"] = args.layers
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.prefill_gemm:
+        return run_prefill_gemm(args)
 
     import numpy as np
     import torch

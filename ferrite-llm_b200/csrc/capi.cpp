@@ -204,6 +204,28 @@ int fb_qtensor_synth(fb_ctx *ctx, int dtype, int64_t n, int64_t k, uint64_t seed
     });
 }
 
+int fb_qtensor_upload_slice(fb_ctx *ctx, int dtype, int64_t n, int64_t k, const void *src_blocks, int src_on_device,
+                            int64_t row0, int64_t rows, int64_t col0, int64_t cols, fb_qtensor **out) {
+    return guarded([&] {
+        FB_REQUIRE(ctx && src_blocks && out, "null argument");
+        *out = nullptr;
+        check_shape(dtype, n, k);
+        FB_REQUIRE(dtype != FB_F32, "slice: use a k-quant dtype");
+        FB_REQUIRE(row0 >= 0 && rows > 0 && row0 + rows <= n, "slice: rows out of range");
+        FB_REQUIRE(col0 >= 0 && cols > 0 && col0 + cols <= k && col0 % 256 == 0 && cols % 256 == 0,
+                   "slice: columns must be whole 256-value super-blocks inside the tensor");
+        const size_t bb = dtype == FB_Q4_K ? 144 : 210;
+        const size_t pitch = (size_t)(k / 256) * bb, width = (size_t)(cols / 256) * bb;
+        const uint8_t *src = static_cast<const uint8_t *>(src_blocks) + (size_t)row0 * pitch + (size_t)(col0 / 256) * bb;
+        DevBuf staging;
+        staging.alloc(width * (size_t)rows);
+        FB_CUDA(cudaMemcpy2DAsync(staging.ptr, width, src, pitch, width, (size_t)rows,
+                                  src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
+        *out = new_qtensor(ctx, dtype, rows, cols, staging.ptr, cudaMemcpyDeviceToDevice);
+        FB_CUDA(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
 int fb_qtensor_concat_rows(fb_ctx *ctx, const fb_qtensor *const *parts, int nparts, fb_qtensor **out) {
     return guarded([&] {
         FB_REQUIRE(ctx && parts && out && nparts > 0, "null argument");

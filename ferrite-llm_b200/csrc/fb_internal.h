@@ -51,6 +51,7 @@ enum : uint32_t {
     ERRBIT_BAD_TOKEN = 1u << 1,     // token id outside [0, vocab)
     ERRBIT_BAD_POS = 1u << 2,       // position outside the KV capacity
     ERRBIT_BAD_PAGE = 1u << 3,      // block-table entry outside the pool
+    ERRBIT_PEER_TIMEOUT = 1u << 4,  // a tensor-parallel peer did not arrive in time
 };
 
 // A device buffer owned by the library.
@@ -167,8 +168,10 @@ void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act
 // ws: argmax_ws_bytes(rows) bytes, zeroed once before first use.
 size_t argmax_ws_bytes(int rows);
 void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out, void *ws);
+// kv_head0: global index of the pool's first kv head (tensor-parallel shards)
 void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
-                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale);
+                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale,
+                     int kv_head0 = 0);
 
 // Paged flash-decode attention (attention.cu).
 constexpr int ATT_SPLITS = 16;  // attention splits (cluster CTAs) per (kv head, sequence)
@@ -200,6 +203,72 @@ struct AttnArgs {
 void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
                         const Q8Act *aq, int *counters, bool pdl, bool want_cluster);
 bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch);
+
+// ---- tensor parallelism (tp.cu) ----
+// Exchange region of one rank (cudaMalloc, mapped by every rank via IPC):
+//   flags    [FB_TP_MAX] u32      flags[src] = sequence number of the last
+//                                 row-parallel exchange src has pushed here
+//   am_flags [FB_TP_MAX][B] u32   argmax exchange: step epoch per (src, row)
+//   inbox_o / inbox_d [W][B][H] f64  partial sums of attn_output / ffn_down
+//   am_inbox [W][B] u64           (f32 bits of the max << 32) | global index
+struct CommLayout {
+    size_t flags, am_flags, inbox_o, inbox_d, am_inbox, total;
+};
+CommLayout comm_layout(int world, int max_batch, int hidden);
+
+// Row-parallel GEMV output: the binary64 row sums (not rounded) are stored
+// to dst[p][col * ld + row] for every rank p < world.
+struct PeerOut {
+    double *dst[FB_TP_MAX];
+    int64_t ld;
+    int world;
+};
+// Residual + RMSNorm after a row-parallel projection (one exchange point).
+struct TpNorm {
+    const double *inbox;             // this rank's inbox [W][B][H]
+    const uint32_t *my_flags;        // this rank's flags [W]
+    uint32_t *peer_flag[FB_TP_MAX];  // &flags[rank] in rank p's region
+    const uint32_t *epoch;           // device step counter (>= 1 inside a step)
+    double *ss_part;                 // [B][H/256] per-block sums of squares
+    uint32_t *ss_tag;                // [B][H/256] exchange sequence of ss_part
+    uint64_t limit_ns;               // bound of every wait
+    int world, batch_cap, nx;        // nx = exchange points per step
+};
+struct TpArgmax {
+    uint64_t *peer_slot[FB_TP_MAX];  // &am_inbox[rank][0] in rank p's region
+    uint32_t *peer_flag[FB_TP_MAX];  // &am_flags[rank][0] in rank p's region
+    const uint64_t *my_inbox;        // [W][B]
+    const uint32_t *my_flags;        // [FB_TP_MAX][B]
+    const uint32_t *epoch;
+    uint64_t limit_ns;
+    int world, batch_cap, vocab_off;
+};
+void launch_tp_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, float *x_out, const float *g, int rows, int dim,
+                                    float eps, const Q8Act &a, const TpNorm &t, int xi);
+// y[m, n] from pre-quantized activations, with the row sums pushed to peers.
+void launch_gemv_peer(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, const PeerOut &po);
+void launch_argmax_tp(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out, void *ws,
+                      const TpArgmax &t);
+// First kernel of a step: embedding + RMSNorm, bumping the step counter.
+void launch_embed_rmsnorm_q8k(fb_ctx *ctx, float *x_out, const float *g, int rows, int dim, float eps,
+                              const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab,
+                              uint32_t *epoch_inc);
+
+}  // namespace fb
+
+struct fb_comm {
+    fb_ctx *ctx = nullptr;
+    int rank = 0, world = 1, max_batch = 0, hidden = 0;
+    fb::CommLayout L{};
+    fb::DevBuf region;                       // this rank's exchange region
+    uint8_t *peer[FB_TP_MAX] = {nullptr};    // every rank's region in this process
+    uint64_t timeout_ns = 10ull * 1000 * 1000 * 1000;  // bound of the device waits on peers
+    bool opened = false;
+    ~fb_comm();
+    template <class T> T *at(int p, size_t off) const { return reinterpret_cast<T *>(peer[p] + off); }
+};
+
+namespace fb {
 
 // RoPE tables [max_pos][hd/2] computed on the host exactly as the oracle does
 // (candle precompute_freqs_cis: angle = pos * theta^(-2i/hd) in f32).

@@ -405,7 +405,7 @@ template <int DT, int NT, bool DOTS, int KS>
 __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W, int64_t n, int nb, int n_tiles,
                                                   Q8Act a, int m, float *__restrict__ y, int64_t ldy,
                                                   int32_t *__restrict__ dots_sc, int32_t *__restrict__ dots_min,
-                                                  uint32_t *err, int depth) {
+                                                  uint32_t *err, int depth, PeerOut po) {
     constexpr int REC = QRec<DT>::bytes;
     const int DEPTH = depth;
     constexpr bool DP4A = NT < 0;
@@ -530,7 +530,13 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
 #pragma unroll
                 for (int w = 0; w < KS; w++) sum = __dadd_rn(sum, red[(w * 16 + r) * (C + 1) + col]);
                 const int64_t row = row0 + r;
-                if (row < n && col < m) y[(int64_t)col * ldy + row] = __double2float_rn(sum);
+                if (row < n && col < m) {
+                    if (po.world) {  // row-parallel shard: binary64 partials to every rank's inbox
+                        for (int p = 0; p < po.world; p++) po.dst[p][(int64_t)col * po.ld + row] = sum;
+                    } else {
+                        y[(int64_t)col * ldy + row] = __double2float_rn(sum);
+                    }
+                }
             }
         }
         __syncthreads();
@@ -540,12 +546,13 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         // let the copies still in flight land before shared memory is released
         for (int k = c; k < issued; k++) mbar_wait_bounded(&wbar[k % DEPTH], (uint32_t)(k / DEPTH) & 1u);
     }
+    if (po.world) __threadfence_system();  // peer stores performed before the grid completes
     pdl_launch();
 }
 
 template <int DT, int NT, bool DOTS, int KS>
 static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
-                          int32_t *dsc, int32_t *dmn) {
+                          int32_t *dsc, int32_t *dmn, const PeerOut &po) {
     constexpr int REC = QRec<DT>::bytes;
     constexpr int M = NT < 0 ? -NT : 0;
     const size_t act = M ? (act_smem_bytes(M, w->k) + 127) & ~(size_t)127 : 0;
@@ -573,46 +580,57 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     FB_CUDA(cudaLaunchKernelEx(&cfg, kernel, w->main(), w->n, (int)w->nb(), n_tiles, a, m, y, ldy, dsc, dmn,
-                               ctx->err_word, depth));
+                               ctx->err_word, depth, po));
 }
 
 // Few tiles (fewer than two per SM): 8-warp CTAs so each SM still runs
 // enough warps; otherwise 4-warp CTAs.
 template <int DT, int NT, bool DOTS>
 static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
-                          int32_t *dsc, int32_t *dmn) {
+                          int32_t *dsc, int32_t *dmn, const PeerOut &po) {
     if (w->n_tiles() < 2 * ctx->num_sms && w->nb() >= 16)
-        launch_gemv_k<DT, NT, DOTS, 8>(ctx, w, a, m, y, ldy, dsc, dmn);
+        launch_gemv_k<DT, NT, DOTS, 8>(ctx, w, a, m, y, ldy, dsc, dmn, po);
     else
-        launch_gemv_k<DT, NT, DOTS, 4>(ctx, w, a, m, y, ldy, dsc, dmn);
+        launch_gemv_k<DT, NT, DOTS, 4>(ctx, w, a, m, y, ldy, dsc, dmn, po);
 }
 
 template <int DT>
-static void launch_gemv_dt(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy) {
+static void launch_gemv_dt(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
+                           const PeerOut &po) {
     switch (m) {
-    case 1: launch_gemv_t<DT, -1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
-    case 2: launch_gemv_t<DT, -2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
-    case 3: launch_gemv_t<DT, -3, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
-    case 4: launch_gemv_t<DT, -4, false>(ctx, w, a, m, y, ldy, nullptr, nullptr); break;
+    case 1: launch_gemv_t<DT, -1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po); break;
+    case 2: launch_gemv_t<DT, -2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po); break;
+    case 3: launch_gemv_t<DT, -3, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po); break;
+    case 4: launch_gemv_t<DT, -4, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po); break;
     default:
-        if (m <= 8) launch_gemv_t<DT, 1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr);
-        else launch_gemv_t<DT, 2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr);
+        if (m <= 8) launch_gemv_t<DT, 1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
+        else launch_gemv_t<DT, 2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
     }
 }
 
-void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy) {
+static void gemv_any(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
+                     const PeerOut &po) {
     FB_REQUIRE(m >= 1 && m <= 16, "gemv: m must be in 1..16");
-    if (w->dtype == FB_Q4_K) launch_gemv_dt<4>(ctx, w, a, m, y, ldy);
-    else if (w->dtype == FB_Q6_K) launch_gemv_dt<6>(ctx, w, a, m, y, ldy);
+    if (w->dtype == FB_Q4_K) launch_gemv_dt<4>(ctx, w, a, m, y, ldy, po);
+    else if (w->dtype == FB_Q6_K) launch_gemv_dt<6>(ctx, w, a, m, y, ldy, po);
     else fail(FB_ERR_INVALID, "gemv: weight dtype must be Q4_K or Q6_K");
+}
+
+void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy) {
+    gemv_any(ctx, w, a, m, y, ldy, PeerOut{});
+}
+
+void launch_gemv_peer(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, const PeerOut &po) {
+    FB_REQUIRE(po.world >= 1 && po.world <= FB_TP_MAX, "gemv: bad peer count");
+    gemv_any(ctx, w, a, m, nullptr, 0, po);
 }
 
 void launch_block_dots(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int32_t *out_sc, int32_t *out_min) {
     if (w->dtype == FB_Q4_K) {
-        launch_gemv_t<4, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, out_min);
+        launch_gemv_t<4, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, out_min, PeerOut{});
     } else if (w->dtype == FB_Q6_K) {
         FB_CUDA(cudaMemsetAsync(out_min, 0, (size_t)(w->n * w->nb()) * 4, ctx->stream));
-        launch_gemv_t<6, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, nullptr);
+        launch_gemv_t<6, -1, true>(ctx, w, a, 1, nullptr, 0, out_sc, nullptr, PeerOut{});
     } else {
         fail(FB_ERR_INVALID, "block_dots: weight dtype must be Q4_K or Q6_K");
     }

@@ -91,6 +91,45 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
+// System-scope flag handoff between GPUs (tensor-parallel exchanges): the
+// writer's release store orders everything that happened before it (the
+// producer grid's peer stores included); the reader's acquire load orders
+// its later reads after it.
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits until the sequence number at p reaches seq (wrap-safe compare);
+// gives up after limit_ns and returns false.
+template <bool SYS>
+__device__ __forceinline__ bool wait_seq(const uint32_t *p, uint32_t seq, uint64_t limit_ns) {
+    auto ld = [&] { return SYS ? ld_acquire_sys(p) : ld_acquire_gpu(p); };
+    if ((int32_t)(ld() - seq) >= 0) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld() - seq) < 0) {
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+        __nanosleep(100);
+    }
+    return true;
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // subsequent async-proxy (TMA) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -14,6 +14,12 @@
 // launched with programmatic dependent launch and captured once per batch
 // size into a CUDA graph.  All buffers are allocated up front; the step reads
 // token ids and positions from device buffers, so replays need no host work.
+//
+// Tensor parallel (fb_model_create_tp): the rank keeps its shard of the
+// heads, the FFN and the vocab; attn_output and ffn_down push binary64
+// partial sums to every rank's inbox and the residual + RMSNorm kernel that
+// follows adds them (one exchange per row-parallel projection, no separate
+// collective launch); the greedy argmax merges the ranks' (max, index).
 #include <cuda_fp16.h>
 #include <math.h>
 #include <string.h>
@@ -75,7 +81,11 @@ uint64_t tensor_seed(uint64_t seed, int layer, int kind) {
 
 struct fb_model {
     fb_ctx *ctx = nullptr;
-    fb_model_config c{};
+    fb_model_config c{};   // full model
+    fb_model_config lc{};  // this rank's shard: n_heads, n_kv_heads, ffn, vocab divided by the world size
+    fb_comm *comm = nullptr;  // tensor parallel when set
+    int W = 1, rank = 0, v_off = 0;
+    DevBuf epoch, ss_part, ss_tag;  // tensor-parallel step counter and norm exchange slots
     std::vector<std::unique_ptr<Layer>> layers;
     QT tok_embd, output;
     DevBuf out_norm;
@@ -96,7 +106,7 @@ struct fb_model {
     int len0 = 0;  // tokens held by sequence slot 0 (forward / prefill API)
     int launches_per_step = 0;
 
-    size_t kv_half_layer() const { return (size_t)num_pages * c.n_kv_heads * kPage * c.head_dim; }
+    size_t kv_half_layer() const { return (size_t)num_pages * lc.n_kv_heads * kPage * c.head_dim; }
     __half *kpool(int l) const { return kv.as<__half>() + (size_t)l * 2 * kv_half_layer(); }
     __half *vpool(int l) const { return kpool(l) + kv_half_layer(); }
 
@@ -151,6 +161,49 @@ struct StepProbe {
     }
 };
 
+// Tensor-parallel exchange arguments (comm regions of all ranks as mapped in
+// this process).
+static PeerOut peer_out(const fb_model *m, size_t inbox_off) {
+    const fb_comm *cm = m->comm;
+    PeerOut po{};
+    for (int p = 0; p < cm->world; p++)
+        po.dst[p] = cm->at<double>(p, inbox_off) + (size_t)cm->rank * cm->max_batch * cm->hidden;
+    po.ld = cm->hidden;
+    po.world = cm->world;
+    return po;
+}
+static TpNorm tp_norm(const fb_model *m, size_t inbox_off) {
+    const fb_comm *cm = m->comm;
+    TpNorm t{};
+    t.inbox = cm->at<double>(cm->rank, inbox_off);
+    t.my_flags = cm->at<uint32_t>(cm->rank, cm->L.flags);
+    for (int p = 0; p < cm->world; p++) t.peer_flag[p] = cm->at<uint32_t>(p, cm->L.flags) + cm->rank;
+    t.epoch = m->epoch.as<uint32_t>();
+    t.ss_part = m->ss_part.as<double>();
+    t.ss_tag = m->ss_tag.as<uint32_t>();
+    t.limit_ns = cm->timeout_ns;
+    t.world = cm->world;
+    t.batch_cap = cm->max_batch;
+    t.nx = 2 * m->c.n_layers;
+    return t;
+}
+static TpArgmax tp_argmax(const fb_model *m) {
+    const fb_comm *cm = m->comm;
+    TpArgmax t{};
+    for (int p = 0; p < cm->world; p++) {
+        t.peer_slot[p] = cm->at<uint64_t>(p, cm->L.am_inbox) + (size_t)cm->rank * cm->max_batch;
+        t.peer_flag[p] = cm->at<uint32_t>(p, cm->L.am_flags) + (size_t)cm->rank * cm->max_batch;
+    }
+    t.my_inbox = cm->at<uint64_t>(cm->rank, cm->L.am_inbox);
+    t.my_flags = cm->at<uint32_t>(cm->rank, cm->L.am_flags);
+    t.epoch = m->epoch.as<uint32_t>();
+    t.limit_ns = cm->timeout_ns;
+    t.world = cm->world;
+    t.batch_cap = cm->max_batch;
+    t.vocab_off = m->v_off;
+    return t;
+}
+
 static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     fb_ctx *ctx = m->ctx;
     int nl = 0;
@@ -159,16 +212,31 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         if (probe) probe->mark(kind, n);
     };
     if (probe) probe->start();
-    const fb_model_config &c = m->c;
-    const int H = c.hidden, qd = c.n_heads * c.head_dim, F = c.ffn;
+    const fb_model_config &c = m->c, &lc = m->lc;
+    const int H = c.hidden, qd = lc.n_heads * c.head_dim, F = lc.ffn;
+    const bool tp = m->comm != nullptr;
+    PeerOut po_o{}, po_d{};
+    TpNorm tn_o{}, tn_d{};
+    TpArgmax tam{};
+    if (tp) {
+        po_o = peer_out(m, m->comm->L.inbox_o);
+        po_d = peer_out(m, m->comm->L.inbox_d);
+        tn_o = tp_norm(m, m->comm->L.inbox_o);
+        tn_d = tp_norm(m, m->comm->L.inbox_d);
+        tam = tp_argmax(m);
+    }
     const Q8Act ah = q8act_view(m->act_h.ptr, b, H);
     const Q8Act aa = q8act_view(m->act_a.ptr, b, qd);
     const Q8Act af = q8act_view(m->act_f.ptr, b, F);
     // residual stream ping-pongs between two buffers (the norm kernels read
     // one row while writing the updated row)
     float *xa = m->x.as<float>(), *xb = m->x2.as<float>();
-    launch_residual_rmsnorm_q8k(ctx, nullptr, nullptr, xa, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
-                                m->tok_embd.t, m->tok.as<int32_t>(), c.vocab);
+    if (tp)
+        launch_embed_rmsnorm_q8k(ctx, xa, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah, m->tok_embd.t,
+                                 m->tok.as<int32_t>(), c.vocab, m->epoch.as<uint32_t>());
+    else
+        launch_residual_rmsnorm_q8k(ctx, nullptr, nullptr, xa, m->layers[0]->attn_norm.as<float>(), b, H, c.eps, ah,
+                                    m->tok_embd.t, m->tok.as<int32_t>(), c.vocab);
     mark(FB_PROF_EMBED_NORM, 1);
     AttnArgs A{};
     A.q = m->q.as<float>();
@@ -177,8 +245,8 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     A.pos = m->pos.as<int32_t>();
     A.part_o = m->part_o.as<double>();
     A.part_ml = m->part_ml.as<double>();
-    A.n_heads = c.n_heads;
-    A.n_kv = c.n_kv_heads;
+    A.n_heads = lc.n_heads;
+    A.n_kv = lc.n_kv_heads;
     A.page_size = kPage;
     A.max_pages = m->pages_per_seq;
     A.num_pages = m->num_pages;
@@ -187,7 +255,7 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
     A.err = ctx->err_word;
     // QK-norm, RoPE and the KV-cache write run in the attention prologue
     A.qkv = m->y_qkv.as<float>();
-    A.qkv_ld = (int64_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    A.qkv_ld = (int64_t)(lc.n_heads + 2 * lc.n_kv_heads) * c.head_dim;
     A.eps = c.eps;
     A.rope_cos = m->rope_cos.as<float>();
     A.rope_sin = m->rope_sin.as<float>();
@@ -202,34 +270,44 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
         A.vpool = m->vpool(l);
         A.q_norm = c.qk_norm ? L.q_norm.as<float>() : nullptr;
         A.k_norm = c.qk_norm ? L.k_norm.as<float>() : nullptr;
-        const bool q8_fused = (c.n_heads / c.n_kv_heads) % 2 == 0;
+        const bool q8_fused = (lc.n_heads / lc.n_kv_heads) % 2 == 0;
         // cluster-free merge: inside the step the 16-CTA clusters would be
         // packed two per SM next to the still-running projection
         launch_attn_decode(ctx, A, b, c.max_ctx, m->attn.as<float>(), q8_fused ? &aa : nullptr,
                            m->att_cnt.as<int>(), true, false);
         if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
         mark(FB_PROF_ATTN, q8_fused ? 1 : 2);
-        launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
+        if (tp) launch_gemv_peer(ctx, L.wo.t, aa, b, po_o);
+        else launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         mark(FB_PROF_O, 1);
-        launch_residual_rmsnorm_q8k(ctx, xa, m->y_o.as<float>(), xb, L.ffn_norm.as<float>(), b, H, c.eps, ah, nullptr,
-                                    nullptr, c.vocab);
+        if (tp)
+            launch_tp_residual_rmsnorm_q8k(ctx, xa, xb, L.ffn_norm.as<float>(), b, H, c.eps, ah, tn_o, 2 * l);
+        else
+            launch_residual_rmsnorm_q8k(ctx, xa, m->y_o.as<float>(), xb, L.ffn_norm.as<float>(), b, H, c.eps, ah,
+                                        nullptr, nullptr, c.vocab);
         std::swap(xa, xb);
         mark(FB_PROF_NORM, 1);
         launch_gemv(ctx, L.wgu.t, ah, b, m->y_gu.as<float>(), 2 * F);
         mark(FB_PROF_GATE_UP, 1);
         launch_swiglu_q8k(ctx, m->y_gu.as<float>(), F, b, af);
         mark(FB_PROF_SWIGLU, 1);
-        launch_gemv(ctx, L.wdown.t, af, b, m->y_d.as<float>(), H);
+        if (tp) launch_gemv_peer(ctx, L.wdown.t, af, b, po_d);
+        else launch_gemv(ctx, L.wdown.t, af, b, m->y_d.as<float>(), H);
         mark(FB_PROF_DOWN, 1);
         const float *gn = (l + 1 < c.n_layers) ? m->layers[l + 1]->attn_norm.as<float>() : m->out_norm.as<float>();
-        launch_residual_rmsnorm_q8k(ctx, xa, m->y_d.as<float>(), xb, gn, b, H, c.eps, ah, nullptr, nullptr, c.vocab);
+        if (tp)
+            launch_tp_residual_rmsnorm_q8k(ctx, xa, xb, gn, b, H, c.eps, ah, tn_d, 2 * l + 1);
+        else
+            launch_residual_rmsnorm_q8k(ctx, xa, m->y_d.as<float>(), xb, gn, b, H, c.eps, ah, nullptr, nullptr,
+                                        c.vocab);
         std::swap(xa, xb);
         mark(FB_PROF_NORM, 1);
     }
     m->x_last = xa;
-    launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), c.vocab);
+    launch_gemv(ctx, m->output.t, ah, b, m->logits.as<float>(), lc.vocab);
     mark(FB_PROF_LM_HEAD, 1);
-    launch_argmax(ctx, m->logits.as<float>(), b, c.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
+    if (tp) launch_argmax_tp(ctx, m->logits.as<float>(), b, lc.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr, tam);
+    else launch_argmax(ctx, m->logits.as<float>(), b, lc.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
     mark(FB_PROF_ARGMAX, 1);
     m->launches_per_step = nl;
 }
@@ -294,71 +372,159 @@ static void check_no_device_error(fb_model *m) {
     }
 }
 
+// Which part of a full tensor a tensor-parallel rank keeps.
+enum Shard { SH_ALL, SH_ROWS, SH_COLS };
+
+// Shard of `kind` for this rank: (row0, rows, col0, cols) of the [n, k] tensor.
+static void shard_range(const fb_model *m, int kind, int64_t n, int64_t k, int64_t &r0, int64_t &nr, int64_t &c0,
+                        int64_t &nc) {
+    const fb_model_config &c = m->c, &lc = m->lc;
+    const int hd = c.head_dim;
+    r0 = 0, nr = n, c0 = 0, nc = k;
+    if (m->W == 1) return;
+    switch (kind) {
+    case T_ATTN_Q: nr = (int64_t)lc.n_heads * hd; r0 = m->rank * nr; break;
+    case T_ATTN_K:
+    case T_ATTN_V: nr = (int64_t)lc.n_kv_heads * hd; r0 = m->rank * nr; break;
+    case T_FFN_GATE:
+    case T_FFN_UP: nr = lc.ffn; r0 = m->rank * nr; break;
+    case T_OUTPUT: nr = lc.vocab; r0 = m->v_off; break;
+    case T_ATTN_OUTPUT: nc = (int64_t)lc.n_heads * hd; c0 = m->rank * nc; break;
+    case T_FFN_DOWN: nc = lc.ffn; c0 = m->rank * nc; break;
+    default: break;  // token_embd and the norms stay whole
+    }
+}
+
+// Device QTensor of this rank's shard of a full GGUF tensor (host or device).
+static fb_qtensor *make_shard(fb_model *m, int kind, int dtype, int64_t n, int64_t k, const void *src, int on_dev) {
+    int64_t r0, nr, c0, nc;
+    shard_range(m, kind, n, k, r0, nr, c0, nc);
+    fb_qtensor *t = nullptr;
+    int rc;
+    if (r0 == 0 && nr == n && c0 == 0 && nc == k)
+        rc = on_dev ? fb_qtensor_upload_dev(m->ctx, dtype, n, k, src, &t) : fb_qtensor_upload(m->ctx, dtype, n, k, src, &t);
+    else
+        rc = fb_qtensor_upload_slice(m->ctx, dtype, n, k, src, on_dev, r0, nr, c0, nc, &t);
+    if (rc != FB_OK) fail(rc, fb_last_error());
+    return t;
+}
+
+static void create_model(fb_ctx *ctx, const fb_model_config *cfg, fb_comm *comm, fb_model **out) {
+    FB_REQUIRE(ctx && cfg && out, "null argument");
+    *out = nullptr;
+    const fb_model_config &c = *cfg;
+    FB_REQUIRE(c.n_layers > 0 && c.hidden > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.ffn > 0 && c.vocab > 0,
+               "model dims must be positive");
+    FB_REQUIRE(c.head_dim == 128, "head_dim must be 128");
+    FB_REQUIRE(c.hidden % 256 == 0 && c.ffn % 256 == 0 && (c.n_heads * c.head_dim) % 256 == 0,
+               "hidden, ffn and n_heads*head_dim must be multiples of 256");
+    FB_REQUIRE(c.n_heads % c.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
+    const int G = c.n_heads / c.n_kv_heads;
+    FB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "GQA group must be 1, 2, 4 or 8");
+    FB_REQUIRE(c.max_ctx >= 1 && c.max_batch >= 1 && c.max_batch <= 16, "need max_ctx >= 1, 1 <= max_batch <= 16");
+    FB_REQUIRE(c.rope_mode == 0 || c.rope_mode == 1, "rope_mode must be 0 or 1");
+    auto m = std::make_unique<fb_model>();
+    m->ctx = ctx;
+    m->c = c;
+    m->lc = c;
+    if (comm) {
+        const int W = comm->world;
+        FB_REQUIRE(comm->opened, "comm not opened (fb_comm_open)");
+        FB_REQUIRE(comm->ctx->device == ctx->device, "comm belongs to another device");
+        FB_REQUIRE(comm->hidden == c.hidden && c.max_batch <= comm->max_batch,
+                   "comm was created for another hidden size or a smaller batch");
+        FB_REQUIRE(c.n_kv_heads % W == 0, "n_kv_heads must be divisible by the world size");
+        FB_REQUIRE(c.ffn % (256 * W) == 0, "ffn / world must be a multiple of 256");
+        FB_REQUIRE((c.n_heads / W * c.head_dim) % 256 == 0, "n_heads * head_dim / world must be a multiple of 256");
+        FB_REQUIRE(c.vocab % W == 0, "vocab must be divisible by the world size");
+        m->comm = comm;
+        m->W = W;
+        m->rank = comm->rank;
+        m->lc.n_heads = c.n_heads / W;
+        m->lc.n_kv_heads = c.n_kv_heads / W;
+        m->lc.ffn = c.ffn / W;
+        m->lc.vocab = c.vocab / W;
+        m->v_off = comm->rank * m->lc.vocab;
+        m->epoch.alloc(256);
+        FB_CUDA(cudaMemsetAsync(m->epoch.ptr, 0, 256, ctx->stream));
+        // the step counter restarts: clear the sequence numbers peers left in
+        // this rank's flags (ranks create their models before the host barrier
+        // that precedes the first step, so no peer is publishing yet)
+        FB_CUDA(cudaMemsetAsync(comm->region.as<uint8_t>() + comm->L.flags, 0, comm->L.inbox_o - comm->L.flags,
+                                ctx->stream));
+        const size_t nslot = (size_t)comm->max_batch * (c.hidden / 256);
+        m->ss_part.alloc(nslot * 8);
+        m->ss_tag.alloc(nslot * 4);
+        FB_CUDA(cudaMemsetAsync(m->ss_tag.ptr, 0, nslot * 4, ctx->stream));
+    }
+    const fb_model_config &lc = m->lc;
+    for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
+    m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
+    m->num_pages = m->pages_per_seq * c.max_batch;
+    m->nsplit_max = ATT_SPLITS;  // cluster-free attention merge (fallback) scratch
+    m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
+    FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
+    std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);
+    for (size_t i = 0; i < bt.size(); i++) bt[i] = (int32_t)i;  // slot s owns pages [s*pps, (s+1)*pps)
+    m->block_table.alloc(bt.size() * 4);
+    FB_CUDA(cudaMemcpyAsync(m->block_table.ptr, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+    std::vector<float> ct, st;
+    rope_tables(c.max_ctx, c.head_dim, c.rope_theta, ct, st);
+    upload_f32(ctx, m->rope_cos, ct.data(), ct.size());
+    upload_f32(ctx, m->rope_sin, st.data(), st.size());
+    const int B = c.max_batch, H = c.hidden, qd = lc.n_heads * c.head_dim;
+    const int kd = lc.n_kv_heads * c.head_dim;
+    m->x.alloc((size_t)B * H * 4);
+    m->x2.alloc((size_t)B * H * 4);
+    m->y_qkv.alloc((size_t)B * (qd + 2 * kd) * 4);
+    m->q.alloc((size_t)B * qd * 4);
+    m->attn.alloc((size_t)B * qd * 4);
+    m->y_o.alloc((size_t)B * H * 4);
+    m->y_gu.alloc((size_t)B * 2 * lc.ffn * 4);
+    m->y_d.alloc((size_t)B * H * 4);
+    m->logits.alloc((size_t)B * lc.vocab * 4);
+    m->argmax_ws.alloc(argmax_ws_bytes(B));
+    FB_CUDA(cudaMemsetAsync(m->argmax_ws.ptr, 0, m->argmax_ws.bytes, ctx->stream));
+    m->part_o.alloc((size_t)B * lc.n_heads * m->nsplit_max * c.head_dim * 8);
+    m->part_ml.alloc((size_t)B * lc.n_heads * m->nsplit_max * 2 * 8);
+    m->att_cnt.alloc((size_t)B * lc.n_kv_heads * 4);
+    FB_CUDA(cudaMemsetAsync(m->att_cnt.ptr, 0, m->att_cnt.bytes, ctx->stream));
+    m->act_h.alloc(q8act_bytes(B, H));
+    m->act_a.alloc(q8act_bytes(B, qd));
+    m->act_f.alloc(q8act_bytes(B, lc.ffn));
+    m->tok.alloc((size_t)B * 4);
+    m->pos.alloc((size_t)B * 4);
+    m->next.alloc((size_t)B * 4);
+    FB_CUDA(cudaMemsetAsync(m->tok.ptr, 0, (size_t)B * 4, ctx->stream));
+    FB_CUDA(cudaMemsetAsync(m->pos.ptr, 0, (size_t)B * 4, ctx->stream));
+    FB_CUDA(cudaMallocHost(&m->pinned, (size_t)3 * B * 4));
+    FB_CUDA(cudaStreamCreateWithFlags(&m->work, cudaStreamNonBlocking));
+    FB_CUDA(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
+    FB_CUDA(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
+    FB_CUDA(cudaStreamSynchronize(ctx->stream));
+    *out = m.release();
+}
+
 extern "C" {
 
 int fb_model_create(fb_ctx *ctx, const fb_model_config *cfg, fb_model **out) {
+    return guarded([&] { create_model(ctx, cfg, nullptr, out); });
+}
+
+int fb_model_create_tp(fb_ctx *ctx, const fb_model_config *cfg, fb_comm *comm, fb_model **out) {
     return guarded([&] {
-        FB_REQUIRE(ctx && cfg && out, "null argument");
-        *out = nullptr;
-        const fb_model_config &c = *cfg;
-        FB_REQUIRE(c.n_layers > 0 && c.hidden > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.ffn > 0 && c.vocab > 0,
-                   "model dims must be positive");
-        FB_REQUIRE(c.head_dim == 128, "head_dim must be 128");
-        FB_REQUIRE(c.hidden % 256 == 0 && c.ffn % 256 == 0 && (c.n_heads * c.head_dim) % 256 == 0,
-                   "hidden, ffn and n_heads*head_dim must be multiples of 256");
-        FB_REQUIRE(c.n_heads % c.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
-        const int G = c.n_heads / c.n_kv_heads;
-        FB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "GQA group must be 1, 2, 4 or 8");
-        FB_REQUIRE(c.max_ctx >= 1 && c.max_batch >= 1 && c.max_batch <= 16, "need max_ctx >= 1, 1 <= max_batch <= 16");
-        FB_REQUIRE(c.rope_mode == 0 || c.rope_mode == 1, "rope_mode must be 0 or 1");
-        auto m = std::make_unique<fb_model>();
-        m->ctx = ctx;
-        m->c = c;
-        for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
-        m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
-        m->num_pages = m->pages_per_seq * c.max_batch;
-        m->nsplit_max = ATT_SPLITS;  // cluster-free attention merge (fallback) scratch
-        m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
-        FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
-        std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);
-        for (size_t i = 0; i < bt.size(); i++) bt[i] = (int32_t)i;  // slot s owns pages [s*pps, (s+1)*pps)
-        m->block_table.alloc(bt.size() * 4);
-        FB_CUDA(cudaMemcpyAsync(m->block_table.ptr, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
-        std::vector<float> ct, st;
-        rope_tables(c.max_ctx, c.head_dim, c.rope_theta, ct, st);
-        upload_f32(ctx, m->rope_cos, ct.data(), ct.size());
-        upload_f32(ctx, m->rope_sin, st.data(), st.size());
-        const int B = c.max_batch, H = c.hidden, qd = c.n_heads * c.head_dim;
-        const int kd = c.n_kv_heads * c.head_dim;
-        m->x.alloc((size_t)B * H * 4);
-        m->x2.alloc((size_t)B * H * 4);
-        m->y_qkv.alloc((size_t)B * (qd + 2 * kd) * 4);
-        m->q.alloc((size_t)B * qd * 4);
-        m->attn.alloc((size_t)B * qd * 4);
-        m->y_o.alloc((size_t)B * H * 4);
-        m->y_gu.alloc((size_t)B * 2 * c.ffn * 4);
-        m->y_d.alloc((size_t)B * H * 4);
-        m->logits.alloc((size_t)B * c.vocab * 4);
-        m->argmax_ws.alloc(argmax_ws_bytes(B));
-        FB_CUDA(cudaMemsetAsync(m->argmax_ws.ptr, 0, m->argmax_ws.bytes, ctx->stream));
-        m->part_o.alloc((size_t)B * c.n_heads * m->nsplit_max * c.head_dim * 8);
-        m->part_ml.alloc((size_t)B * c.n_heads * m->nsplit_max * 2 * 8);
-        m->att_cnt.alloc((size_t)B * c.n_kv_heads * 4);
-        FB_CUDA(cudaMemsetAsync(m->att_cnt.ptr, 0, m->att_cnt.bytes, ctx->stream));
-        m->act_h.alloc(q8act_bytes(B, H));
-        m->act_a.alloc(q8act_bytes(B, qd));
-        m->act_f.alloc(q8act_bytes(B, c.ffn));
-        m->tok.alloc((size_t)B * 4);
-        m->pos.alloc((size_t)B * 4);
-        m->next.alloc((size_t)B * 4);
-        FB_CUDA(cudaMemsetAsync(m->tok.ptr, 0, (size_t)B * 4, ctx->stream));
-        FB_CUDA(cudaMemsetAsync(m->pos.ptr, 0, (size_t)B * 4, ctx->stream));
-        FB_CUDA(cudaMallocHost(&m->pinned, (size_t)3 * B * 4));
-        FB_CUDA(cudaStreamCreateWithFlags(&m->work, cudaStreamNonBlocking));
-        FB_CUDA(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
-        FB_CUDA(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
-        FB_CUDA(cudaStreamSynchronize(ctx->stream));
-        *out = m.release();
+        FB_REQUIRE(comm, "null comm");
+        create_model(ctx, cfg, comm, out);
+    });
+}
+
+int fb_model_tp_info(const fb_model *m, int *rank, int *world, int *vocab_offset, int *vocab_count) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        if (rank) *rank = m->rank;
+        if (world) *world = m->W;
+        if (vocab_offset) *vocab_offset = m->v_off;
+        if (vocab_count) *vocab_count = m->lc.vocab;
     });
 }
 
@@ -390,10 +556,7 @@ int fb_model_set_tensor(fb_model *m, const char *name, int layer, int dtype, int
             FB_REQUIRE(rows == r && cols == k, std::string(name) + ": shape mismatch");
             FB_REQUIRE((dtype == FB_Q6_K && allow_q6) || (dtype == FB_Q4_K && allow_q4),
                        std::string(name) + ": unsupported dtype");
-            fb_qtensor *t = nullptr;
-            const int rc = fb_qtensor_upload(m->ctx, dtype, r, k, data_host, &t);
-            if (rc != FB_OK) fail(rc, fb_last_error());
-            slot.reset(t);
+            slot.reset(make_shard(m, kind, dtype, r, k, data_host, 0));
         };
         switch (kind) {
         case T_TOKEN_EMBD: mat(m->tok_embd, c.vocab, c.hidden, false, true); break;
@@ -427,32 +590,45 @@ int fb_model_synth(fb_model *m, uint64_t seed) {
         const fb_model_config &c = m->c;
         const int qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
         const float sigma = 0.02f;
-        auto mat = [&](QT &slot, int dtype, int64_t r, int64_t k, uint64_t s) {
-            fb_qtensor *t = nullptr;
-            const int rc = fb_qtensor_synth(ctx, dtype, r, k, s, sigma, &t);
-            if (rc != FB_OK) fail(rc, fb_last_error());
-            slot.reset(t);
+        DevBuf staging;  // full GGUF tensor when sharding
+        auto mat_kind = [&](QT &slot, int kind, int dtype, int64_t r, int64_t k, uint64_t s) {
+            int64_t r0, nr, c0, nc;
+            shard_range(m, kind, r, k, r0, nr, c0, nc);
+            if (nr == r && nc == k) {
+                fb_qtensor *t = nullptr;
+                const int rc = fb_qtensor_synth(ctx, dtype, r, k, s, sigma, &t);
+                if (rc != FB_OK) fail(rc, fb_last_error());
+                slot.reset(t);
+                return;
+            }
+            const size_t bytes = (size_t)(r * (k / 256)) * (dtype == FB_Q4_K ? 144 : 210);
+            if (staging.bytes < bytes) staging.alloc(bytes);
+            launch_synth(ctx, dtype, r * (k / 256), s, sigma, staging.ptr);
+            slot.reset(make_shard(m, kind, dtype, r, k, staging.ptr, 1));
         };
         auto vec = [&](DevBuf &buf, int64_t n, uint64_t s) {
             buf.alloc((size_t)n * 4);
             launch_synth_f32(ctx, buf.as<float>(), n, s, 1.0f, 0.02f);
         };
-        mat(m->tok_embd, FB_Q4_K, c.vocab, c.hidden, tensor_seed(seed, -1, T_TOKEN_EMBD));
+        auto mat = [&](QT &slot, int kind, int dtype, int64_t r, int64_t k, int layer) {
+            mat_kind(slot, kind, dtype, r, k, tensor_seed(seed, layer, kind));
+        };
+        mat(m->tok_embd, T_TOKEN_EMBD, FB_Q4_K, c.vocab, c.hidden, -1);
         vec(m->out_norm, c.hidden, tensor_seed(seed, -1, T_OUTPUT_NORM));
-        mat(m->output, FB_Q6_K, c.vocab, c.hidden, tensor_seed(seed, -1, T_OUTPUT));
+        mat(m->output, T_OUTPUT, FB_Q6_K, c.vocab, c.hidden, -1);
         for (int l = 0; l < c.n_layers; l++) {
             Layer &L = *m->layers[l];
             vec(L.attn_norm, c.hidden, tensor_seed(seed, l, T_ATTN_NORM));
-            mat(L.wq, FB_Q4_K, qd, c.hidden, tensor_seed(seed, l, T_ATTN_Q));
-            mat(L.wk, FB_Q4_K, kd, c.hidden, tensor_seed(seed, l, T_ATTN_K));
-            mat(L.wv, FB_Q4_K, kd, c.hidden, tensor_seed(seed, l, T_ATTN_V));
-            mat(L.wo, FB_Q4_K, c.hidden, qd, tensor_seed(seed, l, T_ATTN_OUTPUT));
+            mat(L.wq, T_ATTN_Q, FB_Q4_K, qd, c.hidden, l);
+            mat(L.wk, T_ATTN_K, FB_Q4_K, kd, c.hidden, l);
+            mat(L.wv, T_ATTN_V, FB_Q4_K, kd, c.hidden, l);
+            mat(L.wo, T_ATTN_OUTPUT, FB_Q4_K, c.hidden, qd, l);
             vec(L.q_norm, c.head_dim, tensor_seed(seed, l, T_ATTN_Q_NORM));
             vec(L.k_norm, c.head_dim, tensor_seed(seed, l, T_ATTN_K_NORM));
             vec(L.ffn_norm, c.hidden, tensor_seed(seed, l, T_FFN_NORM));
-            mat(L.wgate, FB_Q4_K, c.ffn, c.hidden, tensor_seed(seed, l, T_FFN_GATE));
-            mat(L.wup, FB_Q4_K, c.ffn, c.hidden, tensor_seed(seed, l, T_FFN_UP));
-            mat(L.wdown, FB_Q6_K, c.hidden, c.ffn, tensor_seed(seed, l, T_FFN_DOWN));
+            mat(L.wgate, T_FFN_GATE, FB_Q4_K, c.ffn, c.hidden, l);
+            mat(L.wup, T_FFN_UP, FB_Q4_K, c.ffn, c.hidden, l);
+            mat(L.wdown, T_FFN_DOWN, FB_Q6_K, c.hidden, c.ffn, l);
         }
         FB_CUDA(cudaStreamSynchronize(ctx->stream));
     });
@@ -505,7 +681,7 @@ int fb_model_decode_dev(fb_model *m, const int32_t *tokens_dev, const int32_t *p
         run_step(m, batch);
         if (next_dev) FB_CUDA(cudaMemcpyAsync(next_dev, m->next.ptr, (size_t)batch * 4, cudaMemcpyDeviceToDevice, s));
         if (logits_dev)
-            FB_CUDA(cudaMemcpyAsync(logits_dev, m->logits.ptr, (size_t)batch * m->c.vocab * 4,
+            FB_CUDA(cudaMemcpyAsync(logits_dev, m->logits.ptr, (size_t)batch * m->lc.vocab * 4,
                                     cudaMemcpyDeviceToDevice, s));
     });
 }
@@ -554,8 +730,8 @@ int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos, fl
             FB_CUDA(cudaStreamSynchronize(s));  // pinned staging is reused next iteration
         }
         m->len0 = pos + n;
-        if (logits_host)
-            FB_CUDA(cudaMemcpyAsync(logits_host, m->logits.ptr, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, s));
+        if (logits_host)  // this rank's vocab slice under tensor parallelism
+            FB_CUDA(cudaMemcpyAsync(logits_host, m->logits.ptr, (size_t)m->lc.vocab * 4, cudaMemcpyDeviceToHost, s));
         FB_CUDA(cudaStreamSynchronize(s));
         check_no_device_error(m);
     });
@@ -580,8 +756,8 @@ int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale) {
         for (int l = 0; l < c.n_layers; l++)
             for (int which = 0; which < 2; which++)
                 launch_synth_kv(m->ctx, which ? (void *)m->vpool(l) : (void *)m->kpool(l), l, which, ctx,
-                                c.n_kv_heads, c.head_dim, kPage, m->block_table.as<int32_t>(), m->pages_per_seq,
-                                c.max_batch, seed, scale);
+                                m->lc.n_kv_heads, c.head_dim, kPage, m->block_table.as<int32_t>(), m->pages_per_seq,
+                                c.max_batch, seed, scale, m->rank * m->lc.n_kv_heads);
         FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
         m->len0 = ctx;
     });
@@ -590,7 +766,7 @@ int fb_model_synth_kv(fb_model *m, uint64_t seed, int ctx, float scale) {
 int fb_model_read_kv(fb_model *m, int layer, int which, int pos, float *out_host) {
     return guarded([&] {
         FB_REQUIRE(m && out_host, "null argument");
-        const fb_model_config &c = m->c;
+        const fb_model_config &c = m->lc;  // this rank's kv heads
         FB_REQUIRE(layer >= 0 && layer < c.n_layers && (which == 0 || which == 1) && pos >= 0 && pos < c.max_ctx,
                    "index out of range");
         const __half *pool = which ? m->vpool(layer) : m->kpool(layer);
@@ -665,7 +841,7 @@ int fb_model_launches_per_step(const fb_model *m, int *launches) {
         FB_REQUIRE(m && launches, "null argument");
         require_ready(m);
         const int L = m->c.n_layers;
-        const bool q8_fused = (m->c.n_heads / m->c.n_kv_heads) % 2 == 0;
+        const bool q8_fused = (m->lc.n_heads / m->lc.n_kv_heads) % 2 == 0;
         // matches step(): embed-norm; per layer qkv, attention (+ Q8_K quantize
         // for odd GQA groups), o, norm, gate_up, swiglu, down, norm; lm_head, argmax
         *launches = 1 + (q8_fused ? 8 : 9) * L + 2;
@@ -675,7 +851,7 @@ int fb_model_launches_per_step(const fb_model *m, int *launches) {
 int fb_model_read_activation(fb_model *m, const char *name, int row, float *out_host, int64_t count) {
     return guarded([&] {
         FB_REQUIRE(m && name && out_host, "null argument");
-        const fb_model_config &c = m->c;
+        const fb_model_config &c = m->lc;  // this rank's shard dims
         FB_REQUIRE(row >= 0 && row < c.max_batch, "row out of range");
         const int64_t qd = (int64_t)c.n_heads * c.head_dim, kd = (int64_t)c.n_kv_heads * c.head_dim;
         const std::string n(name);
@@ -691,6 +867,8 @@ int fb_model_read_activation(fb_model *m, const char *name, int row, float *out_
         } else if (n == "qkv") buf = &m->y_qkv, len = qd + 2 * kd;
         else if (n == "q") buf = &m->q, len = qd;
         else if (n == "attn") buf = &m->attn, len = qd;
+        else if ((n == "o" || n == "down") && m->comm)
+            fail(FB_ERR_STATE, "row-parallel projection outputs are exchanged as partial sums under tensor parallelism");
         else if (n == "o") buf = &m->y_o, len = c.hidden;
         else if (n == "gate_up") buf = &m->y_gu, len = 2LL * c.ffn;
         else if (n == "down") buf = &m->y_d, len = c.hidden;

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     k_residual_rmsnorm_q8k(const float *__restrict__ x, const float *__restrict__ add, float *__restrict__ x_out,
                            const float *__restrict__ g, int dim, float eps, Q8Act a,
                            const uint8_t *__restrict__ emb_tab, const int32_t *__restrict__ tokens, int vocab,
-                           uint32_t *err) {
+                           uint32_t *err, uint32_t *epoch_inc) {
     __shared__ double sh[NORM_THREADS / 32];
     __shared__ __align__(16) float xb[QK];
     const int blk = blockIdx.x;
@@ -149,6 +149,9 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
     pdl_wait();
     pdl_launch();
+    // first kernel of a tensor-parallel step: advance the step counter that
+    // numbers the step's exchanges (read by later kernels after their wait)
+    if (epoch_inc && blk == 0 && row == 0 && threadIdx.x == 0) *epoch_inc += 1u;
     const int nbe = dim / QK;
     int tok = 0;
     if (emb_tab) {
@@ -216,6 +219,81 @@ __global__ void __launch_bounds__(NORM_THREADS)
 }
 
 // ------------------------------------------------------------------------
+// Tensor-parallel residual add + RMSNorm + Q8_K, after a row-parallel
+// projection (attn_output or ffn_down sharded along its inputs).  Every
+// rank's GEMV has pushed its binary64 partial row sums into this rank's
+// inbox [src][row][col]; they are added in rank order and rounded to f32
+// once -- the rounding the single-GPU GEMV applies to the full sum -- and
+// the residual add, RMSNorm and Q8_K follow k_residual_rmsnorm_q8k.
+// Exchange protocol (sequence number seq of this exchange point in the
+// step): one thread per destination rank publishes seq into that rank's
+// flags[rank] with a system-scope release (the GEMV grid's peer stores
+// precede it), and W threads of every CTA wait (bounded) for flags[src] >=
+// seq.  Inboxes alternate between attn_output and ffn_down, so a rank can
+// only overwrite an inbox slot after every rank has passed the exchange in
+// between, i.e. after the slot was read.
+// One CTA per (256-value block, row) reduces only its own block; the blocks'
+// sums of squares meet through global slots tagged with seq.
+__global__ void __launch_bounds__(NORM_THREADS)
+    k_tp_residual_rmsnorm_q8k(const float *__restrict__ x, float *__restrict__ x_out, const float *__restrict__ g,
+                              int dim, float eps, Q8Act a, TpNorm t, int xi, uint32_t *err) {
+    __shared__ double sh[NORM_THREADS / 32];
+    __shared__ __align__(16) float xb[QK];
+    __shared__ double s_ss;
+    const int blk = blockIdx.x, nblk = gridDim.x;
+    const int64_t row = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int64_t j = row * dim + (int64_t)blk * QK + tid;
+    // weights and the residual row first (they do not depend on the GEMV)
+    const float xv = x[j];
+    float gv[8];
+    if (tid < 32) {
+        const float4 g0 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane);
+        const float4 g1 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane + 4);
+        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+    }
+    pdl_wait();
+    pdl_launch();
+    const uint32_t seq = (*t.epoch - 1u) * (uint32_t)t.nx + (uint32_t)xi + 1u;
+    if (blk == 0 && row == 0 && tid < t.world) {
+        __threadfence_system();
+        st_release_sys(t.peer_flag[tid], seq);
+    }
+    if (tid < t.world && !wait_seq<true>(&t.my_flags[tid], seq, t.limit_ns)) atomicOr(err, ERRBIT_PEER_TIMEOUT);
+    __syncthreads();
+    const int64_t plane = (int64_t)t.batch_cap * dim;
+    double s = 0.0;
+    for (int r = 0; r < t.world; r++) s = __dadd_rn(s, __ldcg(t.inbox + r * plane + j));
+    const float xn = __fadd_rn(__double2float_rn(s), xv);
+    x_out[j] = xn;
+    xb[tid] = xn;
+    const double ssb = block_sum64<NORM_THREADS / 32>(__dmul_rn((double)xn, (double)xn), sh);
+    const int64_t slot0 = row * nblk;
+    if (tid == 0) {
+        t.ss_part[slot0 + blk] = ssb;
+        __threadfence();
+        st_release_gpu(&t.ss_tag[slot0 + blk], seq);
+    }
+    if (tid < nblk && !wait_seq<false>(&t.ss_tag[slot0 + tid], seq, t.limit_ns))
+        atomicOr(err, ERRBIT_WAIT_TIMEOUT);
+    __syncthreads();
+    if (tid == 0) {
+        double ss = 0.0;
+        for (int b = 0; b < nblk; b++) ss = __dadd_rn(ss, __ldcg(&t.ss_part[slot0 + b]));
+        s_ss = ss;
+    }
+    __syncthreads();
+    const float m = rms_of(s_ss, dim, eps);
+    if (tid < 32) {
+        float q[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) q[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), gv[e]);
+        q8k_store_warp(q, lane, a, row, blk);
+    }
+}
+
+// ------------------------------------------------------------------------
 // SwiGLU + Q8_K: y[row] = [gate (f) | up (f)] -> act = Q8K(silu(gate) * up).
 // One warp per (row, 256-value block), two warps per CTA; the eight
 // exponentials of a lane are independent and overlap.
@@ -271,12 +349,17 @@ __device__ __forceinline__ void argmax_block(float &best, int &bi, float *sv, in
     for (int off = 16; off > 0; off >>= 1)
         argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, off), __shfl_xor_sync(0xffffffffu, bi, off));
 }
+// Tensor parallel (t.world > 0): each rank holds a vocab slice; the last CTA
+// of a row pushes the slice's (max, global index) to every rank, waits
+// (bounded) for all ranks' pairs of this step and merges them.
 __global__ void __launch_bounds__(256) k_argmax(const float *__restrict__ logits, int64_t vocab,
                                                 int32_t *__restrict__ out, float *__restrict__ ws_v,
-                                                int *__restrict__ ws_i, int *__restrict__ counters) {
+                                                int *__restrict__ ws_i, int *__restrict__ counters, TpArgmax t,
+                                                uint32_t *err) {
     __shared__ float sv[8];
     __shared__ int si[8];
     __shared__ int s_last;
+    __shared__ unsigned long long s_pack;
     pdl_wait();
     const int64_t row = blockIdx.y, chunk = (vocab + gridDim.x - 1) / gridDim.x;
     const int64_t i0 = blockIdx.x * chunk, i1 = min(vocab, i0 + chunk);
@@ -302,7 +385,34 @@ __global__ void __launch_bounds__(256) k_argmax(const float *__restrict__ logits
             argmax_merge(best, bi, __ldcg(&ws_v[row * gridDim.x + c]), __ldcg(&ws_i[row * gridDim.x + c]));
         __syncthreads();  // sv / si are reused
         argmax_block(best, bi, sv, si);
-        if (threadIdx.x == 0) out[row] = bi == 0x7fffffff ? 0 : bi;
+        if (t.world == 0) {
+            if (threadIdx.x == 0) out[row] = bi == 0x7fffffff ? 0 : bi;
+        } else {
+            if (threadIdx.x == 0) {
+                const uint32_t gi = bi == 0x7fffffff ? 0x7fffffffu : (uint32_t)(bi + t.vocab_off);
+                s_pack = ((unsigned long long)__float_as_uint(best) << 32) | gi;
+            }
+            __syncthreads();
+            const uint32_t ep = *t.epoch;
+            if (threadIdx.x < t.world) {
+                t.peer_slot[threadIdx.x][row] = s_pack;
+                __threadfence_system();
+                st_release_sys(t.peer_flag[threadIdx.x] + row, ep);
+                if (!wait_seq<true>(t.my_flags + (int64_t)threadIdx.x * t.batch_cap + row, ep, t.limit_ns))
+                    atomicOr(err, ERRBIT_PEER_TIMEOUT);
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                float gb = -INFINITY;
+                int gx = 0x7fffffff;
+                for (int r = 0; r < t.world; r++) {
+                    const unsigned long long v =
+                        __ldcg(reinterpret_cast<const unsigned long long *>(t.my_inbox) + (int64_t)r * t.batch_cap + row);
+                    argmax_merge(gb, gx, __uint_as_float((uint32_t)(v >> 32)), (int)(uint32_t)v);
+                }
+                out[row] = gx == 0x7fffffff ? 0 : gx;
+            }
+        }
     }
     pdl_launch();
 }
@@ -387,7 +497,25 @@ void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, 
     }
     FB_REQUIRE(x_out != x, "rmsnorm_q8k: x_out must not alias x");
     launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g, dim, eps, a,
-             tab, tokens, vocab, ctx->err_word);
+             tab, tokens, vocab, ctx->err_word, (uint32_t *)nullptr);
+}
+
+void launch_embed_rmsnorm_q8k(fb_ctx *ctx, float *x_out, const float *g, int rows, int dim, float eps,
+                              const Q8Act &a, const fb_qtensor *emb, const int32_t *tokens, int vocab,
+                              uint32_t *epoch_inc) {
+    FB_REQUIRE(dim % QK == 0, "rmsnorm_q8k: dim must be a multiple of 256");
+    FB_REQUIRE(emb && emb->dtype == FB_Q4_K && emb->k == dim, "embedding table must be Q4_K [vocab, hidden]");
+    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, (const float *)nullptr,
+             (const float *)nullptr, x_out, g, dim, eps, a, emb->main(), tokens, vocab, ctx->err_word, epoch_inc);
+}
+
+void launch_tp_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, float *x_out, const float *g, int rows, int dim,
+                                    float eps, const Q8Act &a, const TpNorm &t, int xi) {
+    FB_REQUIRE(dim % QK == 0 && dim / QK <= NORM_THREADS, "tp rmsnorm: dim must be a multiple of 256, <= 65536");
+    FB_REQUIRE(rows <= t.batch_cap && t.world >= 1 && t.world <= FB_TP_MAX, "tp rmsnorm: bad rows / world");
+    FB_REQUIRE(x_out != x, "rmsnorm_q8k: x_out must not alias x");
+    launch_k(ctx, k_tp_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, x_out, g, dim, eps, a, t,
+             xi, ctx->err_word);
 }
 
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a) {
@@ -404,7 +532,18 @@ void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, in
     int *wi = reinterpret_cast<int *>(wv + (size_t)rows * ARGMAX_CHUNKS);
     int *cnt = wi + (size_t)rows * ARGMAX_CHUNKS;
     const int chunks = (int)std::min<int64_t>(ARGMAX_CHUNKS, (vocab + 1023) / 1024);
-    launch_k(ctx, k_argmax, dim3(chunks, rows), dim3(256), 0, logits, vocab, out, wv, wi, cnt);
+    launch_k(ctx, k_argmax, dim3(chunks, rows), dim3(256), 0, logits, vocab, out, wv, wi, cnt, TpArgmax{},
+             ctx->err_word);
+}
+
+void launch_argmax_tp(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, int32_t *out, void *ws,
+                      const TpArgmax &t) {
+    FB_REQUIRE(t.world >= 1 && t.world <= FB_TP_MAX && rows <= t.batch_cap, "argmax: bad tensor-parallel args");
+    float *wv = static_cast<float *>(ws);
+    int *wi = reinterpret_cast<int *>(wv + (size_t)rows * ARGMAX_CHUNKS);
+    int *cnt = wi + (size_t)rows * ARGMAX_CHUNKS;
+    const int chunks = (int)std::min<int64_t>(ARGMAX_CHUNKS, (vocab + 1023) / 1024);
+    launch_k(ctx, k_argmax, dim3(chunks, rows), dim3(256), 0, logits, vocab, out, wv, wi, cnt, t, ctx->err_word);
 }
 
 void rope_tables(int max_pos, int head_dim, float theta, std::vector<float> &cos_t, std::vector<float> &sin_t) {
@@ -446,13 +585,13 @@ __device__ __forceinline__ uint64_t kv_mix64(uint64_t z) {
 
 __global__ void k_synth_kv(__half *__restrict__ pool, int layer, int which, int ctx, int nkv, int hd, int page_size,
                            const int32_t *__restrict__ block_table, int max_pages, int slots, uint64_t sm,
-                           float s3) {
+                           float s3, int e0) {
     const int64_t kd = (int64_t)nkv * hd;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over ctx * kd
     if (i >= (int64_t)ctx * kd) return;
     const int p = (int)(i / kd);
     const int e = (int)(i % kd);
-    const uint64_t idx = (((uint64_t)layer * 2u + (uint64_t)which) << 40) | ((uint64_t)p << 20) | (uint64_t)e;
+    const uint64_t idx = (((uint64_t)layer * 2u + (uint64_t)which) << 40) | ((uint64_t)p << 20) | (uint64_t)(e0 + e);
     const uint64_t h = kv_mix64(sm ^ idx);
     const float u = (float)(h >> 40) * (1.0f / 16777216.0f);
     const __half v = __float2half_rn(__fmul_rn(s3, __fsub_rn(__fmul_rn(2.0f, u), 1.0f)));
@@ -467,12 +606,12 @@ __global__ void k_synth_kv(__half *__restrict__ pool, int layer, int which, int 
 }
 
 void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
-                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale) {
+                     const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale, int kv_head0) {
     const int64_t n = (int64_t)nctx * nkv * hd;
     if (n == 0) return;
     k_synth_kv<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
         (__half *)pool, layer, which, nctx, nkv, hd, page_size, block_table, max_pages, slots, kv_mix64_host(seed),
-        scale * 1.7320508f);
+        scale * 1.7320508f, kv_head0 * hd);
     FB_CUDA(cudaGetLastError());
 }
 

@@ -38,7 +38,10 @@ EXPORTED = (
     "fb_model_finalize", "fb_model_forward", "fb_model_decode_greedy", "fb_model_decode_dev", "fb_model_prefill",
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
+    "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
+    "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms",
 )
+COMM_HANDLE_BYTES = 64
 
 PROF_KINDS = ("embed_norm", "qkv", "rope_kv", "attn", "o", "norm", "gate_up", "swiglu", "down", "lm_head", "argmax")
 
@@ -114,6 +117,14 @@ def _declare(L):
         "fb_model_read_activation": (i32, [vp, C.c_char_p, i32, vp, i64]),
         "fb_model_profile": (i32, [vp, vp, vp, i32, i32, vp, vp]),
         "fb_model_launches_per_step": (i32, [vp, P(i32)]),
+        "fb_qtensor_upload_slice": (i32, [vp, i32, i64, i64, vp, i32, i64, i64, i64, i64, P(vp)]),
+        "fb_comm_create": (i32, [vp, i32, i32, i32, i32, P(vp)]),
+        "fb_comm_handle": (i32, [vp, vp]),
+        "fb_comm_open": (i32, [vp, vp]),
+        "fb_comm_destroy": (i32, [vp]),
+        "fb_comm_set_timeout_ms": (i32, [vp, i32]),
+        "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
+        "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -181,6 +192,17 @@ class QTensor:
         blocks = np.ascontiguousarray(blocks)
         h = C.c_void_p()
         _check(lib().fb_qtensor_upload(ctx.h, dtype, n, k, _np(blocks), C.byref(h)))
+        return cls(ctx, h)
+
+    @classmethod
+    def upload_slice(cls, ctx: Context, dtype: int, n: int, k: int, blocks: np.ndarray, row0: int, rows: int,
+                     col0: int, cols: int) -> "QTensor":
+        """W[row0:row0+rows, col0:col0+cols] of the full GGUF tensor W[n, k]
+        (host blocks); cols and col0 are multiples of 256."""
+        blocks = np.ascontiguousarray(blocks)
+        h = C.c_void_p()
+        _check(lib().fb_qtensor_upload_slice(ctx.h, dtype, n, k, _np(blocks), 0, row0, rows, col0, cols,
+                                             C.byref(h)))
         return cls(ctx, h)
 
     @classmethod
@@ -277,16 +299,87 @@ def tensor_seed(seed: int, layer: int, name: str) -> int:
     return (seed + 0x1000 * (layer + 1) + KIND_ID[name]) & 0xFFFFFFFFFFFFFFFF
 
 
-class Model:
-    """Quantized Llama/Qwen3 model (ferrite_core::InferenceModel counterpart)."""
+class Comm:
+    """Tensor-parallel exchange region of one rank (fb_comm).
 
-    def __init__(self, ctx: Context, cfg: dict):
+    create -> handle() on every rank -> exchange the handles -> open(all).
+    ``Comm.connect`` does the exchange over an initialised torch.distributed
+    process group (any backend; the handles are 64-byte host blobs)."""
+
+    def __init__(self, ctx: Context, rank: int, world: int, max_batch: int, hidden: int):
+        self.ctx, self.rank, self.world = ctx, rank, world
+        h = C.c_void_p()
+        _check(lib().fb_comm_create(ctx.h, rank, world, max_batch, hidden, C.byref(h)))
+        self.h = h
+
+    def set_timeout_ms(self, ms: int):
+        _check(lib().fb_comm_set_timeout_ms(self.h, ms))
+
+    def handle(self) -> bytes:
+        buf = (C.c_uint8 * COMM_HANDLE_BYTES)()
+        _check(lib().fb_comm_handle(self.h, buf))
+        return bytes(buf)
+
+    def open(self, handles: list[bytes]):
+        if len(handles) != self.world or any(len(x) != COMM_HANDLE_BYTES for x in handles):
+            raise ValueError("need one 64-byte handle per rank, in rank order")
+        blob = b"".join(handles)
+        _check(lib().fb_comm_open(self.h, C.c_char_p(blob)))
+
+    @staticmethod
+    def gather_handles(mine: bytes, world: int, group=None) -> list[bytes]:
+        """All ranks' handles in rank order through torch.distributed."""
+        import torch.distributed as dist
+
+        out = [None] * world
+        dist.all_gather_object(out, mine, group=group)
+        return out
+
+    @classmethod
+    def connect(cls, ctx: Context, max_batch: int, hidden: int, group=None) -> "Comm":
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        c = cls(ctx, rank, world, max_batch, hidden)
+        c.open(cls.gather_handles(c.handle(), world, group))
+        dist.barrier(group)
+        return c
+
+    def close(self):
+        if self.h:
+            lib().fb_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Model:
+    """Quantized Llama/Qwen3 model (ferrite_core::InferenceModel counterpart).
+
+    With ``comm`` the model is this rank's tensor-parallel shard: cfg and the
+    tensors given to set_tensor are the full model's; forward returns the
+    rank's vocab slice of the logits (``vocab_range``)."""
+
+    def __init__(self, ctx: Context, cfg: dict, comm: Comm | None = None):
         self.ctx = ctx
         self.cfg = dict(cfg)
+        self.comm = comm
         c = ModelConfig(**{k: cfg[k] for k, _ in ModelConfig._fields_})
         h = C.c_void_p()
-        _check(lib().fb_model_create(ctx.h, C.byref(c), C.byref(h)))
+        if comm is None:
+            _check(lib().fb_model_create(ctx.h, C.byref(c), C.byref(h)))
+        else:
+            _check(lib().fb_model_create_tp(ctx.h, C.byref(c), comm.h, C.byref(h)))
         self.h = h
+        r, w, vo, vn = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        _check(lib().fb_model_tp_info(h, C.byref(r), C.byref(w), C.byref(vo), C.byref(vn)))
+        self.rank, self.world, self.vocab_range = r.value, w.value, (vo.value, vo.value + vn.value)
+        self.local = dict(self.cfg, n_heads=cfg["n_heads"] // w.value, n_kv_heads=cfg["n_kv_heads"] // w.value,
+                          ffn=cfg["ffn"] // w.value, vocab=vn.value)
 
     def set_tensor(self, name: str, layer: int, dtype: int, rows: int, cols: int, data: np.ndarray):
         data = np.ascontiguousarray(data)
@@ -300,13 +393,13 @@ class Model:
 
     def forward(self, tokens, pos: int) -> np.ndarray:
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
-        out = np.zeros(self.cfg["vocab"], dtype=np.float32)
+        out = np.zeros(self.local["vocab"], dtype=np.float32)
         _check(lib().fb_model_forward(self.h, _np(toks), toks.size, pos, _np(out)))
         return out
 
     def prefill(self, tokens) -> np.ndarray:
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
-        out = np.zeros(self.cfg["vocab"], dtype=np.float32)
+        out = np.zeros(self.local["vocab"], dtype=np.float32)
         _check(lib().fb_model_prefill(self.h, _np(toks), toks.size, _np(out)))
         return out
 
@@ -327,12 +420,12 @@ class Model:
         _check(lib().fb_model_synth_kv(self.h, seed, ctx, scale))
 
     def read_kv(self, layer: int, which: int, pos: int) -> np.ndarray:
-        out = np.zeros(self.cfg["n_kv_heads"] * self.cfg["head_dim"], dtype=np.float32)
+        out = np.zeros(self.local["n_kv_heads"] * self.cfg["head_dim"], dtype=np.float32)
         _check(lib().fb_model_read_kv(self.h, layer, which, pos, _np(out)))
         return out
 
     def read_activation(self, name: str, row: int = 0) -> np.ndarray:
-        c = self.cfg
+        c = self.local
         qd, kd = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
         n = {"x": c["hidden"], "qkv": qd + 2 * kd, "q": qd, "attn": qd, "o": c["hidden"], "gate_up": 2 * c["ffn"],
              "down": c["hidden"], "logits": c["vocab"]}[name]

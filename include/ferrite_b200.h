@@ -100,6 +100,16 @@ int fb_qtensor_synth(fb_ctx *ctx, int dtype, int64_t n, int64_t k,
 /* Stacks the rows of several tensors of one dtype and k (fused QKV, gate/up). */
 int fb_qtensor_concat_rows(fb_ctx *ctx, const fb_qtensor *const *parts,
                            int nparts, fb_qtensor **out);
+/* Uploads the sub-matrix W[row0 : row0+rows, col0 : col0+cols] of a GGUF
+ * tensor W[n, k] given in full (blocks in row order; on the host when
+ * src_on_device == 0, else in device memory).  col0 and cols are multiples
+ * of 256 (whole super-blocks), so the slice's blocks are the source's bytes.
+ * Tensor-parallel shards: a row slice is a column-parallel shard (split
+ * output features), a column slice a row-parallel shard (split inputs). */
+int fb_qtensor_upload_slice(fb_ctx *ctx, int dtype, int64_t n, int64_t k,
+                            const void *src_blocks, int src_on_device,
+                            int64_t row0, int64_t rows, int64_t col0,
+                            int64_t cols, fb_qtensor **out);
 int fb_qtensor_info(const fb_qtensor *t, int *dtype, int64_t *n, int64_t *k,
                     int64_t *device_bytes);
 int fb_qtensor_download(fb_ctx *ctx, const fb_qtensor *t, void *host_blocks);
@@ -247,6 +257,53 @@ int fb_model_launches_per_step(const fb_model *m, int *launches);
  * "down", "logits".  count must equal the buffer's row length. */
 int fb_model_read_activation(fb_model *m, const char *name, int row,
                              float *out_host, int64_t count);
+
+/* ------------------------------------------------- tensor parallelism ---
+ * One process (one fb_ctx) per GPU of a node; the reference has no tensor
+ * parallelism (candle runs on one device) and its multi-GPU primitives are
+ * peer copies with gather-to-root reductions (ferrite-os/native/core/runtime/
+ * modules/hot_multi_gpu_primitives.inl:99-123, hot_multi_gpu_reduction.inl).
+ *
+ * fb_comm is a device region per rank (exchange inboxes and flags) that
+ * every rank maps through CUDA IPC.  Setup: fb_comm_create on each rank,
+ * fb_comm_handle -> exchange the FB_COMM_HANDLE_BYTES blobs between the
+ * processes (any host channel), fb_comm_open with all world handles in rank
+ * order.  The ranks must be started in step (a host barrier) before the
+ * first decode step; the device waits on peers are bounded (about 10 s),
+ * after which a kernel sets the error word and the step's output is
+ * undefined.
+ *
+ * A model created with fb_model_create_tp takes the FULL model config and
+ * full tensors in fb_model_set_tensor / fb_model_synth and keeps its shard:
+ * attn_q / attn_k / attn_v rows of its n_heads/world query and
+ * n_kv_heads/world kv heads, ffn_gate / ffn_up rows and ffn_down columns of
+ * its ffn/world slice, attn_output columns of its heads, output (lm_head)
+ * rows of its vocab/world slice; token_embd and the norms whole.  The
+ * outputs of attn_output and ffn_down are partial sums over the rank's
+ * inputs; each rank pushes its binary64 partials into every rank's inbox
+ * from the projection kernel and the residual + RMSNorm kernel adds the
+ * world partials in rank order (one f32 rounding, as on one GPU).  Greedy
+ * argmax exchanges each rank's (max, index) pair.  Every rank calls the
+ * same decode functions with the same tokens; all ranks get the same next
+ * tokens.  fb_model_forward's logits_host receives the rank's vocab slice
+ * (fb_model_tp_info gives its offset and length); fb_model_read_kv returns
+ * the rank's kv heads.  world is 2, 4 or 8 with n_kv_heads, ffn/256 and
+ * n_heads*head_dim/256 divisible by world. */
+typedef struct fb_comm fb_comm;
+#define FB_TP_MAX 8
+#define FB_COMM_HANDLE_BYTES 64
+int fb_comm_create(fb_ctx *ctx, int rank, int world, int max_batch,
+                   int hidden, fb_comm **out);
+int fb_comm_handle(const fb_comm *comm, void *handle_out);
+int fb_comm_open(fb_comm *comm, const void *handles);
+/* Bound of the device waits on peers (default 10 s); read when a model's
+ * decode step is first run or captured for a batch size. */
+int fb_comm_set_timeout_ms(fb_comm *comm, int ms);
+int fb_comm_destroy(fb_comm *comm);
+int fb_model_create_tp(fb_ctx *ctx, const fb_model_config *cfg,
+                       fb_comm *comm, fb_model **out);
+int fb_model_tp_info(const fb_model *m, int *rank, int *world,
+                     int *vocab_offset, int *vocab_count);
 
 #ifdef __cplusplus
 }

@@ -462,7 +462,7 @@ static void q6k_block_int(const or_block_q6k *x, const or_block_q8k *y,
  * fp16 super-block scales in binary64 (one rounding to f32 at the end) so the
  * result does not depend on the order in which blocks are summed.  candle
  * combines in f32 (8 lane sums); the two differ in the last bits only. */
-float or_vec_dot(int dtype, int64_t n, const void *w, const void *a) {
+double or_vec_dot64(int dtype, int64_t n, const void *w, const void *a) {
     int64_t nb = n / OR_QK_K;
     const or_block_q8k *y = (const or_block_q8k *)a;
     double acc = 0.0;
@@ -484,7 +484,11 @@ float or_vec_dot(int dtype, int64_t n, const void *w, const void *a) {
             acc += (double)or_f16_to_f32(x->d) * (double)y[b].d * (double)isum;
         }
     }
-    return (float)acc;
+    return acc;
+}
+
+float or_vec_dot(int dtype, int64_t n, const void *w, const void *a) {
+    return (float)or_vec_dot64(dtype, n, w, a);
 }
 
 void or_block_dots(int dtype, int64_t nrows, int64_t k, const void *w,
@@ -528,6 +532,25 @@ void or_qmatmul(int dtype, const void *w, int64_t n, int64_t k,
 #pragma omp parallel for num_threads(nt) schedule(dynamic, 256)
         for (int64_t c = 0; c < n; c++)
             yr[c] = or_vec_dot(dtype, k, (const uint8_t *)w + (size_t)c * nb * bb, xr);
+    }
+    free(xq);
+}
+
+/* Same sums as or_qmatmul without the final rounding: the binary64 partial
+ * a tensor-parallel rank holding input columns [c0, c0 + k) contributes. */
+void or_qmatmul64(int dtype, const void *w, int64_t n, int64_t k,
+                  const float *x, int64_t m, double *y, int nthreads) {
+    int64_t nb = k / OR_QK_K;
+    size_t bb = or_block_bytes(dtype);
+    or_block_q8k *xq = (or_block_q8k *)malloc((size_t)(m * nb) * sizeof(or_block_q8k));
+    for (int64_t r = 0; r < m; r++) or_quantize_q8k(x + r * k, k, xq + r * nb, 0);
+    int nt = resolve_threads(nthreads);
+    for (int64_t r = 0; r < m; r++) {
+        const or_block_q8k *xr = xq + r * nb;
+        double *yr = y + r * n;
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 256)
+        for (int64_t c = 0; c < n; c++)
+            yr[c] = or_vec_dot64(dtype, k, (const uint8_t *)w + (size_t)c * nb * bb, xr);
     }
     free(xq);
 }

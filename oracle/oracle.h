@@ -97,6 +97,10 @@ void or_qmatmul(int dtype, const void *w, int64_t n, int64_t k,
 
 /* Dequantize-then-f32 matmul (the large-batch form: no activation
  * quantization).  Used as the oracle for the prefill GEMM. */
+/* Unrounded binary64 row sums of or_qmatmul (tensor-parallel partials). */
+double or_vec_dot64(int dtype, int64_t n, const void *w, const void *a);
+void or_qmatmul64(int dtype, const void *w, int64_t n, int64_t k,
+                  const float *x, int64_t m, double *y, int nthreads);
 void or_qmatmul_f32(int dtype, const void *w, int64_t n, int64_t k,
                     const float *x, int64_t m, float *y, int nthreads);
 

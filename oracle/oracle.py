@@ -67,6 +67,7 @@ def _declare(L):
     L.or_block_dots.argtypes = [C.c_int, i64, i64, vp, vp, vp, vp]
     L.or_qmatmul.argtypes = [C.c_int, vp, i64, i64, vp, i64, vp, C.c_int]
     L.or_qmatmul_f32.argtypes = [C.c_int, vp, i64, i64, vp, i64, vp, C.c_int]
+    L.or_qmatmul64.argtypes = [C.c_int, vp, i64, i64, vp, i64, vp, C.c_int]
     L.or_f16_to_f32.argtypes = [C.c_uint16]
     L.or_f16_to_f32.restype = f32
     L.or_f32_to_f16.argtypes = [f32]
@@ -168,6 +169,22 @@ def qmatmul(dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, nthreads: 
     y = np.zeros((x.shape[0], n), dtype=np.float32)
     lib().or_qmatmul(dtype, _p(np.ascontiguousarray(w)), n, k, _p(x), x.shape[0], _p(y), nthreads)
     return y
+
+
+def qmatmul64(dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """qmatmul's binary64 row sums before the final rounding to f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    y = np.zeros((x.shape[0], n), dtype=np.float64)
+    lib().or_qmatmul64(dtype, _p(np.ascontiguousarray(w)), n, k, _p(x), x.shape[0], _p(y), nthreads)
+    return y
+
+
+def shard_blocks(dtype: int, w: np.ndarray, n: int, k: int, row0: int, rows: int, col0: int, cols: int) -> np.ndarray:
+    """GGUF blocks of W[row0:row0+rows, col0:col0+cols] (col0, cols multiples
+    of 256): the tensor-parallel shard a rank keeps."""
+    bb = {Q4_K: 144, Q6_K: 210}[dtype]
+    rowsv = np.asarray(w, dtype=np.uint8).reshape(n, k // 256 * bb)
+    return np.ascontiguousarray(rowsv[row0:row0 + rows, col0 // 256 * bb:(col0 + cols) // 256 * bb]).reshape(-1)
 
 
 def qmatmul_f32(dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
