@@ -19,6 +19,10 @@ when decoding starts, batch 1 by default.
 N > 1 (torchrun): every rank runs an independent replica on its own GPU
 (decode of independent sequences; no data-path collective); value is the
 total over ranks divided by the max-over-ranks elapsed time.
+--tp (with --model llama3-70b, ctx 8192): the N ranks hold one
+tensor-parallel model instead (column/row-parallel shards, the row-parallel
+partial sums exchanged over NVLink by the projection and norm kernels);
+value is the batch's tokens per second (strong scaling).
 --impl reference: the CPU oracle alone (the reference's path restated; the
 reference itself is Rust + candle and cannot be built here), rank 0 only.
 """
@@ -55,11 +59,12 @@ def peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def step_bytes(cfg: dict, batch: int, ctx: int) -> dict:
+def step_bytes(cfg: dict, batch: int, ctx: int, world: int = 1) -> dict:
     """Algorithmic bytes per decode step by kernel class (weights once per
-    step, KV once per sequence, activations f32/Q8_K once)."""
-    H, F, V, L = cfg["hidden"], cfg["ffn"], cfg["vocab"], cfg["n_layers"]
-    qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    step, KV once per sequence, activations f32/Q8_K once), for one rank of
+    a `world`-way tensor-parallel model (world 1: the whole model)."""
+    H, F, V, L = cfg["hidden"], cfg["ffn"] // world, cfg["vocab"] // world, cfg["n_layers"]
+    qd, kd = cfg["n_heads"] // world * cfg["head_dim"], cfg["n_kv_heads"] // world * cfg["head_dim"]
     q4, q6 = 144 / 256, 210 / 256
 
     def q8(k):  # Q8_K activation row: qs + d + bsums(16 and 32)
@@ -246,10 +251,14 @@ def run_prefill_gemm(args):
 
 
 def workload_config(args) -> dict:
-    return {"workload": f"{args.model}-arch Q4_K_M random-init decode, batch {args.batch}, fp16 KV ctx {args.ctx}",
-            "model_arch": args.model, "batch": args.batch, "kv_ctx": args.ctx, "weights": "Q4_K (+Q6_K ffn_down, output)",
-            "parallelism": "replicas" if args.gpus > 1 else "single-gpu",
-            "l2": "not flushed: each step streams ~4.9 GB of weights, >> 126 MB L2"}
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    par = f"tp{ws}" if args.tp else ("replicas" if ws > 1 else "single-gpu")
+    wl = f"{args.model}-arch Q4_K_M random-init decode, batch {args.batch}, fp16 KV ctx {args.ctx}"
+    if args.tp:
+        wl += f", tensor-parallel over {ws} GPU(s)"
+    return {"workload": wl, "model_arch": args.model, "batch": args.batch, "kv_ctx": args.ctx,
+            "weights": "Q4_K (+Q6_K ffn_down, output)", "parallelism": par,
+            "l2": "not flushed: each step streams the weights (GBs per GPU), >> 126 MB L2"}
 
 
 def main():
@@ -266,6 +275,7 @@ def main():
     ap.add_argument("--profile-run", type=int, default=0,
                     help="build the workload, run N untimed decode steps and exit (driver for ncu captures)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
+    ap.add_argument("--tp", action="store_true", help="one tensor-parallel model over all ranks (strong scaling)")
     ap.add_argument("--prefill-gemm", type=int, default=0, metavar="T",
                     help="instead of decode: time one layer's prefill QMatMuls at T rows (1 GPU)")
     args = ap.parse_args()
@@ -297,10 +307,14 @@ def main():
     B = args.batch
     max_ctx = args.ctx + args.warmup + args.steps + args.e2e_steps + 16
     mcfg = dict(cfg, max_ctx=max_ctx, max_batch=B)
-    model = fb.Model(ctx, mcfg)
+    comm = fb.Comm.connect(ctx, B, cfg["hidden"]) if (args.tp and ws > 1) else None
+    W = ws if comm else 1
+    model = fb.Model(ctx, mcfg, comm)
     model.synth(SEED)
     model.finalize()
     model.synth_kv(SEED + 7, args.ctx)
+    if pg:
+        pg.barrier()  # tensor-parallel ranks start stepping together
     nsteps = args.warmup + args.steps
     pos_all = torch.arange(args.ctx, args.ctx + nsteps + 8, dtype=torch.int32, device="cuda")
     pos_all = pos_all.repeat_interleave(B).reshape(-1, B).contiguous()
@@ -338,7 +352,8 @@ def main():
         pg.barrier()
     torch.cuda.synchronize()
     ms_per_step = ms / args.steps
-    value = ws * B * args.steps / (ms / 1e3)
+    seqs = B if args.tp else ws * B  # sequences decoded by the whole job per step
+    value = seqs * args.steps / (ms / 1e3)
     err = ctx.error_word()
 
     # ---- e2e through the public host API (pinned H2D + D2H every step)
@@ -357,11 +372,11 @@ def main():
         t = torch.tensor([e2e_s], device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = ws * B * args.e2e_steps / e2e_s
+    e2e = seqs * args.e2e_steps / e2e_s
 
     # ---- live per-kernel profile (CUDA events per kernel class, serialised)
     prof = model.profile(tok.data_ptr(), pos_all[0].data_ptr(), B, 3)
-    sb = step_bytes(cfg, B, args.ctx)
+    sb = step_bytes(cfg, B, args.ctx, W)
     peak, peak_kind = peaks()
     gemv_classes = ("qkv", "o", "gate_up", "down", "lm_head")
     dom = max(gemv_classes, key=lambda k: prof[k][0])
@@ -377,7 +392,8 @@ def main():
     prof_ms = {k: round(v[0] / 3, 4) for k, v in prof.items()}
 
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if args.tp else "weak",
             "vs_baseline": None, "dtype": "int8 (Q4_K/Q6_K weights x Q8_K activations, int8 MMA, f32/f64 combine)",
             "data": "synthetic (random-init weights and KV, seeded)", "config": workload_config(args),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
@@ -394,7 +410,7 @@ def main():
     clocks = clk.summary()
     if clocks:
         line["clocks"] = clocks
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.model == "qwen3-8b":
         model.close()
         torch.cuda.empty_cache()
         tps, n, cores = cpu_oracle_decode(cfg, args.ctx, 1, budget_s=20.0, max_tokens=8)
@@ -404,6 +420,10 @@ def main():
                                           f"quantized path) on all host threads"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    model.close()
+    if comm:
+        pg.barrier()  # no rank unmaps its region while a peer still steps
+        comm.close()
     if pg:
         pg.destroy_process_group()
 
