@@ -11,15 +11,18 @@
 // scale is applied in the epilogue.
 //
 // B200 design (tensor-bound: 2 T N K flops):
-//  * one CTA per 128 x 128 output tile (cta_group::1, M = 128 tokens, N = 128
-//    weight rows), 6 warps: warp 0 feeds the pipeline (TMA tensor loads of
+//  * one CTA per 256 x 128 output tile (256 tokens, 128 weight rows) as two
+//    cta_group::1 MMAs of M = 128 sharing each dequantized B slice, so the
+//    dequantization -- the CTA's CUDA-core work -- is amortized over 256
+//    token rows; 10 warps: warp 0 feeds the pipeline (TMA tensor loads of
 //    fp16 X tiles with 128-byte swizzle; cp.async.bulk of the tile-major
 //    weight records, one contiguous 16-row x 256-column record per copy),
-//    warp 1 allocates tensor memory and issues tcgen05.mma from one thread,
-//    warps 2..9 (two threads per weight row) dequantize each 64-column
-//    slice of the weight records into the K-major, 128-byte-swizzled fp16 B
-//    operand and then drain the f32 accumulator with tcgen05.ld;
-//  * 4 smem stages of (A 16 KB + B 16 KB) plus two record buffers;
+//    warp 1 allocates tensor memory (two 128-column f32 accumulators) and
+//    issues tcgen05.mma from one thread, warps 2..9 (two threads per weight
+//    row) dequantize each 64-column slice of the weight records into the
+//    K-major, 128-byte-swizzled fp16 B operand and then drain the
+//    accumulators with tcgen05.ld;
+//  * 3 smem stages of (A 32 KB + B 16 KB) plus two record buffers;
 //    mbarriers between the roles, every wait bounded (a timeout raises
 //    ERRBIT_WAIT_TIMEOUT and all roles stop).
 #include <cuda.h>
@@ -33,11 +36,13 @@
 
 namespace fb {
 
-constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;  // tile; K step = one 128-byte swizzle row of fp16
-constexpr int PF_STAGES = 4;
+constexpr int PF_BM = 256, PF_BN = 128, PF_BK = 64;  // tile; K step = one 128-byte swizzle row of fp16
+constexpr int PF_MH = 128;                            // rows of one MMA (accumulator half of the tile)
+constexpr int PF_STAGES = 3;
 constexpr int PF_DQ_WARPS = 8;                        // dequant / epilogue warps (two per weight row)
 constexpr int PF_THREADS = 64 + 32 * PF_DQ_WARPS;
-constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2, PF_B_BYTES = PF_BN * PF_BK * 2;  // 16 KB each
+constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2, PF_B_BYTES = PF_BN * PF_BK * 2;  // 32 KB, 16 KB
+constexpr uint32_t PF_TMEM_COLS = 2 * PF_BN;  // two f32 accumulators of 128 columns
 constexpr int PF_TILES_N = PF_BN / 16;                                              // weight row tiles per CTA
 
 template <int DT> struct PfRec;
@@ -65,7 +70,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 // kind::f16 instruction descriptor: A = B = fp16, D = f32, both K-major,
 // M = 128, N = 128
 constexpr uint32_t PF_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(PF_BN >> 3) << 17) |
-                              ((uint32_t)(PF_BM >> 4) << 24);
+                              ((uint32_t)(PF_MH >> 4) << 24);
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
     asm volatile(
@@ -172,7 +177,7 @@ __device__ __forceinline__ void dequant_slice_q6k(const uint8_t *rec, int r, int
     }
 }
 
-// grid (N / 128, ceil(T / 128)), PF_THREADS threads.
+// grid (N / 128, ceil(T / 256)), PF_THREADS threads.
 template <int DT>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t nb, int T,
@@ -205,9 +210,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         s_abort = 0;
     }
     if (warp == 1) {
-        // 128 f32 accumulator columns (one per output column) x 128 lanes (rows)
+        // two accumulators (token rows m0.. and m0+128..) of 128 f32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(PF_BN)
+                     "r"(PF_TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -254,9 +259,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_BK / 16; kk++) {
-                    const uint64_t da = umma_desc_sw128(aBase + st * PF_A_BYTES + kk * 32);
                     const uint64_t db = umma_desc_sw128(bBase + st * PF_B_BYTES + kk * 32);
-                    umma_f16(tmem, da, db, (s > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {  // token rows 128h .. 128h + 127 of the tile
+                        const uint64_t da = umma_desc_sw128(aBase + st * PF_A_BYTES + h * (PF_MH * 128) + kk * 32);
+                        umma_f16(tmem + h * PF_BN, da, db, (s > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 umma_commit(&empty[st]);  // frees the stage once these MMAs have read it
             }
@@ -298,13 +306,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         if (!s_abort && mbar_wait_bounded(&acc_full, 0)) {
             tc_fence_after();
             const int q = warp & 3;                  // TMEM lane quarter of this warp
-            const int ch0 = (warp - 2) >> 2;         // column half: warps 2..5 -> 0, 6..9 -> 1
-            const int orow = m0 + 32 * q + lane;
+            const int h = (warp - 2) >> 2;           // accumulator: warps 2..5 -> rows 0..127, 6..9 -> 128..255
+            const int orow = m0 + PF_MH * h + 32 * q + lane;
             const float sc = orow < T ? rowscale[orow] : 0.f;
 #pragma unroll 1
-            for (int cc = 2 * ch0; cc < 2 * ch0 + 2; cc++) {
+            for (int cc = 0; cc < PF_BN / 32; cc++) {
                 uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + h * PF_BN + 32 * cc, v);
                 if (orow < T) {
                     float *dst = Y + (int64_t)orow * N + (int64_t)n_tile * PF_BN + 32 * cc;
 #pragma unroll
@@ -324,7 +332,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     if (s_abort && threadIdx.x == 0) atomicOr(err, ERRBIT_WAIT_TIMEOUT);
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS)
+                     : "memory");
     }
     pdl_launch();
 }
