@@ -147,6 +147,8 @@ void launch_synth_f32(fb_ctx *ctx, float *out, int64_t n, uint64_t seed, float m
 void launch_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out, int out_dtype);
 // y[m, n] (+)= x.W^T for m <= 16 from pre-quantized activations.
 void launch_gemv(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy);
+// y[n] = W . x for one f32 row with the f32 dequantized weights (float form).
+void launch_gemv_float(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y);
 // m > 16 QMatMul (prefill form).
 void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m);
 // Tensor-core prefill QMatMul (fp16 operands, f32 accumulation): m >= 17 rows,
@@ -172,6 +174,24 @@ void launch_argmax(fb_ctx *ctx, const float *logits, int rows, int64_t vocab, in
 void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, int nkv, int hd, int page_size,
                      const int32_t *block_table, int max_pages, int slots, uint64_t seed, float scale,
                      int kv_head0 = 0);
+
+// Batched prefill (ops.cu, prefill_attn.cu): T token rows, f32 activations.
+void launch_embed_rows(fb_ctx *ctx, const fb_qtensor *emb, const int32_t *tokens, int T, int vocab, int dim,
+                       float *x);
+// x += y (y may be null), xn = RMSNorm(x) * g, row by row
+void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float *g, float *xn, int T, int dim,
+                             float eps);
+void launch_swiglu_rows(fb_ctx *ctx, const float *y, int f, int T, float *act);
+void launch_prefill_qkv_rope(fb_ctx *ctx, const float *y, int64_t ld, int T, int pos0, int n_heads, int n_kv,
+                             const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
+                             const float *rope_sin, int rope_mode, float *q_out, void *kpool, void *vpool,
+                             const int32_t *bt, int page_size, int num_pages);
+// Causal attention of T queries (positions pos0 .. pos0 + T - 1, q f32
+// [T][n_heads][128]) over one sequence's paged fp16 KV cache (64-token
+// pages, dim-major K); out f32 [T][n_heads][128].
+void launch_attn_prefill(fb_ctx *ctx, const float *q, const void *kpool, const void *vpool, const int32_t *bt,
+                         int max_pages, int num_pages, int pos0, int T, int n_heads, int n_kv, float scale,
+                         float *out);
 
 // Paged flash-decode attention (attention.cu).
 constexpr int ATT_SPLITS = 16;  // attention splits (cluster CTAs) per (kv head, sequence)

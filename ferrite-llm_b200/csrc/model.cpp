@@ -24,6 +24,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <string>
@@ -105,6 +106,9 @@ struct fb_model {
     std::map<int, cudaGraphExec_t> graphs;
     int len0 = 0;  // tokens held by sequence slot 0 (forward / prefill API)
     int launches_per_step = 0;
+    // batched prefill buffers (allocated on first use, rows = pf_cap)
+    DevBuf pf_tok, pf_x, pf_xn, pf_yd, pf_yqkv, pf_q, pf_attn, pf_ygu, pf_act;
+    int pf_cap = 0;
 
     size_t kv_half_layer() const { return (size_t)num_pages * lc.n_kv_heads * kPage * c.head_dim; }
     __half *kpool(int l) const { return kv.as<__half>() + (size_t)l * 2 * kv_half_layer(); }
@@ -711,6 +715,83 @@ int fb_model_decode_greedy(fb_model *m, const int32_t *tokens_host, const int32_
     });
 }
 
+}  // extern "C"
+
+// Batched prefill of slot 0 (prompt tokens at positions pos0 .. pos0 + T - 1):
+// the projections run as tensor-core GEMMs over all T rows (the float form
+// candle's CUDA QMatMul uses for more than 8 rows), the attention as one
+// causal prefill kernel per layer, and the last row's lm_head in float as
+// well (dequantized weights, binary64 accumulation): an integer lm_head
+// would re-quantize the last hidden row to 8 bits and turn the prompt
+// pass's 16-bit-operand differences into ~20x larger logit differences.
+static constexpr int kPrefillRows = 2048;   // rows per chunk
+static constexpr int kPrefillMinRows = 17;  // shorter prompts go token by token
+
+static void ensure_prefill(fb_model *m, int T) {
+    if (m->pf_cap >= T) return;
+    const fb_model_config &c = m->c, &lc = m->lc;
+    const size_t H = c.hidden, qd = (size_t)lc.n_heads * c.head_dim, kd = (size_t)lc.n_kv_heads * c.head_dim;
+    m->pf_tok.alloc((size_t)T * 4);
+    m->pf_x.alloc((size_t)T * H * 4);
+    m->pf_xn.alloc((size_t)T * H * 4);
+    m->pf_yd.alloc((size_t)T * H * 4);
+    m->pf_yqkv.alloc((size_t)T * (qd + 2 * kd) * 4);
+    m->pf_q.alloc((size_t)T * qd * 4);
+    m->pf_attn.alloc((size_t)T * qd * 4);
+    m->pf_ygu.alloc((size_t)T * 2 * lc.ffn * 4);
+    m->pf_act.alloc((size_t)T * lc.ffn * 4);
+    m->pf_cap = T;
+}
+
+static void prefill_chunk(fb_model *m, int T, int pos0) {
+    fb_ctx *ctx = m->ctx;
+    const fb_model_config &c = m->c, &lc = m->lc;
+    const int H = c.hidden, qd = lc.n_heads * c.head_dim, kd = lc.n_kv_heads * c.head_dim, F = lc.ffn;
+    float *x = m->pf_x.as<float>(), *xn = m->pf_xn.as<float>(), *yd = m->pf_yd.as<float>();
+    const int32_t *bt = m->block_table.as<int32_t>();  // slot 0's row
+    const float scale = (float)(1.0 / sqrt((double)c.head_dim));
+    launch_embed_rows(ctx, m->tok_embd.t, m->pf_tok.as<int32_t>(), T, c.vocab, H, x);
+    for (int l = 0; l < c.n_layers; l++) {
+        Layer &L = *m->layers[l];
+        // x += down projection of the previous layer; xn = attn_norm(x)
+        launch_add_rmsnorm_rows(ctx, x, l ? yd : nullptr, L.attn_norm.as<float>(), xn, T, H, c.eps);
+        qmatmul_prefill(ctx, L.wqkv.t, xn, m->pf_yqkv.as<float>(), T);
+        launch_prefill_qkv_rope(ctx, m->pf_yqkv.as<float>(), qd + 2 * kd, T, pos0, lc.n_heads, lc.n_kv_heads,
+                                c.qk_norm ? L.q_norm.as<float>() : nullptr,
+                                c.qk_norm ? L.k_norm.as<float>() : nullptr, c.eps, m->rope_cos.as<float>(),
+                                m->rope_sin.as<float>(), c.rope_mode, m->pf_q.as<float>(), m->kpool(l), m->vpool(l),
+                                bt, kPage, m->num_pages);
+        launch_attn_prefill(ctx, m->pf_q.as<float>(), m->kpool(l), m->vpool(l), bt, m->pages_per_seq, m->num_pages,
+                            pos0, T, lc.n_heads, lc.n_kv_heads, scale, m->pf_attn.as<float>());
+        qmatmul_prefill(ctx, L.wo.t, m->pf_attn.as<float>(), yd, T);
+        launch_add_rmsnorm_rows(ctx, x, yd, L.ffn_norm.as<float>(), xn, T, H, c.eps);
+        qmatmul_prefill(ctx, L.wgu.t, xn, m->pf_ygu.as<float>(), T);
+        launch_swiglu_rows(ctx, m->pf_ygu.as<float>(), F, T, m->pf_act.as<float>());
+        qmatmul_prefill(ctx, L.wdown.t, m->pf_act.as<float>(), yd, T);
+    }
+    // last row: x + down, final RMSNorm, float lm_head, argmax
+    float *xl = x + (size_t)(T - 1) * H, *xnl = xn + (size_t)(T - 1) * H;
+    launch_add_rmsnorm_rows(ctx, xl, yd + (size_t)(T - 1) * H, m->out_norm.as<float>(), xnl, 1, H, c.eps);
+    FB_CUDA(cudaMemcpyAsync(m->x.ptr, xl, (size_t)H * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    m->x_last = m->x.as<float>();
+    launch_gemv_float(ctx, m->output.t, xnl, m->logits.as<float>());
+    launch_argmax(ctx, m->logits.as<float>(), 1, lc.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
+}
+
+static void prefill_batched(fb_model *m, const int32_t *tokens_host, int n, int pos) {
+    cudaStream_t s = m->ctx->stream;
+    for (int done = 0; done < n;) {
+        const int T = std::min(kPrefillRows, n - done);
+        ensure_prefill(m, std::min(kPrefillRows, n));
+        FB_CUDA(cudaMemcpyAsync(m->pf_tok.ptr, tokens_host + done, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+        prefill_chunk(m, T, pos + done);
+        FB_CUDA(cudaStreamSynchronize(s));  // host tokens are pageable: keep them alive until copied
+        done += T;
+    }
+}
+
+extern "C" {
+
 int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos, float *logits_host) {
     return guarded([&] {
         FB_REQUIRE(m && tokens_host, "null argument");
@@ -720,6 +801,16 @@ int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos, fl
         for (int i = 0; i < n; i++)
             FB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->c.vocab, "token id out of range");
         cudaStream_t s = m->ctx->stream;
+        if (n >= kPrefillMinRows && !m->comm) {
+            prefill_batched(m, tokens_host, n, pos);
+            m->len0 = pos + n;
+            if (logits_host)
+                FB_CUDA(cudaMemcpyAsync(logits_host, m->logits.ptr, (size_t)m->lc.vocab * 4, cudaMemcpyDeviceToHost,
+                                        s));
+            FB_CUDA(cudaStreamSynchronize(s));
+            check_no_device_error(m);
+            return;
+        }
         // token by token through the decode step (causal by construction)
         for (int i = 0; i < n; i++) {
             m->pinned[0] = tokens_host[i];
@@ -882,6 +973,18 @@ int fb_model_read_activation(fb_model *m, const char *name, int row, float *out_
 }
 
 // ---------------------------------------------------------------------------
+int fb_attn_prefill(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, const void *v_pages_dev,
+                    const int32_t *block_table_dev, int max_pages, int num_pages, int pos0, int n_tokens,
+                    int n_heads, int n_kv_heads, int head_dim, int page_size, float scale, float *out_dev) {
+    return guarded([&] {
+        FB_REQUIRE(ctx && q_dev && k_pages_dev && v_pages_dev && block_table_dev && out_dev, "null argument");
+        FB_REQUIRE(head_dim == 128 && page_size == 64, "prefill attention: head_dim 128, page_size 64");
+        FB_REQUIRE(n_tokens >= 1 && n_heads >= 1 && n_kv_heads >= 1 && num_pages >= 1, "bad shape");
+        launch_attn_prefill(ctx, q_dev, k_pages_dev, v_pages_dev, block_table_dev, max_pages, num_pages, pos0,
+                            n_tokens, n_heads, n_kv_heads, scale, out_dev);
+    });
+}
+
 int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, const void *v_pages_dev,
                    const int32_t *block_table_dev, const int32_t *seq_lens_dev, float *out_dev, int batch,
                    int n_heads, int n_kv_heads, int head_dim, int page_size, int max_pages, int max_seq_len,

@@ -418,6 +418,133 @@ __global__ void __launch_bounds__(256) k_argmax(const float *__restrict__ logits
 }
 
 // ------------------------------------------------------------------------
+// Batched prefill (T token rows at once, f32 in and out; the projections run
+// on the tensor cores in between).
+//
+// x[t] = dequantized embedding row of tokens[t]; one CTA per row.
+__global__ void __launch_bounds__(256) k_embed_rows(const uint8_t *__restrict__ emb, const int32_t *__restrict__ tokens,
+                                                    int vocab, int dim, float *__restrict__ x, uint32_t *err) {
+    const int64_t row = blockIdx.x;
+    int tok = tokens[row];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
+        tok = 0;
+    }
+    const int nbe = dim / QK;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        x[row * dim + i] = q4k_value(emb + q4k_offset(tok, i / QK, nbe), i % QK);
+}
+
+// x[t] (+= y[t] when y != null), xn[t] = RMSNorm(x[t]) * g: the decode
+// step's residual + RMSNorm arithmetic (binary64 sum of squares), without
+// the Q8_K quantization.  One CTA per row.
+__global__ void __launch_bounds__(256) k_add_rmsnorm_rows(float *__restrict__ x, const float *__restrict__ y,
+                                                          const float *__restrict__ g, float *__restrict__ xn, int dim,
+                                                          float eps) {
+    __shared__ double sh[8];
+    const int64_t row = blockIdx.x;
+    float *xr = x + row * dim;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        float v = xr[i];
+        if (y) {
+            v = __fadd_rn(y[row * dim + i], v);
+            xr[i] = v;
+        }
+        ss = __fma_rn((double)v, (double)v, ss);
+    }
+    ss = block_sum64<8>(ss, sh);
+    const float m = rms_of(ss, dim, eps);
+    for (int i = threadIdx.x; i < dim; i += 256) xn[row * dim + i] = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
+}
+
+// act[t][i] = silu(gate) * up for the rows y[t] = [gate (f) | up (f)].
+__global__ void __launch_bounds__(256) k_swiglu_rows(const float *__restrict__ y, int f, int64_t rows,
+                                                     float *__restrict__ act) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * f) return;
+    const int64_t r = i / f, c = i % f;
+    act[i] = __fmul_rn(silu64(y[r * 2 * f + c]), y[r * 2 * f + f + c]);
+}
+
+// Prefill prologue of attention for T new tokens at positions pos0 + t: one
+// warp per (token, head) of the projection output y[t] = (q | k | v): QK
+// RMSNorm (optional) and RoPE of q (-> q_out f32 [T][n_heads][hd]) and k,
+// and the fp16 KV-cache write of k (dim-major pages) and v (token-major) --
+// the decode attention prologue's arithmetic, token by token.
+__global__ void __launch_bounds__(256) k_prefill_qkv_rope(const float *__restrict__ y, int64_t ld, int T, int pos0,
+                                                          int n_heads, int n_kv, const float *__restrict__ q_norm,
+                                                          const float *__restrict__ k_norm, float eps,
+                                                          const float *__restrict__ rope_cos,
+                                                          const float *__restrict__ rope_sin, int rope_mode,
+                                                          float *__restrict__ q_out, __half *__restrict__ kpool,
+                                                          __half *__restrict__ vpool, const int32_t *__restrict__ bt,
+                                                          int page_size, int num_pages, uint32_t *err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nh = n_heads + 2 * n_kv;
+    if (wid >= (int64_t)T * nh) return;
+    const int t = (int)(wid / nh), hh = (int)(wid % nh);
+    const int p = pos0 + t;
+    const bool is_q = hh < n_heads, is_k = !is_q && hh < n_heads + n_kv;
+    const float4 x4 = *reinterpret_cast<const float4 *>(y + (int64_t)t * ld + (int64_t)hh * 128 + 4 * lane);
+    float v[4] = {x4.x, x4.y, x4.z, x4.w};
+    if (is_q || is_k) {
+        const QkHead qh = qk_head_load(lane, q_norm ? (is_q ? q_norm : k_norm) : nullptr, rope_cos + (int64_t)p * 64,
+                                       rope_sin + (int64_t)p * 64, rope_mode);
+        qk_head_apply(v, lane, qh, eps, rope_mode);
+    }
+    if (is_q) {
+        *reinterpret_cast<float4 *>(q_out + ((int64_t)t * n_heads + hh) * 128 + 4 * lane) =
+            make_float4(v[0], v[1], v[2], v[3]);
+        return;
+    }
+    const int kvh = is_k ? hh - n_heads : hh - n_heads - n_kv;
+    const int page = bt[p / page_size], slot = p % page_size;
+    if (page < 0 || page >= num_pages) {
+        if (lane == 0) atomicOr(err, ERRBIT_BAD_PAGE);
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int d = 4 * lane + e;
+        const __half h = __float2half_rn(v[e]);
+        if (is_k) kpool[(((size_t)page * n_kv + kvh) * 128 + d) * page_size + slot] = h;
+        else vpool[(((size_t)page * n_kv + kvh) * page_size + slot) * 128 + d] = h;
+    }
+}
+
+void launch_embed_rows(fb_ctx *ctx, const fb_qtensor *emb, const int32_t *tokens, int T, int vocab, int dim,
+                       float *x) {
+    FB_REQUIRE(emb->dtype == FB_Q4_K && emb->k == dim, "embedding table must be Q4_K [vocab, hidden]");
+    k_embed_rows<<<T, 256, 0, ctx->stream>>>(emb->main(), tokens, vocab, dim, x, ctx->err_word);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float *g, float *xn, int T, int dim,
+                             float eps) {
+    k_add_rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(x, y, g, xn, dim, eps);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_swiglu_rows(fb_ctx *ctx, const float *y, int f, int T, float *act) {
+    const int64_t n = (int64_t)T * f;
+    k_swiglu_rows<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(y, f, T, act);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_prefill_qkv_rope(fb_ctx *ctx, const float *y, int64_t ld, int T, int pos0, int n_heads, int n_kv,
+                             const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
+                             const float *rope_sin, int rope_mode, float *q_out, void *kpool, void *vpool,
+                             const int32_t *bt, int page_size, int num_pages) {
+    const int64_t warps = (int64_t)T * (n_heads + 2 * n_kv);
+    k_prefill_qkv_rope<<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(
+        y, ld, T, pos0, n_heads, n_kv, q_norm, k_norm, eps, rope_cos, rope_sin, rope_mode, q_out, (__half *)kpool,
+        (__half *)vpool, bt, page_size, num_pages, ctx->err_word);
+    FB_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------
 // Standalone ops for the C ABI.
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ g, float *__restrict__ y, int64_t dim,
                           float eps) {

@@ -381,13 +381,11 @@ template <> __device__ __forceinline__ float cvt_out<float>(float v) { return v;
 template <> __device__ __forceinline__ __half cvt_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
-template <typename T>
-__global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
-                                                     T *__restrict__ y) {
-    const int lane = threadIdx.x & 31;
-    const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (b >= nblocks) return;
-    const uint8_t *blk = w + q4k_offset(b / nb, b % nb, nb);
+// Values 8 lane .. 8 lane + 7 of super-block b of row `row` (f32, exact
+// candle `to_float` arithmetic).
+__device__ __forceinline__ void dq8_q4k(const uint8_t *__restrict__ w, int64_t row, int64_t b, int64_t nb, int lane,
+                                        float (&v)[8]) {
+    const uint8_t *blk = w + q4k_offset(row, b, nb);
     const uint32_t *hw = reinterpret_cast<const uint32_t *>(blk);
     Q4Scales s = q4k_unpack_scales(hw[1], hw[2], hw[3]);
     const float d = h2f((uint16_t)(hw[0] & 0xFFFF)), dmin = h2f((uint16_t)(hw[0] >> 16));
@@ -399,24 +397,18 @@ __global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__
     const int mn = byte_of(j < 4 ? s.mn_lo : s.mn_hi, j & 3);
     const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
     const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * g);
-    T *out = y + b * QK + 8 * lane;
 #pragma unroll
     for (int e = 0; e < 8; e++) {
         uint32_t word = e < 4 ? q.x : q.y;
         int nib = (int)((word >> (8 * (e & 3) + 4 * hi)) & 0xF);
-        out[e] = cvt_out<T>(__fsub_rn(__fmul_rn(d1, (float)nib), m1));
+        v[e] = __fsub_rn(__fmul_rn(d1, (float)nib), m1);
     }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
-                                                     T *__restrict__ y) {
-    const int lane = threadIdx.x & 31;
-    const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (b >= nblocks) return;
-    const uint32_t *blk = reinterpret_cast<const uint32_t *>(w + q6k_offset(b / nb, b % nb, nb));
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(w + q6k_d_offset(b / nb, b % nb, nb)));
-    T *out = y + b * QK + 8 * lane;
+__device__ __forceinline__ void dq8_q6k(const uint8_t *__restrict__ w, int64_t row, int64_t b, int64_t nb, int lane,
+                                        float (&v)[8]) {
+    const uint32_t *blk = reinterpret_cast<const uint32_t *>(w + q6k_offset(row, b, nb));
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(w + q6k_d_offset(row, b, nb)));
 #pragma unroll
     for (int e = 0; e < 8; e++) {
         const int i = 8 * lane + e;
@@ -427,8 +419,67 @@ __global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__
         const int lo = (int)((qlw >> (8 * e4 + 4 * (p >> 1))) & 0xF);
         const int hi2 = (int)((qhw >> (8 * e4 + 2 * p)) & 0x3);
         const int sc = sbyte_of(blk[48 + (i >> 6)], (i >> 4) & 3);
-        out[e] = cvt_out<T>(__fmul_rn(__fmul_rn(d, (float)sc), (float)((lo | (hi2 << 4)) - 32)));
+        v[e] = __fmul_rn(__fmul_rn(d, (float)sc), (float)((lo | (hi2 << 4)) - 32));
     }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_dequant_q4k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
+                                                     T *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= nblocks) return;
+    float v[8];
+    dq8_q4k(w, b / nb, b % nb, nb, lane, v);
+    T *out = y + b * QK + 8 * lane;
+#pragma unroll
+    for (int e = 0; e < 8; e++) out[e] = cvt_out<T>(v[e]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_dequant_q6k(const uint8_t *__restrict__ w, int64_t nblocks, int64_t nb,
+                                                     T *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= nblocks) return;
+    float v[8];
+    dq8_q6k(w, b / nb, b % nb, nb, lane, v);
+    T *out = y + b * QK + 8 * lane;
+#pragma unroll
+    for (int e = 0; e < 8; e++) out[e] = cvt_out<T>(v[e]);
+}
+
+// y[r] = f32(sum_i W[r, i] * x[i]) with the f32 dequantized weights and a
+// binary64 accumulation: the float form of QMatMul for one activation row
+// (candle's dequantize + float matmul; the oracle's or_qmatmul_f32).  One
+// warp per weight row.
+template <int DT>
+__global__ void __launch_bounds__(256) k_gemv_float(const uint8_t *__restrict__ w, int64_t n, int64_t nb,
+                                                    const float *__restrict__ x, float *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= n) return;
+    double acc = 0.0;
+    for (int64_t b = 0; b < nb; b++) {
+        float v[8];
+        if constexpr (DT == 4) dq8_q4k(w, r, b, nb, lane, v);
+        else dq8_q6k(w, r, b, nb, lane, v);
+        const float4 x0 = *reinterpret_cast<const float4 *>(x + b * QK + 8 * lane);
+        const float4 x1 = *reinterpret_cast<const float4 *>(x + b * QK + 8 * lane + 4);
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc = __fma_rn((double)v[e], (double)xv[e], acc);
+    }
+    acc = warp_sum64(acc);
+    if (lane == 0) y[r] = __double2float_rn(acc);
+}
+
+void launch_gemv_float(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y) {
+    const unsigned grid = (unsigned)((w->n + 7) / 8);
+    if (w->dtype == FB_Q4_K) k_gemv_float<4><<<grid, 256, 0, ctx->stream>>>(w->main(), w->n, w->nb(), x, y);
+    else if (w->dtype == FB_Q6_K) k_gemv_float<6><<<grid, 256, 0, ctx->stream>>>(w->main(), w->n, w->nb(), x, y);
+    else fail(FB_ERR_INVALID, "gemv_float: weight dtype must be Q4_K or Q6_K");
+    FB_CUDA(cudaGetLastError());
 }
 
 void launch_dequantize(fb_ctx *ctx, const fb_qtensor *t, void *out, int out_dtype) {

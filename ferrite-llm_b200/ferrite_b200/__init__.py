@@ -39,7 +39,7 @@ EXPORTED = (
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
-    "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms",
+    "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -123,6 +123,7 @@ def _declare(L):
         "fb_comm_open": (i32, [vp, vp]),
         "fb_comm_destroy": (i32, [vp]),
         "fb_comm_set_timeout_ms": (i32, [vp, i32]),
+        "fb_attn_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, vp]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -276,6 +277,12 @@ def attn_decode(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, ba
                 page_size, max_pages, max_seq_len, scale):
     _check(lib().fb_attn_decode(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
                                 head_dim, page_size, max_pages, max_seq_len, scale))
+
+
+def attn_prefill(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, max_pages, num_pages, pos0, n_tokens, n_heads, n_kv,
+                 head_dim, page_size, scale, out_ptr):
+    _check(lib().fb_attn_prefill(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, max_pages, num_pages, pos0, n_tokens, n_heads,
+                                 n_kv, head_dim, page_size, scale, out_ptr))
 
 
 def attn_decode_noalloc(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,

@@ -164,6 +164,20 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
                    int n_heads, int n_kv_heads, int head_dim, int page_size,
                    int max_pages, int max_seq_len, float scale);
 
+/* Causal attention of a prompt chunk: n_tokens queries q_dev [n_tokens]
+ * [n_heads][128] at positions pos0 .. pos0 + n_tokens - 1 of one sequence
+ * (block_table_dev: its max_pages page ids) over the cache pages, which must
+ * already hold positions 0 .. pos0 + n_tokens - 1 (K dim-major, V
+ * token-major, page_size 64); out_dev [n_tokens][n_heads][128] f32.
+ * Tensor cores (fp16 operands with q and the probabilities split into two
+ * fp16 parts, f32 accumulation).  Replaces the prompt pass of candle's
+ * quantized_llama attention (adapter.rs:61-70 with all prompt tokens). */
+int fb_attn_prefill(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
+                    const void *v_pages_dev, const int32_t *block_table_dev,
+                    int max_pages, int num_pages, int pos0, int n_tokens,
+                    int n_heads, int n_kv_heads, int head_dim, int page_size,
+                    float scale, float *out_dev);
+
 /* Same computation and arguments as fb_attn_decode, for callers that cannot
  * allocate device memory: no reference counterpart (the reference's candle
  * path allocates freely).  fb_attn_decode may grow a workspace with
@@ -210,7 +224,11 @@ int fb_model_synth(fb_model *m, uint64_t seed);
 /* Must be called after all tensors are set (fuses QKV and gate/up). */
 int fb_model_finalize(fb_model *m);
 /* InferenceModel::forward for one sequence: tokens_host[n] at positions
- * pos..pos+n-1; logits of the last token -> logits_host[vocab] (may be NULL). */
+ * pos..pos+n-1; logits of the last token -> logits_host[vocab] (may be NULL).
+ * n >= 17 (single GPU) runs as a batched prefill: the projections as
+ * tensor-core GEMMs over chunks of up to 2048 rows, causal prefill attention,
+ * then the last row through the decode step's final norm, lm_head and argmax;
+ * shorter inputs (and tensor-parallel models) go token by token. */
 int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos,
                      float *logits_host);
 /* Greedy decode step for a batch: tokens_host[b] at positions pos_host[b]

@@ -260,6 +260,10 @@ static int nthreads_of(const or_model *m) {
 
 static void linear(const or_model *m, const or_tensor *w, const float *x,
                    int64_t rows, float *y, int mode) {
+    /* mode 2: candle 0.8.4's CUDA QMatMul dispatch -- more than 8 activation
+     * rows dequantize the weights and run a float matmul, up to 8 rows take
+     * the quantized-activation integer path. */
+    if (mode == 2) mode = rows > 8 ? 1 : 0;
     if (w->dtype == OR_F32) {
         const float *wf = (const float *)w->data;
         int nt = nthreads_of(m);

@@ -153,7 +153,8 @@ void or_model_clear(or_model *m);
 /* Runs tokens[0..n) at positions pos..pos+n-1 (causal), appending to the KV
  * cache.  logits: [n, vocab] when all_logits, else [vocab] for the last token.
  * matmul_mode 0 = Q8_K integer path (decode), 1 = dequantize + f32 matmul
- * (prefill form).  Returns 0 on success. */
+ * (prefill form), 2 = per call by row count as candle's CUDA QMatMul
+ * dispatches (> 8 rows float, else integer).  Returns 0 on success. */
 int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
                      float *logits, int all_logits, int matmul_mode);
 /* Fill the first ctx KV positions of every layer with synthetic values
