@@ -250,6 +250,83 @@ def run_prefill_gemm(args):
     print(json.dumps(line), flush=True)
 
 
+def prefill_flops(cfg: dict, T: int) -> float:
+    """FLOPs of a T-token prompt pass: the projections (2 T per weight), the
+    causal attention (q.k and p.v over T (T + 1) / 2 query-key pairs per
+    head) and the last row's lm_head."""
+    H, F, L = cfg["hidden"], cfg["ffn"], cfg["n_layers"]
+    qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    lin = 2.0 * T * L * (H * (qd + 2 * kd) + qd * H + 2 * F * H + F * H)
+    att = 4.0 * L * cfg["n_heads"] * cfg["head_dim"] * T * (T + 1) / 2
+    return lin + att + 2.0 * H * cfg["vocab"]
+
+
+def run_prefill(args, cfg):
+    """Prompt pass of T uniform random token ids (seed 2) through the public
+    API fb_model_forward (batched prefill: tensor-core projections and
+    attention), then 64 greedy decode steps (fb_model_decode_greedy)."""
+    import numpy as np
+    import torch
+
+    import ferrite_b200 as fb
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    ctx = fb.Context(0, stream.cuda_stream)
+    T, ndec = args.prefill, 64
+    model = fb.Model(ctx, dict(cfg, max_ctx=T + ndec + 8, max_batch=1))
+    model.synth(SEED)
+    model.finalize()
+    prompt = np.random.default_rng(2).integers(0, cfg["vocab"], T).astype(np.int32)
+    for _ in range(args.warmup):
+        model.clear_cache()
+        model.forward(prompt, 0)
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            model.clear_cache()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            logits = model.forward(prompt, 0)  # host tokens in, host logits out
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        tok = int(np.argmax(logits))
+        t0 = time.perf_counter()
+        toks = []
+        for i in range(ndec):
+            tok = int(model.decode_greedy([tok], [T + i])[0])
+            toks.append(tok)
+        dec_s = time.perf_counter() - t0
+    fl = prefill_flops(cfg, T)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    achieved = fl / (ms * 1e-3) / 1e12
+    line = {"metric": f"prefill tok/s ({T}-token prompt, then {ndec} greedy decode steps)", "value": T / (ms * 1e-3),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 x fp16 -> f32 (tensor cores) for the prompt; int8 Q8_K for decode",
+            "data": "synthetic (random-init weights, uniform random prompt ids, seed 2)",
+            "config": {"workload": f"{args.model}-arch Q4_K_M random-init prefill of {T} tokens, batch 1, "
+                                   f"then {ndec} greedy decode steps", "prompt_tokens": T, "decode_steps": ndec},
+            "e2e": {"value": T / (ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4 * T,
+                    "d2h_bytes_per_step": 4 * cfg["vocab"]},
+            "decode_after_prefill_tok_s": ndec / dec_s,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops_per_step": fl, "peak_source": kind},
+            "error_word": ctx.error_word()}
+    clocks = clk.summary()
+    if clocks:
+        line["clocks"] = clocks
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def workload_config(args) -> dict:
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     par = f"tp{ws}" if args.tp else ("replicas" if ws > 1 else "single-gpu")
@@ -276,6 +353,8 @@ def main():
                     help="build the workload, run N untimed decode steps and exit (driver for ncu captures)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
     ap.add_argument("--tp", action="store_true", help="one tensor-parallel model over all ranks (strong scaling)")
+    ap.add_argument("--prefill", type=int, default=0, metavar="T",
+                    help="instead of decode: time a T-token prompt pass (then 64 greedy decode steps), 1 GPU")
     ap.add_argument("--prefill-gemm", type=int, default=0, metavar="T",
                     help="instead of decode: time one layer's prefill QMatMuls at T rows (1 GPU)")
     args = ap.parse_args()
@@ -287,6 +366,8 @@ def main():
         return run_reference(args, cfg)
     if args.prefill_gemm:
         return run_prefill_gemm(args)
+    if args.prefill:
+        return run_prefill(args, cfg)
 
     import numpy as np
     import torch
