@@ -414,6 +414,7 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     constexpr int NTA = DP4A ? 1 : NT;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bars[KS * 8];
+    __shared__ uint64_t actbar;
     __shared__ double red[KS * 16 * (C + 1)];
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -429,7 +430,13 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         for (int i = 0; i < DEPTH; i++) mbar_init(&wbar[i], 1);
         mbar_fence_init();
     }
-    if (threadIdx.x == 0) s_abort = 0;
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        if (DP4A) {
+            mbar_init(&actbar, 1);
+            mbar_fence_init();
+        }
+    }
     __syncthreads();
     int issued = 0;
     auto issue = [&](int c) {
@@ -445,31 +452,31 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     pdl_wait();
     pdl_launch();  // let the next kernel start streaming its weights
     Q8Act act = a;
+    bool ok = true;
     if constexpr (DP4A) {
-        // the activation rows are read by every record: keep them in shared memory
+        // the activation rows are read by every record: four bulk copies
+        // (one round trip) bring them into shared memory.  Regions are
+        // rounded up to 16 bytes; the global arrays are padded to 256 bytes
+        // (q8act_view), so the rounded copies stay inside them.
         const int64_t k = a.k;
-        // regions rounded up to 16 bytes; the global arrays are padded to 256
-        // bytes (q8act_view), so the rounded copies stay inside them
         const size_t bq = r16((size_t)M * k), bd = r16((size_t)M * (k / 256) * 4), b16 = r16((size_t)M * (k / 16) * 2),
                      b32 = r16((size_t)M * (k / 32) * 2);
         uint8_t *sq = smem;
         float *sd = reinterpret_cast<float *>(smem + bq);
         int16_t *s16 = reinterpret_cast<int16_t *>(smem + bq + bd);
         int16_t *s32 = reinterpret_cast<int16_t *>(smem + bq + bd + b16);
-        const int64_t nq = (int64_t)(bq / 16), nd = (int64_t)(bd / 16), n16 = (int64_t)(b16 / 16), n32 = (int64_t)(b32 / 16);
-        for (int64_t i = threadIdx.x; i < nq; i += blockDim.x)
-            reinterpret_cast<uint4 *>(sq)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.qs) + i);
-        for (int64_t i = threadIdx.x; i < nd; i += blockDim.x)
-            reinterpret_cast<uint4 *>(sd)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.d) + i);
-        for (int64_t i = threadIdx.x; i < n16; i += blockDim.x)
-            reinterpret_cast<uint4 *>(s16)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.bs16) + i);
-        for (int64_t i = threadIdx.x; i < n32; i += blockDim.x)
-            reinterpret_cast<uint4 *>(s32)[i] = ld_act16(reinterpret_cast<const uint4 *>(a.bs32) + i);
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&actbar, (uint32_t)(bq + bd + b16 + b32));
+            bulk_g2s(sq, a.qs, (uint32_t)bq, &actbar);
+            bulk_g2s(sd, a.d, (uint32_t)bd, &actbar);
+            bulk_g2s(s16, a.bs16, (uint32_t)b16, &actbar);
+            bulk_g2s(s32, a.bs32, (uint32_t)b32, &actbar);
+        }
+        ok = mbar_wait_bounded(&actbar, 0);
         act = Q8Act{reinterpret_cast<int8_t *>(sq), sd, s16, s32, k};
-        __syncthreads();
     }
-    bool ok = true;
-    int c = 0;
+    const bool act_ok = ok;
+    int c = 0, waited = 0;  // records visited / records whose copy has landed
     for (int ti = 0; ti < ntl; ti++) {
         const int64_t row0 = ((int64_t)blockIdx.x + (int64_t)ti * gridDim.x) * 16;
         double acc[NTA][4];
@@ -482,7 +489,10 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         for (int c2 = 0; c2 < M; c2++) accd[c2] = 0.0;
         for (int bl = 0; bl < nmine; bl++, c++) {
             const int slot = c % DEPTH;
-            if (ok) ok = mbar_wait_bounded(&wbar[slot], (uint32_t)(c / DEPTH) & 1u);
+            if (ok) {
+                ok = mbar_wait_bounded(&wbar[slot], (uint32_t)(c / DEPTH) & 1u);
+                if (ok) waited = c + 1;
+            }
             if (ok) {
                 const uint8_t *rec = ring + (size_t)slot * REC;
                 if constexpr (DP4A) {
@@ -544,7 +554,8 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     }
     if (!ok && lane == 0) {
         // let the copies still in flight land before shared memory is released
-        for (int k = c; k < issued; k++) mbar_wait_bounded(&wbar[k % DEPTH], (uint32_t)(k / DEPTH) & 1u);
+        for (int k = waited; k < issued; k++) mbar_wait_bounded(&wbar[k % DEPTH], (uint32_t)(k / DEPTH) & 1u);
+        if (DP4A && !act_ok && threadIdx.x == 0) mbar_wait_bounded(&actbar, 0);
     }
     if (po.world) __threadfence_system();  // peer stores performed before the grid completes
     pdl_launch();
