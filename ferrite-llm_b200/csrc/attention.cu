@@ -83,8 +83,8 @@ __host__ __device__ inline AttnLayout attn_layout(int G, int depth, int bt_cap) 
     off += part_bytes > o_bytes ? part_bytes : o_bytes;
     L.p = off;  // p[chunk][G] f64
     off += (size_t)ATT_CHUNK * G * 8;
-    L.misc = off;  // alpha[G] M[G] L[G] ls[warps] wts[G][S] wl[G][S] f64
-    off += (size_t)(3 * G + att_warps(G) + 2 * G * ATT_SPLITS) * 8;
+    L.misc = off;  // alpha[G] M[G] L[G] ls[warps] wts[G][S] wl[G][S] f64 (S up to ATT_SPLITS_MAX)
+    off += (size_t)(3 * G + att_warps(G) + 2 * G * ATT_SPLITS_MAX) * 8;
     L.inbox = off;  // cluster merge: [src rank][G][ATT_DPR + 2] f64 pushed by the peers
     off += (size_t)ATT_SPLITS * G * (ATT_DPR + 2) * 8;
     L.q8in = off;  // cluster merge: [2][hd] f32 outputs of one Q8_K block
@@ -103,7 +103,8 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// grid (ATT_SPLITS, n_kv, batch); CLUSTER: cluster dims (ATT_SPLITS, 1, 1).
+// grid (splits, n_kv, batch): CLUSTER: ATT_SPLITS splits, cluster dims
+// (ATT_SPLITS, 1, 1); otherwise A.nsplit (<= ATT_SPLITS_MAX) splits.
 //
 // Numerics (identical to the CPU oracle, or_attn_dot / or_exp64):
 //   s_t = f32 dot of q and k_t in eight 16-dim fused-multiply-add slices,
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
     __shared__ int s_len, s_first, s_mine, s_last;
     __shared__ __half s_newkv[2 * ATT_HD];  // fused prologue: the new token's k and v (fp16)
     constexpr int S = ATT_SPLITS;
+    const int ns = CLUSTER ? S : (int)gridDim.x;  // splits of this (kv head, sequence)
     constexpr int NW = att_warps(G), NT = 32 * NW;
     constexpr int TPC = ATT_CHUNK / NW;          // tokens per warp in the P.V phase
     constexpr int TPL = ATT_CHUNK * ATT_SLICES / NT;  // tokens per lane in the score phase (2 or 1)
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
     float *part = reinterpret_cast<float *>(smem + Ly.part);
     double *p_s = reinterpret_cast<double *>(smem + Ly.p);
     double *alpha_s = reinterpret_cast<double *>(smem + Ly.misc);
-    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + NW, *wl = wts + G * S;
+    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + NW, *wl = wts + G * ATT_SPLITS_MAX;
     double *inbox = reinterpret_cast<double *>(smem + Ly.inbox);
     float *q8in = reinterpret_cast<float *>(smem + Ly.q8in);
     int *bt_s = reinterpret_cast<int *>(smem + Ly.bt);
@@ -159,7 +161,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             len = 0;  // no work: the output of this sequence is zero
         }
         const int nch = (len + ATT_CHUNK - 1) / ATT_CHUNK;
-        const int cpr = (nch + S - 1) / S;  // chunks per rank
+        const int cpr = (nch + ns - 1) / ns;  // chunks per rank
         const int first = min(rank * cpr, nch);
         s_len = len;
         s_first = first;
@@ -478,15 +480,15 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             }
         }
     } else {
-        const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * S;
+        const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ns;
         __syncthreads();
         for (int i = tid; i < G * ATT_HD; i += NT) {
             const int g = i / ATT_HD, d = i % ATT_HD;
-            A.part_o[(hb0 + (int64_t)g * S + rank) * ATT_HD + d] = O_s[i];
+            A.part_o[(hb0 + (int64_t)g * ns + rank) * ATT_HD + d] = O_s[i];
         }
         if (tid < G) {
-            A.part_ml[2 * (hb0 + (int64_t)tid * S + rank)] = M_s[tid];
-            A.part_ml[2 * (hb0 + (int64_t)tid * S + rank) + 1] = L_s[tid];
+            A.part_ml[2 * (hb0 + (int64_t)tid * ns + rank)] = M_s[tid];
+            A.part_ml[2 * (hb0 + (int64_t)tid * ns + rank) + 1] = L_s[tid];
         }
         // the last CTA of this (kv head, sequence) merges
         __threadfence();
@@ -494,34 +496,51 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
         if (tid == 0) {
             int *cnt = counters + (int64_t)b * A.n_kv + kvh;
             const int prev = atomicAdd(cnt, 1);
-            s_last = prev == S - 1;
+            s_last = prev == ns - 1;
             if (s_last) *cnt = 0;  // ready for the next call
         }
         __syncthreads();
         if (s_last) {
             __threadfence();
-            if (tid < G * S) {
-                const int g = tid / S, r = tid % S;
-                const double Mr = __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * S + r)]);
-                const double Lr = __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * S + r) + 1]);
-                double M = Mr;
+            // warp g < G: split weights of head g (lane = splits r, r + 32)
+            if (warp < G) {
+                const int g = warp;
+                double Mr[ATT_SPLITS_MAX / 32], Lr[ATT_SPLITS_MAX / 32];
+                double M = -INFINITY;
 #pragma unroll
-                for (int off = S / 2; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(wmask, M, off));
-                const double w = Mr == -INFINITY ? 0.0 : exp64(__dsub_rn(Mr, M));
-                wts[tid] = w;
-                wl[tid] = __dmul_rn(w, Lr);
+                for (int k = 0; k < ATT_SPLITS_MAX / 32; k++) {
+                    const int r = lane + 32 * k;
+                    Mr[k] = r < ns ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * ns + r)]) : -INFINITY;
+                    Lr[k] = r < ns ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * ns + r) + 1]) : 0.0;
+                    M = fmax(M, Mr[k]);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(0xffffffffu, M, off));
+#pragma unroll
+                for (int k = 0; k < ATT_SPLITS_MAX / 32; k++) {
+                    const int r = lane + 32 * k;
+                    if (r < ns) {
+                        const double w = Mr[k] == -INFINITY ? 0.0 : exp64(__dsub_rn(Mr[k], M));
+                        wts[g * ATT_SPLITS_MAX + r] = w;
+                        wl[g * ATT_SPLITS_MAX + r] = __dmul_rn(w, Lr[k]);
+                    }
+                }
             }
             __syncthreads();
             for (int i = tid; i < G * ATT_HD; i += NT) {
                 const int g = i / ATT_HD, d = i % ATT_HD;
-                double Or[S];
-#pragma unroll
-                for (int r = 0; r < S; r++) Or[r] = __ldcg(&A.part_o[(hb0 + (int64_t)g * S + r) * ATT_HD + d]);
                 double L = 0.0, O = 0.0;
+                for (int r0 = 0; r0 < ns; r0 += 16) {  // 16 partial loads in flight, summed in split order
+                    double Or[16];
 #pragma unroll
-                for (int r = 0; r < S; r++) {
-                    L = __dadd_rn(L, wl[g * S + r]);
-                    O = __dadd_rn(O, __dmul_rn(wts[g * S + r], Or[r]));
+                    for (int k = 0; k < 16; k++)
+                        Or[k] = r0 + k < ns ? __ldcg(&A.part_o[(hb0 + (int64_t)g * ns + r0 + k) * ATT_HD + d]) : 0.0;
+#pragma unroll
+                    for (int k = 0; k < 16; k++)
+                        if (r0 + k < ns) {
+                            L = __dadd_rn(L, wl[g * ATT_SPLITS_MAX + r0 + k]);
+                            O = __dadd_rn(O, __dmul_rn(wts[g * ATT_SPLITS_MAX + r0 + k], Or[k]));
+                        }
                 }
                 const float val = L > 0.0 ? __double2float_rn(__ddiv_rn(O, L)) : 0.f;
                 if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
@@ -655,11 +674,20 @@ bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch) {
 }
 
 template <int G>
-static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, float *out_f32, const Q8Act *aq,
-                          int *counters, bool pdl, bool want_cluster) {
+static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_len, float *out_f32,
+                          const Q8Act *aq, int *counters, bool pdl, bool want_cluster) {
     int depth, bt_cap;
     size_t smem;
     const bool cluster = attn_plan<G>(ctx, A, batch, want_cluster, &depth, &bt_cap, &smem);
+    // cluster-free merge: more splits while the grid is under one wave (one
+    // CTA per SM) and every split still gets a chunk of the longest sequence
+    int ns = ATT_SPLITS;
+    if (!cluster) {
+        const int nch = (max_seq_len + ATT_CHUNK - 1) / ATT_CHUNK;
+        while (2 * ns <= A.nsplit_max && 2 * ns <= ATT_SPLITS_MAX && (int64_t)A.n_kv * batch * 2 * ns <= ctx->num_sms &&
+               2 * ns <= nch)
+            ns *= 2;
+    }
     FB_REQUIRE(cluster || (counters && A.part_o && A.part_ml), "attn: the cluster-free merge needs scratch");
     Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
     cudaLaunchConfig_t cfg = {};
@@ -672,7 +700,7 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, float *out_
     attr[1].val.clusterDim.x = ATT_SPLITS;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(ATT_SPLITS, A.n_kv, batch);
+    cfg.gridDim = dim3(cluster ? ATT_SPLITS : ns, A.n_kv, batch);
     cfg.blockDim = dim3(32 * att_warps(G));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
@@ -703,10 +731,10 @@ void launch_attn_decode(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq_l
     FB_REQUIRE(!aq || G % 2 == 0, "attn: fused Q8_K output needs an even GQA group");
     FB_REQUIRE(max_seq_len >= 1 && max_seq_len <= A.max_pages * A.page_size, "attn: max_seq_len exceeds the block table");
     switch (G) {
-        case 1: launch_attn_g<1>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
-        case 2: launch_attn_g<2>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
-        case 4: launch_attn_g<4>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
-        case 8: launch_attn_g<8>(ctx, A, batch, out_f32, aq, counters, pdl, want_cluster); break;
+        case 1: launch_attn_g<1>(ctx, A, batch, max_seq_len, out_f32, aq, counters, pdl, want_cluster); break;
+        case 2: launch_attn_g<2>(ctx, A, batch, max_seq_len, out_f32, aq, counters, pdl, want_cluster); break;
+        case 4: launch_attn_g<4>(ctx, A, batch, max_seq_len, out_f32, aq, counters, pdl, want_cluster); break;
+        case 8: launch_attn_g<8>(ctx, A, batch, max_seq_len, out_f32, aq, counters, pdl, want_cluster); break;
         default: fail(FB_ERR_INVALID, "attn: GQA group size must be 1, 2, 4 or 8");
     }
 }

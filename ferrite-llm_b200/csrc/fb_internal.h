@@ -194,7 +194,8 @@ void launch_attn_prefill(fb_ctx *ctx, const float *q, const void *kpool, const v
                          float *out);
 
 // Paged flash-decode attention (attention.cu).
-constexpr int ATT_SPLITS = 16;  // attention splits (cluster CTAs) per (kv head, sequence)
+constexpr int ATT_SPLITS = 16;      // attention splits (cluster CTAs) per (kv head, sequence)
+constexpr int ATT_SPLITS_MAX = 64;  // cluster-free merge: splits when the grid is small
 struct AttnArgs {
     const float *q;              // [b, n_heads, hd]
     const void *kpool;           // fp16 [num_pages, n_kv, hd, page] (dim-major pages)

@@ -91,6 +91,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // System-scope flag handoff between GPUs (tensor-parallel exchanges): the
 // writer's release store orders everything that happened before it (the
 // producer grid's peer stores included); the reader's acquire load orders

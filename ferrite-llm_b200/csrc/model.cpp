@@ -465,7 +465,7 @@ static void create_model(fb_ctx *ctx, const fb_model_config *cfg, fb_comm *comm,
     for (int l = 0; l < c.n_layers; l++) m->layers.push_back(std::make_unique<Layer>());
     m->pages_per_seq = (c.max_ctx + kPage - 1) / kPage;
     m->num_pages = m->pages_per_seq * c.max_batch;
-    m->nsplit_max = ATT_SPLITS;  // cluster-free attention merge (fallback) scratch
+    m->nsplit_max = ATT_SPLITS_MAX;  // cluster-free attention merge scratch (splits per kv head and sequence)
     m->kv.alloc(m->kv_half_layer() * 2 * c.n_layers * sizeof(__half));
     FB_CUDA(cudaMemsetAsync(m->kv.ptr, 0, m->kv.bytes, ctx->stream));
     std::vector<int32_t> bt((size_t)c.max_batch * m->pages_per_seq);

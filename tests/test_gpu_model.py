@@ -117,6 +117,23 @@ def test_synth_kv_then_decode(fbctx):
     assert_close(dm.forward([11], 300), om.forward([11], 300), what="decode at ctx 300")
 
 
+@pytest.mark.parametrize("n_kv,ctx", [(2, 1500), (1, 3000), (4, 2100)])
+def test_long_context_many_splits(fbctx, n_kv, ctx):
+    """Few kv heads and long contexts: the attention grid takes 32 or 64
+    splits per kv head (one wave of CTAs); the result must not change."""
+    cfg = tiny_config(n_heads=4 * n_kv, n_kv_heads=n_kv, max_ctx=ctx + 8, vocab=2048)
+    dm = fb.Model(fbctx, cfg)
+    dm.synth(seed=5)
+    dm.finalize()
+    om = O.Model(cfg, synth_weights(cfg, seed=5))
+    dm.synth_kv(seed=9, ctx=ctx)
+    om.synth_kv(9, ctx)
+    for i, t in enumerate([17, 4]):
+        got, want = dm.forward([t], ctx + i), om.forward([t], ctx + i)
+        assert_close(got, want, what=f"decode at ctx {ctx + i}")
+        assert np.array_equal(got, want), f"ctx {ctx + i}: not bit-identical to the oracle"
+
+
 def test_bad_inputs_rejected(fbctx):
     cfg = tiny_config()
     dm = fb.Model(fbctx, cfg)
