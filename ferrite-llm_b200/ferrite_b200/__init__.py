@@ -39,7 +39,8 @@ EXPORTED = (
     "fb_model_clear_cache", "fb_model_synth_kv", "fb_model_read_kv", "fb_model_weight_bytes",
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
-    "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill",
+    "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill", "fb_gguf_config",
+    "fb_model_load_gguf",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -124,6 +125,8 @@ def _declare(L):
         "fb_comm_destroy": (i32, [vp]),
         "fb_comm_set_timeout_ms": (i32, [vp, i32]),
         "fb_attn_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, vp]),
+        "fb_gguf_config": (i32, [C.c_char_p, P(ModelConfig), P(i32)]),
+        "fb_model_load_gguf": (i32, [vp, C.c_char_p]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -306,6 +309,16 @@ def tensor_seed(seed: int, layer: int, name: str) -> int:
     return (seed + 0x1000 * (layer + 1) + KIND_ID[name]) & 0xFFFFFFFFFFFFFFFF
 
 
+def gguf_config(path: str) -> dict:
+    """Model config from a GGUF file's metadata (plus 'arch': llama / qwen3)."""
+    c = ModelConfig()
+    arch = C.c_int()
+    _check(lib().fb_gguf_config(os.fsencode(path), C.byref(c), C.byref(arch)))
+    d = {k: getattr(c, k) for k, _ in ModelConfig._fields_}
+    d["arch"] = "qwen3" if arch.value == 1 else "llama"
+    return d
+
+
 class Comm:
     """Tensor-parallel exchange region of one rank (fb_comm).
 
@@ -387,6 +400,18 @@ class Model:
         self.rank, self.world, self.vocab_range = r.value, w.value, (vo.value, vo.value + vn.value)
         self.local = dict(self.cfg, n_heads=cfg["n_heads"] // w.value, n_kv_heads=cfg["n_kv_heads"] // w.value,
                           ffn=cfg["ffn"] // w.value, vocab=vn.value)
+
+    @classmethod
+    def from_gguf(cls, ctx: Context, path: str, max_ctx: int | None = None, max_batch: int = 1,
+                  comm: "Comm | None" = None) -> "Model":
+        """Model with the config and tensors of a llama / qwen3 GGUF file."""
+        cfg = gguf_config(path)
+        if max_ctx:
+            cfg["max_ctx"] = max_ctx
+        cfg["max_batch"] = max_batch
+        m = cls(ctx, cfg, comm)
+        _check(lib().fb_model_load_gguf(m.h, os.fsencode(path)))
+        return m
 
     def set_tensor(self, name: str, layer: int, dtype: int, rows: int, cols: int, data: np.ndarray):
         data = np.ascontiguousarray(data)

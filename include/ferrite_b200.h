@@ -276,6 +276,20 @@ int fb_model_launches_per_step(const fb_model *m, int *launches);
 int fb_model_read_activation(fb_model *m, const char *name, int row,
                              float *out_host, int64_t count);
 
+/* ------------------------------------------------------ GGUF ingest ---
+ * Replaces candle's gguf_file::Content + ModelWeights::from_gguf
+ * (crates/ferrite-wasm-host/src/adapter.rs:48-54) and the reference's
+ * metadata reader (crates/ferrite-core/src/registry/loader.rs:247-339).
+ * fb_gguf_config reads a GGUF v2/v3 file's metadata into a model config
+ * (architecture "llama" -> arch 0, "qwen3" -> arch 1 with qk_norm and
+ * rotate-half RoPE; max_ctx = the file's context_length, max_batch = 1: set
+ * both before fb_model_create).  fb_model_load_gguf reads every tensor of the
+ * file into a created model (full tensors; a tensor-parallel model keeps its
+ * shard), uses token_embd as the lm_head when the file has no output tensor,
+ * and finalizes the model.  Tensor types: F32, Q4_K, Q6_K. */
+int fb_gguf_config(const char *path, fb_model_config *cfg_out, int *arch_out);
+int fb_model_load_gguf(fb_model *m, const char *path);
+
 /* ------------------------------------------------- tensor parallelism ---
  * One process (one fb_ctx) per GPU of a node; the reference has no tensor
  * parallelism (candle runs on one device) and its multi-GPU primitives are
