@@ -121,20 +121,16 @@ __global__ void __launch_bounds__(NORM_THREADS)
                            uint32_t *err, uint32_t *epoch_inc) {
     __shared__ double sh[NORM_THREADS / 32];
     __shared__ __align__(16) float xb[QK];
+    __shared__ __align__(16) float qb[QK];
     const int blk = blockIdx.x;
     const int64_t row = blockIdx.y;
     const int lane = threadIdx.x & 31;
-    // Loads that do not depend on the preceding kernel come first: the gains
-    // of this block (weights; usually evicted from L2 by the weight stream)
-    // and the residual row x, written two or more launches earlier.  Only
-    // `add` (the preceding projection's output) is read after the wait.
-    float gv[8];
-    if (threadIdx.x < 32) {
-        const float4 g0 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane);
-        const float4 g1 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane + 4);
-        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-    }
+    // Loads that do not depend on the preceding kernel come first: the gain
+    // of this thread's value of the block (weights; usually evicted from L2
+    // by the weight stream) and the residual row x, written two or more
+    // launches earlier.  Only `add` (the preceding projection's output) is
+    // read after the wait.
+    const float gt = g[blk * QK + threadIdx.x];
     constexpr int MAXP = 8;  // passes held in registers: dim <= 8192
     const float *xr = x ? x + row * dim : nullptr;
     const int nv = dim / 4;
@@ -209,11 +205,14 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
     ss = block_sum64<NORM_THREADS / 32>(ss, sh);  // (has a __syncthreads before the shared reads)
     const float m = rms_of(ss, dim, eps);
-    if (x_out) x_out[row * dim + blk * QK + threadIdx.x] = xb[threadIdx.x];
+    const float xv = xb[threadIdx.x];
+    if (x_out) x_out[row * dim + blk * QK + threadIdx.x] = xv;
+    qb[threadIdx.x] = __fmul_rn(__fdiv_rn(xv, m), gt);  // one value per thread
+    __syncthreads();
     if (threadIdx.x < 32) {
-        float q[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) q[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), gv[e]);
+        const float4 q0 = *reinterpret_cast<const float4 *>(&qb[8 * lane]);
+        const float4 q1 = *reinterpret_cast<const float4 *>(&qb[8 * lane + 4]);
+        const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         q8k_store_warp(q, lane, a, row, blk);
     }
 }
@@ -246,13 +245,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const int64_t j = row * dim + (int64_t)blk * QK + tid;
     // weights and the residual row first (they do not depend on the GEMV)
     const float xv = x[j];
-    float gv[8];
-    if (tid < 32) {
-        const float4 g0 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane);
-        const float4 g1 = *reinterpret_cast<const float4 *>(g + blk * QK + 8 * lane + 4);
-        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-    }
+    const float gt = g[blk * QK + tid];
     pdl_wait();
     pdl_launch();
     const uint32_t seq = (*t.epoch - 1u) * (uint32_t)t.nx + (uint32_t)xi + 1u;
@@ -285,36 +278,36 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
     __syncthreads();
     const float m = rms_of(s_ss, dim, eps);
+    xb[tid] = __fmul_rn(__fdiv_rn(xn, m), gt);  // one value per thread (xb is not read again)
+    __syncthreads();
     if (tid < 32) {
-        float q[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) q[e] = __fmul_rn(__fdiv_rn(xb[8 * lane + e], m), gv[e]);
+        const float4 q0 = *reinterpret_cast<const float4 *>(&xb[8 * lane]);
+        const float4 q1 = *reinterpret_cast<const float4 *>(&xb[8 * lane + 4]);
+        const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         q8k_store_warp(q, lane, a, row, blk);
     }
 }
 
 // ------------------------------------------------------------------------
 // SwiGLU + Q8_K: y[row] = [gate (f) | up (f)] -> act = Q8K(silu(gate) * up).
-// One warp per (row, 256-value block), two warps per CTA; the eight
-// exponentials of a lane are independent and overlap.
-constexpr int SWIGLU_WARPS = 2;
-__global__ void __launch_bounds__(32 * SWIGLU_WARPS) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows,
-                                                                  Q8Act a) {
+// One CTA of 256 threads per (row, 256-value block): every thread evaluates
+// one binary64 SiLU (the exponential and division chains run side by side
+// instead of eight per lane), warp 0 quantizes the block.
+__global__ void __launch_bounds__(QK) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
+    __shared__ __align__(16) float vb[QK];
     pdl_wait();
     pdl_launch();
-    const int lane = threadIdx.x & 31;
     const int64_t nbk = f / QK;
-    const int64_t wid = (int64_t)blockIdx.x * SWIGLU_WARPS + (threadIdx.x >> 5);
-    if (wid < rows * nbk) {
-        const int64_t row = wid / nbk, blk = wid % nbk;
-        const float4 *gp = reinterpret_cast<const float4 *>(y + row * 2 * f + blk * QK + 8 * lane);
-        const float4 *up = reinterpret_cast<const float4 *>(y + row * 2 * f + f + blk * QK + 8 * lane);
-        const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(silu64(g[e]), u[e]);
+    const int64_t row = blockIdx.x / nbk, blk = blockIdx.x % nbk;
+    if (row >= rows) return;
+    const int t = threadIdx.x, lane = t & 31;
+    const float g = y[row * 2 * f + blk * QK + t], u = y[row * 2 * f + f + blk * QK + t];
+    vb[t] = __fmul_rn(silu64(g), u);
+    __syncthreads();
+    if (t < 32) {
+        const float4 v0 = *reinterpret_cast<const float4 *>(&vb[8 * lane]);
+        const float4 v1 = *reinterpret_cast<const float4 *>(&vb[8 * lane + 4]);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         q8k_store_warp(v, lane, a, row, blk);
     }
 }
@@ -646,9 +639,8 @@ void launch_tp_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, float *x_out, c
 }
 
 void launch_swiglu_q8k(fb_ctx *ctx, const float *y, int f, int rows, const Q8Act &a) {
-    const int64_t warps = (int64_t)rows * (f / QK);
-    launch_k(ctx, k_swiglu_q8k, dim3((unsigned)((warps + SWIGLU_WARPS - 1) / SWIGLU_WARPS)), dim3(32 * SWIGLU_WARPS), 0,
-             y, f, (int64_t)rows, a);
+    const int64_t blocks = (int64_t)rows * (f / QK);
+    launch_k(ctx, k_swiglu_q8k, dim3((unsigned)blocks), dim3(QK), 0, y, f, (int64_t)rows, a);
 }
 
 size_t argmax_ws_bytes(int rows) { return (size_t)rows * ARGMAX_CHUNKS * 8 + (size_t)rows * 4; }
