@@ -743,7 +743,9 @@ static void ensure_prefill(fb_model *m, int T) {
     m->pf_cap = T;
 }
 
-static void prefill_chunk(fb_model *m, int T, int pos0) {
+// all_logits != null: the logits of every row [T][vocab] (prefill GEMM over
+// the final-normed rows) instead of the last row's float lm_head + argmax.
+static void prefill_chunk(fb_model *m, int T, int pos0, float *all_logits = nullptr) {
     fb_ctx *ctx = m->ctx;
     const fb_model_config &c = m->c, &lc = m->lc;
     const int H = c.hidden, qd = lc.n_heads * c.head_dim, kd = lc.n_kv_heads * c.head_dim, F = lc.ffn;
@@ -769,6 +771,11 @@ static void prefill_chunk(fb_model *m, int T, int pos0) {
         launch_swiglu_rows(ctx, m->pf_ygu.as<float>(), F, T, m->pf_act.as<float>());
         qmatmul_prefill(ctx, L.wdown.t, m->pf_act.as<float>(), yd, T);
     }
+    if (all_logits) {
+        launch_add_rmsnorm_rows(ctx, x, yd, m->out_norm.as<float>(), xn, T, H, c.eps);
+        qmatmul_prefill(ctx, m->output.t, xn, all_logits, T);
+        return;
+    }
     // last row: x + down, final RMSNorm, float lm_head, argmax
     float *xl = x + (size_t)(T - 1) * H, *xnl = xn + (size_t)(T - 1) * H;
     launch_add_rmsnorm_rows(ctx, xl, yd + (size_t)(T - 1) * H, m->out_norm.as<float>(), xnl, 1, H, c.eps);
@@ -778,10 +785,17 @@ static void prefill_chunk(fb_model *m, int T, int pos0) {
     launch_argmax(ctx, m->logits.as<float>(), 1, lc.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
 }
 
+// Rows of the next chunk when `rem` rows are left: at most `cap`, and never
+// leaving a tail shorter than the tensor-core GEMM's 17 rows.
+static int chunk_rows(int rem, int cap) {
+    if (rem <= cap) return rem;
+    return rem - cap < kPrefillMinRows ? rem / 2 : cap;
+}
+
 static void prefill_batched(fb_model *m, const int32_t *tokens_host, int n, int pos) {
     cudaStream_t s = m->ctx->stream;
     for (int done = 0; done < n;) {
-        const int T = std::min(kPrefillRows, n - done);
+        const int T = chunk_rows(n - done, kPrefillRows);
         ensure_prefill(m, std::min(kPrefillRows, n));
         FB_CUDA(cudaMemcpyAsync(m->pf_tok.ptr, tokens_host + done, (size_t)T * 4, cudaMemcpyHostToDevice, s));
         prefill_chunk(m, T, pos + done);
@@ -791,6 +805,48 @@ static void prefill_batched(fb_model *m, const int32_t *tokens_host, int n, int 
 }
 
 extern "C" {
+
+int fb_model_forward_all(fb_model *m, const int32_t *tokens_host, int n, int pos, float *logits_host) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_host && logits_host, "null argument");
+        require_ready(m);
+        FB_REQUIRE(n >= 1 && pos >= 0 && pos + n <= m->c.max_ctx, "tokens do not fit the KV capacity");
+        FB_REQUIRE(pos <= m->len0, "pos beyond the cached sequence");
+        for (int i = 0; i < n; i++)
+            FB_REQUIRE(tokens_host[i] >= 0 && tokens_host[i] < m->c.vocab, "token id out of range");
+        cudaStream_t s = m->ctx->stream;
+        const size_t V = (size_t)m->lc.vocab;
+        if (n >= kPrefillMinRows && !m->comm && m->output.t->n % 128 == 0) {
+            constexpr int kRows = 256;  // rows per chunk: logits [256][vocab] on the device
+            DevBuf lg;
+            lg.alloc((size_t)std::min(kRows, n) * V * 4);
+            ensure_prefill(m, std::min(kRows, n));
+            for (int done = 0; done < n;) {
+                const int T = chunk_rows(n - done, kRows);
+                if (T > m->pf_cap) ensure_prefill(m, T);
+                if ((size_t)T * V * 4 > lg.bytes) lg.alloc((size_t)T * V * 4);
+                FB_CUDA(cudaMemcpyAsync(m->pf_tok.ptr, tokens_host + done, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+                prefill_chunk(m, T, pos + done, lg.as<float>());
+                FB_CUDA(cudaMemcpyAsync(logits_host + (size_t)done * V, lg.ptr, (size_t)T * V * 4,
+                                        cudaMemcpyDeviceToHost, s));
+                FB_CUDA(cudaStreamSynchronize(s));
+                done += T;
+            }
+        } else {
+            for (int i = 0; i < n; i++) {
+                m->pinned[0] = tokens_host[i];
+                m->pinned[1] = pos + i;
+                FB_CUDA(cudaMemcpyAsync(m->tok.ptr, &m->pinned[0], 4, cudaMemcpyHostToDevice, s));
+                FB_CUDA(cudaMemcpyAsync(m->pos.ptr, &m->pinned[1], 4, cudaMemcpyHostToDevice, s));
+                run_step(m, 1);
+                FB_CUDA(cudaMemcpyAsync(logits_host + (size_t)i * V, m->logits.ptr, V * 4, cudaMemcpyDeviceToHost, s));
+                FB_CUDA(cudaStreamSynchronize(s));
+            }
+        }
+        m->len0 = pos + n;
+        check_no_device_error(m);
+    });
+}
 
 int fb_model_forward(fb_model *m, const int32_t *tokens_host, int n, int pos, float *logits_host) {
     return guarded([&] {

@@ -40,7 +40,7 @@ EXPORTED = (
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
     "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill", "fb_gguf_config",
-    "fb_model_load_gguf",
+    "fb_model_load_gguf", "fb_model_forward_all",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -127,6 +127,7 @@ def _declare(L):
         "fb_attn_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, vp]),
         "fb_gguf_config": (i32, [C.c_char_p, P(ModelConfig), P(i32)]),
         "fb_model_load_gguf": (i32, [vp, C.c_char_p]),
+        "fb_model_forward_all": (i32, [vp, vp, i32, i32, vp]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -427,6 +428,13 @@ class Model:
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         out = np.zeros(self.local["vocab"], dtype=np.float32)
         _check(lib().fb_model_forward(self.h, _np(toks), toks.size, pos, _np(out)))
+        return out
+
+    def forward_all(self, tokens, pos: int) -> np.ndarray:
+        """Logits of every token, [n, vocab] (multi-token verification)."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.zeros((toks.size, self.local["vocab"]), dtype=np.float32)
+        _check(lib().fb_model_forward_all(self.h, _np(toks), toks.size, pos, _np(out)))
         return out
 
     def prefill(self, tokens) -> np.ndarray:

@@ -243,6 +243,15 @@ int fb_model_decode_dev(fb_model *m, const int32_t *tokens_dev,
                         float *logits_dev);
 int fb_model_prefill(fb_model *m, const int32_t *tokens_host, int n,
                      float *logits_host);
+/* Multi-token forward (speculative verification, re-prefill after a context
+ * slide; the reference runs these token by token: crates/ferrite-core/src/
+ * generation.rs:340-535, chat_session.rs:576-629): like fb_model_forward but
+ * logits_host receives the logits of every token, [n][vocab] (the rank's
+ * vocab slice under tensor parallelism).  n >= 17 on one GPU: batched, the
+ * lm_head as a tensor-core GEMM over the final-normed rows (fp16 operands,
+ * f32 accumulation); otherwise token by token through the decode step. */
+int fb_model_forward_all(fb_model *m, const int32_t *tokens_host, int n,
+                         int pos, float *logits_host);
 int fb_model_clear_cache(fb_model *m);
 /* Fill the first ctx positions of every sequence slot's KV cache with
  * synthetic fp16 values (bench / parity setup). */

@@ -118,3 +118,18 @@ def test_prefill_continuation_and_decode(pair):
             break
         tok_d = tok_o = no
         pos += 1
+
+
+@pytest.mark.parametrize("n", [5, 40, 300])
+def test_forward_all_logits(pair, n):
+    """Multi-token forward: the logits of every token against the oracle's
+    (float forward for the batched path, integer decode steps for short
+    inputs)."""
+    cfg, dm, om = pair
+    dm.clear_cache()
+    om.clear()
+    toks = O.synth_tokens(n + 11, n, cfg["vocab"])
+    got = dm.forward_all(toks, 0)
+    ref = om.forward(toks, 0, all_logits=True, matmul_mode=1 if n >= 17 else 0)
+    assert got.shape == ref.shape == (n, cfg["vocab"])
+    assert_close(got, ref, what=f"all logits of {n} tokens")
