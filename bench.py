@@ -300,6 +300,16 @@ def run_prefill(args, cfg):
             tok = int(model.decode_greedy([tok], [T + i])[0])
             toks.append(tok)
         dec_s = time.perf_counter() - t0
+        # on-device sampling of one vocab row with the reference sampler's
+        # default config (fb_sample), the cost a sampled decode step adds
+        lg = torch.from_numpy(np.asarray(logits, dtype=np.float32)).cuda()
+        smp = fb.Sampler(ctx)
+        prev = prompt[-64:].tolist()
+        smp.sample(lg.data_ptr(), cfg["vocab"], prev)
+        t1 = time.perf_counter()
+        for _ in range(32):
+            smp.sample(lg.data_ptr(), cfg["vocab"], prev)
+        sample_ms = (time.perf_counter() - t1) / 32 * 1e3
     fl = prefill_flops(cfg, T)
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -317,6 +327,7 @@ def run_prefill(args, cfg):
             "e2e": {"value": T / (ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4 * T,
                     "d2h_bytes_per_step": 4 * cfg["vocab"]},
             "decode_after_prefill_tok_s": ndec / dec_s,
+            "sampler_ms_per_token": sample_ms,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "flops_per_step": fl, "peak_source": kind},
             "error_word": ctx.error_word()}

@@ -40,7 +40,7 @@ EXPORTED = (
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
     "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill", "fb_gguf_config",
-    "fb_model_load_gguf", "fb_model_forward_all",
+    "fb_model_load_gguf", "fb_model_forward_all", "fb_sample",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -51,6 +51,11 @@ class FerriteError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"[{code}] {msg}")
         self.code = code
+
+
+class SamplerConfig(C.Structure):
+    _fields_ = [("temperature", C.c_double), ("top_p", C.c_double), ("top_k", C.c_int), ("min_p", C.c_float),
+                ("repetition_penalty", C.c_float)]
 
 
 class ModelConfig(C.Structure):
@@ -128,6 +133,7 @@ def _declare(L):
         "fb_gguf_config": (i32, [C.c_char_p, P(ModelConfig), P(i32)]),
         "fb_model_load_gguf": (i32, [vp, C.c_char_p]),
         "fb_model_forward_all": (i32, [vp, vp, i32, i32, vp]),
+        "fb_sample": (i32, [vp, vp, i32, P(SamplerConfig), vp, i32, P(C.c_uint64), P(i32)]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -308,6 +314,24 @@ KIND_ID = {"token_embd": 1, "output_norm": 2, "output": 3, "attn_norm": 10, "att
 def tensor_seed(seed: int, layer: int, name: str) -> int:
     """Per-tensor seed used by Model.synth (layer = -1 for global tensors)."""
     return (seed + 0x1000 * (layer + 1) + KIND_ID[name]) & 0xFFFFFFFFFFFFFFFF
+
+
+class Sampler:
+    """Sampler::sample of the reference on the device (fb_sample); the RNG
+    state advances like the reference's xorshift64."""
+
+    def __init__(self, ctx: Context, temperature=0.7, top_p=0.9, top_k=0, min_p=0.05, repetition_penalty=1.1,
+                 seed=42):
+        self.ctx = ctx
+        self.cfg = SamplerConfig(temperature, top_p, top_k, min_p, repetition_penalty)
+        self.state = C.c_uint64(seed)
+
+    def sample(self, logits_ptr: int, vocab: int, previous_tokens=()) -> int:
+        prev = np.ascontiguousarray(np.asarray(previous_tokens, dtype=np.int32))
+        out = C.c_int32()
+        _check(lib().fb_sample(self.ctx.h, logits_ptr, vocab, C.byref(self.cfg), _np(prev) if prev.size else None,
+                               prev.size, C.byref(self.state), C.byref(out)))
+        return out.value
 
 
 def gguf_config(path: str) -> dict:

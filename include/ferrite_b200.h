@@ -285,6 +285,25 @@ int fb_model_launches_per_step(const fb_model *m, int *launches);
 int fb_model_read_activation(fb_model *m, const char *name, int row,
                              float *out_host, int64_t count);
 
+/* --------------------------------------------------------- sampling ---
+ * Sampler::sample of the reference (crates/ferrite-core/src/sampling.rs:
+ * 61-239; config fields as its SamplerConfig): repetition penalty over the
+ * distinct previous tokens, temperature == 0 -> argmax, else softmax of
+ * logits / temperature, min-p, top-p, top-k (each renormalizing), and a draw
+ * with the reference's xorshift64 uniform (rng_state is advanced in place,
+ * seeded with SamplerConfig::seed).  logits_dev: one row of vocab f32 on the
+ * device (e.g. fb_model_decode_dev's logits); the token is returned on the
+ * host.  Runs on the device (one CTA); sorting is replaced by threshold
+ * searches with the same keep rules (ties in index order). */
+typedef struct {
+    double temperature, top_p;
+    int top_k;
+    float min_p, repetition_penalty;
+} fb_sampler_config;
+int fb_sample(fb_ctx *ctx, const float *logits_dev, int vocab,
+              const fb_sampler_config *cfg, const int32_t *prev_tokens_host,
+              int n_prev, uint64_t *rng_state, int32_t *token_out);
+
 /* ------------------------------------------------------ GGUF ingest ---
  * Replaces candle's gguf_file::Content + ModelWeights::from_gguf
  * (crates/ferrite-wasm-host/src/adapter.rs:48-54) and the reference's
