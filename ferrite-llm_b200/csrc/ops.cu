@@ -72,6 +72,74 @@ __device__ __forceinline__ void q8k_store_warp(const float (&v)[8], int lane, co
     if (lane == 0) a.d[row * (k / QK) + blk] = d;
 }
 
+// The same Q8_K quantization of one 256-value block by a CTA of 256 threads,
+// one value per thread (index t = threadIdx.x in the block): the pivot (the
+// value of largest magnitude, first index on ties), iscale = -128 / pivot,
+// q = min(127, round(iscale * v)), the 16- and 32-value sums and
+// d = 1 / iscale -- identical results to q8k_store_warp, without the
+// per-lane loops over eight values.
+__device__ __forceinline__ void q8k_store_block(float v, const Q8Act &a, int64_t row, int64_t blk, float *shv,
+                                                int *shi) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float amax = fabsf(v), piv = v;
+    int idx = t;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float op = __shfl_xor_sync(0xffffffffu, piv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            piv = op;
+            idx = oi;
+        }
+    }
+    if (lane == 0) {
+        shv[2 * warp] = amax;
+        shv[2 * warp + 1] = piv;
+        shi[warp] = idx;
+    }
+    __syncthreads();
+    amax = shv[0];
+    piv = shv[1];
+    idx = shi[0];
+#pragma unroll
+    for (int w = 1; w < QK / 32; w++) {
+        const float oa = shv[2 * w];
+        if (oa > amax || (oa == amax && shi[w] < idx)) {
+            amax = oa;
+            piv = shv[2 * w + 1];
+            idx = shi[w];
+        }
+    }
+    int q = 0;
+    float iscale = 0.f;
+    if (amax != 0.f) {
+        iscale = __fdiv_rn(-128.f, piv);
+        q = (int)roundf(__fmul_rn(iscale, v));
+        q = q > 127 ? 127 : q;
+    }
+    // 16- and 32-value sums (the block's values 32w .. 32w + 31 are warp w's lanes)
+    int s16 = q;
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, off);
+    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
+    const int64_t k = a.k;
+    // permuted byte position: value 8l + e -> 64 (l & 3) + 8 (l >> 2) + e; four
+    // consecutive values form one 32-bit word
+    const uint32_t b0 = (uint32_t)(uint8_t)q;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 1), b2 = __shfl_down_sync(0xffffffffu, b0, 2),
+                   b3 = __shfl_down_sync(0xffffffffu, b0, 3);
+    if ((t & 3) == 0) {
+        const int l = t >> 3, e = t & 7;
+        *reinterpret_cast<uint32_t *>(a.qs + row * k + blk * QK + 64 * (l & 3) + 8 * (l >> 2) + e) =
+            b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    if ((t & 15) == 0) a.bs16[row * (k / 16) + blk * 16 + (t >> 4)] = (int16_t)s16;
+    if (lane == 0) a.bs32[row * (k / 32) + blk * 8 + warp] = (int16_t)s32;
+    if (t == 0) a.d[row * (k / QK) + blk] = amax != 0.f ? __fdiv_rn(1.f, iscale) : 0.f;
+}
+
 // Block sum in binary64 (RMSNorm sums of squares: each f32 square is exact
 // in binary64, so the result is independent of the summation order up to
 // binary64 rounding, and rounds to the same f32 as the oracle's).
@@ -121,10 +189,10 @@ __global__ void __launch_bounds__(NORM_THREADS)
                            uint32_t *err, uint32_t *epoch_inc) {
     __shared__ double sh[NORM_THREADS / 32];
     __shared__ __align__(16) float xb[QK];
-    __shared__ __align__(16) float qb[QK];
+    __shared__ float qb[2 * QK / 32];
+    __shared__ int s_qi[QK / 32];
     const int blk = blockIdx.x;
     const int64_t row = blockIdx.y;
-    const int lane = threadIdx.x & 31;
     // Loads that do not depend on the preceding kernel come first: the gain
     // of this thread's value of the block (weights; usually evicted from L2
     // by the weight stream) and the residual row x, written two or more
@@ -207,14 +275,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const float m = rms_of(ss, dim, eps);
     const float xv = xb[threadIdx.x];
     if (x_out) x_out[row * dim + blk * QK + threadIdx.x] = xv;
-    qb[threadIdx.x] = __fmul_rn(__fdiv_rn(xv, m), gt);  // one value per thread
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        const float4 q0 = *reinterpret_cast<const float4 *>(&qb[8 * lane]);
-        const float4 q1 = *reinterpret_cast<const float4 *>(&qb[8 * lane + 4]);
-        const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        q8k_store_warp(q, lane, a, row, blk);
-    }
+    q8k_store_block(__fmul_rn(__fdiv_rn(xv, m), gt), a, row, blk, qb, s_qi);
 }
 
 // ------------------------------------------------------------------------
@@ -241,7 +302,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     __shared__ double s_ss;
     const int blk = blockIdx.x, nblk = gridDim.x;
     const int64_t row = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int64_t j = row * dim + (int64_t)blk * QK + tid;
     // weights and the residual row first (they do not depend on the GEMV)
     const float xv = x[j];
@@ -278,14 +339,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
     __syncthreads();
     const float m = rms_of(s_ss, dim, eps);
-    xb[tid] = __fmul_rn(__fdiv_rn(xn, m), gt);  // one value per thread (xb is not read again)
-    __syncthreads();
-    if (tid < 32) {
-        const float4 q0 = *reinterpret_cast<const float4 *>(&xb[8 * lane]);
-        const float4 q1 = *reinterpret_cast<const float4 *>(&xb[8 * lane + 4]);
-        const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        q8k_store_warp(q, lane, a, row, blk);
-    }
+    q8k_store_block(__fmul_rn(__fdiv_rn(xn, m), gt), a, row, blk, xb, reinterpret_cast<int *>(xb + 16));
 }
 
 // ------------------------------------------------------------------------
@@ -294,22 +348,16 @@ __global__ void __launch_bounds__(NORM_THREADS)
 // one binary64 SiLU (the exponential and division chains run side by side
 // instead of eight per lane), warp 0 quantizes the block.
 __global__ void __launch_bounds__(QK) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
-    __shared__ __align__(16) float vb[QK];
+    __shared__ float shv[2 * QK / 32];
+    __shared__ int shi[QK / 32];
     pdl_wait();
     pdl_launch();
     const int64_t nbk = f / QK;
     const int64_t row = blockIdx.x / nbk, blk = blockIdx.x % nbk;
     if (row >= rows) return;
-    const int t = threadIdx.x, lane = t & 31;
+    const int t = threadIdx.x;
     const float g = y[row * 2 * f + blk * QK + t], u = y[row * 2 * f + f + blk * QK + t];
-    vb[t] = __fmul_rn(silu64(g), u);
-    __syncthreads();
-    if (t < 32) {
-        const float4 v0 = *reinterpret_cast<const float4 *>(&vb[8 * lane]);
-        const float4 v1 = *reinterpret_cast<const float4 *>(&vb[8 * lane + 4]);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        q8k_store_warp(v, lane, a, row, blk);
-    }
+    q8k_store_block(__fmul_rn(silu64(g), u), a, row, blk, shv, shi);
 }
 
 // ------------------------------------------------------------------------
