@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
                   int depth, int bt_cap) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[ATT_MAX_DEPTH];
-    __shared__ int s_len, s_first, s_mine, s_last;
+    __shared__ int s_len, s_first, s_mine, s_last, s_last2;
     __shared__ __half s_newkv[2 * ATT_HD];  // fused prologue: the new token's k and v (fp16)
     constexpr int S = ATT_SPLITS;
     const int ns = CLUSTER ? S : (int)gridDim.x;  // splits of this (kv head, sequence)
@@ -480,38 +480,37 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             }
         }
     } else {
-        const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ns;
+        // partial slots per head: the ns splits, then -- more than ATT_SPLITS
+        // splits -- one merged slot per group of ATT_GROUP splits (two-level
+        // merge: the last CTA of a group merges its group, the last group
+        // merger merges the groups)
+        const int ng = ns > ATT_SPLITS ? ns / ATT_GROUP : 0;
+        const int sst = ns + ng;
+        const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * sst;
         __syncthreads();
         for (int i = tid; i < G * ATT_HD; i += NT) {
             const int g = i / ATT_HD, d = i % ATT_HD;
-            A.part_o[(hb0 + (int64_t)g * ns + rank) * ATT_HD + d] = O_s[i];
+            A.part_o[(hb0 + (int64_t)g * sst + rank) * ATT_HD + d] = O_s[i];
         }
         if (tid < G) {
-            A.part_ml[2 * (hb0 + (int64_t)tid * ns + rank)] = M_s[tid];
-            A.part_ml[2 * (hb0 + (int64_t)tid * ns + rank) + 1] = L_s[tid];
+            A.part_ml[2 * (hb0 + (int64_t)tid * sst + rank)] = M_s[tid];
+            A.part_ml[2 * (hb0 + (int64_t)tid * sst + rank) + 1] = L_s[tid];
         }
-        // the last CTA of this (kv head, sequence) merges
         __threadfence();
         __syncthreads();
-        if (tid == 0) {
-            int *cnt = counters + (int64_t)b * A.n_kv + kvh;
-            const int prev = atomicAdd(cnt, 1);
-            s_last = prev == ns - 1;
-            if (s_last) *cnt = 0;  // ready for the next call
-        }
-        __syncthreads();
-        if (s_last) {
-            __threadfence();
-            // warp g < G: split weights of head g (lane = splits r, r + 32)
-            if (warp < G) {
+        int *cnt = counters + ((int64_t)b * A.n_kv + kvh) * (ng ? ATT_CNT_PER : 1);
+        // merges slots [s0, s0 + n) of every head: dst < 0 -> the output
+        // (f32 and Q8_K), else a merged partial (max, sum, o) into slot dst
+        auto merge = [&](int s0, int n, int dst) {
+            if (warp < G) {  // warp g: weights of head g (lane = slots r, r + 32)
                 const int g = warp;
                 double Mr[ATT_SPLITS_MAX / 32], Lr[ATT_SPLITS_MAX / 32];
                 double M = -INFINITY;
 #pragma unroll
                 for (int k = 0; k < ATT_SPLITS_MAX / 32; k++) {
                     const int r = lane + 32 * k;
-                    Mr[k] = r < ns ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * ns + r)]) : -INFINITY;
-                    Lr[k] = r < ns ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * ns + r) + 1]) : 0.0;
+                    Mr[k] = r < n ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * sst + s0 + r)]) : -INFINITY;
+                    Lr[k] = r < n ? __ldcg(&A.part_ml[2 * (hb0 + (int64_t)g * sst + s0 + r) + 1]) : 0.0;
                     M = fmax(M, Mr[k]);
                 }
 #pragma unroll
@@ -519,40 +518,86 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
 #pragma unroll
                 for (int k = 0; k < ATT_SPLITS_MAX / 32; k++) {
                     const int r = lane + 32 * k;
-                    if (r < ns) {
+                    if (r < n) {
                         const double w = Mr[k] == -INFINITY ? 0.0 : exp64(__dsub_rn(Mr[k], M));
                         wts[g * ATT_SPLITS_MAX + r] = w;
                         wl[g * ATT_SPLITS_MAX + r] = __dmul_rn(w, Lr[k]);
                     }
                 }
+                if (lane == 0) alpha_s[g] = M;
             }
             __syncthreads();
             for (int i = tid; i < G * ATT_HD; i += NT) {
                 const int g = i / ATT_HD, d = i % ATT_HD;
                 double L = 0.0, O = 0.0;
-                for (int r0 = 0; r0 < ns; r0 += 16) {  // 16 partial loads in flight, summed in split order
+                for (int r0 = 0; r0 < n; r0 += 16) {  // 16 partial loads in flight, summed in slot order
                     double Or[16];
 #pragma unroll
                     for (int k = 0; k < 16; k++)
-                        Or[k] = r0 + k < ns ? __ldcg(&A.part_o[(hb0 + (int64_t)g * ns + r0 + k) * ATT_HD + d]) : 0.0;
+                        Or[k] = r0 + k < n ? __ldcg(&A.part_o[(hb0 + (int64_t)g * sst + s0 + r0 + k) * ATT_HD + d])
+                                           : 0.0;
 #pragma unroll
                     for (int k = 0; k < 16; k++)
-                        if (r0 + k < ns) {
+                        if (r0 + k < n) {
                             L = __dadd_rn(L, wl[g * ATT_SPLITS_MAX + r0 + k]);
                             O = __dadd_rn(O, __dmul_rn(wts[g * ATT_SPLITS_MAX + r0 + k], Or[k]));
                         }
                 }
-                const float val = L > 0.0 ? __double2float_rn(__ddiv_rn(O, L)) : 0.f;
-                if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
-                fin[i] = val;
+                if (dst >= 0) {
+                    A.part_o[(hb0 + (int64_t)g * sst + dst) * ATT_HD + d] = O;
+                    if (d == 0) {
+                        A.part_ml[2 * (hb0 + (int64_t)g * sst + dst)] = alpha_s[g];
+                        A.part_ml[2 * (hb0 + (int64_t)g * sst + dst) + 1] = L;
+                    }
+                } else {
+                    const float val = L > 0.0 ? __double2float_rn(__ddiv_rn(O, L)) : 0.f;
+                    if (out_f32) out_f32[((int64_t)b * A.n_heads + (int64_t)kvh * G + g) * ATT_HD + d] = val;
+                    fin[i] = val;
+                }
             }
-            if (use_q8) {
+            if (dst < 0 && use_q8) {
                 __syncthreads();
                 for (int blk = warp; blk < G / 2; blk += NW) {
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = fin[blk * 256 + 8 * lane + e];
                     q8k_store_warp_ext(v, lane, aq, b, (int64_t)kvh * G / 2 + blk);
+                }
+            }
+        };
+        if (ng == 0) {
+            if (tid == 0) {
+                const int prev = atomicAdd(&cnt[0], 1);
+                s_last = prev == ns - 1;
+                if (s_last) cnt[0] = 0;  // ready for the next call
+            }
+            __syncthreads();
+            if (s_last) {
+                __threadfence();
+                merge(0, ns, -1);
+            }
+        } else {
+            const int grp = rank / ATT_GROUP;
+            if (tid == 0) {
+                const int prev = atomicAdd(&cnt[1 + grp], 1);
+                s_last = prev == ATT_GROUP - 1;
+                if (s_last) cnt[1 + grp] = 0;
+            }
+            __syncthreads();
+            if (s_last) {
+                __threadfence();
+                merge(grp * ATT_GROUP, ATT_GROUP, ns + grp);
+                __threadfence();
+                __syncthreads();
+                if (tid == 0) {
+                    const int prev = atomicAdd(&cnt[0], 1);
+                    s_last2 = prev == ng - 1;
+                    if (s_last2) cnt[0] = 0;
+                }
+                __syncthreads();
+                if (s_last2) {
+                    __threadfence();
+                    merge(ns, ng, -1);
                 }
             }
         }

@@ -489,9 +489,9 @@ static void create_model(fb_ctx *ctx, const fb_model_config *cfg, fb_comm *comm,
     m->logits.alloc((size_t)B * lc.vocab * 4);
     m->argmax_ws.alloc(argmax_ws_bytes(B));
     FB_CUDA(cudaMemsetAsync(m->argmax_ws.ptr, 0, m->argmax_ws.bytes, ctx->stream));
-    m->part_o.alloc((size_t)B * lc.n_heads * m->nsplit_max * c.head_dim * 8);
-    m->part_ml.alloc((size_t)B * lc.n_heads * m->nsplit_max * 2 * 8);
-    m->att_cnt.alloc((size_t)B * lc.n_kv_heads * 4);
+    m->part_o.alloc((size_t)B * lc.n_heads * ATT_SLOTS_MAX * c.head_dim * 8);
+    m->part_ml.alloc((size_t)B * lc.n_heads * ATT_SLOTS_MAX * 2 * 8);
+    m->att_cnt.alloc((size_t)B * lc.n_kv_heads * ATT_CNT_PER * 4);
     FB_CUDA(cudaMemsetAsync(m->att_cnt.ptr, 0, m->att_cnt.bytes, ctx->stream));
     m->act_h.alloc(q8act_bytes(B, H));
     m->act_a.alloc(q8act_bytes(B, qd));
