@@ -1,4 +1,4 @@
-"""Pins the oracle against the reference's own code.
+"""Pins the oracle (and this library) against the reference's own code.
 
 The reference's CUDA dequantization kernels (ferrite-os/crates/internal/
 ptx-kernels/kernels/candle/quantized.cu:936-1151, `dequantize_block_q4_K_f32`
@@ -75,3 +75,45 @@ def test_dequant_matches_reference_cuda(fbctx, torch_cuda, ref_lib, dtype):
         dev.dequantize(out.data_ptr(), fb.F32)
         got = out.cpu().numpy()
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"device vs reference CUDA ({what})"
+
+
+def ref_qmatmul(lib, dtype, mode, w, n, k, x):
+    lib.ref_qmatmul_vec_host.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    lib.ref_qmatmul_vec_host.restype = C.c_int
+    w = np.ascontiguousarray(w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(n, dtype=np.float32)
+    rc = lib.ref_qmatmul_vec_host(dtype, mode, w.ctypes.data, n, k, x.ctypes.data, y.ctypes.data)
+    assert rc == 0, f"reference kernel launch failed: cudaError {rc}"
+    return y
+
+
+@pytest.mark.parametrize("dtype,n,k", [(O.Q4_K, 4096, 4096), (O.Q4_K, 1024, 4096), (O.Q6_K, 4096, 12288),
+                                       (O.Q6_K, 2048, 4096)])
+def test_qmatmul_vs_reference_cuda(fbctx, torch_cuda, ref_lib, dtype, n, k):
+    """The reference's own decode QMatMul kernels on the same weights and
+    activation: its float DMMV kernel (dequantize_mul_mat_vec_q*_k) against
+    the oracle's float QMatMul (f32 accumulation order only: 1e-5 relative of
+    the row's scale), and its integer MMVQ kernel (Q8_1 activations, blocks of
+    32) against this library's integer GEMV (Q8_K activations, the CPU
+    path's): the two 8-bit activation roundings differ, so the bar is their
+    quantization noise -- a relative RMS difference below 1%."""
+    torch = torch_cuda
+    w = gaussian_qweight(dtype, n, k, seed=n + k + dtype)
+    x = np.random.default_rng(k).normal(0, 1, k).astype(np.float32)
+    ref_float = ref_qmatmul(ref_lib, dtype, 1, w, n, k, x)
+    orc_float = O.qmatmul_f32(dtype, w, n, k, x[None])[0]
+    scale = np.abs(orc_float).max()
+    assert np.abs(ref_float - orc_float).max() <= 1e-5 * scale, "oracle float QMatMul vs the reference's DMMV kernel"
+    ref_int = ref_qmatmul(ref_lib, dtype, 0, w, n, k, x)
+    t = fb.QTensor.upload(fbctx, dtype, n, k, w)
+    xd = torch.from_numpy(x[None].copy()).cuda()
+    yd = torch.empty((1, n), dtype=torch.float32, device="cuda")
+    fb.QMatMul(t).forward(xd.data_ptr(), yd.data_ptr(), 1)
+    dev = yd.cpu().numpy()[0]
+    rel = np.sqrt(np.mean((dev - ref_int) ** 2)) / np.sqrt(np.mean(ref_int.astype(np.float64) ** 2))
+    assert rel < 1e-2, f"integer paths: relative RMS difference {rel:.3g}"
+    # and each integer path stays that close to the float product
+    for what, v in (("device", dev), ("reference MMVQ", ref_int)):
+        r = np.sqrt(np.mean((v - orc_float) ** 2)) / np.sqrt(np.mean(orc_float.astype(np.float64) ** 2))
+        assert r < 1e-2, f"{what} vs float product: {r:.3g}"
