@@ -36,6 +36,8 @@
 #include "kq_common.cuh"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 namespace fb {
 
@@ -574,9 +576,22 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
     depth = std::max(depth, 3);
     const size_t smem = act + (size_t)KS * depth * REC;
     auto kernel = k_gemv<DT, NT, DOTS, KS>;
-    FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // the shared-memory attribute and the occupancy query cost more host time
+    // than a small GEMV's device time: done once per (device, size)
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> occ_cache;
     int occ = 0;
-    FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, KS * 32, smem));
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = occ_cache.find({ctx->device, smem});
+        if (it != occ_cache.end()) {
+            occ = it->second;
+        } else {
+            FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, KS * 32, smem));
+            occ_cache[{ctx->device, smem}] = occ;
+        }
+    }
     FB_REQUIRE(occ > 0, "gemv: configuration does not fit on an SM");
     const int n_tiles = (int)w->n_tiles();
     const int grid = std::min(n_tiles, occ * ctx->num_sms);

@@ -177,6 +177,10 @@ class Context:
     def stream(self) -> int:
         return lib().fb_ctx_stream(self.h) or 0
 
+    def set_stream(self, stream: int):
+        """Order later work on `stream` (the old stream is synchronised first)."""
+        _check(lib().fb_ctx_set_stream(self.h, stream or None))
+
     def close(self):
         if self.h:
             lib().fb_ctx_destroy(self.h)

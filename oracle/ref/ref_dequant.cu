@@ -81,3 +81,48 @@ extern "C" int ref_qmatmul_vec_host(int dtype, int mode, const void *w, int n, i
     cudaFree(dq);
     return (int)e;
 }
+
+// Device time of the reference's integer decode QMatMul (quantize_q8_1 +
+// mul_mat_vec_q*_K_q8_1_cuda1, one activation row) averaged over `iters`
+// back-to-back launches after `warm` untimed ones; inputs resident on the
+// device.  Returns a cudaError_t; *ms_out = milliseconds per QMatMul.
+extern "C" int ref_qmatmul_vec_time(int dtype, const void *w, int n, int k, const float *x, int warm, int iters,
+                                    float *ms_out) {
+    const size_t bb = dtype == 12 ? 144 : 210;
+    const size_t wbytes = bb * (size_t)n * (size_t)(k / 256);
+    const int kpad = (k + 511) / 512 * 512;
+    void *dw = nullptr, *dq = nullptr;
+    float *dx = nullptr, *dy = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaMalloc(&dw, wbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&dx, sizeof(float) * (size_t)k);
+    if (e == cudaSuccess) e = cudaMalloc(&dy, sizeof(float) * (size_t)n);
+    if (e == cudaSuccess) e = cudaMalloc(&dq, (size_t)(kpad / 32) * 36);
+    if (e == cudaSuccess) e = cudaMemcpy(dw, w, wbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dx, x, sizeof(float) * (size_t)k, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    auto run = [&] {
+        quantize_q8_1<<<dim3((unsigned)((kpad + 255) / 256), 1), dim3(256, 1)>>>(dx, dq, k, kpad);
+        if (dtype == 12) mul_mat_vec_q4_K_q8_1_cuda1<<<(unsigned)n, dim3(32, 4)>>>(dw, dq, dy, k, n, kpad, n);
+        else mul_mat_vec_q6_K_q8_1_cuda1<<<(unsigned)n, dim3(32, 4)>>>(dw, dq, dy, k, n, kpad, n);
+    };
+    if (e == cudaSuccess) {
+        for (int i = 0; i < warm; i++) run();
+        cudaEventRecord(e0);
+        for (int i = 0; i < iters; i++) run();
+        cudaEventRecord(e1);
+        e = cudaEventSynchronize(e1);
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    *ms_out = iters > 0 ? ms / iters : 0.f;
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaFree(dw);
+    cudaFree(dx);
+    cudaFree(dy);
+    cudaFree(dq);
+    return (int)e;
+}

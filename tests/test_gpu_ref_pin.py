@@ -117,3 +117,71 @@ def test_qmatmul_vs_reference_cuda(fbctx, torch_cuda, ref_lib, dtype, n, k):
     for what, v in (("device", dev), ("reference MMVQ", ref_int)):
         r = np.sqrt(np.mean((v - orc_float) ** 2)) / np.sqrt(np.mean(orc_float.astype(np.float64) ** 2))
         assert r < 1e-2, f"{what} vs float product: {r:.3g}"
+
+
+# configs[1]-style decode shapes at batch 1 (n x k): attention q/o, k/v,
+# gate and up (each), down (Q6_K), lm_head (Q6_K)
+SPEED_SHAPES = [(O.Q4_K, 4096, 4096), (O.Q4_K, 1024, 4096), (O.Q4_K, 12288, 4096), (O.Q6_K, 4096, 12288),
+                (O.Q6_K, 151936, 4096)]
+
+
+def test_gemv_speed_vs_reference_cuda(fbctx, torch_cuda, ref_lib):
+    """Device time of one decode QMatMul (activation quantization + GEMV) of
+    this library vs the reference's MMVQ kernels on the same B200, both with
+    resident inputs and back-to-back launches; prints a table (run with -s)
+    and requires this library to be faster on every shape.  The reference
+    is launched from a C loop; this library's calls are captured in a CUDA
+    graph and replayed, so both columns are device time (the Python-launched
+    column is shown beside it: at 1024 rows it is ctypes-bound)."""
+    torch = torch_cuda
+    ref_lib.ref_qmatmul_vec_time.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                             C.c_void_p]
+    ref_lib.ref_qmatmul_vec_time.restype = C.c_int
+    rows = []
+    for dtype, n, k in SPEED_SHAPES:
+        w = fb.QTensor.synth(fbctx, dtype, n, k, seed=n + k)
+        blocks = w.download()
+        x = np.random.default_rng(1).normal(0, 1, k).astype(np.float32)
+        ms = np.zeros(1, dtype=np.float32)
+        rc = ref_lib.ref_qmatmul_vec_time(dtype, blocks.ctypes.data, n, k, x.ctypes.data, 5, 50, ms.ctypes.data)
+        assert rc == 0
+        xd = torch.from_numpy(x[None].copy()).cuda()
+        yd = torch.empty((1, n), dtype=torch.float32, device="cuda")
+        mm = fb.QMatMul(w)
+        for _ in range(5):
+            mm.forward(xd.data_ptr(), yd.data_ptr(), 1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(50):
+            mm.forward(xd.data_ptr(), yd.data_ptr(), 1)
+        e1.record()
+        torch.cuda.synchronize()
+        eager = e0.elapsed_time(e1) / 50
+        # the same 50 calls captured once and replayed: device time without
+        # the Python/ctypes launch cost the reference's C loop does not pay
+        old_stream, cap = fbctx.stream, torch.cuda.Stream()
+        fbctx.set_stream(cap.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for _ in range(50):
+                mm.forward(xd.data_ptr(), yd.data_ptr(), 1)
+        fbctx.set_stream(old_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ours = e0.elapsed_time(e1) / 50
+        del g
+        gb = n * k / 256 * (144 if dtype == O.Q4_K else 210) / 1e9
+        rows.append((dtype, n, k, float(ms[0]), ours, eager, gb / (ms[0] * 1e-3), gb / (ours * 1e-3)))
+    print("\n| weight | n x k | reference MMVQ us | this library us (graph) | this library us (Python launches) | "
+          "reference GB/s | this library GB/s | speed-up |")
+    print("|---|---|---|---|---|---|---|---|")
+    for dtype, n, k, r, o, ea, rg, og in rows:
+        print(f"| {'Q4_K' if dtype == O.Q4_K else 'Q6_K'} | {n} x {k} | {r * 1e3:.1f} | {o * 1e3:.1f} | {ea * 1e3:.1f} | "
+              f"{rg:.0f} | {og:.0f} | {r / o:.2f}x |")
+    for row in rows:
+        assert row[4] < row[3], f"slower than the reference on {row[:3]}"
