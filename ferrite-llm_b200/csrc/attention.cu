@@ -11,30 +11,32 @@
 // tokens], V pages token-major, [page][kv head][page tokens][hd], fp16.
 //
 // B200 design (HBM-bound: 2 * ctx * n_kv * hd * 2 bytes per layer and token):
-//  * one thread-block cluster of ATT_SPLITS CTAs per (kv head, sequence); the
-//    sequence's 64-token chunks are split evenly over the cluster at run time
-//    (from the sequence length on the device), so the grid does not depend on
-//    the context length;
+//  * one CTA per (split, kv head, sequence); the sequence's 64-token chunks
+//    are split evenly over the splits at run time (from the sequence length
+//    on the device), so the grid does not depend on the context length;
 //  * each CTA streams its chunks through a ring of `depth` shared-memory
-//    stages with cp.async.bulk (TMA, no multicast) on per-stage mbarriers;
-//  * scores: warp w owns 16 of the 128 dims, lane owns two adjacent tokens;
-//    dim-major K rows are read conflict-free and the G query heads (held as
-//    binary64 in shared memory) are broadcast, so each K element is
-//    converted once and feeds 2G DFMAs; the eight per-warp partial dots are
-//    summed in a fixed order;
-//  * online softmax over the chunks (running max per head, rescale factor
-//    exp(m_old - m_new)); P.V with the lane owning 4 dims of V rows;
-//  * the cluster merges its 16 partial (max, sum, o) sets through
-//    distributed shared memory: CTA r writes dims [8r, 8r+8) of every head,
-//    then (model path) the first G/2 CTAs quantize the result to Q8_K for
-//    the output projection.  No global scratch, counters or atomics.
-//  * a variant without clusters (for the allocation-free entry point, or a
-//    GPU partition that cannot hold a 16-CTA cluster) writes the partials to
-//    global scratch and lets the last CTA of each (kv head, sequence) merge.
-// Dots, exponentials and sums run in binary64 with one rounding to f32 at the
-// end, so the result equals the CPU oracle's single-pass softmax bit for bit
-// whatever the split layout.  All mbarrier waits are bounded: on timeout the
-// kernel raises ERRBIT_WAIT_TIMEOUT in the context's error word.
+//    stages with cp.async.bulk (TMA, no multicast) on per-stage mbarriers; the
+//    four 32-dim quarters of a K page land 32 bytes apart (bank shift);
+//  * warps work independently, without CTA barriers: a chunk is four units
+//    of 16 tokens and warp w takes units w, w + NW, ... (NW divides the 4 *
+//    depth units of one pass over the ring, so a warp meets every stage it
+//    waits on once per pass and never waits a phase ahead).  Per unit the
+//    warp computes the f32 scores (lane = 2 tokens x one 32-dim quarter, the
+//    quarters' slice sums chained in slice order through shuffles), its own
+//    online softmax (running max per head, binary64 exponentials spread over
+//    all lanes) and P.V (lane = 4 dims, binary64).  The last of a chunk's four
+//    units refills its stage;
+//  * the CTA merges its warps' (max, sum, o) partials in shared memory, then
+//    the splits merge either through distributed shared memory in a 16-CTA
+//    cluster (CTA r owns dims [8r, 8r+8) of every head; push, no atomics), or
+//    through global partials and a last-CTA merge (model path, and the
+//    allocation-free entry point); the result is written as f32 and, in the
+//    model path, as the Q8_K rows of the output projection.
+// Dots are f32 in the CPU oracle's fixed order; exponentials, sums and P.V
+// run in binary64 with one rounding to f32 at the end, so the result equals
+// the CPU oracle's single-pass softmax bit for bit whatever the split and
+// warp layout.  All mbarrier waits are bounded: on timeout the kernel raises
+// ERRBIT_WAIT_TIMEOUT in the context's error word.
 #include <math.h>
 
 #include <algorithm>
@@ -51,40 +53,50 @@ namespace fb {
 
 constexpr int ATT_HD = 128;
 constexpr int ATT_CHUNK = 64;  // tokens per pipeline stage (one or two pages)
-constexpr int ATT_SLICES = 8;  // 16-dim slices of the f32 score dot (fixed: the oracle's order)
-// warps per CTA: 16 for GQA groups up to 4, 8 for groups of 8 (whose per-warp
-// P.V partials would not fit the ring)
-__host__ __device__ constexpr int att_warps(int G) { return G <= 4 ? 16 : 8; }
+constexpr int ATT_UNIT = 16;   // tokens per warp work unit (four per chunk)
+// warps per CTA: 16 for GQA groups up to 4, 8 for groups of 8 (their binary64
+// P.V accumulators double) and for the cluster variant (two-stage ring)
+__host__ __device__ constexpr int att_warps(int G, bool cluster) { return G <= 4 && !cluster ? 16 : 8; }
+__host__ __device__ constexpr int att_depth(bool cluster) { return cluster ? 2 : 4; }
 constexpr int ATT_DPR = ATT_HD / ATT_SPLITS;  // output dims merged per cluster rank
 constexpr int ATT_MAX_DEPTH = 4;
-constexpr int ATT_KPAD = 64;  // bytes between the two K pages of a 32-token-page chunk (bank shift)
-constexpr uint32_t ATT_STAGE_K = ATT_CHUNK * ATT_HD * 2 + ATT_KPAD;  // K^T region of a stage
-constexpr uint32_t ATT_STAGE = ATT_STAGE_K + ATT_CHUNK * ATT_HD * 2;  // + V region
+constexpr int ATT_QPAD = 32;  // bytes between the four 32-dim quarters of a staged K page
+constexpr uint32_t ATT_STAGE_K = 2 * (32 * ATT_HD * 2 + 4 * ATT_QPAD);  // K region of a stage (two 32-token pages)
+constexpr uint32_t ATT_STAGE = ATT_STAGE_K + ATT_CHUNK * ATT_HD * 2;     // + V region
+static_assert(ATT_CHUNK * ATT_HD * 2 + 4 * ATT_QPAD <= ATT_STAGE_K, "one 64-token K page must fit the K region");
+static_assert(4 * att_depth(false) % att_warps(1, false) == 0 && 4 * att_depth(false) % att_warps(8, false) == 0 &&
+                  4 * att_depth(true) % att_warps(1, true) == 0,
+              "a pass over the ring must hand every warp whole units");
 
 __device__ __forceinline__ int seq_len_of(const AttnArgs &A, int b) {
     return A.seq_lens ? A.seq_lens[b] : A.pos[b] + 1;
 }
+
+// q in shared memory: [hd][G] f32 with G floats of padding after each 32-dim
+// quarter, so the four quarter groups of a warp read different banks
+__host__ __device__ constexpr int att_qidx(int d, int g, int G) { return (d + (d >> 5)) * G + g; }
 
 __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane, const Q8Act &a, int64_t row,
                                                    int64_t blk);
 
 // Dynamic shared memory of one CTA (byte offsets).
 struct AttnLayout {
-    size_t q, part, p, misc, inbox, q8in, bt, total;
+    size_t q, ss, pb, misc, inbox, q8in, bt, total;
 };
-__host__ __device__ inline AttnLayout attn_layout(int G, int depth, int bt_cap) {
+__host__ __device__ inline AttnLayout attn_layout(int G, int NW, int depth, int bt_cap) {
     AttnLayout L;
-    size_t off = (size_t)depth * ATT_STAGE;
+    size_t off = (size_t)depth * ATT_STAGE;  // the ring; [NW][G][hd] f64 warp partials at the end
     off = (off + 127) & ~(size_t)127;
-    L.q = off;  // q[hd][G] f32; merged outputs (f32) at the end
-    off += (size_t)ATT_HD * G * 4;
-    L.part = off;  // part[warp][G][chunk] f32 slice dots; CTA partial o[G][hd] f64 at the end
-    const size_t part_bytes = (size_t)ATT_SLICES * G * ATT_CHUNK * 4, o_bytes = (size_t)G * ATT_HD * 8;
-    off += part_bytes > o_bytes ? part_bytes : o_bytes;
-    L.p = off;  // p[chunk][G] f64
-    off += (size_t)ATT_CHUNK * G * 8;
-    L.misc = off;  // alpha[G] M[G] L[G] ls[warps] wts[G][S] wl[G][S] f64 (S up to ATT_SPLITS_MAX)
-    off += (size_t)(3 * G + att_warps(G) + 2 * G * ATT_SPLITS_MAX) * 8;
+    L.q = off;  // q (att_qidx layout); merged outputs [G][hd] f32 at the end
+    off += (size_t)(ATT_HD + 4) * G * 4;
+    off = (off + 15) & ~(size_t)15;
+    L.ss = off;  // per warp: scores [unit token][G] f32
+    off += (size_t)NW * ATT_UNIT * G * 4;
+    off = (off + 15) & ~(size_t)15;
+    L.pb = off;  // per warp: p [unit token][G] f64; CTA partial o [G][hd] f64 at the end
+    off += (size_t)NW * ATT_UNIT * G * 8;
+    L.misc = off;  // M[G] L[G] tmp[G] mw[NW][G] lw[NW][G] wt[NW][G] wts[G][S] wl[G][S] f64
+    off += (size_t)(3 * G + 3 * NW * G + 2 * G * ATT_SPLITS_MAX) * 8;
     L.inbox = off;  // cluster merge: [src rank][G][ATT_DPR + 2] f64 pushed by the peers
     off += (size_t)ATT_SPLITS * G * (ATT_DPR + 2) * 8;
     L.q8in = off;  // cluster merge: [2][hd] f32 outputs of one Q8_K block
@@ -103,55 +115,78 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// G consecutive f32 from shared memory (16-byte aligned for G >= 4).
+template <int G>
+__device__ __forceinline__ void lds_f32(float (&v)[G], const float *p) {
+    if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < G; i += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(p + i);
+            v[i] = x.x;
+            v[i + 1] = x.y;
+            v[i + 2] = x.z;
+            v[i + 3] = x.w;
+        }
+    } else if constexpr (G == 2) {
+        const float2 x = *reinterpret_cast<const float2 *>(p);
+        v[0] = x.x;
+        v[1] = x.y;
+    } else {
+        v[0] = p[0];
+    }
+}
+
 // grid (splits, n_kv, batch): CLUSTER: ATT_SPLITS splits, cluster dims
-// (ATT_SPLITS, 1, 1); otherwise A.nsplit (<= ATT_SPLITS_MAX) splits.
+// (ATT_SPLITS, 1, 1); otherwise gridDim.x (<= ATT_SPLITS_MAX) splits.
 //
 // Numerics (identical to the CPU oracle, or_attn_dot / or_exp64):
 //   s_t = f32 dot of q and k_t in eight 16-dim fused-multiply-add slices,
 //         summed in slice order, times scale
-//   per CTA:  running max m, p_t = exp64(s_t - m), l = sum p_t,
+//   per warp: running max m, p_t = exp64(s_t - m), l = sum p_t,
 //             o = sum p_t v_t, rescaled by exp64(m_old - m_new)  (binary64)
-//   merge:    M = max m, w = exp64(m - M), out = f32(sum w*o / sum w*l)
+//   merges (warps of a CTA, then splits): M = max m, w = exp64(m - M),
+//             out = f32(sum w*o / sum w*l)
 // The binary64 stages make the result independent of how the tokens are
 // split (up to binary64 rounding, far below the final f32 rounding).
 template <int G, bool CLUSTER>
-__global__ void __launch_bounds__(32 * att_warps(G), 1)
+__global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq, int use_q8, int *__restrict__ counters,
                   int depth, int bt_cap) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[ATT_MAX_DEPTH];
+    __shared__ int used[ATT_MAX_DEPTH];  // units consumed per stage (the fourth of a chunk refills it)
     __shared__ int s_len, s_first, s_mine, s_last, s_last2;
     __shared__ __half s_newkv[2 * ATT_HD];  // fused prologue: the new token's k and v (fp16)
     constexpr int S = ATT_SPLITS;
     const int ns = CLUSTER ? S : (int)gridDim.x;  // splits of this (kv head, sequence)
-    constexpr int NW = att_warps(G), NT = 32 * NW;
-    constexpr int TPC = ATT_CHUNK / NW;          // tokens per warp in the P.V phase
-    constexpr int TPL = ATT_CHUNK * ATT_SLICES / NT;  // tokens per lane in the score phase (2 or 1)
-    constexpr int NWB = 2 * G < NW ? 2 * G : NW;      // softmax warps: one lane per (token, head)
-    constexpr int TPB = ATT_CHUNK * G / NWB;          // tokens per softmax warp (32 or 64)
-    constexpr int IB = ATT_DPR + 2;                 // inbox doubles per (source rank, head)
+    constexpr int NW = att_warps(G, CLUSTER), NT = 32 * NW;
+    constexpr int GH = G >= 2 ? G / 2 : 1;  // heads exponentiated per lane
+    constexpr int IB = ATT_DPR + 2;         // inbox doubles per (source rank, head)
+    constexpr unsigned FULL = 0xffffffffu;
     // peers may push into this CTA's shared memory once every CTA of the
     // cluster has started: arrive now, wait just before the first push
     if constexpr (CLUSTER) cluster_arrive_relaxed();
     const int rank = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int P = A.page_size, PPC = ATT_CHUNK / P;  // pages per chunk
-    const AttnLayout Ly = attn_layout(G, depth, bt_cap);
+    const AttnLayout Ly = attn_layout(G, NW, depth, bt_cap);
     uint8_t *ring = smem;
     float *q_s = reinterpret_cast<float *>(smem + Ly.q);
-    float *part = reinterpret_cast<float *>(smem + Ly.part);
-    double *p_s = reinterpret_cast<double *>(smem + Ly.p);
-    double *alpha_s = reinterpret_cast<double *>(smem + Ly.misc);
-    double *M_s = alpha_s + G, *L_s = M_s + G, *ls = L_s + G, *wts = ls + NW, *wl = wts + G * ATT_SPLITS_MAX;
+    double *M_s = reinterpret_cast<double *>(smem + Ly.misc);
+    double *L_s = M_s + G, *tmpM = L_s + G, *mw = tmpM + G, *lw = mw + NW * G, *wt = lw + NW * G;
+    double *wts = wt + NW * G, *wl = wts + G * ATT_SPLITS_MAX;
     double *inbox = reinterpret_cast<double *>(smem + Ly.inbox);
     float *q8in = reinterpret_cast<float *>(smem + Ly.q8in);
     int *bt_s = reinterpret_cast<int *>(smem + Ly.bt);
-    double *O_s = reinterpret_cast<double *>(part);  // [G][hd] CTA partial at the end
-    double *red = reinterpret_cast<double *>(ring);  // [warps][G][hd] at the end
-    float *fin = q_s;                                // merged outputs at the end
+    double *O_s = reinterpret_cast<double *>(smem + Ly.pb);  // [G][hd] CTA partial at the end
+    double *red = reinterpret_cast<double *>(ring);          // [NW][G][hd] warp partials at the end
+    float *fin = q_s;                                        // merged outputs at the end
 
     if (tid == 0) {
-        for (int i = 0; i < depth; i++) mbar_init(&full[i], 1);
+        for (int i = 0; i < depth; i++) {
+            mbar_init(&full[i], 1);
+            used[i] = 0;
+        }
         mbar_fence_init();
         // sequence lengths are inputs of the whole step (written before it began)
         int len = seq_len_of(A, b);
@@ -182,9 +217,31 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
         }
         bt_s[i] = page;
     }
+    // the chunk holding the newest position: without the fused prologue its
+    // newest token is written by the preceding kernel, so it is copied after
+    // griddepcontrol.wait; every other copy streams in before the wait
+    const int jf = len > 0 ? (len - 1) / ATT_CHUNK - first : -1;
+    const bool owner = jf >= 0 && jf < mine;
+    const int pre = min(mine, depth);
+    // fused prologue: warp hh < G transforms q head hh, warps G and G + 1 (the
+    // newest chunk's owner) the new k and v; their gains and RoPE factors
+    // depend only on weights and the position: their loads are issued here,
+    // in flight together with the block-table reads above
+    const int nwork = A.qkv && len > 0 ? G + (owner ? 2 : 0) : 0;
+    QkHead qh{};
+    if (warp < nwork && warp <= G)
+        qh = qk_head_load(lane, A.q_norm ? (warp < G ? A.q_norm : A.k_norm) : nullptr,
+                          A.rope_cos + (int64_t)(len - 1) * (ATT_HD / 2), A.rope_sin + (int64_t)(len - 1) * (ATT_HD / 2),
+                          A.rope_mode);
     __syncthreads();
-    const uint32_t pbytes = (uint32_t)P * ATT_HD * 2;  // one K (or V) page
-    auto issue = [&](int j) {                          // chunk j of this CTA into stage j % depth
+    const uint32_t pbytes = (uint32_t)P * ATT_HD * 2;         // one K (or V) page
+    const uint32_t KPG = pbytes + 4 * ATT_QPAD;               // staged K page stride
+    const uint32_t KQS = pbytes / 4 + ATT_QPAD;               // staged K quarter stride (32 dims)
+    const uint32_t KROW = 2u * P;                             // bytes between consecutive dims
+    auto k_at = [&](uint8_t *kst, int d, int tc) -> __half * {  // staged K element (dim d, chunk token tc)
+        return reinterpret_cast<__half *>(kst + (tc / P) * KPG + (d >> 5) * KQS + (d & 31) * KROW + (tc % P) * 2);
+    };
+    auto issue = [&](int j) {  // chunk j of this CTA into stage j % depth
         const int st = j % depth;
         uint8_t *kd = ring + (size_t)st * ATT_STAGE;
         uint8_t *vd = kd + ATT_STAGE_K;
@@ -196,29 +253,15 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             const int page = bt_s[j * PPC + i];
             if (page < 0) continue;
             const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
-            bulk_g2s(kd + i * (pbytes + ATT_KPAD), reinterpret_cast<const __half *>(A.kpool) + off, pbytes,
-                     &full[st]);
+            const uint8_t *ks = reinterpret_cast<const uint8_t *>(reinterpret_cast<const __half *>(A.kpool) + off);
+#pragma unroll
+            for (int h = 0; h < 4; h++) bulk_g2s(kd + i * KPG + h * KQS, ks + h * (pbytes / 4), pbytes / 4, &full[st]);
             bulk_g2s(vd + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes, &full[st]);
         }
     };
-    // the chunk holding the newest position: without the fused prologue its
-    // newest token is written by the preceding kernel, so it is copied after
-    // griddepcontrol.wait; every other copy streams in before the wait
-    const int jf = len > 0 ? (len - 1) / ATT_CHUNK - first : -1;
-    const bool owner = jf >= 0 && jf < mine;
-    const int pre = min(mine, depth);
     if (tid == 0)
         for (int j = 0; j < pre; j++)
             if (j != jf || A.qkv) issue(j);
-    // fused prologue: warp hh < G transforms q head hh, warps G and G + 1 (the
-    // newest chunk's owner) the new k and v; their gains and RoPE factors
-    // depend only on weights and the position, so they are loaded before the wait
-    const int nwork = A.qkv && len > 0 ? G + (owner ? 2 : 0) : 0;
-    QkHead qh{};
-    if (warp < nwork && warp <= G)
-        qh = qk_head_load(lane, A.q_norm ? (warp < G ? A.q_norm : A.k_norm) : nullptr,
-                          A.rope_cos + (int64_t)(len - 1) * (ATT_HD / 2), A.rope_sin + (int64_t)(len - 1) * (ATT_HD / 2),
-                          A.rope_mode);
     pdl_wait();
     pdl_launch();  // the next kernel may start streaming its weights
     if (tid == 0 && !A.qkv && jf >= 0 && jf < pre) issue(jf);
@@ -239,12 +282,12 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             if (is_q || is_k) qk_head_apply(v, lane, qh, A.eps, A.rope_mode);
             if (is_q) {
 #pragma unroll
-                for (int e = 0; e < 4; e++) q_s[(4 * lane + e) * G + hh] = v[e];
+                for (int e = 0; e < 4; e++) q_s[att_qidx(4 * lane + e, hh, G)] = v[e];
                 if (rank == 0 && A.q_out)
                     *reinterpret_cast<float4 *>(A.q_out + ((int64_t)b * A.n_heads + kvh * G + hh) * ATT_HD +
                                                 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
             } else {
-                // into the KV pool (for later steps) and, below, into the staged chunk
+                // into the KV pool (for later steps) and, in the main loop, into the staged chunk
                 const int tc = p % ATT_CHUNK, page = bt_s[jf * PPC + tc / P], slot = p % P;
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
@@ -264,137 +307,171 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
         }
     } else {
         const float *qg = A.q + ((int64_t)b * A.n_heads + (int64_t)kvh * G) * ATT_HD;
-        for (int i = tid; i < G * ATT_HD; i += NT) q_s[(i % ATT_HD) * G + i / ATT_HD] = qg[i];
+        for (int i = tid; i < G * ATT_HD; i += NT) q_s[att_qidx(i % ATT_HD, i / ATT_HD, G)] = qg[i];
     }
+    __syncthreads();  // q and the new token's k / v are staged
 
-    const int hg = warp % G, kb = warp / G;  // softmax phase: head and token block of this warp
-    float m_run = -INFINITY;
-    double l_lane = 0.0, psum = 0.0;
-    double o[G][4];
+    // ---- main loop: this warp's units
+    float *ssw = reinterpret_cast<float *>(smem + Ly.ss) + warp * ATT_UNIT * G;
+    double *pbw = reinterpret_cast<double *>(smem + Ly.pb) + warp * ATT_UNIT * G;
+    const int ti = lane & 7, qq4 = lane >> 3;  // score phase: token pair, 32-dim quarter
+    float m_run[G];
+    double o[G][4], lp[GH];
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int g = 0; g < G; g++) {
+        m_run[g] = -INFINITY;
 #pragma unroll
         for (int e = 0; e < 4; e++) o[g][e] = 0.0;
+    }
+#pragma unroll
+    for (int k = 0; k < GH; k++) lp[k] = 0.0;
     bool ok = true;
-    // score phase: warp = (slice sl, token group); the lane's TPL adjacent
-    // tokens start at tk inside a stage's K^T region
-    const int sl = warp % ATT_SLICES;
-    const int tk = TPL * lane + 32 * TPL * (warp / ATT_SLICES);
-    const uint32_t k_lane = (uint32_t)((tk / P) * (pbytes + ATT_KPAD) + (tk % P) * 2);
-    const uint32_t k_row = 2u * P;  // bytes between consecutive dims
-
-    for (int j = 0; j < mine; j++) {
-        // every warp is done with chunk j-1 (and q is staged): its stage takes chunk j-1+depth
-        __syncthreads();
-        if (tid == 0 && j >= 1 && j - 1 + depth < mine) {
-            fence_proxy_async_smem();
-            issue(j - 1 + depth);
-        }
-        const int st = j % depth;
-        const uint8_t *kst = ring + (size_t)st * ATT_STAGE;
-        const __half *Vs = reinterpret_cast<const __half *>(kst + ATT_STAGE_K);
-        const int ntok = min(ATT_CHUNK, len - (first + j) * ATT_CHUNK);
+    for (int u = warp; u < 4 * mine; u += NW) {
+        const int j = u >> 2, qu = u & 3, st = j % depth;
+        uint8_t *kst = ring + (size_t)st * ATT_STAGE;
+        __half *Vs = reinterpret_cast<__half *>(kst + ATT_STAGE_K);
+        const int tok0 = (first + j) * ATT_CHUNK + ATT_UNIT * qu;  // position of the unit's first token
+        const int nt = min(ATT_UNIT, len - tok0);                  // tokens of the unit (<= 0: none)
         ok = mbar_wait_bounded(&full[st], (uint32_t)(j / depth) & 1u) && ok;
-        if (A.qkv && j == jf) {
-            // the staged copy of the newest chunk predates this step's token: patch it in
-            if (tid < ATT_HD) {
+        if (nt > 0) {
+            if (A.qkv && len - 1 < tok0 + ATT_UNIT) {
+                // this unit holds the newest token, whose staged copy predates
+                // this step: patch in the k / v the prologue produced
                 const int tc = (len - 1) % ATT_CHUNK;
-                *reinterpret_cast<__half *>(const_cast<uint8_t *>(kst) + (tc / P) * (pbytes + ATT_KPAD) +
-                                            tid * k_row + (tc % P) * 2) = s_newkv[tid];
-                const_cast<__half *>(Vs)[(size_t)tc * ATT_HD + tid] = s_newkv[ATT_HD + tid];
-            }
-            __syncthreads();
-        }
-        // ---- scores: f32 dot over slice sl (16 dims) for this lane's tokens
-        {
-            float acc[TPL][G];
 #pragma unroll
-            for (int u = 0; u < TPL; u++)
-#pragma unroll
-                for (int g = 0; g < G; g++) acc[u][g] = 0.f;
-            const uint8_t *kp = kst + k_lane + (size_t)(sl * 16) * k_row;
-            const float *qw = q_s + sl * 16 * G;
-#pragma unroll
-            for (int e = 0; e < 16; e++) {
-                float kf[TPL];
-                if constexpr (TPL == 2) {
-                    const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(kp + e * k_row));
-                    kf[0] = k2.x;
-                    kf[TPL - 1] = k2.y;
-                } else {
-                    kf[0] = __half2float(*reinterpret_cast<const __half *>(kp + e * k_row));
+                for (int e = 0; e < 4; e++) {
+                    const int d = 4 * lane + e;
+                    *k_at(kst, d, tc) = s_newkv[d];
+                    Vs[(size_t)tc * ATT_HD + d] = s_newkv[ATT_HD + d];
                 }
+                __syncwarp();
+            }
+            // ---- scores: lane (ti, qq4) dots tokens 2ti, 2ti + 1 of the unit
+            // over dims [32 qq4, 32 qq4 + 32) as two 16-dim slices
+            float acc[2][2][G];
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    const float qv = qw[e * G + g];
+            for (int sl = 0; sl < 2; sl++)
 #pragma unroll
-                    for (int u = 0; u < TPL; u++) acc[u][g] = __fmaf_rn(qv, kf[u], acc[u][g]);
+                for (int t = 0; t < 2; t++)
+#pragma unroll
+                    for (int g = 0; g < G; g++) acc[sl][t][g] = 0.f;
+            {
+                const int tc = ATT_UNIT * qu + 2 * ti;
+                const uint8_t *kp = reinterpret_cast<const uint8_t *>(k_at(kst, 32 * qq4, tc));
+                const float *qw = q_s + att_qidx(32 * qq4, 0, G);
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+#pragma unroll
+                    for (int sl = 0; sl < 2; sl++) {
+                        const int r = 16 * sl + e;
+                        const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(kp + r * KROW));
+                        float qv[G];
+                        lds_f32<G>(qv, qw + r * G);
+#pragma unroll
+                        for (int g = 0; g < G; g++) {
+                            acc[sl][0][g] = __fmaf_rn(qv[g], k2.x, acc[sl][0][g]);
+                            acc[sl][1][g] = __fmaf_rn(qv[g], k2.y, acc[sl][1][g]);
+                        }
+                    }
                 }
             }
+            // slice sums in slice order: quarter 0 adds s0 + s1, quarter q
+            // continues with s_2q, s_2q+1 from quarter q - 1's running sum
+            float T[2][G];
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+#pragma unroll
+                for (int g = 0; g < G; g++) T[t][g] = __fadd_rn(acc[0][t][g], acc[1][t][g]);
+#pragma unroll
+            for (int q = 1; q < 4; q++)
+#pragma unroll
+                for (int t = 0; t < 2; t++)
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        const float x = __shfl_sync(FULL, T[t][g], ti + 8 * (q - 1));
+                        if (qq4 == q) T[t][g] = __fadd_rn(__fadd_rn(x, acc[0][t][g]), acc[1][t][g]);
+                    }
+            // quarter 3 holds the full dots: scale, mask, unit max per head
+            float mx[G];
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                if constexpr (TPL == 2)
-                    *reinterpret_cast<float2 *>(&part[(sl * G + g) * ATT_CHUNK + tk]) = make_float2(acc[0][g], acc[TPL - 1][g]);
-                else
-                    part[(sl * G + g) * ATT_CHUNK + tk] = acc[0][g];
-            }
-        }
-        __syncthreads();
-        // ---- softmax on the first NWB warps, each with full lanes: warp
-        // (hg, kb) sums the slice dots of all 64 tokens of head hg (for the
-        // chunk max) and exponentiates its block of TPB tokens; the rescale
-        // factor exp(m_old - m_new) is computed once per head (kb == 0)
-        if (warp < NWB) {
-            float sc[2];
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int t = lane + 32 * h;
-                float sum = part[hg * ATT_CHUNK + t];
-#pragma unroll
-                for (int w = 1; w < ATT_SLICES; w++) sum = __fadd_rn(sum, part[(w * G + hg) * ATT_CHUNK + t]);
-                sc[h] = t < ntok ? __fmul_rn(sum, A.scale) : -INFINITY;
-            }
-            float mp = fmaxf(sc[0], sc[1]);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, off));
-            const float m_new = fmaxf(m_run, mp);  // finite: the chunk holds at least one token
-            if (kb == 0 && lane == 0)
-                alpha_s[hg] = m_run == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run, (double)m_new));
-            m_run = m_new;
-            psum = 0.0;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int t = lane + 32 * h;
-                if (t / TPB == kb) {  // warp-uniform
-                    const double p = t < ntok ? exp64(__dsub_rn((double)sc[h], (double)m_new)) : 0.0;
-                    p_s[t * G + hg] = p;
-                    psum = __dadd_rn(psum, p);
+                const float s0 = 2 * ti < nt ? __fmul_rn(T[0][g], A.scale) : -INFINITY;
+                const float s1 = 2 * ti + 1 < nt ? __fmul_rn(T[1][g], A.scale) : -INFINITY;
+                if (qq4 == 3) {
+                    ssw[(2 * ti) * G + g] = s0;
+                    ssw[(2 * ti + 1) * G + g] = s1;
                 }
+                mx[g] = fmaxf(s0, s1);
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) mx[g] = fmaxf(mx[g], __shfl_xor_sync(FULL, mx[g], off));
+                mx[g] = __shfl_sync(FULL, mx[g], 24);
             }
-        }
-        __syncthreads();
-        // ---- o = alpha * o + sum_t p_t v_t over this warp's TPC tokens; lane owns 4 dims
-        {
+            __syncwarp();
+            // online softmax of this warp: the rescale factor only when the running max moves
+            double al[G];
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const double al = alpha_s[g];
-                if (al != 1.0)  // the running max moved (uniform across the CTA)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al);
+                const float mn = fmaxf(m_run[g], mx[g]);  // finite: the unit holds a token
+                al[g] = 1.0;
+                if (mn != m_run[g]) {  // warp-uniform
+                    al[g] = m_run[g] == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run[g], (double)mn));
+                    m_run[g] = mn;
+                }
             }
-            if (warp < NWB) l_lane = __dadd_rn(__dmul_rn(l_lane, alpha_s[hg]), psum);
-            const int t0 = warp * TPC, t1 = min(t0 + TPC, ntok);
-            for (int t = t0; t < t1; t++) {
-                const uint2 vr = *reinterpret_cast<const uint2 *>(Vs + (size_t)t * ATT_HD + 4 * lane);
+            // p = exp64(s - m): lane (t = lane & 15) takes heads of parity lane >> 4
+            {
+                const int t = lane & 15, hp = lane >> 4;
+#pragma unroll
+                for (int k = 0; k < GH; k++) {
+                    if (G >= 2 || hp == 0) {
+                        const int g = G >= 2 ? 2 * k + hp : 0;
+                        const float mg = G >= 2 ? (hp ? m_run[G >= 2 ? 2 * k + 1 : 0] : m_run[2 * k]) : m_run[0];
+                        const double ag = G >= 2 ? (hp ? al[G >= 2 ? 2 * k + 1 : 0] : al[2 * k]) : al[0];
+                        const double p = t < nt ? exp64(__dsub_rn((double)ssw[t * G + g], (double)mg)) : 0.0;
+                        pbw[t * G + g] = p;
+                        lp[k] = __dadd_rn(__dmul_rn(lp[k], ag), p);
+                    }
+                }
+            }
+            __syncwarp();
+            // ---- o = al * o + sum_t p_t v_t; lane owns dims [4 lane, 4 lane + 4)
+#pragma unroll
+            for (int g = 0; g < G; g++)
+                if (al[g] != 1.0)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al[g]);
+            const __half *vrow = Vs + (size_t)(ATT_UNIT * qu) * ATT_HD + 4 * lane;
+#pragma unroll 4
+            for (int t = 0; t < nt; t++) {
+                const uint2 vr = *reinterpret_cast<const uint2 *>(vrow + (size_t)t * ATT_HD);
                 const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
                 const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
                 const double vd[4] = {(double)v01.x, (double)v01.y, (double)v23.x, (double)v23.y};
+                double pg[G];
+                if constexpr (G >= 2) {
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    const double pg = p_s[t * G + g];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) o[g][e] = __fma_rn(pg, vd[e], o[g][e]);
+                    for (int g = 0; g < G; g += 2) {
+                        const double2 x = *reinterpret_cast<const double2 *>(pbw + t * G + g);
+                        pg[g] = x.x;
+                        pg[g + 1] = x.y;
+                    }
+                } else {
+                    pg[0] = pbw[t];
                 }
+#pragma unroll
+                for (int g = 0; g < G; g++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) o[g][e] = __fma_rn(pg[g], vd[e], o[g][e]);
+            }
+        }
+        // this warp is done with the unit's slice of stage st; the fourth unit
+        // of the chunk refills the stage with chunk j + depth
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if ((atomicAdd(&used[st], 1) & 3) == 3 && j + depth < mine) {
+                fence_proxy_async_smem();
+                issue(j + depth);
             }
         }
     }
@@ -410,28 +487,48 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
         }
         __syncthreads();
     }
-    // ---- CTA partial: o summed over warps (fixed order), l, running max
-    {
-        const double lw = warp_sum64(l_lane);  // zero outside the softmax warps
-        if (lane == 0) ls[warp] = lw;
-        if (lane == 0 && warp < G) M_s[warp] = (double)m_run;  // warp g < G owns head g
-    }
+    // ---- CTA partial: the warps' (max, sum, o) merged in fixed warp order
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
+#pragma unroll
+    for (int k = 0; k < GH; k++) {
+        double v = lp[k];
+        if constexpr (G >= 2) {
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(FULL, v, off));
+            if ((lane & 15) == 0) lw[warp * G + 2 * k + (lane >> 4)] = v;
+        } else {
+            v = warp_sum64(v);
+            if (lane == 0) lw[warp * G] = v;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        if (lane == g) mw[warp * G + g] = (double)m_run[g];
+    __syncthreads();
+    if (tid < NW * G) {
+        const int g = tid % G;
+        double M = -INFINITY;
+        for (int w = 0; w < NW; w++) M = fmax(M, mw[w * G + g]);
+        const double m = mw[tid];
+        wt[tid] = m == -INFINITY ? 0.0 : exp64(__dsub_rn(m, M));
+        if (tid < G) tmpM[g] = M;
+    }
     __syncthreads();
     for (int i = tid; i < G * ATT_HD; i += NT) {
         const int g = i / ATT_HD, d = i % ATT_HD;
-        double sum = red[g * ATT_HD + d];
-#pragma unroll
-        for (int w = 1; w < NW; w++) sum = __dadd_rn(sum, red[(w * G + g) * ATT_HD + d]);
+        double sum = 0.0;
+#pragma unroll 8
+        for (int w = 0; w < NW; w++) sum = __fma_rn(wt[w * G + g], red[(w * G + g) * ATT_HD + d], sum);
         O_s[i] = sum;
     }
     if (tid < G) {
         double l = 0.0;
-        for (int w = tid; w < NW; w += G) l = __dadd_rn(l, ls[w]);
+        for (int w = 0; w < NW; w++) l = __fma_rn(wt[w * G + tid], lw[w * G + tid], l);
         L_s[tid] = l;
+        M_s[tid] = tmpM[tid];
     }
     constexpr unsigned wmask = G * S >= 32 ? 0xffffffffu : (1u << (G * S)) - 1u;
     if constexpr (CLUSTER) {
@@ -480,11 +577,11 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
             }
         }
     } else {
-        // partial slots per head: the ns splits, then -- more than ATT_SPLITS
-        // splits -- one merged slot per group of ATT_GROUP splits (two-level
-        // merge: the last CTA of a group merges its group, the last group
-        // merger merges the groups)
-        const int ng = ns > ATT_SPLITS ? ns / ATT_GROUP : 0;
+        // partial slots per head: the ns splits, then -- more than
+        // ATT_MERGE1_MAX splits (a multiple of ATT_GROUP) -- one merged slot per
+        // group of ATT_GROUP splits (two-level merge: the last CTA of a group
+        // merges its group, the last group merger merges the groups)
+        const int ng = ns > ATT_MERGE1_MAX ? ns / ATT_GROUP : 0;
         const int sst = ns + ng;
         const int64_t hb0 = ((int64_t)b * A.n_heads + (int64_t)kvh * G) * sst;
         __syncthreads();
@@ -524,7 +621,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
                         wl[g * ATT_SPLITS_MAX + r] = __dmul_rn(w, Lr[k]);
                     }
                 }
-                if (lane == 0) alpha_s[g] = M;
+                if (lane == 0) tmpM[g] = M;
             }
             __syncthreads();
             for (int i = tid; i < G * ATT_HD; i += NT) {
@@ -546,7 +643,7 @@ __global__ void __launch_bounds__(32 * att_warps(G), 1)
                 if (dst >= 0) {
                     A.part_o[(hb0 + (int64_t)g * sst + dst) * ATT_HD + d] = O;
                     if (d == 0) {
-                        A.part_ml[2 * (hb0 + (int64_t)g * sst + dst)] = alpha_s[g];
+                        A.part_ml[2 * (hb0 + (int64_t)g * sst + dst)] = tmpM[g];
                         A.part_ml[2 * (hb0 + (int64_t)g * sst + dst) + 1] = L;
                     }
                 } else {
@@ -680,7 +777,7 @@ static bool attn_cluster_fits(int device, size_t smem) {
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(ATT_SPLITS, 1, 1);
-        cfg.blockDim = dim3(32 * att_warps(G));
+        cfg.blockDim = dim3(32 * att_warps(G, true));
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
@@ -698,12 +795,20 @@ static bool attn_plan(fb_ctx *ctx, const AttnArgs &A, int batch, bool want_clust
     *bt_cap = attn_bt_cap(A.max_pages, A.page_size);
     // clusters: two stages keep a CTA under half of an SM's shared memory, so
     // a 16-CTA cluster fits a GPC even where other work holds some SMs.
-    // Without clusters: three stages (over half of the shared memory, so one
+    // Without clusters: four stages (over half of the shared memory, so one
     // CTA per SM: the scheduler spreads the grid over all SMs).
     (void)batch;
-    *depth = want_cluster ? 2 : 3;
-    *smem = attn_layout(G, *depth, *bt_cap).total;
-    return want_cluster && attn_cluster_fits<G>(ctx->device, *smem);
+    bool cluster = false;
+    if (want_cluster) {
+        *depth = att_depth(true);
+        *smem = attn_layout(G, att_warps(G, true), *depth, *bt_cap).total;
+        cluster = attn_cluster_fits<G>(ctx->device, *smem);
+    }
+    if (!cluster) {
+        *depth = att_depth(false);
+        *smem = attn_layout(G, att_warps(G, false), *depth, *bt_cap).total;
+    }
+    return cluster;
 }
 
 bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch) {
@@ -724,14 +829,16 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
     int depth, bt_cap;
     size_t smem;
     const bool cluster = attn_plan<G>(ctx, A, batch, want_cluster, &depth, &bt_cap, &smem);
-    // cluster-free merge: more splits while the grid is under one wave (one
-    // CTA per SM) and every split still gets a chunk of the longest sequence
+    // cluster-free merge: as many splits as fill one wave (one CTA per SM),
+    // at least ATT_SPLITS, each with a chunk of the longest sequence; above
+    // ATT_MERGE1_MAX a multiple of ATT_GROUP (two-level merge)
     int ns = ATT_SPLITS;
     if (!cluster) {
-        const int nch = (max_seq_len + ATT_CHUNK - 1) / ATT_CHUNK;
-        while (2 * ns <= A.nsplit_max && 2 * ns <= ATT_SPLITS_MAX && (int64_t)A.n_kv * batch * 2 * ns <= ctx->num_sms &&
-               2 * ns <= nch)
-            ns *= 2;
+        const int64_t nch = (max_seq_len + ATT_CHUNK - 1) / ATT_CHUNK;
+        int64_t want = std::min<int64_t>({(int64_t)ctx->num_sms / ((int64_t)A.n_kv * batch), (int64_t)A.nsplit_max,
+                                          (int64_t)ATT_SPLITS_MAX, nch});
+        if (want > ATT_MERGE1_MAX) want -= want % ATT_GROUP;
+        ns = (int)std::max<int64_t>(ns, want);
     }
     FB_REQUIRE(cluster || (counters && A.part_o && A.part_ml), "attn: the cluster-free merge needs scratch");
     Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};
@@ -746,7 +853,7 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.gridDim = dim3(cluster ? ATT_SPLITS : ns, A.n_kv, batch);
-    cfg.blockDim = dim3(32 * att_warps(G));
+    cfg.blockDim = dim3(32 * att_warps(G, cluster));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
     cfg.attrs = attr;

@@ -196,7 +196,8 @@ void launch_attn_prefill(fb_ctx *ctx, const float *q, const void *kpool, const v
 // Paged flash-decode attention (attention.cu).
 constexpr int ATT_SPLITS = 16;      // attention splits (cluster CTAs) per (kv head, sequence)
 constexpr int ATT_SPLITS_MAX = 64;  // cluster-free merge: splits when the grid is small
-constexpr int ATT_GROUP = 8;        // more than ATT_SPLITS splits merge in groups of 8, then the groups
+constexpr int ATT_MERGE1_MAX = 32;  // up to this many splits merge in one level
+constexpr int ATT_GROUP = 8;        // more than ATT_MERGE1_MAX splits merge in groups of 8, then the groups
 constexpr int ATT_CNT_PER = 1 + ATT_SPLITS_MAX / ATT_GROUP;  // merge counters per (kv head, sequence) then
 constexpr int ATT_SLOTS_MAX = ATT_SPLITS_MAX + ATT_SPLITS_MAX / ATT_GROUP;  // partial slots per head
 struct AttnArgs {
@@ -208,7 +209,7 @@ struct AttnArgs {
     const int32_t *pos;          // [b]
     double *part_o;              // cluster-free merge: [b, n_heads, slots, hd] unnormalised sum p*v
     double *part_ml;             // cluster-free merge: [b, n_heads, slots, 2] (running max, sum p)
-                                 // (slots = splits, + splits / ATT_GROUP above ATT_SPLITS splits)
+                                 // (slots = splits, + splits / ATT_GROUP above ATT_MERGE1_MAX splits)
     int n_heads, n_kv, page_size, max_pages, num_pages, nsplit_max;
     float scale;
     uint32_t *err;

@@ -577,9 +577,12 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
     const size_t smem = act + (size_t)KS * depth * REC;
     auto kernel = k_gemv<DT, NT, DOTS, KS>;
     // the shared-memory attribute and the occupancy query cost more host time
-    // than a small GEMV's device time: done once per (device, size)
+    // than a small GEMV's device time: the attribute only ever grows (to the
+    // largest size this kernel has been launched with on the device) and the
+    // occupancy is cached per (device, size)
     static std::mutex mu;
     static std::map<std::pair<int, size_t>, int> occ_cache;
+    static std::map<int, size_t> smem_max;
     int occ = 0;
     {
         std::lock_guard<std::mutex> lock(mu);
@@ -587,7 +590,11 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
         if (it != occ_cache.end()) {
             occ = it->second;
         } else {
-            FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            size_t &mx = smem_max[ctx->device];
+            if (smem > mx) {
+                FB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                mx = smem;
+            }
             FB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, KS * 32, smem));
             occ_cache[{ctx->device, smem}] = occ;
         }

@@ -117,10 +117,12 @@ def test_synth_kv_then_decode(fbctx):
     assert_close(dm.forward([11], 300), om.forward([11], 300), what="decode at ctx 300")
 
 
-@pytest.mark.parametrize("n_kv,ctx", [(2, 1500), (1, 3000), (4, 2100)])
+@pytest.mark.parametrize("n_kv,ctx", [(2, 1500), (1, 3000), (4, 2100), (8, 4500)])
 def test_long_context_many_splits(fbctx, n_kv, ctx):
     """Few kv heads and long contexts: the attention grid takes 32 or 64
-    splits per kv head (one wave of CTAs); the result must not change."""
+    splits per kv head (one wave of CTAs); with 8 kv heads at ctx 4500 it
+    keeps 16 splits of 5 chunks each, more than the ring's 4 stages.  The
+    result must not change."""
     cfg = tiny_config(n_heads=4 * n_kv, n_kv_heads=n_kv, max_ctx=ctx + 8, vocab=2048)
     dm = fb.Model(fbctx, cfg)
     dm.synth(seed=5)

@@ -88,3 +88,36 @@ def test_attn_decode_paged(fbctx, torch_cuda, nh, nkv, page):
     ref = attn_reference(q, kp, vp, perm, lens, page)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=1e-5)
     assert fbctx.error_word() == 0
+
+
+@pytest.mark.parametrize("nh,nkv", [(32, 8), (8, 1)])
+@pytest.mark.parametrize("page", [32, 64])
+def test_attn_decode_long_ring_reuse(fbctx, torch_cuda, nh, nkv, page):
+    """Contexts whose splits hold more 64-token chunks than the shared-memory
+    ring has stages (16 splits: > 4 chunks without clusters, > 2 with), so
+    stages are refilled while other warps still work on the ring; both entry
+    points (cluster merge where the GPU holds one, and the cluster-free merge
+    of the allocation-free entry) against an f64 reference and each other."""
+    torch = torch_cuda
+    rng = np.random.default_rng(nh * 7 + page)
+    hd, lens = 128, np.array([4100, 2500, 1, 5000 - page + 3], dtype=np.int32)
+    b = lens.size
+    max_pages = int(math.ceil(lens.max() / page))
+    num_pages = b * max_pages + 5
+    perm = rng.permutation(num_pages)[: b * max_pages].reshape(b, max_pages).astype(np.int32)
+    kp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    vp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    qd, kd, vd, btd, ld = t(q), t(kp.transpose(0, 1, 3, 2)), t(vp), t(perm), t(lens)
+    ref = attn_reference(q, kp, vp, perm, lens, page)
+    outs = []
+    for fn in (fb.attn_decode, fb.attn_decode_noalloc):
+        out = torch.full((b, nh, hd), float("nan"), dtype=torch.float32, device="cuda")
+        fn(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(), out.data_ptr(), b, nh,
+           nkv, hd, page, max_pages, int(lens.max()), 1.0 / math.sqrt(hd))
+        outs.append(out.cpu().numpy())
+        np.testing.assert_allclose(outs[-1], ref, rtol=1e-4, atol=1e-5)
+    # binary64 softmax and P.V: the split and warp layout does not show in the f32 result
+    assert np.array_equal(outs[0], outs[1])
+    assert fbctx.error_word() == 0
