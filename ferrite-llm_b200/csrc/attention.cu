@@ -241,27 +241,42 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     auto k_at = [&](uint8_t *kst, int d, int tc) -> __half * {  // staged K element (dim d, chunk token tc)
         return reinterpret_cast<__half *>(kst + (tc / P) * KPG + (d >> 5) * KQS + (d & 31) * KROW + (tc % P) * 2);
     };
-    auto issue = [&](int j) {  // chunk j of this CTA into stage j % depth
-        const int st = j % depth;
-        uint8_t *kd = ring + (size_t)st * ATT_STAGE;
-        uint8_t *vd = kd + ATT_STAGE_K;
+    // copy `piece` (0..3: the K quarters, 4: the V page) of page i of chunk j
+    // into stage j % depth
+    auto issue_piece = [&](int j, int i, int piece) {
+        const int page = bt_s[j * PPC + i];
+        if (page < 0) return;
+        uint8_t *kd = ring + (size_t)(j % depth) * ATT_STAGE;
+        const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
+        if (piece < 4)
+            bulk_g2s(kd + i * KPG + piece * KQS,
+                     reinterpret_cast<const uint8_t *>(reinterpret_cast<const __half *>(A.kpool) + off) +
+                         piece * (pbytes / 4),
+                     pbytes / 4, &full[j % depth]);
+        else
+            bulk_g2s(kd + ATT_STAGE_K + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes,
+                     &full[j % depth]);
+    };
+    auto arm = [&](int j) {  // the bytes chunk j brings (zero: the phase completes without data)
         uint32_t bytes = 0;
         for (int i = 0; i < PPC; i++)
             if (bt_s[j * PPC + i] >= 0) bytes += 2 * pbytes;
-        mbar_expect_tx(&full[st], bytes);  // zero bytes: the phase completes without data
-        for (int i = 0; i < PPC; i++) {
-            const int page = bt_s[j * PPC + i];
-            if (page < 0) continue;
-            const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
-            const uint8_t *ks = reinterpret_cast<const uint8_t *>(reinterpret_cast<const __half *>(A.kpool) + off);
-#pragma unroll
-            for (int h = 0; h < 4; h++) bulk_g2s(kd + i * KPG + h * KQS, ks + h * (pbytes / 4), pbytes / 4, &full[st]);
-            bulk_g2s(vd + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes, &full[st]);
-        }
+        mbar_expect_tx(&full[j % depth], bytes);
     };
-    if (tid == 0)
-        for (int j = 0; j < pre; j++)
-            if (j != jf || A.qkv) issue(j);
+    auto issue = [&](int j) {  // chunk j of this CTA into stage j % depth
+        arm(j);
+        for (int i = 0; i < PPC; i++)
+            for (int piece = 0; piece < 5; piece++) issue_piece(j, i, piece);
+    };
+    // the first chunks stream in before the wait, one copy per lane of warp 0
+    // (lane j < pre arms stage j; the copies may complete before the arm)
+    if (warp == 0) {
+        for (int c = lane; c < pre * PPC * 5; c += 32) {
+            const int j = c / (PPC * 5);
+            if (j != jf || A.qkv) issue_piece(j, (c / 5) % PPC, c % 5);
+        }
+        if (lane < pre && (lane != jf || A.qkv)) arm(lane);
+    }
     pdl_wait();
     pdl_launch();  // the next kernel may start streaming its weights
     if (tid == 0 && !A.qkv && jf >= 0 && jf < pre) issue(jf);
@@ -666,13 +681,13 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
             if (tid == 0) {
                 const int prev = atomicAdd(&cnt[0], 1);
                 s_last = prev == ns - 1;
-                if (s_last) cnt[0] = 0;  // ready for the next call
+                if (s_last) {
+                    cnt[0] = 0;        // ready for the next call
+                    __threadfence();  // the partials' reads below follow the counter
+                }
             }
             __syncthreads();
-            if (s_last) {
-                __threadfence();
-                merge(0, ns, -1);
-            }
+            if (s_last) merge(0, ns, -1);
         } else {
             const int grp = rank / ATT_GROUP;
             if (tid == 0) {
