@@ -766,6 +766,8 @@ __device__ __forceinline__ void q8k_store_warp_ext(const float (&v)[8], int lane
 }
 
 
+constexpr int ATT_BT_MAX = 8192;  // block-table entries one CTA stages in shared memory
+
 static int attn_bt_cap(int max_pages, int page_size) {
     const int nch = (int)(((int64_t)max_pages * page_size + ATT_CHUNK - 1) / ATT_CHUNK);
     return (nch + ATT_SPLITS - 1) / ATT_SPLITS * (ATT_CHUNK / page_size);
@@ -844,16 +846,24 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
     int depth, bt_cap;
     size_t smem;
     const bool cluster = attn_plan<G>(ctx, A, batch, want_cluster, &depth, &bt_cap, &smem);
-    // cluster-free merge: as many splits as fill one wave (one CTA per SM),
-    // at least ATT_SPLITS, each with a chunk of the longest sequence; above
-    // ATT_MERGE1_MAX a multiple of ATT_GROUP (two-level merge)
+    // cluster-free merge: as many splits as fill one wave (one CTA per SM;
+    // one split per (kv head, sequence) once those alone fill it), each with a
+    // chunk of the longest sequence; above ATT_MERGE1_MAX a multiple of
+    // ATT_GROUP (two-level merge).  The CTA's block-table entries (shared
+    // memory) bound the chunks per split from below.
     int ns = ATT_SPLITS;
     if (!cluster) {
+        const int PPC = ATT_CHUNK / A.page_size;
         const int64_t nch = (max_seq_len + ATT_CHUNK - 1) / ATT_CHUNK;
+        const int64_t nch_cap = ((int64_t)A.max_pages * A.page_size + ATT_CHUNK - 1) / ATT_CHUNK;
         int64_t want = std::min<int64_t>({(int64_t)ctx->num_sms / ((int64_t)A.n_kv * batch), (int64_t)A.nsplit_max,
                                           (int64_t)ATT_SPLITS_MAX, nch});
         if (want > ATT_MERGE1_MAX) want -= want % ATT_GROUP;
-        ns = (int)std::max<int64_t>(ns, want);
+        want = std::max<int64_t>({want, (int64_t)1, (nch_cap * PPC + ATT_BT_MAX - 1) / ATT_BT_MAX});
+        FB_REQUIRE(want <= ATT_SPLITS_MAX && want <= A.nsplit_max, "attn: block table too long for the split scratch");
+        ns = (int)want;
+        bt_cap = (int)((nch_cap + ns - 1) / ns) * PPC;
+        smem = attn_layout(G, att_warps(G, false), depth, bt_cap).total;
     }
     FB_REQUIRE(cluster || (counters && A.part_o && A.part_ml), "attn: the cluster-free merge needs scratch");
     Q8Act q = aq ? *aq : Q8Act{nullptr, nullptr, nullptr, nullptr, 0};

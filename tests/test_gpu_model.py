@@ -148,3 +148,32 @@ def test_bad_inputs_rejected(fbctx):
     with pytest.raises(fb.FerriteError):
         dm.decode_greedy([1], [cfg["max_ctx"]])
     assert fbctx.error_word() == 0
+
+
+def test_batch16_single_split_per_kv_head(fbctx, torch_cuda):
+    """16 sequences x 8 kv heads fill one wave of attention CTAs with one
+    split each: every CTA walks the whole context (18 chunks, several passes
+    over its 4-stage shared-memory ring).  Each sequence's logits must equal
+    the oracle's single-sequence forward bit for bit."""
+    torch = torch_cuda
+    ctx = 1100
+    cfg = tiny_config(n_heads=32, n_kv_heads=8, max_ctx=ctx + 8, max_batch=16, vocab=2048)
+    dm = fb.Model(fbctx, cfg)
+    dm.synth(seed=5)
+    dm.finalize()
+    dm.synth_kv(seed=9, ctx=ctx)
+    w = synth_weights(cfg, seed=5)
+    toks = [(7 * i + 3) % cfg["vocab"] for i in range(16)]
+    tok_d = torch.tensor(toks, dtype=torch.int32, device="cuda")
+    pos_d = torch.full((16,), ctx, dtype=torch.int32, device="cuda")
+    logits = torch.empty((16, cfg["vocab"]), dtype=torch.float32, device="cuda")
+    dm.decode_dev(tok_d.data_ptr(), pos_d.data_ptr(), 16, logits_ptr=logits.data_ptr())
+    torch.cuda.synchronize()
+    got = logits.cpu().numpy()
+    for i, t in enumerate(toks):
+        om = O.Model(cfg, w)
+        om.synth_kv(9, ctx)
+        want = om.forward([t], ctx)
+        assert_close(got[i], want, what=f"sequence {i} at ctx {ctx}")
+        assert np.array_equal(got[i], want), f"sequence {i}: not bit-identical to the oracle"
+    assert fbctx.error_word() == 0
