@@ -637,13 +637,14 @@ static void launch_gemv_dt(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int
     case 4: launch_gemv_t<DT, -4, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po); break;
     default:
         if (m <= 8) launch_gemv_t<DT, 1, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
-        else launch_gemv_t<DT, 2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
+        else if (m <= 16) launch_gemv_t<DT, 2, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
+        else launch_gemv_t<DT, 4, false>(ctx, w, a, m, y, ldy, nullptr, nullptr, po);
     }
 }
 
 static void gemv_any(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
                      const PeerOut &po) {
-    FB_REQUIRE(m >= 1 && m <= 16, "gemv: m must be in 1..16");
+    FB_REQUIRE(m >= 1 && m <= 32, "gemv: m must be in 1..32");
     if (w->dtype == FB_Q4_K) launch_gemv_dt<4>(ctx, w, a, m, y, ldy, po);
     else if (w->dtype == FB_Q6_K) launch_gemv_dt<6>(ctx, w, a, m, y, ldy, po);
     else fail(FB_ERR_INVALID, "gemv: weight dtype must be Q4_K or Q6_K");

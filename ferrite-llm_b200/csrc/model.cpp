@@ -425,7 +425,7 @@ static void create_model(fb_ctx *ctx, const fb_model_config *cfg, fb_comm *comm,
     FB_REQUIRE(c.n_heads % c.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
     const int G = c.n_heads / c.n_kv_heads;
     FB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "GQA group must be 1, 2, 4 or 8");
-    FB_REQUIRE(c.max_ctx >= 1 && c.max_batch >= 1 && c.max_batch <= 16, "need max_ctx >= 1, 1 <= max_batch <= 16");
+    FB_REQUIRE(c.max_ctx >= 1 && c.max_batch >= 1 && c.max_batch <= 32, "need max_ctx >= 1, 1 <= max_batch <= 32");
     FB_REQUIRE(c.rope_mode == 0 || c.rope_mode == 1, "rope_mode must be 0 or 1");
     auto m = std::make_unique<fb_model>();
     m->ctx = ctx;

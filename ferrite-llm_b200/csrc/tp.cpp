@@ -53,8 +53,8 @@ int fb_comm_create(fb_ctx *ctx, int rank, int world, int max_batch, int hidden, 
         *out = nullptr;
         FB_REQUIRE(world == 2 || world == 4 || world == 8, "world must be 2, 4 or 8");
         FB_REQUIRE(rank >= 0 && rank < world, "rank out of range");
-        FB_REQUIRE(max_batch >= 1 && max_batch <= 16 && hidden > 0 && hidden % 256 == 0,
-                   "need 1 <= max_batch <= 16 and hidden a multiple of 256");
+        FB_REQUIRE(max_batch >= 1 && max_batch <= 32 && hidden > 0 && hidden % 256 == 0,
+                   "need 1 <= max_batch <= 32 and hidden a multiple of 256");
         static_assert(sizeof(cudaIpcMemHandle_t) == FB_COMM_HANDLE_BYTES, "IPC handle size");
         FB_CUDA(cudaSetDevice(ctx->device));
         auto c = std::make_unique<fb_comm>();

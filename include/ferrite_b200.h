@@ -204,7 +204,7 @@ int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,
 typedef struct {
     int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
     int max_ctx;      /* KV capacity per sequence (tokens) */
-    int max_batch;    /* decode batch capacity */
+    int max_batch;    /* decode batch capacity (1..32) */
     float rope_theta, eps;
     int qk_norm;      /* 1: Qwen3 per-head RMSNorm on q and k */
     int rope_mode;    /* 0 interleaved (llama), 1 rotate-half (qwen3) */

@@ -150,24 +150,27 @@ def test_bad_inputs_rejected(fbctx):
     assert fbctx.error_word() == 0
 
 
-def test_batch16_single_split_per_kv_head(fbctx, torch_cuda):
-    """16 sequences x 8 kv heads fill one wave of attention CTAs with one
-    split each: every CTA walks the whole context (18 chunks, several passes
-    over its 4-stage shared-memory ring).  Each sequence's logits must equal
-    the oracle's single-sequence forward bit for bit."""
+@pytest.mark.parametrize("batch", [16, 32])
+def test_large_batch_single_split_per_kv_head(fbctx, torch_cuda, batch):
+    """16 or 32 sequences x 8 kv heads fill one wave (or two) of attention
+    CTAs with one split each: every CTA walks the whole context (18 chunks,
+    several passes over its 4-stage shared-memory ring); at 32 rows the
+    projections take the widest MMA consumer (four 8-column n-tiles).  Each
+    sequence's logits must equal the oracle's single-sequence forward bit for
+    bit."""
     torch = torch_cuda
     ctx = 1100
-    cfg = tiny_config(n_heads=32, n_kv_heads=8, max_ctx=ctx + 8, max_batch=16, vocab=2048)
+    cfg = tiny_config(n_heads=32, n_kv_heads=8, max_ctx=ctx + 8, max_batch=batch, vocab=2048)
     dm = fb.Model(fbctx, cfg)
     dm.synth(seed=5)
     dm.finalize()
     dm.synth_kv(seed=9, ctx=ctx)
     w = synth_weights(cfg, seed=5)
-    toks = [(7 * i + 3) % cfg["vocab"] for i in range(16)]
+    toks = [(7 * i + 3) % cfg["vocab"] for i in range(batch)]
     tok_d = torch.tensor(toks, dtype=torch.int32, device="cuda")
-    pos_d = torch.full((16,), ctx, dtype=torch.int32, device="cuda")
-    logits = torch.empty((16, cfg["vocab"]), dtype=torch.float32, device="cuda")
-    dm.decode_dev(tok_d.data_ptr(), pos_d.data_ptr(), 16, logits_ptr=logits.data_ptr())
+    pos_d = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    logits = torch.empty((batch, cfg["vocab"]), dtype=torch.float32, device="cuda")
+    dm.decode_dev(tok_d.data_ptr(), pos_d.data_ptr(), batch, logits_ptr=logits.data_ptr())
     torch.cuda.synchronize()
     got = logits.cpu().numpy()
     for i, t in enumerate(toks):
