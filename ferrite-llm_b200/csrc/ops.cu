@@ -77,8 +77,8 @@ __global__ void __launch_bounds__(NORM_THREADS)
             v[p] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
+    pdl_launch();  // the next projection may launch and stream its weights now
     pdl_wait();
-    pdl_launch();
     // first kernel of a tensor-parallel step: advance the step counter that
     // numbers the step's exchanges (read by later kernels after their wait)
     if (epoch_inc && blk == 0 && row == 0 && threadIdx.x == 0) *epoch_inc += 1u;
@@ -216,8 +216,8 @@ __global__ void __launch_bounds__(NORM_THREADS)
 __global__ void __launch_bounds__(QK) k_swiglu_q8k(const float *__restrict__ y, int f, int64_t rows, Q8Act a) {
     __shared__ float shv[2 * QK / 32];
     __shared__ int shi[QK / 32];
+    pdl_launch();  // the next projection may launch and stream its weights now
     pdl_wait();
-    pdl_launch();
     const int64_t nbk = f / QK;
     const int64_t row = blockIdx.x / nbk, blk = blockIdx.x % nbk;
     if (row >= rows) return;
