@@ -569,9 +569,11 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
     constexpr int REC = QRec<DT>::bytes;
     constexpr int M = NT < 0 ? -NT : 0;
     const size_t act = M ? (act_smem_bytes(M, w->k) + 127) & ~(size_t)127 : 0;
-    // ring depth: as deep as fits next to the staged activations while keeping
-    // 16 warps per SM (4 CTAs of 4 warps or 2 of 8), 3..8 stages per warp
-    const size_t budget = (size_t)(KS == 4 ? 56 : 112) * 1024;
+    // ring depth: as deep as fits next to the staged activations in 40 KB
+    // (4-warp CTAs: three stages of Q4_K or Q6_K records) or 112 KB (8-warp
+    // CTAs), 3..8 stages per warp.  In the decode step, deeper 4-warp rings
+    // (56 KB: five stages, 72 KB) and shallower 8-warp ones measured slower.
+    const size_t budget = (size_t)(KS == 4 ? 40 : 112) * 1024;
     int depth = (int)std::min<size_t>(8, (budget - std::min(act, budget / 2)) / ((size_t)KS * REC));
     depth = std::max(depth, 3);
     const size_t smem = act + (size_t)KS * depth * REC;
