@@ -618,12 +618,14 @@ static void launch_gemv_k(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int 
                                ctx->err_word, depth, po));
 }
 
-// Few tiles (fewer than two per SM): 8-warp CTAs so each SM still runs
-// enough warps; otherwise 4-warp CTAs.
+// Few tiles (fewer than two per SM; for the dp4a consumer, m <= 4, fewer
+// than three): 8-warp CTAs so each SM still runs enough warps; otherwise
+// 4-warp CTAs.  (Measured in the decode step: the b = 1 qkv projection, 384
+// tiles, is faster with 8-warp CTAs, the b = 16 one with 4-warp CTAs.)
 template <int DT, int NT, bool DOTS>
 static void launch_gemv_t(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int m, float *y, int64_t ldy,
                           int32_t *dsc, int32_t *dmn, const PeerOut &po) {
-    if (w->n_tiles() < 2 * ctx->num_sms && w->nb() >= 16)
+    if (w->n_tiles() < (NT < 0 ? 3 : 2) * ctx->num_sms && w->nb() >= 16)
         launch_gemv_k<DT, NT, DOTS, 8>(ctx, w, a, m, y, ldy, dsc, dmn, po);
     else
         launch_gemv_k<DT, NT, DOTS, 4>(ctx, w, a, m, y, ldy, dsc, dmn, po);
