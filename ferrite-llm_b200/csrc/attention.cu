@@ -458,9 +458,11 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
 #pragma unroll 4
             for (int t = 0; t < nt; t++) {
                 const uint2 vr = *reinterpret_cast<const uint2 *>(vrow + (size_t)t * ATT_HD);
-                const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
-                const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
-                const double vd[4] = {(double)v01.x, (double)v01.y, (double)v23.x, (double)v23.y};
+                double vd[4];  // fp16 -> binary64 directly (exact), one conversion per value
+                asm("{\n .reg .b16 h0, h1, h2, h3;\n mov.b32 {h0, h1}, %4;\n mov.b32 {h2, h3}, %5;\n"
+                    " cvt.f64.f16 %0, h0;\n cvt.f64.f16 %1, h1;\n cvt.f64.f16 %2, h2;\n cvt.f64.f16 %3, h3;\n}"
+                    : "=d"(vd[0]), "=d"(vd[1]), "=d"(vd[2]), "=d"(vd[3])
+                    : "r"(vr.x), "r"(vr.y));
                 double pg[G];
                 if constexpr (G >= 2) {
 #pragma unroll
