@@ -864,8 +864,12 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
         const int64_t nch_cap = ((int64_t)A.max_pages * A.page_size + ATT_CHUNK - 1) / ATT_CHUNK;
         int64_t want = std::min<int64_t>({(int64_t)ctx->num_sms / ((int64_t)A.n_kv * batch), (int64_t)A.nsplit_max,
                                           (int64_t)ATT_SPLITS_MAX, nch});
-        if (want > ATT_MERGE1_MAX) want -= want % ATT_GROUP;
-        want = std::max<int64_t>({want, (int64_t)1, (nch_cap * PPC + ATT_BT_MAX - 1) / ATT_BT_MAX});
+        const int64_t lo = std::max<int64_t>(1, (nch_cap * PPC + ATT_BT_MAX - 1) / ATT_BT_MAX);
+        want = std::max(want, lo);
+        if (want > ATT_MERGE1_MAX) {
+            want -= want % ATT_GROUP;
+            if (want < lo) want += ATT_GROUP;
+        }
         FB_REQUIRE(want <= ATT_SPLITS_MAX && want <= A.nsplit_max, "attn: block table too long for the split scratch");
         ns = (int)want;
         bt_cap = (int)((nch_cap + ns - 1) / ns) * PPC;
