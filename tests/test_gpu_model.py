@@ -150,14 +150,15 @@ def test_bad_inputs_rejected(fbctx):
     assert fbctx.error_word() == 0
 
 
-@pytest.mark.parametrize("batch", [16, 32])
-def test_large_batch_single_split_per_kv_head(fbctx, torch_cuda, batch):
+@pytest.mark.parametrize("batch,ragged", [(16, False), (32, False), (16, True)])
+def test_large_batch_single_split_per_kv_head(fbctx, torch_cuda, batch, ragged):
     """16 or 32 sequences x 8 kv heads fill one wave (or two) of attention
     CTAs with one split each: every CTA walks the whole context (18 chunks,
     several passes over its 4-stage shared-memory ring); at 32 rows the
-    projections take the widest MMA consumer (four 8-column n-tiles).  Each
-    sequence's logits must equal the oracle's single-sequence forward bit for
-    bit."""
+    projections take the widest MMA consumer (four 8-column n-tiles).  With
+    `ragged` every sequence decodes at its own position (1 to 1100 tokens of
+    context).  Each sequence's logits must equal the oracle's single-sequence
+    forward bit for bit."""
     torch = torch_cuda
     ctx = 1100
     cfg = tiny_config(n_heads=32, n_kv_heads=8, max_ctx=ctx + 8, max_batch=batch, vocab=2048)
@@ -168,7 +169,10 @@ def test_large_batch_single_split_per_kv_head(fbctx, torch_cuda, batch):
     w = synth_weights(cfg, seed=5)
     toks = [(7 * i + 3) % cfg["vocab"] for i in range(batch)]
     tok_d = torch.tensor(toks, dtype=torch.int32, device="cuda")
-    pos_d = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    positions = [ctx - 73 * i for i in range(batch)] if ragged else [ctx] * batch
+    if ragged:
+        positions[-1] = 0  # a sequence with only the new token
+    pos_d = torch.tensor(positions, dtype=torch.int32, device="cuda")
     logits = torch.empty((batch, cfg["vocab"]), dtype=torch.float32, device="cuda")
     dm.decode_dev(tok_d.data_ptr(), pos_d.data_ptr(), batch, logits_ptr=logits.data_ptr())
     torch.cuda.synchronize()
@@ -176,7 +180,7 @@ def test_large_batch_single_split_per_kv_head(fbctx, torch_cuda, batch):
     for i, t in enumerate(toks):
         om = O.Model(cfg, w)
         om.synth_kv(9, ctx)
-        want = om.forward([t], ctx)
-        assert_close(got[i], want, what=f"sequence {i} at ctx {ctx}")
+        want = om.forward([t], positions[i])
+        assert_close(got[i], want, what=f"sequence {i} at position {positions[i]}")
         assert np.array_equal(got[i], want), f"sequence {i}: not bit-identical to the oracle"
     assert fbctx.error_word() == 0
