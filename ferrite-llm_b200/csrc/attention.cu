@@ -977,7 +977,7 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
                                       const void *v_pages_dev, const int32_t *block_table_dev,
                                       const int32_t *seq_lens_dev, float *out_dev, int batch, int n_heads,
                                       int n_kv_heads, int head_dim, int page_size, int max_pages,
-                                      int max_seq_len, float scale) {
+                                      int num_pages, int max_seq_len, float scale) {
     using namespace fb;
     return guarded([&] {
         FB_REQUIRE(ctx && q_dev && k_pages_dev && v_pages_dev && block_table_dev && seq_lens_dev && out_dev,
@@ -987,6 +987,7 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
+        FB_REQUIRE(num_pages >= 1, "num_pages must be positive");
         const int nsplit = ATT_SPLITS;
         const size_t cnt_bytes = ((size_t)batch * n_kv_heads * sizeof(int) + 255) & ~(size_t)255;
         const size_t need = (size_t)batch * n_heads * nsplit * (head_dim + 2) * sizeof(double) + cnt_bytes;
@@ -1013,7 +1014,7 @@ extern "C" int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev, const voi
         A.n_kv = n_kv_heads;
         A.page_size = page_size;
         A.max_pages = max_pages;
-        A.num_pages = 0x7fffffff;
+        A.num_pages = num_pages;  // block-table ids outside the pool set ERRBIT_BAD_PAGE and are skipped
         A.nsplit_max = nsplit;
         A.scale = scale;
         A.err = ctx->err_word;

@@ -1043,8 +1043,8 @@ int fb_attn_prefill(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, co
 
 int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, const void *v_pages_dev,
                    const int32_t *block_table_dev, const int32_t *seq_lens_dev, float *out_dev, int batch,
-                   int n_heads, int n_kv_heads, int head_dim, int page_size, int max_pages, int max_seq_len,
-                   float scale) {
+                   int n_heads, int n_kv_heads, int head_dim, int page_size, int max_pages, int num_pages,
+                   int max_seq_len, float scale) {
     return guarded([&] {
         FB_REQUIRE(ctx && q_dev && k_pages_dev && v_pages_dev && block_table_dev && seq_lens_dev && out_dev,
                    "null argument");
@@ -1052,6 +1052,7 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         FB_REQUIRE(page_size == 32 || page_size == 64, "page_size must be 32 or 64");
         FB_REQUIRE(batch >= 1 && n_heads >= 1 && n_kv_heads >= 1 && max_pages >= 1 && max_seq_len >= 1,
                    "bad shape");
+        FB_REQUIRE(num_pages >= 1, "num_pages must be positive");
         FB_REQUIRE(max_seq_len <= max_pages * page_size, "max_seq_len exceeds the block table");
         AttnArgs A{};
         A.q = q_dev;
@@ -1064,7 +1065,7 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev, con
         A.n_kv = n_kv_heads;
         A.page_size = page_size;
         A.max_pages = max_pages;
-        A.num_pages = 0x7fffffff;  // caller-owned pool: ids are trusted up to int range
+        A.num_pages = num_pages;  // block-table ids outside the pool set ERRBIT_BAD_PAGE and are skipped
         A.nsplit_max = ATT_SPLITS;
         A.scale = scale;
         A.err = ctx->err_word;

@@ -303,3 +303,145 @@ int fb_sample(fb_ctx *ctx, const float *logits_dev, int vocab, const fb_sampler_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Top-k logits candidates for the logits-hook path (k <= 16).
+//
+// The reference collects them on the host: the whole vocab row is copied out,
+// sorted by descending logit with a stable sort (ties keep index order) and
+// the first `limit` taken (crates/ferrite-core/src/hooks.rs:19-38); the GPU
+// logits executor rewrites 16 of them (crates/ferrite-wasm-host/src/
+// adapter.rs:508-515).  Here the selection stays on the device in two
+// launches: grid (chunks, rows) picks each chunk's k best (value, index)
+// pairs by k rounds of a block-wide selection, each round taking the best
+// pair ordered strictly after the previous pick; a second kernel (one CTA per
+// row) selects the row's k best from the chunks' candidates the same way.
+// Order: a before b when a.v > b.v, or a.v == b.v and a.i < b.i -- the
+// stable descending sort's order for non-NaN logits (NaN logits are never
+// selected here; the reference's comparator treats NaN as equal to
+// everything, which has no stable-sort equivalent).
+namespace fb {
+
+constexpr int TOPK_MAX = 16;
+constexpr int TOPK_THREADS = 256;
+constexpr int TOPK_PER_THREAD = 8;  // values a thread holds per chunk
+constexpr int TOPK_CHUNK = TOPK_THREADS * TOPK_PER_THREAD;
+
+struct VI {
+    float v;
+    int i;
+};
+__device__ __forceinline__ bool vi_before(float av, int ai, float bv, int bi) {
+    return av > bv || (av == bv && ai < bi);
+}
+// Best pair of the block among (vals[j], idx[j]) entries strictly after
+// (pv, pi) in the order; returns (-inf, INT_MAX) when none is left.
+template <int PER>
+__device__ __forceinline__ VI topk_round(const float (&vals)[PER], const int (&idx)[PER], float pv, int pi, VI *sh) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const float v = vals[j];
+        const int i = idx[j];
+        if (i != 0x7fffffff && vi_before(pv, pi, v, i) && vi_before(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (vi_before(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // the previous round's readers of sh are done
+    if (lane == 0) sh[warp] = VI{bv, bi};
+    __syncthreads();
+    VI r = sh[0];
+#pragma unroll
+    for (int w = 1; w < TOPK_THREADS / 32; w++)
+        if (vi_before(sh[w].v, sh[w].i, r.v, r.i)) r = sh[w];
+    return r;
+}
+
+// Candidates of chunk blockIdx.x of row blockIdx.y -> cand[row][chunk][k].
+__global__ void __launch_bounds__(TOPK_THREADS) k_topk_chunks(const float *__restrict__ logits, int64_t vocab, int k,
+                                                              VI *__restrict__ cand) {
+    __shared__ VI sh[TOPK_THREADS / 32];
+    const int64_t row = blockIdx.y;
+    const int64_t base = (int64_t)blockIdx.x * TOPK_CHUNK;
+    float vals[TOPK_PER_THREAD];
+    int idx[TOPK_PER_THREAD];
+#pragma unroll
+    for (int j = 0; j < TOPK_PER_THREAD; j++) {
+        const int64_t i = base + threadIdx.x + (int64_t)j * TOPK_THREADS;
+        const float v = i < vocab ? logits[row * vocab + i] : -INFINITY;
+        const bool ok = i < vocab && !isnan(v);
+        vals[j] = ok ? v : -INFINITY;
+        idx[j] = ok ? (int)i : 0x7fffffff;
+    }
+    float pv = INFINITY;  // before every finite or infinite value: (+inf, -1)
+    int pi = -1;
+    VI *out = cand + (row * gridDim.x + blockIdx.x) * k;
+    for (int r = 0; r < k; r++) {
+        const VI b = topk_round<TOPK_PER_THREAD>(vals, idx, pv, pi, sh);
+        if (threadIdx.x == 0) out[r] = b;
+        pv = b.v;
+        pi = b.i;
+    }
+}
+
+// Final selection of one row from its chunks' candidates.
+__global__ void __launch_bounds__(TOPK_THREADS) k_topk_final(const VI *__restrict__ cand, int ncand, int k,
+                                                             int32_t *__restrict__ ids, float *__restrict__ vals_out) {
+    __shared__ VI sh[TOPK_THREADS / 32];
+    constexpr int PER = 8;  // ncand <= TOPK_THREADS * PER (checked on the host)
+    const int64_t row = blockIdx.x;
+    float vals[PER];
+    int idx[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int c = threadIdx.x + j * TOPK_THREADS;
+        const VI x = c < ncand ? cand[row * ncand + c] : VI{-INFINITY, 0x7fffffff};
+        vals[j] = x.v;
+        idx[j] = x.i;
+    }
+    float pv = INFINITY;
+    int pi = -1;
+    for (int r = 0; r < k; r++) {
+        const VI b = topk_round<PER>(vals, idx, pv, pi, sh);
+        if (threadIdx.x == 0) {
+            ids[row * k + r] = b.i == 0x7fffffff ? -1 : b.i;
+            vals_out[row * k + r] = b.i == 0x7fffffff ? -INFINITY : b.v;
+        }
+        pv = b.v;
+        pi = b.i;
+    }
+}
+
+}  // namespace fb
+
+extern "C" int fb_top_logits(fb_ctx *ctx, const float *logits_dev, int rows, int64_t vocab, int k, int32_t *ids_dev,
+                             float *vals_dev) {
+    using namespace fb;
+    return guarded([&] {
+        FB_REQUIRE(ctx && logits_dev && ids_dev && vals_dev, "null argument");
+        FB_REQUIRE(rows >= 1 && vocab >= 1 && vocab < 0x7fffffff, "bad shape");
+        FB_REQUIRE(k >= 1 && k <= TOPK_MAX, "k must be in 1..16");
+        const int64_t nchunk = (vocab + TOPK_CHUNK - 1) / TOPK_CHUNK;
+        const int64_t ncand = nchunk * k;
+        FB_REQUIRE(ncand <= (int64_t)TOPK_THREADS * 8, "top_logits: ceil(vocab / 2048) * k must be <= 2048");
+        FB_REQUIRE(rows <= 65535, "top_logits: at most 65535 rows");
+        VI *cand = static_cast<VI *>(ctx->ensure_scratch((size_t)rows * ncand * sizeof(VI)));
+        k_topk_chunks<<<dim3((unsigned)nchunk, (unsigned)rows), TOPK_THREADS, 0, ctx->stream>>>(logits_dev, vocab, k,
+                                                                                               cand);
+        FB_CUDA(cudaGetLastError());
+        k_topk_final<<<rows, TOPK_THREADS, 0, ctx->stream>>>(cand, (int)ncand, k, ids_dev, vals_dev);
+        FB_CUDA(cudaGetLastError());
+    });
+}

@@ -40,7 +40,7 @@ EXPORTED = (
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
     "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill", "fb_gguf_config",
-    "fb_model_load_gguf", "fb_model_forward_all", "fb_sample",
+    "fb_model_load_gguf", "fb_model_forward_all", "fb_sample", "fb_top_logits",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -105,8 +105,8 @@ def _declare(L):
         "fb_rmsnorm": (i32, [vp, vp, vp, vp, i64, i64, f32]),
         "fb_rope": (i32, [vp, vp, i64, i64, i64, i64, f32, i32]),
         "fb_swiglu": (i32, [vp, vp, vp, vp, i64, i64]),
-        "fb_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32]),
-        "fb_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32]),
+        "fb_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32]),
+        "fb_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32]),
         "fb_model_create": (i32, [vp, P(ModelConfig), P(vp)]),
         "fb_model_destroy": (i32, [vp]),
         "fb_model_set_tensor": (i32, [vp, C.c_char_p, i32, i32, i64, i64, vp]),
@@ -134,6 +134,7 @@ def _declare(L):
         "fb_model_load_gguf": (i32, [vp, C.c_char_p]),
         "fb_model_forward_all": (i32, [vp, vp, i32, i32, vp]),
         "fb_sample": (i32, [vp, vp, i32, P(SamplerConfig), vp, i32, P(C.c_uint64), P(i32)]),
+        "fb_top_logits": (i32, [vp, vp, i32, i64, i32, vp, vp]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -288,9 +289,11 @@ def swiglu(ctx: Context, g_ptr, u_ptr, o_ptr, m, f):
 
 
 def attn_decode(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv, head_dim,
-                page_size, max_pages, max_seq_len, scale):
+                page_size, max_pages, num_pages, max_seq_len, scale):
+    """num_pages: pages the K / V pools hold; block-table ids outside
+    [0, num_pages) are skipped and set the error word's bad-page bit."""
     _check(lib().fb_attn_decode(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
-                                head_dim, page_size, max_pages, max_seq_len, scale))
+                                head_dim, page_size, max_pages, num_pages, max_seq_len, scale))
 
 
 def attn_prefill(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, max_pages, num_pages, pos0, n_tokens, n_heads, n_kv,
@@ -300,11 +303,11 @@ def attn_prefill(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, max_pages, num_pages
 
 
 def attn_decode_noalloc(ctx: Context, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
-                        head_dim, page_size, max_pages, max_seq_len, scale):
+                        head_dim, page_size, max_pages, num_pages, max_seq_len, scale):
     """fb_attn_decode without any device allocation (fixed 4 MiB scratch in
     the library's device image; see include/ferrite_b200.h)."""
     _check(lib().fb_attn_decode_noalloc(ctx.h, q_ptr, k_ptr, v_ptr, bt_ptr, lens_ptr, out_ptr, batch, n_heads, n_kv,
-                                        head_dim, page_size, max_pages, max_seq_len, scale))
+                                        head_dim, page_size, max_pages, num_pages, max_seq_len, scale))
 
 
 # GGUF tensor names of one layer / of the whole model.
@@ -336,6 +339,13 @@ class Sampler:
         _check(lib().fb_sample(self.ctx.h, logits_ptr, vocab, C.byref(self.cfg), _np(prev) if prev.size else None,
                                prev.size, C.byref(self.state), C.byref(out)))
         return out.value
+
+
+def top_logits(ctx: Context, logits_ptr: int, rows: int, vocab: int, k: int, ids_ptr: int, vals_ptr: int):
+    """The k (1..16) largest logits of each row, ordered like the reference
+    hook's stable descending sort: ids [rows][k] int32, vals [rows][k] f32 on
+    the device (fb_top_logits)."""
+    _check(lib().fb_top_logits(ctx.h, logits_ptr, rows, vocab, k, ids_ptr, vals_ptr))
 
 
 def gguf_config(path: str) -> dict:

@@ -152,8 +152,11 @@ int fb_swiglu(fb_ctx *ctx, const float *gate_dev, const float *up_dev,
  * cache.  q[b, n_heads, head_dim] f32; K pages fp16 dim-major
  * [num_pages, n_kv_heads, head_dim, page_size]; V pages fp16
  * [num_pages, n_kv_heads, page_size, head_dim]; block_table[b, max_pages]
- * int32 physical page ids; seq_lens[b] int32 (tokens to attend, including
- * the current one); out[b, n_heads, head_dim] f32.  scale = 1/sqrt(hd).
+ * int32 physical page ids, each checked against num_pages (the pages the
+ * K and V pools hold): an id outside [0, num_pages) is not read, its tokens
+ * are skipped and the context's error word gets its bad-page bit
+ * (fb_ctx_error_word); seq_lens[b] int32 (tokens to attend, including the
+ * current one); out[b, n_heads, head_dim] f32.  scale = 1/sqrt(hd).
  * head_dim 128, page_size 32 or 64, n_heads / n_kv_heads in {1, 2, 4, 8}.
  * Allocates nothing when the GPU can hold a 16-CTA thread-block cluster
  * (the split merge runs in distributed shared memory); otherwise grows a
@@ -162,7 +165,8 @@ int fb_attn_decode(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
                    const void *v_pages_dev, const int32_t *block_table_dev,
                    const int32_t *seq_lens_dev, float *out_dev, int batch,
                    int n_heads, int n_kv_heads, int head_dim, int page_size,
-                   int max_pages, int max_seq_len, float scale);
+                   int max_pages, int num_pages, int max_seq_len,
+                   float scale);
 
 /* Causal attention of a prompt chunk: n_tokens queries q_dev [n_tokens]
  * [n_heads][128] at positions pos0 .. pos0 + n_tokens - 1 of one sequence
@@ -187,9 +191,10 @@ int fb_attn_prefill(fb_ctx *ctx, const float *q_dev, const void *k_pages_dev,
  * those calls can imply, uses this entry point instead.  It allocates
  * nothing: its split scratch (16 splits per kv head and sequence) is a fixed
  * 4 MiB array in the library's device image, so it accepts
- * batch * n_heads * 16 * (head_dim + 2) * 8 bytes (plus 256 bytes of merge
- * counters) <= 4 MiB (e.g. batch 7 with 32 heads, any context length) and
- * returns FB_ERR_INVALID beyond that.  Its first call on a device looks up the array's
+ * batch * n_heads * 16 * (head_dim + 2) * 8 bytes plus the merge counters,
+ * round_up(batch * n_kv_heads * 4, 256) bytes, <= 4 MiB (e.g. batch 7 with
+ * 32 heads and 8 kv heads, any context length) and returns FB_ERR_INVALID
+ * beyond that.  Its first call on a device looks up the array's
  * device address (make that first call before any stream capture).  All calls
  * on a device share the array, so calls that overlap on the GPU race. */
 int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,
@@ -198,7 +203,7 @@ int fb_attn_decode_noalloc(fb_ctx *ctx, const float *q_dev,
                            const int32_t *seq_lens_dev, float *out_dev,
                            int batch, int n_heads, int n_kv_heads,
                            int head_dim, int page_size, int max_pages,
-                           int max_seq_len, float scale);
+                           int num_pages, int max_seq_len, float scale);
 
 /* -------------------------------------------------------------- model --- */
 typedef struct {
@@ -303,6 +308,19 @@ typedef struct {
 int fb_sample(fb_ctx *ctx, const float *logits_dev, int vocab,
               const fb_sampler_config *cfg, const int32_t *prev_tokens_host,
               int n_prev, uint64_t *rng_state, int32_t *token_out);
+/* Top-k logits candidates of each row for the logits-hook path: the k
+ * largest logits of logits_dev [rows][vocab] in the order of the reference's
+ * stable descending sort (larger logit first, equal logits in index order),
+ * ids_dev [rows][k] int32 and vals_dev [rows][k] f32 on the device (stream
+ * ordered, no synchronisation).  Replaces top_logits_candidates
+ * (crates/ferrite-core/src/hooks.rs:19-38), which copies the row to the host
+ * and sorts all of it, as used with GpuLogitsExecutor::WIDTH = 16
+ * (crates/ferrite-wasm-host/src/adapter.rs:508-515).  k in 1..16 (the
+ * reference takes limit.max(1)); rows with fewer than k selectable entries
+ * are padded with id -1, value -inf; NaN logits are never selected.
+ * ceil(vocab / 2048) * k <= 2048 (vocab 262144 at k = 16). */
+int fb_top_logits(fb_ctx *ctx, const float *logits_dev, int rows,
+                  int64_t vocab, int k, int32_t *ids_dev, float *vals_dev);
 
 /* ------------------------------------------------------ GGUF ingest ---
  * Replaces candle's gguf_file::Content + ModelWeights::from_gguf

@@ -425,6 +425,8 @@ void or_dequantize(int dtype, const void *blocks, int64_t n, float *y) {
     }
 }
 
+static int resolve_threads(int nthreads);
+
 /* ---------------------------------------------------------- vec_dot ---- */
 /* Per-block integer partials.  lanes[l] accumulates sc_j * q * a over the
  * weights whose index is l mod 8 (the scalar k_quants vec_dot shape). */
@@ -489,6 +491,56 @@ double or_vec_dot64(int dtype, int64_t n, const void *w, const void *a) {
 
 float or_vec_dot(int dtype, int64_t n, const void *w, const void *a) {
     return (float)or_vec_dot64(dtype, n, w, a);
+}
+
+/* The same integer partials combined in f32 the way candle-core 0.8.4's
+ * scalar k_quants vec_dot does (the published ggml reference form): per
+ * super-block d = d_w * d_y in f32, eight lane sums sums[l] += d * lane[l],
+ * for Q4_K sumf -= (dmin_w * d_y) * sum_min, and at the end the lane sums
+ * are added to sumf in lane order.  Used by the oracle's candle-f32 forward
+ * (or_model_forward numerics 3) to measure how far the binary64 combine
+ * sits from candle's own float order. */
+float or_vec_dot_candle_f32(int dtype, int64_t n, const void *w, const void *a) {
+    int64_t nb = n / OR_QK_K;
+    const or_block_q8k *y = (const or_block_q8k *)a;
+    float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float sumf = 0.f;
+    for (int64_t b = 0; b < nb; b++) {
+        int32_t lanes[8] = {0};
+        if (dtype == OR_Q4_K) {
+            const or_block_q4k *x = (const or_block_q4k *)w + b;
+            int32_t smin;
+            q4k_block_int(x, y + b, lanes, &smin);
+            const float d = or_f16_to_f32(x->d) * y[b].d;
+            for (int l = 0; l < 8; l++) sums[l] += d * (float)lanes[l];
+            const float dmin = or_f16_to_f32(x->dmin) * y[b].d;
+            sumf -= dmin * (float)smin;
+        } else {
+            const or_block_q6k *x = (const or_block_q6k *)w + b;
+            q6k_block_int(x, y + b, lanes);
+            const float d = or_f16_to_f32(x->d) * y[b].d;
+            for (int l = 0; l < 8; l++) sums[l] += d * (float)lanes[l];
+        }
+    }
+    for (int l = 0; l < 8; l++) sumf += sums[l];
+    return sumf;
+}
+
+void or_qmatmul_candle_f32(int dtype, const void *w, int64_t n, int64_t k, const float *x, int64_t m, float *y,
+                           int nthreads) {
+    int64_t nb = k / OR_QK_K;
+    size_t bb = or_block_bytes(dtype);
+    or_block_q8k *xq = (or_block_q8k *)malloc((size_t)(m * nb) * sizeof(or_block_q8k));
+    for (int64_t r = 0; r < m; r++) or_quantize_q8k(x + r * k, k, xq + r * nb, 0);
+    int nt = resolve_threads(nthreads);
+    for (int64_t r = 0; r < m; r++) {
+        const or_block_q8k *xr = xq + r * nb;
+        float *yr = y + r * n;
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 256)
+        for (int64_t c = 0; c < n; c++)
+            yr[c] = or_vec_dot_candle_f32(dtype, k, (const uint8_t *)w + (size_t)c * nb * bb, xr);
+    }
+    free(xq);
 }
 
 void or_block_dots(int dtype, int64_t nrows, int64_t k, const void *w,

@@ -95,6 +95,19 @@ void or_rope(float *x, int64_t n_heads, int64_t head_dim, int64_t pos,
     }
 }
 
+/* candle-nn's CPU rms_norm in its own order: the f32 sum of squares left to
+ * right, m = sqrt(sum / dim + eps), y = x / m * g. */
+static void rmsnorm_f32(const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float *xr = x + r * dim;
+        float *yr = y + r * dim;
+        float ss = 0.f;
+        for (int64_t i = 0; i < dim; i++) ss += xr[i] * xr[i];
+        const float m = sqrtf(ss / (float)dim + eps);
+        for (int64_t i = 0; i < dim; i++) yr[i] = xr[i] / m * g[i];
+    }
+}
+
 void or_softmax(float *x, int64_t n) {
     float mx = -INFINITY;
     for (int64_t i = 0; i < n; i++) mx = x[i] > mx ? x[i] : mx;
@@ -264,6 +277,10 @@ static void linear(const or_model *m, const or_tensor *w, const float *x,
      * rows dequantize the weights and run a float matmul, up to 8 rows take
      * the quantized-activation integer path. */
     if (mode == 2) mode = rows > 8 ? 1 : 0;
+    if (mode == 3 && w->dtype != OR_F32) {
+        or_qmatmul_candle_f32(w->dtype, w->data, w->rows, w->cols, x, rows, y, m->nthreads);
+        return;
+    }
     if (w->dtype == OR_F32) {
         const float *wf = (const float *)w->data;
         int nt = nthreads_of(m);
@@ -314,17 +331,19 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
     for (int i = 0; i < n; i++) embed_row(&m->tok_embd, tokens[i], x + (size_t)i * H);
     const float scale = (float)(1.0 / sqrt((double)hd));
     const int nt = nthreads_of(m);
+    const int f32 = matmul_mode == 3;
+    void (*norm)(const float *, const float *, float *, int64_t, int64_t, float) = f32 ? rmsnorm_f32 : or_rmsnorm;
     for (int l = 0; l < c->n_layers; l++) {
         const or_layer *L = &m->layers[l];
-        or_rmsnorm(x, (const float *)L->attn_norm.data, h, n, H, c->eps);
+        norm(x, (const float *)L->attn_norm.data, h, n, H, c->eps);
         linear(m, &L->wq, h, n, q, matmul_mode);
         linear(m, &L->wk, h, n, k, matmul_mode);
         linear(m, &L->wv, h, n, v, matmul_mode);
         for (int i = 0; i < n; i++) {
             float *qi = q + (size_t)i * qd, *ki = k + (size_t)i * kd;
             if (c->qk_norm) {
-                or_rmsnorm(qi, (const float *)L->q_norm.data, qi, nq, hd, c->eps);
-                or_rmsnorm(ki, (const float *)L->k_norm.data, ki, nkv, hd, c->eps);
+                norm(qi, (const float *)L->q_norm.data, qi, nq, hd, c->eps);
+                norm(ki, (const float *)L->k_norm.data, ki, nkv, hd, c->eps);
             }
             or_rope(qi, nq, hd, pos + i, c->rope_theta, c->rope_mode);
             or_rope(ki, nkv, hd, pos + i, c->rope_theta, c->rope_mode);
@@ -351,8 +370,31 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
                 float mx = -INFINITY;
                 for (int s = 0; s < T; s++) {
                     const float *ks = kl + (size_t)s * kd + (size_t)hk * hd;
-                    sc[s] = or_attn_dot(qh, ks, hd) * scale;
+                    if (f32) {
+                        float d = 0.f;
+                        for (int e = 0; e < hd; e++) d += qh[e] * ks[e];
+                        sc[s] = d * scale;
+                    } else {
+                        sc[s] = or_attn_dot(qh, ks, hd) * scale;
+                    }
                     mx = sc[s] > mx ? sc[s] : mx;
+                }
+                if (f32) {  /* softmax_last_dim then att.v, f32 left to right */
+                    float l32 = 0.f;
+                    for (int s = 0; s < T; s++) {
+                        sc[s] = expf(sc[s] - mx);
+                        l32 += sc[s];
+                    }
+                    float *oh = o + (size_t)i * qd + (size_t)hq * hd;
+                    for (int e = 0; e < hd; e++) {
+                        float a32 = 0.f;
+                        for (int s = 0; s < T; s++) a32 += (sc[s] / l32) * vl[(size_t)s * kd + (size_t)hk * hd + e];
+                        oh[e] = a32;
+                    }
+                    free(sc);
+                    free(pr);
+                    free(acc);
+                    continue;
                 }
                 double l = 0.0;
                 for (int s = 0; s < T; s++) {
@@ -371,17 +413,18 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
             }
         linear(m, &L->wo, o, n, t, matmul_mode);
         for (size_t e = 0; e < (size_t)n * H; e++) x[e] = t[e] + x[e];
-        or_rmsnorm(x, (const float *)L->ffn_norm.data, h, n, H, c->eps);
+        norm(x, (const float *)L->ffn_norm.data, h, n, H, c->eps);
         linear(m, &L->w_gate, h, n, g, matmul_mode);
         linear(m, &L->w_up, h, n, u, matmul_mode);
-        for (size_t e = 0; e < (size_t)n * F; e++) g[e] = or_silu(g[e]) * u[e];
+        for (size_t e = 0; e < (size_t)n * F; e++)
+            g[e] = (f32 ? g[e] / (1.0f + expf(-g[e])) : or_silu(g[e])) * u[e];
         linear(m, &L->w_down, g, n, t, matmul_mode);
         for (size_t e = 0; e < (size_t)n * H; e++) x[e] = t[e] + x[e];
     }
     m->len = pos + n;
     int first = all_logits ? 0 : n - 1;
     int rows = n - first;
-    or_rmsnorm(x + (size_t)first * H, (const float *)m->out_norm.data, h, rows, H, c->eps);
+    norm(x + (size_t)first * H, (const float *)m->out_norm.data, h, rows, H, c->eps);
     linear(m, &m->output, h, rows, logits, matmul_mode);
     free(x); free(h); free(q); free(k); free(v); free(o); free(t); free(g); free(u);
     return 0;

@@ -99,6 +99,10 @@ void or_qmatmul(int dtype, const void *w, int64_t n, int64_t k,
  * quantization).  Used as the oracle for the prefill GEMM. */
 /* Unrounded binary64 row sums of or_qmatmul (tensor-parallel partials). */
 double or_vec_dot64(int dtype, int64_t n, const void *w, const void *a);
+/* candle's own f32 combine of the same integer partials (8 lane sums). */
+float or_vec_dot_candle_f32(int dtype, int64_t n, const void *w, const void *a);
+void or_qmatmul_candle_f32(int dtype, const void *w, int64_t n, int64_t k, const float *x, int64_t m, float *y,
+                           int nthreads);
 void or_qmatmul64(int dtype, const void *w, int64_t n, int64_t k,
                   const float *x, int64_t m, double *y, int nthreads);
 void or_qmatmul_f32(int dtype, const void *w, int64_t n, int64_t k,
@@ -154,7 +158,12 @@ void or_model_clear(or_model *m);
  * cache.  logits: [n, vocab] when all_logits, else [vocab] for the last token.
  * matmul_mode 0 = Q8_K integer path (decode), 1 = dequantize + f32 matmul
  * (prefill form), 2 = per call by row count as candle's CUDA QMatMul
- * dispatches (> 8 rows float, else integer).  Returns 0 on success. */
+ * dispatches (> 8 rows float, else integer), 3 = candle's f32 CPU order
+ * throughout: the Q8_K integer path with candle's f32 lane combine, RMSNorm
+ * sums of squares, attention dots, softmax sums and P.V in f32 left to
+ * right, f32 exp in softmax and SiLU -- no binary64 step (measures the
+ * binary64 oracle's distance from candle's float arithmetic).  Returns 0 on
+ * success. */
 int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
                      float *logits, int all_logits, int matmul_mode);
 /* Fill the first ctx KV positions of every layer with synthetic values

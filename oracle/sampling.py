@@ -105,3 +105,15 @@ class Sampler:
             return int(hit[0])
         nz = np.nonzero(p > 0)[0]
         return int(nz[-1]) if nz.size else 0
+
+
+def top_logits_candidates(logits: np.ndarray, limit: int):
+    """Restates crates/ferrite-core/src/hooks.rs:19-38 for finite logits:
+    (index, value) pairs sorted by descending logit with a stable sort (equal
+    logits keep index order), the first max(limit, 1) of them.  Written as a
+    stable merge sort (Python's sorted), the same kind of sort as Rust's
+    slice::sort_by, on the key -logit."""
+    x = np.asarray(logits, dtype=np.float32).reshape(-1)
+    order = sorted(range(x.size), key=lambda i: -float(x[i]))
+    take = order[: max(int(limit), 1)]
+    return [(int(i), float(x[i])) for i in take]

@@ -84,7 +84,7 @@ def test_attn_decode_paged(fbctx, torch_cuda, nh, nkv, page):
     qd, kd, vd, btd, ld = t(q), t(kp.transpose(0, 1, 3, 2)), t(vp), t(perm), t(lens)
     out = torch.zeros((b, nh, hd), dtype=torch.float32, device="cuda")
     fb.attn_decode(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(),
-                   out.data_ptr(), b, nh, nkv, hd, page, max_pages, int(lens.max()), 1.0 / math.sqrt(hd))
+                   out.data_ptr(), b, nh, nkv, hd, page, max_pages, num_pages, int(lens.max()), 1.0 / math.sqrt(hd))
     ref = attn_reference(q, kp, vp, perm, lens, page)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=1e-5)
     assert fbctx.error_word() == 0
@@ -115,9 +115,41 @@ def test_attn_decode_long_ring_reuse(fbctx, torch_cuda, nh, nkv, page):
     for fn in (fb.attn_decode, fb.attn_decode_noalloc):
         out = torch.full((b, nh, hd), float("nan"), dtype=torch.float32, device="cuda")
         fn(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(), out.data_ptr(), b, nh,
-           nkv, hd, page, max_pages, int(lens.max()), 1.0 / math.sqrt(hd))
+           nkv, hd, page, max_pages, num_pages, int(lens.max()), 1.0 / math.sqrt(hd))
         outs.append(out.cpu().numpy())
         np.testing.assert_allclose(outs[-1], ref, rtol=1e-4, atol=1e-5)
     # binary64 softmax and P.V: the split and warp layout does not show in the f32 result
     assert np.array_equal(outs[0], outs[1])
+    assert fbctx.error_word() == 0
+
+
+@pytest.mark.parametrize("entry", ["attn_decode", "attn_decode_noalloc"])
+def test_attn_decode_rejects_page_ids_outside_the_pool(fbctx, torch_cuda, entry):
+    """A block-table entry outside [0, num_pages) (a stale or corrupt id from
+    the caller) is never dereferenced: the kernel skips that page and sets
+    the error word's bad-page bit.  The pools here are exactly num_pages
+    pages long, so a read through the bad id would leave the allocation."""
+    torch = torch_cuda
+    rng = np.random.default_rng(77)
+    hd, nh, nkv, page, b = 128, 32, 8, 64, 2
+    lens = np.array([200, 130], dtype=np.int32)
+    max_pages = 4
+    num_pages = b * max_pages
+    bt = np.arange(num_pages, dtype=np.int32).reshape(b, max_pages)
+    bt[1, 1] = num_pages + 1000  # sequence 1's second page: outside the pool
+    kp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    vp = rng.normal(0, 1, (num_pages, nkv, page, hd)).astype(np.float16)
+    q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    qd, kd, vd, btd, ld = t(q), t(kp.transpose(0, 1, 3, 2)), t(vp), t(bt), t(lens)
+    out = torch.zeros((b, nh, hd), dtype=torch.float32, device="cuda")
+    assert fbctx.error_word() == 0
+    getattr(fb, entry)(fbctx, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), btd.data_ptr(), ld.data_ptr(),
+                       out.data_ptr(), b, nh, nkv, hd, page, max_pages, num_pages, int(lens.max()),
+                       1.0 / math.sqrt(hd))
+    torch.cuda.synchronize()
+    assert fbctx.error_word() & 0x8, "bad-page bit not set"
+    # sequence 0 only uses pages inside the pool: its result is unaffected
+    ref = attn_reference(q[:1], kp, vp, bt[:1], lens[:1], page)
+    np.testing.assert_allclose(out.cpu().numpy()[:1], ref, rtol=1e-4, atol=1e-5)
     assert fbctx.error_word() == 0

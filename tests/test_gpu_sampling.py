@@ -61,3 +61,39 @@ def test_sample_matches_rules_f64(fbctx, torch_cuda, vocab, ci):
 def test_sample_matches_reference_f32_concentrated(fbctx, torch_cuda, ci):
     mism = run(fbctx, torch_cuda, 151936, ci, "f32", 1.0, 14.0)
     assert not mism, f"draws differ (step, device, oracle): {mism}"
+
+
+@pytest.mark.parametrize("vocab,k,rows", [(151936, 16, 1), (151936, 5, 3), (128256, 16, 2), (37, 16, 1), (10, 16, 1),
+                                          (4096, 1, 1)])
+def test_top_logits_matches_hook_order(fbctx, torch_cuda, vocab, k, rows):
+    """fb_top_logits against the restated hook candidate list (stable
+    descending sort): ties of the top value across chunks, repeated values
+    inside one chunk, +-0.0, -inf entries, and rows shorter than k."""
+    torch = torch_cuda
+    rng = np.random.default_rng(vocab + k + rows)
+    x = rng.normal(0, 3, (rows, vocab)).astype(np.float32)
+    for r in range(rows):
+        top = float(x[r].max())
+        # the row maximum repeated at indices in different 2048-value chunks
+        for i in rng.choice(vocab, min(vocab, 5), replace=False):
+            x[r, i] = top
+        # a run of equal values inside one chunk, and signed zeros
+        j = int(rng.integers(0, max(1, vocab - 8)))
+        x[r, j:j + 6] = top - 0.25 if vocab > 8 else x[r, j:j + 6]
+        x[r, rng.integers(0, vocab)] = -np.inf
+    if vocab > 2:
+        x[0, 0], x[0, 1] = -0.0, 0.0
+    xd = torch.from_numpy(x).cuda()
+    ids = torch.full((rows, k), -7, dtype=torch.int32, device="cuda")
+    vals = torch.zeros((rows, k), dtype=torch.float32, device="cuda")
+    fb.top_logits(fbctx, xd.data_ptr(), rows, vocab, k, ids.data_ptr(), vals.data_ptr())
+    torch.cuda.synchronize()
+    gi, gv = ids.cpu().numpy(), vals.cpu().numpy()
+    for r in range(rows):
+        want = S.top_logits_candidates(x[r], k)
+        n = len(want)
+        assert gi[r, :n].tolist() == [i for i, _ in want], f"row {r}"
+        assert np.array_equal(gv[r, :n], np.array([v for _, v in want], np.float32))
+        assert (gi[r, n:] == -1).all() and np.isneginf(gv[r, n:]).all()
+    with pytest.raises(fb.FerriteError):
+        fb.top_logits(fbctx, xd.data_ptr(), rows, vocab, 17, ids.data_ptr(), vals.data_ptr())

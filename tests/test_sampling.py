@@ -52,3 +52,19 @@ def test_top_p_keeps_crossing_token():
     sm = S.Sampler(temperature=1.0, top_p=0.7, top_k=0, min_p=0.0, repetition_penalty=1.0, seed=1)
     seen = {sm.sample(p) for _ in range(400)}
     assert seen == {0, 1}  # 0.5 < 0.7 keeps token 1 as well; 0.8 >= 0.7 stops
+
+
+def test_top_logits_candidates_stable_order():
+    """The hook's candidate list (hooks.rs:19-38): descending logits, equal
+    logits in index order, limit 0 taken as 1, a short row returns it all."""
+    x = np.array([0.5, 2.0, -1.0, 2.0, 0.5, -0.0, 0.0, 3.0], dtype=np.float32)
+    got = S.top_logits_candidates(x, 6)
+    assert [i for i, _ in got] == [7, 1, 3, 0, 4, 5]
+    assert S.top_logits_candidates(x, 0) == [(7, 3.0)]
+    assert len(S.top_logits_candidates(x, 16)) == x.size
+    # -0.0 and 0.0 compare equal: index order
+    assert [i for i, _ in S.top_logits_candidates(np.array([-0.0, 0.0], np.float32), 2)] == [0, 1]
+    rng = np.random.default_rng(3)
+    y = rng.normal(0, 1, 5000).astype(np.float32)
+    want = np.argsort(-y, kind="stable")[:16]
+    assert [i for i, _ in S.top_logits_candidates(y, 16)] == list(want)

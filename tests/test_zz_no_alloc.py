@@ -30,14 +30,14 @@ def make_inputs(torch, seed, b, nh, nkv, page, lens):
     q = rng.normal(0, 1, (b, nh, hd)).astype(np.float32)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
     # K pages are dim-major on the device: [page][kv head][hd][page tokens]
-    return dict(q=t(q), k=t(kp.transpose(0, 1, 3, 2)), v=t(vp), bt=t(bt), lens=t(np.asarray(lens, np.int32)), b=b, nh=nh, nkv=nkv,
-                page=page, max_pages=max_pages, max_len=int(max(lens)))
+    return dict(q=t(q), k=t(kp.transpose(0, 1, 3, 2)), v=t(vp), bt=t(bt), lens=t(np.asarray(lens, np.int32)), b=b,
+                nh=nh, nkv=nkv, page=page, max_pages=max_pages, num_pages=num_pages, max_len=int(max(lens)))
 
 
 def run(fn, ctx, torch, d):
     out = torch.full((d["b"], d["nh"], 128), float("nan"), dtype=torch.float32, device="cuda")
     fn(ctx, d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["bt"].data_ptr(), d["lens"].data_ptr(),
-       out.data_ptr(), d["b"], d["nh"], d["nkv"], 128, d["page"], d["max_pages"], d["max_len"],
+       out.data_ptr(), d["b"], d["nh"], d["nkv"], 128, d["page"], d["max_pages"], d["num_pages"], d["max_len"],
        1.0 / math.sqrt(128))
     torch.cuda.synchronize()
     return out.cpu().numpy()
@@ -62,4 +62,29 @@ def test_noalloc_rejects_oversized_request(fbctx, torch_cuda):
     # 16 sequences x 64 heads x 16 splits x 1040 B = 17 MB: > 4 MiB
     with pytest.raises(fb.FerriteError, match="exceeds the fixed"):
         fb.attn_decode_noalloc(fbctx, d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["bt"].data_ptr(),
-                               d["lens"].data_ptr(), d["q"].data_ptr(), 16, 64, 8, 128, 64, 128, 8192, 0.088)
+                               d["lens"].data_ptr(), d["q"].data_ptr(), 16, 64, 8, 128, 64, 128, 128, 8192,
+                               0.088)
+
+
+def noalloc_bytes(b, nh, nkv):
+    """Scratch a call needs: split partials (16 splits x (128 dims + max,
+    sum) binary64 per head) plus the merge counters rounded up to 256 bytes."""
+    return b * nh * 16 * 130 * 8 + (b * nkv * 4 + 255) // 256 * 256
+
+
+def test_noalloc_largest_accepted_shape(fbctx, torch_cuda):
+    """The largest batch the fixed scratch accepts for 32 heads / 8 kv heads
+    runs and matches fb_attn_decode; one more sequence is rejected."""
+    torch = torch_cuda
+    limit = 4 << 20
+    b = max(x for x in range(1, 64) if noalloc_bytes(x, 32, 8) <= limit)
+    assert noalloc_bytes(b + 1, 32, 8) > limit
+    lens = [1 + (97 * i) % 600 for i in range(b)]
+    d = make_inputs(torch, 4, b=b, nh=32, nkv=8, page=64, lens=lens)
+    ref = run(fb.attn_decode, fbctx, torch, d)
+    got = run(fb.attn_decode_noalloc, fbctx, torch, d)
+    assert_close(got, ref, what=f"noalloc at its largest batch ({b})")
+    d2 = make_inputs(torch, 5, b=b + 1, nh=32, nkv=8, page=64, lens=lens + [64])
+    with pytest.raises(fb.FerriteError, match="exceeds the fixed"):
+        run(fb.attn_decode_noalloc, fbctx, torch, d2)
+    assert fbctx.error_word() == 0
