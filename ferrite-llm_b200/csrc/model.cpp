@@ -29,6 +29,7 @@
 #include <memory>
 #include <string>
 
+#include "decode_step.h"
 #include "fb_internal.h"
 
 using namespace fb;
@@ -106,6 +107,14 @@ struct fb_model {
     std::map<int, cudaGraphExec_t> graphs;
     int len0 = 0;  // tokens held by sequence slot 0 (forward / prefill API)
     int launches_per_step = 0;
+    // persistent decode step (batch 1, single GPU): per-layer tensor table,
+    // barrier counters and launch plan; ds_on selects it over the kernel chain
+    // (off by default: measured slower than the chain on B200, 3.4-4.1 vs
+    // 2.07 ms per Qwen3-8B step -- one 9-warp CTA per SM cannot hide the
+    // consumers' latency and each layer pays six grid barriers)
+    DevBuf ds_layers, ds_sync;
+    DsPlan ds_plan;
+    bool ds_ok = false, ds_on = false;
     // batched prefill buffers (allocated on first use, rows = pf_cap)
     DevBuf pf_tok, pf_x, pf_xn, pf_yd, pf_yqkv, pf_q, pf_attn, pf_ygu, pf_act;
     int pf_cap = 0;
@@ -208,7 +217,67 @@ static TpArgmax tp_argmax(const fb_model *m) {
     return t;
 }
 
+// The batch-1 step as one persistent kernel (decode_step.cu) + argmax.
+static bool persistent_step(fb_model *m, int b, StepProbe *probe, unsigned long long *trace = nullptr) {
+    if (!(m->ds_ok && m->ds_on && b == 1 && !probe && !m->comm)) return false;
+    fb_ctx *ctx = m->ctx;
+    const fb_model_config &c = m->c, &lc = m->lc;
+    const int qd = lc.n_heads * c.head_dim;
+    DsArgs A{};
+    A.layers = m->ds_layers.as<DsLayer>();
+    A.n_layers = c.n_layers;
+    A.H = c.hidden;
+    A.F = lc.ffn;
+    A.n_heads = lc.n_heads;
+    A.n_kv = lc.n_kv_heads;
+    A.vocab = lc.vocab;
+    A.qkv_n = (lc.n_heads + 2 * lc.n_kv_heads) * c.head_dim;
+    A.emb = m->tok_embd.t->main();
+    A.out = m->output.t->main();
+    A.dt_out = m->output.t->dtype == FB_Q4_K ? 4 : 6;
+    A.out_norm = m->out_norm.as<float>();
+    A.eps = c.eps;
+    A.scale = (float)(1.0 / sqrt((double)c.head_dim));
+    A.tok = m->tok.as<int32_t>();
+    A.pos = m->pos.as<int32_t>();
+    A.kv = m->kv.as<__half>();
+    A.kv_layer = m->kv_half_layer();
+    A.block_table = m->block_table.as<int32_t>();
+    A.pages_per_seq = m->pages_per_seq;
+    A.num_pages = m->num_pages;
+    A.rope_cos = m->rope_cos.as<float>();
+    A.rope_sin = m->rope_sin.as<float>();
+    A.rope_rows = c.max_ctx;
+    A.rope_mode = c.rope_mode;
+    A.qk_norm = c.qk_norm;
+    A.xa = m->x.as<float>();
+    A.xb = m->x2.as<float>();
+    A.y_qkv = m->y_qkv.as<float>();
+    A.q_out = m->q.as<float>();
+    A.attn = m->attn.as<float>();
+    A.y_o = m->y_o.as<float>();
+    A.y_gu = m->y_gu.as<float>();
+    A.y_d = m->y_d.as<float>();
+    A.logits = m->logits.as<float>();
+    A.act_a = q8act_view(m->act_a.ptr, c.max_batch, qd);
+    A.act_f = q8act_view(m->act_f.ptr, c.max_batch, lc.ffn);
+    A.part_o = m->part_o.as<double>();
+    A.part_ml = m->part_ml.as<double>();
+    A.att_cnt = m->att_cnt.as<int>();
+    A.sync = m->ds_sync.as<unsigned>();
+    A.err = ctx->err_word;
+    A.ns = m->ds_plan.ns;
+    A.nstage = m->ds_plan.nstage;
+    A.trace = trace;
+    launch_decode_step(ctx, A, m->ds_plan.smem);
+    launch_argmax(ctx, m->logits.as<float>(), b, lc.vocab, m->next.as<int32_t>(), m->argmax_ws.ptr);
+    m->x_last = m->x2.as<float>();
+    m->launches_per_step = 2;
+    return true;
+}
+
 static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
+    if (persistent_step(m, b, probe)) return;
     fb_ctx *ctx = m->ctx;
     int nl = 0;
     auto mark = [&](int kind, int n) {
@@ -669,7 +738,59 @@ int fb_model_finalize(fb_model *m) {
             L.wgate.reset();
             L.wup.reset();
         }
+        // the persistent batch-1 step, where the shape allows it
+        const fb_model_config &lc = m->lc;
+        bool dt_ok = m->tok_embd.t->dtype == FB_Q4_K;
+        for (int l = 0; l < c.n_layers && dt_ok; l++) {
+            const Layer &L = *m->layers[l];
+            for (const fb_qtensor *t : {L.wqkv.t, L.wo.t, L.wgu.t, L.wdown.t, m->output.t})
+                dt_ok = dt_ok && (t->dtype == FB_Q4_K || t->dtype == FB_Q6_K);
+        }
+        m->ds_ok = !m->comm && dt_ok &&
+                   decode_step_plan(ctx, c.hidden, lc.ffn, lc.n_heads, lc.n_kv_heads, m->pages_per_seq, kPage,
+                                    &m->ds_plan);
+        if (m->ds_ok) {
+            std::vector<DsLayer> tab((size_t)c.n_layers);
+            auto dt = [](const fb_qtensor *t) { return t->dtype == FB_Q4_K ? 4 : 6; };
+            for (int l = 0; l < c.n_layers; l++) {
+                const Layer &L = *m->layers[l];
+                DsLayer &d = tab[(size_t)l];
+                d.qkv = L.wqkv.t->main();
+                d.o = L.wo.t->main();
+                d.gu = L.wgu.t->main();
+                d.down = L.wdown.t->main();
+                d.dt_qkv = dt(L.wqkv.t);
+                d.dt_o = dt(L.wo.t);
+                d.dt_gu = dt(L.wgu.t);
+                d.dt_down = dt(L.wdown.t);
+                d.attn_norm = L.attn_norm.as<float>();
+                d.ffn_norm = L.ffn_norm.as<float>();
+                d.q_norm = c.qk_norm ? L.q_norm.as<float>() : nullptr;
+                d.k_norm = c.qk_norm ? L.k_norm.as<float>() : nullptr;
+            }
+            m->ds_layers.alloc(tab.size() * sizeof(DsLayer));
+            FB_CUDA(cudaMemcpyAsync(m->ds_layers.ptr, tab.data(), tab.size() * sizeof(DsLayer), cudaMemcpyHostToDevice,
+                                    ctx->stream));
+            m->ds_sync.alloc(256);
+            FB_CUDA(cudaMemsetAsync(m->ds_sync.ptr, 0, 256, ctx->stream));
+            FB_CUDA(cudaStreamSynchronize(ctx->stream));
+        }
         m->finalized = true;
+    });
+}
+
+int fb_model_set_persistent(fb_model *m, int enable, int *supported) {
+    return guarded([&] {
+        FB_REQUIRE(m, "null model");
+        require_ready(m);
+        if (supported) *supported = m->ds_ok ? 1 : 0;
+        const bool on = enable != 0;
+        if (on != m->ds_on) {
+            FB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+            for (auto &g : m->graphs) cudaGraphExecDestroy(g.second);
+            m->graphs.clear();
+            m->ds_on = on;
+        }
     });
 }
 
@@ -983,6 +1104,29 @@ int fb_model_profile(fb_model *m, const int32_t *tokens_dev, const int32_t *pos_
     });
 }
 
+int fb_model_step_timeline(fb_model *m, const int32_t *tokens_dev, const int32_t *pos_dev, uint64_t *stamps_host,
+                           int64_t capacity, int *ctas_out, int *slots_out) {
+    return guarded([&] {
+        FB_REQUIRE(m && tokens_dev && pos_dev && stamps_host && ctas_out && slots_out, "null argument");
+        require_ready(m);
+        FB_REQUIRE(m->ds_ok && m->ds_on && !m->comm, "the persistent step is not in use for this model");
+        const int ctas = m->ctx->num_sms, per = (m->c.n_layers + 1) * DS_TRACE_SLOTS;
+        const int64_t n = (int64_t)ctas * per;
+        FB_REQUIRE(capacity >= n, "stamps_host holds fewer than num_sms * (n_layers + 1) * 16 entries");
+        cudaStream_t s = m->ctx->stream;
+        DevBuf tr;
+        tr.alloc((size_t)n * 8);
+        FB_CUDA(cudaMemsetAsync(tr.ptr, 0, (size_t)n * 8, s));
+        FB_CUDA(cudaMemcpyAsync(m->tok.ptr, tokens_dev, 4, cudaMemcpyDeviceToDevice, s));
+        FB_CUDA(cudaMemcpyAsync(m->pos.ptr, pos_dev, 4, cudaMemcpyDeviceToDevice, s));
+        persistent_step(m, 1, nullptr, tr.as<unsigned long long>());
+        FB_CUDA(cudaMemcpyAsync(stamps_host, tr.ptr, (size_t)n * 8, cudaMemcpyDeviceToHost, s));
+        FB_CUDA(cudaStreamSynchronize(s));
+        *ctas_out = ctas;
+        *slots_out = DS_TRACE_SLOTS;
+    });
+}
+
 int fb_model_launches_per_step(const fb_model *m, int *launches) {
     return guarded([&] {
         FB_REQUIRE(m && launches, "null argument");
@@ -990,8 +1134,9 @@ int fb_model_launches_per_step(const fb_model *m, int *launches) {
         const int L = m->c.n_layers;
         const bool q8_fused = (m->lc.n_heads / m->lc.n_kv_heads) % 2 == 0;
         // matches step(): embed-norm; per layer qkv, attention (+ Q8_K quantize
-        // for odd GQA groups), o, norm, gate_up, swiglu, down, norm; lm_head, argmax
-        *launches = 1 + (q8_fused ? 8 : 9) * L + 2;
+        // for odd GQA groups), o, norm, gate_up, swiglu, down, norm; lm_head,
+        // argmax -- or, batch 1 with the persistent step, its kernel and argmax
+        *launches = m->launches_per_step > 0 ? m->launches_per_step : 1 + (q8_fused ? 8 : 9) * L + 2;
     });
 }
 

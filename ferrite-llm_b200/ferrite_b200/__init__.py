@@ -40,7 +40,8 @@ EXPORTED = (
     "fb_model_read_activation", "fb_model_profile", "fb_model_launches_per_step", "fb_attn_decode_noalloc",
     "fb_qtensor_upload_slice", "fb_comm_create", "fb_comm_handle", "fb_comm_open", "fb_comm_destroy",
     "fb_model_create_tp", "fb_model_tp_info", "fb_comm_set_timeout_ms", "fb_attn_prefill", "fb_gguf_config",
-    "fb_model_load_gguf", "fb_model_forward_all", "fb_sample", "fb_top_logits",
+    "fb_model_load_gguf", "fb_model_forward_all", "fb_sample", "fb_top_logits", "fb_model_set_persistent",
+    "fb_model_step_timeline",
 )
 COMM_HANDLE_BYTES = 64
 
@@ -135,6 +136,8 @@ def _declare(L):
         "fb_model_forward_all": (i32, [vp, vp, i32, i32, vp]),
         "fb_sample": (i32, [vp, vp, i32, P(SamplerConfig), vp, i32, P(C.c_uint64), P(i32)]),
         "fb_top_logits": (i32, [vp, vp, i32, i64, i32, vp, vp]),
+        "fb_model_set_persistent": (i32, [vp, i32, P(i32)]),
+        "fb_model_step_timeline": (i32, [vp, vp, vp, vp, i64, P(i32), P(i32)]),
         "fb_model_create_tp": (i32, [vp, P(ModelConfig), vp, P(vp)]),
         "fb_model_tp_info": (i32, [vp, P(i32), P(i32), P(i32), P(i32)]),
     }
@@ -518,6 +521,24 @@ class Model:
         nl = np.zeros(len(PROF_KINDS), dtype=np.int32)
         _check(lib().fb_model_profile(self.h, tok_ptr, pos_ptr, batch, steps, _np(ms), _np(nl)))
         return {k: (float(ms[i]), int(nl[i])) for i, k in enumerate(PROF_KINDS)}
+
+    def set_persistent(self, enable: bool) -> bool:
+        """Batch-1 decode as one persistent kernel (True) or as the per-op
+        kernel chain (False, the default); returns whether the model supports
+        the persistent kernel."""
+        sup = C.c_int32()
+        _check(lib().fb_model_set_persistent(self.h, int(bool(enable)), C.byref(sup)))
+        return bool(sup.value)
+
+    def step_timeline(self, tok_ptr: int, pos_ptr: int, n_sms: int = 148) -> np.ndarray:
+        """Phase timeline of one eager persistent step: uint64 ns stamps
+        [cta][layer + 1][16] (fb_model_step_timeline)."""
+        per = (self.cfg["n_layers"] + 1) * 16
+        buf = np.zeros(n_sms * per + 1024 * per, dtype=np.uint64)
+        ctas, slots = C.c_int32(), C.c_int32()
+        _check(lib().fb_model_step_timeline(self.h, tok_ptr, pos_ptr, _np(buf), buf.size, C.byref(ctas),
+                                            C.byref(slots)))
+        return buf[: ctas.value * per].reshape(ctas.value, self.cfg["n_layers"] + 1, slots.value)
 
     def launches_per_step(self) -> int:
         v = C.c_int()

@@ -280,8 +280,29 @@ enum fb_prof_kind {
 int fb_model_profile(fb_model *m, const int32_t *tokens_dev,
                      const int32_t *pos_dev, int batch, int steps,
                      float *ms_out, int *launches_out);
-/* Kernels one decode step launches (graph nodes of the captured step). */
+/* Kernels the last decode step launched (graph nodes of the captured step;
+ * before any step, the kernel-chain count). */
 int fb_model_launches_per_step(const fb_model *m, int *launches);
+/* Selects how a single-GPU batch-1 decode step runs: enable = 1 as one
+ * persistent cooperative kernel that streams every layer's weights and KV
+ * pages through shared memory across grid barriers (plus the argmax kernel),
+ * enable = 0 (default, faster on B200) as the chain of per-op kernels.  Both
+ * compute the same values.  *supported (may be NULL) tells whether the model's shape allows
+ * the persistent kernel (GQA group 2, 4 or 8; Q4_K / Q6_K tensors; not
+ * tensor parallel); batches above 1 always run the chain.  No reference
+ * counterpart: candle runs one kernel per op. */
+int fb_model_set_persistent(fb_model *m, int enable, int *supported);
+/* Runs one batch-1 persistent decode step eagerly (device-resident token and
+ * position as in fb_model_decode_dev) and returns its phase timeline:
+ * stamps_host[(cta * (n_layers + 1) + layer) * 16 + k] = %globaltimer (ns)
+ * when CTA cta's consumers finished phase k of layer `layer` (k: 0 norm,
+ * 1 QKV, 2 barrier, 3 attention, 4 barrier, 5 O, 6 barrier, 7 norm, 8
+ * gate/up, 9 barrier, 10 SwiGLU, 11 barrier, 12 down, 13 barrier; slot 15 of
+ * layer 0 = kernel start; layer n_layers: 0 final norm, 1 lm_head), 0 where
+ * not reached.  capacity >= num_sms * (n_layers + 1) * 16. */
+int fb_model_step_timeline(fb_model *m, const int32_t *tokens_dev,
+                           const int32_t *pos_dev, uint64_t *stamps_host,
+                           int64_t capacity, int *ctas_out, int *slots_out);
 /* Diagnostic read of the last decode step's f32 activations of batch row
  * `row` (values of the last layer for per-layer buffers): "x" (residual
  * stream, hidden), "qkv", "q" (after QK-norm + RoPE), "attn" (attention
