@@ -357,6 +357,29 @@ def use_tp(args) -> bool:
     return int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.replicas
 
 
+def timeline_table(tl) -> dict:
+    """Per-phase microseconds of the persistent step's timeline [cta][layer
+    + 1][16] (fb_model_step_timeline): median and max over CTAs of each
+    phase's duration, averaged over the inner layers."""
+    import numpy as np
+
+    L = tl.shape[1] - 1
+    names = ["qkv", "barrier_qkv", "attention", "barrier_attention", "o", "barrier_o", "norm_ffn", "gate_up",
+             "barrier_gate_up", "swiglu", "barrier_swiglu", "down", "barrier_down", "norm_attn"]
+    acc = {n: [] for n in names}
+    for l in range(1, L - 1):
+        prev = tl[:, l, 0]
+        for k, n in enumerate(names):
+            cur = tl[:, l, k + 1] if k < 13 else tl[:, l + 1, 0]
+            acc[n].append((np.median(cur - prev), np.max(cur - prev)))
+            prev = cur
+    out = {n: {"median_us": float(np.mean([a for a, _ in v]) / 1e3), "max_us": float(np.mean([b for _, b in v]) / 1e3)}
+           for n, v in acc.items()}
+    out["layer_us"] = float((tl[:, L - 1, 13].max() - tl[:, 0, 0].min()) / 1e3 / L)
+    out["lm_head_us"] = float(np.median(tl[:, L, 1] - tl[:, L, 0]) / 1e3)
+    return out
+
+
 def prefill_extra(model, cfg: dict, stream, T: int = 2048) -> dict:
     """The batched prompt pass of the decode model (T uniform random ids,
     seed 2) through fb_model_forward: host tokens in, host logits out; two
@@ -420,6 +443,10 @@ def main():
                     help="(default under torchrun) one tensor-parallel model over all ranks (strong scaling)")
     ap.add_argument("--replicas", action="store_true",
                     help="under torchrun: an independent replica per GPU instead of tensor parallelism")
+    ap.add_argument("--persistent", action="store_true",
+                    help="batch 1: run the opt-in persistent decode-step kernel instead of the kernel chain")
+    ap.add_argument("--timeline", action="store_true",
+                    help="with --persistent: print the per-phase timeline of one eager step and exit")
     ap.add_argument("--no-prefill-extra", action="store_true",
                     help="skip the 2048-token prefill measurement added to the N=1 decode line")
     ap.add_argument("--prefill", type=int, default=0, metavar="T",
@@ -463,6 +490,8 @@ def main():
     model.synth(SEED)
     model.finalize()
     model.synth_kv(SEED + 7, args.ctx)
+    if args.persistent:
+        assert model.set_persistent(True), "the persistent step does not support this model"
     if pg:
         pg.barrier()  # tensor-parallel ranks start stepping together
     nsteps = args.warmup + args.steps
@@ -473,6 +502,14 @@ def main():
 
     def dstep(i):
         model.decode_dev(tok.data_ptr(), pos_all[i].data_ptr(), B, next_ptr=tok.data_ptr())
+
+    if args.timeline:
+        for i in range(3):
+            dstep(i)
+        tl = model.step_timeline(tok.data_ptr(), pos_all[3].data_ptr(), torch.cuda.get_device_properties(local)
+                                 .multi_processor_count).astype(np.int64)
+        print(json.dumps(timeline_table(tl)))
+        return
 
     if args.profile_run:
         for i in range(args.profile_run):
