@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "fb_internal.h"
@@ -335,6 +336,206 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     pdl_launch();
 }
 
+// ---------------------------------------------------------------------------
+// Two-pass form for long prompts.  The fused kernel above dequantizes each
+// weight slice once per 256-token tile, i.e. T / 256 times per prompt; from
+// T = 512 rows on, the weights are instead dequantized once (per chunk of
+// rows, k_dequant_rows_f16: the same fp16 values dequant_slice_* feed the
+// fused kernel's B operand) and multiplied by a plain fp16 tensor-core GEMM
+// with TMA on both operands (k_gemm_f16).  Same operands, same MMA shape and
+// k order: the two forms give the same bits.
+
+// Wh[r][k] fp16 (r < rows, weight rows row0 + r) from the tile-major records.
+// Thread (row, super-block b, 64-column slice c, half hf) writes 32 columns.
+template <int DT>
+__global__ void __launch_bounds__(256) k_dequant_rows_f16(const uint8_t *__restrict__ W, int64_t nb, int64_t row0,
+                                                          int64_t rows, __half *__restrict__ Wh) {
+    constexpr int REC = PfRec<DT>::bytes;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nb * 8) return;
+    const int hf = (int)(i & 1), c = (int)((i >> 1) & 3);
+    const int64_t b = (i >> 3) % nb, rr = (i >> 3) / nb;
+    const int64_t row = row0 + rr;
+    const uint8_t *rec = W + ((size_t)(row >> 4) * nb + b) * REC;
+    uint4 ch[4];
+    if constexpr (DT == 4) dequant_slice_q4k(rec, (int)(row & 15), c, hf, ch);
+    else dequant_slice_q6k(rec, (int)(row & 15), c, hf, ch);
+    uint4 *dst = reinterpret_cast<uint4 *>(Wh + rr * (nb * 256) + b * 256 + 64 * c + 32 * hf);
+#pragma unroll
+    for (int qq = 0; qq < 4; qq++) dst[qq] = ch[qq];
+}
+
+constexpr int GM_BM = 256, GM_BK = 64;
+constexpr uint32_t GM_A_BYTES = GM_BM * GM_BK * 2;  // 32 KB
+constexpr int GM_EPI_WARPS = 4;
+constexpr int GM_THREADS = 64 + 32 * GM_EPI_WARPS;
+constexpr uint32_t GM_TMEM_COLS = 512;
+// BN = 128: 4 stages of 48 KB, two accumulator sets (the epilogue of tile i
+// overlaps the mainloop of tile i + 1); BN = 256: 3 stages of 64 KB, one
+// accumulator set filling TMEM, half the L2 re-reads of X per output.
+template <int BN> struct GmCfg {
+    static constexpr uint32_t B_BYTES = BN * GM_BK * 2;
+    static constexpr int STAGES = BN == 128 ? 4 : 3;
+    static constexpr int NACC = (int)GM_TMEM_COLS / (2 * BN);
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * (GM_A_BYTES + B_BYTES);
+    // kind::f16 instruction descriptor: fp16 A / B, f32 D, K-major, M = 128, N = BN
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(PF_MH >> 4) << 24);
+};
+static_assert(GmCfg<128>::SMEM <= 227 * 1024 && GmCfg<256>::SMEM <= 227 * 1024, "gemm stages must fit");
+
+__device__ __forceinline__ void umma_f16_desc(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Y[t, n_base + n] = rowscale[t] * sum_k Xh[t, k] Wh[n, k] for the chunk's
+// rows n < BN * tiles_n.  Persistent: CTA b takes tiles b, b + grid, ...
+// (tile = (n tile) * tiles_m + (m tile)); warp 0 issues the TMA loads of
+// both operands into the stage ring, warp 1 the MMAs (two M = 128 halves of
+// the 256-row tile per 16-wide k step) into TMEM, warps 2..5 drain a finished
+// accumulator set (tcgen05.ld, row scale, f32 stores).  Every wait is bounded.
+template <int BN>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    k_gemm_f16(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap, int T,
+               int64_t ldy, int64_t n_base, int tiles_m, int tiles_n, int ksteps, const float *__restrict__ rowscale,
+               float *__restrict__ Y, uint32_t *err) {
+    using Cfg = GmCfg<BN>;
+    constexpr int ST_N = Cfg::STAGES, NACC = Cfg::NACC;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full[ST_N], empty[ST_N], acc_full[NACC], acc_empty[NACC];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort_raw;
+    volatile int &s_abort = s_abort_raw;
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem, *sB = smem + ST_N * GM_A_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles = tiles_m * tiles_n;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ST_N; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < NACC; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], GM_EPI_WARPS);
+        }
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(GM_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            long long s = 0;
+            for (int t = blockIdx.x; t < tiles && !s_abort; t += gridDim.x) {
+                const int m0 = (t % tiles_m) * GM_BM, n0 = (t / tiles_m) * BN;
+                for (int k = 0; k < ksteps; k++, s++) {
+                    const int st = (int)(s % ST_N);
+                    if (s >= ST_N && !mbar_wait_bounded(&empty[st], (uint32_t)((s / ST_N) - 1) & 1u)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&full[st], GM_A_BYTES + Cfg::B_BYTES);
+                    tma_load_2d(sA + st * GM_A_BYTES, &xmap, k * GM_BK, m0, &full[st]);
+                    tma_load_2d(sB + st * Cfg::B_BYTES, &wmap, k * GM_BK, n0, &full[st]);
+                }
+            }
+            // copies in flight land before shared memory is released
+            for (long long k = s > ST_N ? s - ST_N : 0; k < s; k++)
+                mbar_wait_bounded(&full[k % ST_N], (uint32_t)(k / ST_N) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+            long long s = 0;
+            int li = 0;
+            for (int t = blockIdx.x; t < tiles && !s_abort; t += gridDim.x, li++) {
+                const int a = li % NACC;
+                if (li >= NACC && !mbar_wait_bounded(&acc_empty[a], (uint32_t)((li / NACC) - 1) & 1u)) {
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                for (int k = 0; k < ksteps; k++, s++) {
+                    const int st = (int)(s % ST_N);
+                    if (!mbar_wait_bounded(&full[st], (uint32_t)(s / ST_N) & 1u)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < GM_BK / 16; kk++) {
+                        const uint64_t db = umma_desc_sw128(bBase + st * Cfg::B_BYTES + kk * 32);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const uint64_t da = umma_desc_sw128(aBase + st * GM_A_BYTES + h * (PF_MH * 128) + kk * 32);
+                            umma_f16_desc(tmem + a * (2 * BN) + h * BN, da, db, Cfg::IDESC, (k > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                    umma_commit(&empty[st]);  // frees the stage once these MMAs have read it
+                }
+                if (s_abort) break;
+                umma_commit(&acc_full[a]);
+            }
+        }
+    } else {
+        // warps 2..5: TMEM lane quarter q = warp % 4 holds tile rows 32 q .. 32 q + 31 of each half
+        const int q = warp & 3;
+        int li = 0;
+        for (int t = blockIdx.x; t < tiles && !s_abort; t += gridDim.x, li++) {
+            const int a = li % NACC;
+            const int m0 = (t % tiles_m) * GM_BM, n0 = (t / tiles_m) * BN;
+            if (!mbar_wait_bounded(&acc_full[a], (uint32_t)(li / NACC) & 1u)) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int h = 0; h < 2; h++) {
+                const int orow = m0 + PF_MH * h + 32 * q + lane;
+                const float sc = orow < T ? rowscale[orow] : 0.f;
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 32; cc++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + a * (2 * BN) + h * BN + 32 * cc, v);
+                    if (orow < T) {
+                        float *dst = Y + (int64_t)orow * ldy + n_base + n0 + 32 * cc;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4 *>(dst + i) = make_float4(
+                                __fmul_rn(__uint_as_float(v[i]), sc), __fmul_rn(__uint_as_float(v[i + 1]), sc),
+                                __fmul_rn(__uint_as_float(v[i + 2]), sc), __fmul_rn(__uint_as_float(v[i + 3]), sc));
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (s_abort && threadIdx.x == 0) atomicOr(err, ERRBIT_WAIT_TIMEOUT);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GM_TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // X [T, K] f32 -> fp16 with a per-row power-of-two scale s (|x / s| <= 32768):
 // one warp per row.
 __global__ void __launch_bounds__(256) k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh,
@@ -392,29 +593,91 @@ static void launch_prefill_dt(fb_ctx *ctx, const fb_qtensor *w, const CUtensorMa
     FB_CUDA(cudaGetLastError());
 }
 
+// fp16 row-major [rows][K] tensor map, boxes of 64 columns x box_rows rows, 128-byte swizzle.
+static CUtensorMap f16_map(const __half *p, int64_t rows, int64_t K, uint32_t box_rows) {
+    auto encode = tensor_map_encoder();
+    FB_REQUIRE(encode != nullptr, "prefill gemm: cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {PF_BK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(p), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FB_REQUIRE(cr == CUDA_SUCCESS, "prefill gemm: tensor map encoding failed");
+    return map;
+}
+
+// From this many rows on, the weights are dequantized once per prompt chunk
+// (two-pass form) instead of once per 256-row tile.
+constexpr int64_t PF_TWO_PASS_MIN_ROWS = 512;
+// Weight rows dequantized per pass: at most 256 MB of fp16 (a whole Qwen3-8B
+// projection; Llama-3-70B's gate/up in four passes), a multiple of 256.  (32
+// MB passes, which stay in L2, left the Q6_K down projection 80 tiles for
+// 148 SMs: slower.)
+static int64_t two_pass_chunk_rows(int64_t n, int64_t K) {
+    int64_t r = ((int64_t)256 << 20) / (K * 2);
+    r = std::max<int64_t>(256, r / 256 * 256);
+    return std::min(n, r);
+}
+
 // Y[m, n] = X[m, k] . W^T on the tensor cores (prefill_gemm_supported(w, m)).
 void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
     FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
-    auto encode = tensor_map_encoder();
-    FB_REQUIRE(encode != nullptr, "prefill gemm: cuTensorMapEncodeTiled is unavailable");
-    const int64_t K = w->k;
+    const int64_t K = w->k, N = w->n;
+    const bool two_pass = m >= PF_TWO_PASS_MIN_ROWS;
+    const int64_t chunk = two_pass ? two_pass_chunk_rows(N, K) : 0;
     const size_t xh_bytes = ((size_t)m * K * 2 + 255) & ~(size_t)255;
-    uint8_t *scratch = static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + (size_t)m * 4));
+    const size_t rs_bytes = ((size_t)m * 4 + 255) & ~(size_t)255;
+    uint8_t *scratch = static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + rs_bytes + (size_t)chunk * K * 2));
     __half *xh = reinterpret_cast<__half *>(scratch);
     float *rowscale = reinterpret_cast<float *>(scratch + xh_bytes);
     k_x_to_f16<<<(unsigned)((m + 7) / 8), 256, 0, ctx->stream>>>(x, xh, rowscale, (int)m, K);
     FB_CUDA(cudaGetLastError());
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)m};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {PF_BK, PF_BM};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    FB_REQUIRE(cr == CUDA_SUCCESS, "prefill gemm: tensor map encoding failed");
-    if (w->dtype == FB_Q4_K) launch_prefill_dt<4>(ctx, w, map, rowscale, y, (int)m);
-    else launch_prefill_dt<6>(ctx, w, map, rowscale, y, (int)m);
+    if (!two_pass) {
+        const CUtensorMap map = f16_map(xh, m, K, PF_BM);
+        if (w->dtype == FB_Q4_K) launch_prefill_dt<4>(ctx, w, map, rowscale, y, (int)m);
+        else launch_prefill_dt<6>(ctx, w, map, rowscale, y, (int)m);
+        return;
+    }
+    __half *wh = reinterpret_cast<__half *>(scratch + xh_bytes + rs_bytes);
+    const CUtensorMap xmap = f16_map(xh, m, K, GM_BM);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        FB_CUDA(cudaFuncSetAttribute(k_gemm_f16<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GmCfg<128>::SMEM));
+        FB_CUDA(cudaFuncSetAttribute(k_gemm_f16<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GmCfg<256>::SMEM));
+    });
+    const int tiles_m = (int)((m + GM_BM - 1) / GM_BM);
+    for (int64_t r0 = 0; r0 < N; r0 += chunk) {
+        const int64_t rows = std::min(chunk, N - r0);
+        const int64_t nthr = rows * w->nb() * 8;
+        if (w->dtype == FB_Q4_K)
+            k_dequant_rows_f16<4><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(), r0,
+                                                                                          rows, wh);
+        else
+            k_dequant_rows_f16<6><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(), r0,
+                                                                                          rows, wh);
+        FB_CUDA(cudaGetLastError());
+        // 256-column tiles where the rows allow and they still give every SM a tile
+        const bool wide = rows % 256 == 0 && (int64_t)tiles_m * (rows / 256) >= ctx->num_sms;
+        if (wide) {
+            const CUtensorMap wmap = f16_map(wh, rows, K, 256);
+            const int tiles_n = (int)(rows / 256);
+            const int grid = std::min(tiles_m * tiles_n, ctx->num_sms);
+            k_gemm_f16<256><<<grid, GM_THREADS, GmCfg<256>::SMEM, ctx->stream>>>(
+                xmap, wmap, (int)m, N, r0, tiles_m, tiles_n, (int)(K / GM_BK), rowscale, y, ctx->err_word);
+        } else {
+            const CUtensorMap wmap = f16_map(wh, rows, K, 128);
+            const int tiles_n = (int)(rows / 128);
+            const int grid = std::min(tiles_m * tiles_n, ctx->num_sms);
+            k_gemm_f16<128><<<grid, GM_THREADS, GmCfg<128>::SMEM, ctx->stream>>>(
+                xmap, wmap, (int)m, N, r0, tiles_m, tiles_n, (int)(K / GM_BK), rowscale, y, ctx->err_word);
+        }
+        FB_CUDA(cudaGetLastError());
+    }
 }
 
 }  // namespace fb

@@ -53,7 +53,10 @@ def emulate(dtype, w, n, k, x):
 
 @pytest.mark.parametrize("dtype,n,k,m", [(O.Q4_K, 512, 1024, 200), (O.Q4_K, 128, 256, 17),
                                          (O.Q6_K, 256, 2048, 130), (O.Q4_K, 1024, 4096, 333),
-                                         (O.Q6_K, 4096, 12288, 64)])
+                                         (O.Q6_K, 4096, 12288, 64),
+                                         # from 512 rows: weights dequantized once, then the fp16 GEMM
+                                         (O.Q4_K, 1024, 4096, 512), (O.Q6_K, 4096, 12288, 600),
+                                         (O.Q4_K, 6144, 4096, 2048), (O.Q4_K, 8192, 1024, 777)])
 def test_prefill_gemm(fbctx, torch_cuda, dtype, n, k, m):
     w = gaussian_qweight(dtype, n, k, seed=n + 3 * k + dtype)
     x = np.random.default_rng(m + n).normal(0, 1, (m, k)).astype(np.float32)
@@ -78,3 +81,16 @@ def test_prefill_gemm_large_rows(fbctx, torch_cuda):
     rel = np.abs(got - emu) / (np.abs(emu).max(axis=1, keepdims=True) + 1e-30)
     assert rel.max() <= 2e-5, f"max row-relative err {rel.max():.3g}"
     assert np.isfinite(got).all()
+
+
+@pytest.mark.parametrize("dtype,n,k", [(O.Q4_K, 1024, 4096), (O.Q6_K, 512, 12288)])
+def test_two_pass_equals_fused(fbctx, torch_cuda, dtype, n, k):
+    """Below 512 rows the weights are dequantized inside the GEMM (once per
+    256-row tile); from 512 rows they are dequantized once into fp16 and
+    multiplied by the plain fp16 GEMM.  Same fp16 operands, same MMA shape
+    and k order: the rows the two runs share must be bit-identical."""
+    w = gaussian_qweight(dtype, n, k, seed=n + k)
+    x = np.random.default_rng(9).normal(0, 1, (700, k)).astype(np.float32)
+    fused = run(fbctx, torch_cuda, dtype, n, k, w, x[:333])
+    two = run(fbctx, torch_cuda, dtype, n, k, w, x)
+    assert np.array_equal(fused, two[:333])
