@@ -661,8 +661,13 @@ void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, in
             k_dequant_rows_f16<6><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(), r0,
                                                                                           rows, wh);
         FB_CUDA(cudaGetLastError());
-        // 256-column tiles where the rows allow and they still give every SM a tile
-        const bool wide = rows % 256 == 0 && (int64_t)tiles_m * (rows / 256) >= ctx->num_sms;
+        // 256-column tiles (half the L2 re-reads of X per output) or 128-column
+        // ones, whichever needs less time in whole waves of one tile per SM;
+        // a 256-column tile is counted as 1.8 of the narrow ones (measured:
+        // 948 vs ~700 TFLOP/s per tile-time on the Qwen3-8B gate/up shape)
+        const int64_t waves128 = ((int64_t)tiles_m * (rows / 128) + ctx->num_sms - 1) / ctx->num_sms;
+        const int64_t waves256 = ((int64_t)tiles_m * (rows / 256) + ctx->num_sms - 1) / ctx->num_sms;
+        const bool wide = rows % 256 == 0 && 18 * waves256 < 10 * waves128;
         if (wide) {
             const CUtensorMap wmap = f16_map(wh, rows, K, 256);
             const int tiles_n = (int)(rows / 256);
