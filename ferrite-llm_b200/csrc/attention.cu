@@ -243,19 +243,20 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     };
     // copy `piece` (0..3: the K quarters, 4: the V page) of page i of chunk j
     // into stage j % depth
+    const uint64_t kvpol = l2_evict_first_policy();  // the cache is read once per step
     auto issue_piece = [&](int j, int i, int piece) {
         const int page = bt_s[j * PPC + i];
         if (page < 0) return;
         uint8_t *kd = ring + (size_t)(j % depth) * ATT_STAGE;
         const size_t off = ((size_t)page * A.n_kv + kvh) * (size_t)P * ATT_HD;
         if (piece < 4)
-            bulk_g2s(kd + i * KPG + piece * KQS,
-                     reinterpret_cast<const uint8_t *>(reinterpret_cast<const __half *>(A.kpool) + off) +
-                         piece * (pbytes / 4),
-                     pbytes / 4, &full[j % depth]);
+            bulk_g2s_stream(kd + i * KPG + piece * KQS,
+                            reinterpret_cast<const uint8_t *>(reinterpret_cast<const __half *>(A.kpool) + off) +
+                                piece * (pbytes / 4),
+                            pbytes / 4, &full[j % depth], kvpol);
         else
-            bulk_g2s(kd + ATT_STAGE_K + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes,
-                     &full[j % depth]);
+            bulk_g2s_stream(kd + ATT_STAGE_K + i * pbytes, reinterpret_cast<const __half *>(A.vpool) + off, pbytes,
+                            &full[j % depth], kvpol);
     };
     auto arm = [&](int j) {  // the bytes chunk j brings (zero: the phase completes without data)
         uint32_t bytes = 0;

@@ -314,12 +314,13 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     }
     __syncthreads();
     int issued = 0;
+    const uint64_t wpol = l2_evict_first_policy();  // weights are read once per step
     auto issue = [&](int c) {
         const int ti = c / nmine, bl = c - ti * nmine;
         const int64_t T = (int64_t)blockIdx.x + (int64_t)ti * gridDim.x;
         const int slot = c % DEPTH;
         mbar_expect_tx(&wbar[slot], REC);
-        bulk_g2s(ring + (size_t)slot * REC, W + ((size_t)T * nb + bbeg + bl) * REC, REC, &wbar[slot]);
+        bulk_g2s_stream(ring + (size_t)slot * REC, W + ((size_t)T * nb + bbeg + bl) * REC, REC, &wbar[slot], wpol);
     };
     // weights do not depend on the previous kernel: start streaming them now
     if (lane == 0)
