@@ -22,20 +22,20 @@
 //    depth units of one pass over the ring, so a warp meets every stage it
 //    waits on once per pass and never waits a phase ahead).  Per unit the
 //    warp computes the f32 scores (lane = 2 tokens x one 32-dim quarter, the
-//    quarters' slice sums chained in slice order through shuffles), its own
-//    online softmax (running max per head, binary64 exponentials spread over
-//    all lanes) and P.V (lane = 4 dims, binary64).  The last of a chunk's four
-//    units refills its stage;
+//    quarters' slice sums chained in slice order through shuffles), the
+//    unit's softmax partial in f32 (exponentials spread over all lanes, P.V
+//    with lane = 4 dims) and folds it into its binary64 running state.  The
+//    last of a chunk's four units refills its stage;
 //  * the CTA merges its warps' (max, sum, o) partials in shared memory, then
 //    the splits merge either through distributed shared memory in a 16-CTA
 //    cluster (CTA r owns dims [8r, 8r+8) of every head; push, no atomics), or
 //    through global partials and a last-CTA merge (model path, and the
 //    allocation-free entry point); the result is written as f32 and, in the
 //    model path, as the Q8_K rows of the output projection.
-// Dots are f32 in the CPU oracle's fixed order; exponentials, sums and P.V
-// run in binary64 with one rounding to f32 at the end, so the result equals
-// the CPU oracle's single-pass softmax bit for bit whatever the split and
-// warp layout.  All mbarrier waits are bounded: on timeout the kernel raises
+// Dots and the 16-token unit partials are f32 in the CPU oracle's fixed
+// order; everything above the units runs in binary64 with one rounding to
+// f32 at the end, so the result equals the CPU oracle's bit for bit whatever
+// the split and warp layout.  All mbarrier waits are bounded: on timeout the kernel raises
 // ERRBIT_WAIT_TIMEOUT in the context's error word.
 #include <math.h>
 
@@ -46,6 +46,7 @@
 
 #include "fb_internal.h"
 #include "kq_common.cuh"
+#include "attn_unit.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -93,7 +94,7 @@ __host__ __device__ inline AttnLayout attn_layout(int G, int NW, int depth, int 
     L.ss = off;  // per warp: scores [unit token][G] f32
     off += (size_t)NW * ATT_UNIT * G * 4;
     off = (off + 15) & ~(size_t)15;
-    L.pb = off;  // per warp: p [unit token][G] f64; CTA partial o [G][hd] f64 at the end
+    L.pb = off;  // per warp: p [unit token][G] f32 (room for f64); CTA partial o [G][hd] f64 at the end
     off += (size_t)NW * ATT_UNIT * G * 8;
     L.misc = off;  // M[G] L[G] tmp[G] mw[NW][G] lw[NW][G] wt[NW][G] wts[G][S] wl[G][S] f64
     off += (size_t)(3 * G + 3 * NW * G + 2 * G * ATT_SPLITS_MAX) * 8;
@@ -142,12 +143,18 @@ __device__ __forceinline__ void lds_f32(float (&v)[G], const float *p) {
 // Numerics (identical to the CPU oracle, or_attn_dot / or_exp64):
 //   s_t = f32 dot of q and k_t in eight 16-dim fused-multiply-add slices,
 //         summed in slice order, times scale
-//   per warp: running max m, p_t = exp64(s_t - m), l = sum p_t,
-//             o = sum p_t v_t, rescaled by exp64(m_old - m_new)  (binary64)
+//   per 16-token unit u (positions 16u .. 16u + 15; f32, fixed order):
+//             m_u = max s_t, p_t = f32(exp64(s_t - m_u)), l_u = pairwise
+//             sum of the 16 slots (absent tokens 0), o_u = FMA chain of
+//             p_t v_t in token order
+//   per warp (binary64): the units' (m_u, l_u, o_u) folded into a running
+//             (m, l, o), the side with the smaller max weighted by exp64 of
+//             the difference
 //   merges (warps of a CTA, then splits): M = max m, w = exp64(m - M),
 //             out = f32(sum w*o / sum w*l)
-// The binary64 stages make the result independent of how the tokens are
-// split (up to binary64 rounding, far below the final f32 rounding).
+// The unit partials do not depend on how the units are spread over warps and
+// CTAs, and the binary64 stages above them make the result independent of it
+// too (up to binary64 rounding, far below the final f32 rounding).
 template <int G, bool CLUSTER>
 __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq, int use_q8, int *__restrict__ counters,
@@ -328,18 +335,17 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
 
     // ---- main loop: this warp's units
     float *ssw = reinterpret_cast<float *>(smem + Ly.ss) + warp * ATT_UNIT * G;
-    double *pbw = reinterpret_cast<double *>(smem + Ly.pb) + warp * ATT_UNIT * G;
+    float *pbw = reinterpret_cast<float *>(smem + Ly.pb) + warp * ATT_UNIT * G;
     const int ti = lane & 7, qq4 = lane >> 3;  // score phase: token pair, 32-dim quarter
     float m_run[G];
-    double o[G][4], lp[GH];
+    double o[G][4], Lw[G];  // the warp's binary64 state (Lw, m_run warp-uniform; o: this lane's dims)
 #pragma unroll
     for (int g = 0; g < G; g++) {
         m_run[g] = -INFINITY;
+        Lw[g] = 0.0;
 #pragma unroll
         for (int e = 0; e < 4; e++) o[g][e] = 0.0;
     }
-#pragma unroll
-    for (int k = 0; k < GH; k++) lp[k] = 0.0;
     bool ok = true;
     for (int u = warp; u < 4 * mine; u += NW) {
         const int j = u >> 2, qu = u & 3, st = j % depth;
@@ -422,64 +428,9 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
                 mx[g] = __shfl_sync(FULL, mx[g], 24);
             }
             __syncwarp();
-            // online softmax of this warp: the rescale factor only when the running max moves
-            double al[G];
-#pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float mn = fmaxf(m_run[g], mx[g]);  // finite: the unit holds a token
-                al[g] = 1.0;
-                if (mn != m_run[g]) {  // warp-uniform
-                    al[g] = m_run[g] == -INFINITY ? 0.0 : exp64(__dsub_rn((double)m_run[g], (double)mn));
-                    m_run[g] = mn;
-                }
-            }
-            // p = exp64(s - m): lane (t = lane & 15) takes heads of parity lane >> 4
-            {
-                const int t = lane & 15, hp = lane >> 4;
-#pragma unroll
-                for (int k = 0; k < GH; k++) {
-                    if (G >= 2 || hp == 0) {
-                        const int g = G >= 2 ? 2 * k + hp : 0;
-                        const float mg = G >= 2 ? (hp ? m_run[G >= 2 ? 2 * k + 1 : 0] : m_run[2 * k]) : m_run[0];
-                        const double ag = G >= 2 ? (hp ? al[G >= 2 ? 2 * k + 1 : 0] : al[2 * k]) : al[0];
-                        const double p = t < nt ? exp64(__dsub_rn((double)ssw[t * G + g], (double)mg)) : 0.0;
-                        pbw[t * G + g] = p;
-                        lp[k] = __dadd_rn(__dmul_rn(lp[k], ag), p);
-                    }
-                }
-            }
-            __syncwarp();
-            // ---- o = al * o + sum_t p_t v_t; lane owns dims [4 lane, 4 lane + 4)
-#pragma unroll
-            for (int g = 0; g < G; g++)
-                if (al[g] != 1.0)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) o[g][e] = __dmul_rn(o[g][e], al[g]);
-            const __half *vrow = Vs + (size_t)(ATT_UNIT * qu) * ATT_HD + 4 * lane;
-#pragma unroll 4
-            for (int t = 0; t < nt; t++) {
-                const uint2 vr = *reinterpret_cast<const uint2 *>(vrow + (size_t)t * ATT_HD);
-                double vd[4];  // fp16 -> binary64 directly (exact), one conversion per value
-                asm("{\n .reg .b16 h0, h1, h2, h3;\n mov.b32 {h0, h1}, %4;\n mov.b32 {h2, h3}, %5;\n"
-                    " cvt.f64.f16 %0, h0;\n cvt.f64.f16 %1, h1;\n cvt.f64.f16 %2, h2;\n cvt.f64.f16 %3, h3;\n}"
-                    : "=d"(vd[0]), "=d"(vd[1]), "=d"(vd[2]), "=d"(vd[3])
-                    : "r"(vr.x), "r"(vr.y));
-                double pg[G];
-                if constexpr (G >= 2) {
-#pragma unroll
-                    for (int g = 0; g < G; g += 2) {
-                        const double2 x = *reinterpret_cast<const double2 *>(pbw + t * G + g);
-                        pg[g] = x.x;
-                        pg[g + 1] = x.y;
-                    }
-                } else {
-                    pg[0] = pbw[t];
-                }
-#pragma unroll
-                for (int g = 0; g < G; g++)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) o[g][e] = __fma_rn(pg[g], vd[e], o[g][e]);
-            }
+            // ---- the unit's softmax partial in f32, folded into the warp's
+            // binary64 state (attn_unit.cuh)
+            att_unit_fold<G>(ssw, pbw, Vs + (size_t)(ATT_UNIT * qu) * ATT_HD + 4 * lane, nt, mx, lane, m_run, Lw, o);
         }
         // this warp is done with the unit's slice of stage st; the fourth unit
         // of the chunk refills the stage with chunk j + depth
@@ -515,17 +466,8 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
 #pragma unroll
         for (int e = 0; e < 4; e++) red[(warp * G + g) * ATT_HD + 4 * lane + e] = o[g][e];
 #pragma unroll
-    for (int k = 0; k < GH; k++) {
-        double v = lp[k];
-        if constexpr (G >= 2) {
-#pragma unroll
-            for (int off = 1; off < 16; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(FULL, v, off));
-            if ((lane & 15) == 0) lw[warp * G + 2 * k + (lane >> 4)] = v;
-        } else {
-            v = warp_sum64(v);
-            if (lane == 0) lw[warp * G] = v;
-        }
-    }
+    for (int g = 0; g < G; g++)
+        if (lane == 0) lw[warp * G + g] = Lw[g];
 #pragma unroll
     for (int g = 0; g < G; g++)
         if (lane == g) mw[warp * G + g] = (double)m_run[g];

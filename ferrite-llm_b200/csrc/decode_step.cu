@@ -44,6 +44,7 @@
 #include "fb_internal.h"
 #include "gemv_dp4a.cuh"
 #include "kq_common.cuh"
+#include "attn_unit.cuh"
 #include "q8k_store.cuh"
 #include "decode_step.h"
 
@@ -449,17 +450,17 @@ template <int G>
 struct AttRegs {
     static constexpr int GH = G >= 2 ? G / 2 : 1;
     float m_run[G];
-    double o[G][4], lp[GH];
+    double o[G][4], Lw[G];
 };
 
 // One 16-token unit of a staged 64-token chunk (the unit loop body of
 // k_attn_decode: f32 scores in eight 16-dim FMA slices summed in slice
-// order, per-warp binary64 online softmax, binary64 P.V; lane = 4 dims).
+// order, then the unit's f32 softmax partial folded into the warp's binary64
+// state, attn_unit.cuh; lane = 4 dims).
 template <int G>
 __device__ __forceinline__ void ds_att_unit(const uint8_t *kst, const __half *Vs, int qu, int nt, const float *q_s,
-                                            float *ssw, double *pbw, float scale, int lane, AttRegs<G> &R) {
+                                            float *ssw, float *pbw, float scale, int lane, AttRegs<G> &R) {
     constexpr unsigned FULL = 0xffffffffu;
-    constexpr int GH = AttRegs<G>::GH;
     const int ti = lane & 7, qq4 = lane >> 3;
     float acc[2][2][G];
 #pragma unroll
@@ -518,53 +519,7 @@ __device__ __forceinline__ void ds_att_unit(const uint8_t *kst, const __half *Vs
         mx[g] = __shfl_sync(FULL, mx[g], 24);
     }
     __syncwarp();
-    double al[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float mn = fmaxf(R.m_run[g], mx[g]);
-        al[g] = 1.0;
-        if (mn != R.m_run[g]) {
-            al[g] = R.m_run[g] == -INFINITY ? 0.0 : exp64(__dsub_rn((double)R.m_run[g], (double)mn));
-            R.m_run[g] = mn;
-        }
-    }
-    {
-        const int t = lane & 15, hp = lane >> 4;
-#pragma unroll
-        for (int k = 0; k < GH; k++) {
-            if (G >= 2 || hp == 0) {
-                const int g = G >= 2 ? 2 * k + hp : 0;
-                const float mg = G >= 2 ? (hp ? R.m_run[G >= 2 ? 2 * k + 1 : 0] : R.m_run[2 * k]) : R.m_run[0];
-                const double ag = G >= 2 ? (hp ? al[G >= 2 ? 2 * k + 1 : 0] : al[2 * k]) : al[0];
-                const double p = t < nt ? exp64(__dsub_rn((double)ssw[t * G + g], (double)mg)) : 0.0;
-                pbw[t * G + g] = p;
-                R.lp[k] = __dadd_rn(__dmul_rn(R.lp[k], ag), p);
-            }
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int g = 0; g < G; g++)
-        if (al[g] != 1.0)
-#pragma unroll
-            for (int e = 0; e < 4; e++) R.o[g][e] = __dmul_rn(R.o[g][e], al[g]);
-    const __half *vrow = Vs + (size_t)(DS_UNIT * qu) * DS_HD + 4 * lane;
-#pragma unroll 4
-    for (int t = 0; t < nt; t++) {
-        const uint2 vr = *reinterpret_cast<const uint2 *>(vrow + (size_t)t * DS_HD);
-        double vd[4];
-        asm("{\n .reg .b16 h0, h1, h2, h3;\n mov.b32 {h0, h1}, %4;\n mov.b32 {h2, h3}, %5;\n"
-            " cvt.f64.f16 %0, h0;\n cvt.f64.f16 %1, h1;\n cvt.f64.f16 %2, h2;\n cvt.f64.f16 %3, h3;\n}"
-            : "=d"(vd[0]), "=d"(vd[1]), "=d"(vd[2]), "=d"(vd[3])
-            : "r"(vr.x), "r"(vr.y));
-        double pg[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) pg[g] = pbw[t * G + g];
-#pragma unroll
-        for (int g = 0; g < G; g++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) R.o[g][e] = __fma_rn(pg[g], vd[e], R.o[g][e]);
-    }
+    att_unit_fold<G>(ssw, pbw, Vs + (size_t)(DS_UNIT * qu) * DS_HD + 4 * lane, nt, mx, lane, R.m_run, R.Lw, R.o);
     __syncwarp();
 }
 
@@ -837,7 +792,6 @@ struct Ds {
 
 template <int G>
 __device__ void Ds<G>::attention(int l, const AttItem &it, const int *bt, const QkHead &pre) {
-    constexpr int GH = AttRegs<G>::GH;
     const DsAttLayout AL = ds_att_layout(G);
     uint8_t *u = smem + L.uni;
     float *q_s = reinterpret_cast<float *>(u + AL.q);
@@ -853,7 +807,7 @@ __device__ void Ds<G>::attention(int l, const AttItem &it, const int *bt, const 
         for (int e = 0; e < 4; e++) R.o[g][e] = 0.0;
     }
 #pragma unroll
-    for (int k = 0; k < GH; k++) R.lp[k] = 0.0;
+    for (int g = 0; g < G; g++) R.Lw[g] = 0.0;
     if (active && it.len > 0) {
         // prologue: q heads (every split), k / v of the new token (owner split)
         const bool owner = it.jf >= 0 && it.jf < it.mine;
@@ -896,7 +850,7 @@ __device__ void Ds<G>::attention(int l, const AttItem &it, const int *bt, const 
     cons_sync();  // q and the new k / v staged
     // ---- chunks: warps 0..3 take units 0..3 of even chunks, warps 4..7 of odd ones
     float *ssw = reinterpret_cast<float *>(u + AL.ss) + warp * DS_UNIT * G;
-    double *pbw = reinterpret_cast<double *>(u + AL.pb) + warp * DS_UNIT * G;
+    float *pbw = reinterpret_cast<float *>(u + AL.pb) + warp * DS_UNIT * G;
     for (int j = 0; j < (active ? it.mine : 0); j++) {
         const uint8_t *kst = wait_stage();
         if (ok && (j & 1) == (warp >> 2)) {
@@ -927,17 +881,8 @@ __device__ void Ds<G>::attention(int l, const AttItem &it, const int *bt, const 
     double *tree = reinterpret_cast<double *>(u + AL.tree);
     double *mmax = reinterpret_cast<double *>(u + AL.mmax);
 #pragma unroll
-    for (int k = 0; k < GH; k++) {
-        double v = R.lp[k];
-        if constexpr (G >= 2) {
-#pragma unroll
-            for (int off = 1; off < 16; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-            if ((lane & 15) == 0) lw[warp * G + 2 * k + (lane >> 4)] = v;
-        } else {
-            v = warp_sum64(v);
-            if (lane == 0) lw[warp * G] = v;
-        }
-    }
+    for (int g = 0; g < G; g++)
+        if (lane == 0) lw[warp * G + g] = R.Lw[g];
 #pragma unroll
     for (int g = 0; g < G; g++)
         if (lane == g) mw[warp * G + g] = (double)R.m_run[g];

@@ -31,8 +31,8 @@ namespace fb {
 // KB in L2) and then normalizes and quantizes only its own block, so the row
 // is processed by dim/256 CTAs in parallel.  x[row] (+= add[row] when add !=
 // null) is written to x_out block by block (a different buffer: other CTAs
-// are still reading x); emb_tab != null takes the dequantized embedding row
-// of token[row] instead of x.
+// are still reading x); the EMB instantiation takes the dequantized
+// embedding row of token[row] (emb_tab) instead of x.
 constexpr int NORM_THREADS = 256;
 
 __device__ __forceinline__ float q4k_value(const uint8_t *blk, int i) {
@@ -48,6 +48,10 @@ __device__ __forceinline__ float q4k_value(const uint8_t *blk, int i) {
     return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)nib), __fmul_rn(dmin, (float)mn));
 }
 
+// EMB: the first norm of the step, which dequantizes the token's embedding
+// row instead of reading a residual (a separate instantiation keeps the
+// per-layer kernel's code small).
+template <bool EMB>
 __global__ void __launch_bounds__(NORM_THREADS)
     k_residual_rmsnorm_q8k(const float *__restrict__ x, const float *__restrict__ add, float *__restrict__ x_out,
                            const float *__restrict__ g, int dim, float eps, Q8Act a,
@@ -69,7 +73,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const float *xr = x ? x + row * dim : nullptr;
     const int nv = dim / 4;
     float4 v[MAXP];
-    if (!emb_tab) {
+    if constexpr (!EMB) {
         const float4 *x4 = reinterpret_cast<const float4 *>(xr);
 #pragma unroll
         for (int p = 0; p < MAXP; p++) {
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
     if (epoch_inc && blk == 0 && row == 0 && threadIdx.x == 0) *epoch_inc += 1u;
     const int nbe = dim / QK;
     int tok = 0;
-    if (emb_tab) {
+    if constexpr (EMB) {
         tok = tokens[row];
         if (tok < 0 || tok >= vocab) {
             if (threadIdx.x == 0 && blk == 0) atomicOr(err, ERRBIT_BAD_TOKEN);
@@ -92,7 +96,7 @@ __global__ void __launch_bounds__(NORM_THREADS)
         }
     }
     double ss = 0.0;
-    if (emb_tab) {
+    if constexpr (EMB) {
         for (int i = threadIdx.x; i < dim; i += NORM_THREADS) {
             const float e = q4k_value(emb_tab + q4k_offset(tok, i / QK, nbe), i % QK);
             ss = __fma_rn((double)e, (double)e, ss);
@@ -530,8 +534,12 @@ void launch_residual_rmsnorm_q8k(fb_ctx *ctx, const float *x, const float *add, 
         tab = emb->main();
     }
     FB_REQUIRE(x_out != x, "rmsnorm_q8k: x_out must not alias x");
-    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g, dim, eps, a,
-             tab, tokens, vocab, ctx->err_word, (uint32_t *)nullptr);
+    if (tab)
+        launch_k(ctx, k_residual_rmsnorm_q8k<true>, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g, dim,
+                 eps, a, tab, tokens, vocab, ctx->err_word, (uint32_t *)nullptr);
+    else
+        launch_k(ctx, k_residual_rmsnorm_q8k<false>, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, x, add, x_out, g,
+                 dim, eps, a, tab, tokens, vocab, ctx->err_word, (uint32_t *)nullptr);
 }
 
 void launch_embed_rmsnorm_q8k(fb_ctx *ctx, float *x_out, const float *g, int rows, int dim, float eps,
@@ -539,7 +547,7 @@ void launch_embed_rmsnorm_q8k(fb_ctx *ctx, float *x_out, const float *g, int row
                               uint32_t *epoch_inc) {
     FB_REQUIRE(dim % QK == 0, "rmsnorm_q8k: dim must be a multiple of 256");
     FB_REQUIRE(emb && emb->dtype == FB_Q4_K && emb->k == dim, "embedding table must be Q4_K [vocab, hidden]");
-    launch_k(ctx, k_residual_rmsnorm_q8k, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, (const float *)nullptr,
+    launch_k(ctx, k_residual_rmsnorm_q8k<true>, dim3(dim / QK, rows), dim3(NORM_THREADS), 0, (const float *)nullptr,
              (const float *)nullptr, x_out, g, dim, eps, a, emb->main(), tokens, vocab, ctx->err_word, epoch_inc);
 }
 

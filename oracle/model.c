@@ -360,12 +360,13 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
         for (int i = 0; i < n; i++)
             for (int hq = 0; hq < nq; hq++) {
                 /* softmax(q.k^T * scale) . v; the score dots in f32 in the
-                 * fixed order of or_attn_dot, exponentials and sums in
-                 * binary64 with one rounding to f32 at the end */
+                 * fixed order of or_attn_dot, 16-position unit partials in
+                 * f32, their combination in binary64 with one rounding to f32
+                 * at the end */
                 int T = pos + i + 1, hk = hq / grp;
                 const float *qh = q + (size_t)i * qd + (size_t)hq * hd;
                 float *sc = (float *)malloc(sizeof(float) * (size_t)T);
-                double *pr = (double *)malloc(sizeof(double) * (size_t)T);
+                double *pr = (double *)malloc(sizeof(double) * (size_t)(T > hd ? T : hd));
                 double *acc = (double *)calloc((size_t)hd, sizeof(double));
                 float mx = -INFINITY;
                 for (int s = 0; s < T; s++) {
@@ -396,14 +397,30 @@ int or_model_forward(or_model *m, const int32_t *tokens, int n, int pos,
                     free(acc);
                     continue;
                 }
+                /* Positions in units of 16 (16u .. 16u + 15), as the device
+                 * kernel splits them: per unit, in f32 and a fixed order, its
+                 * max m_u, p_t = f32(exp64(s_t - m_u)), l_u = the pairwise
+                 * sum of the 16 slots (absent positions 0) and o_u = the FMA
+                 * chain of p_t v_t in position order; the units then combine
+                 * in binary64 with weights exp64(m_u - max). */
                 double l = 0.0;
-                for (int s = 0; s < T; s++) {
-                    pr[s] = or_exp64((double)sc[s] - (double)mx);
-                    l += pr[s];
-                }
-                for (int s = 0; s < T; s++) {
-                    const float *vs = vl + (size_t)s * kd + (size_t)hk * hd;
-                    for (int e = 0; e < hd; e++) acc[e] += pr[s] * (double)vs[e];
+                float *ou = (float *)pr; /* hd floats */
+                for (int u0 = 0; u0 < T; u0 += 16) {
+                    const int nu = T - u0 < 16 ? T - u0 : 16;
+                    float mu = -INFINITY, pu[16], tr[16];
+                    for (int t = 0; t < nu; t++) mu = sc[u0 + t] > mu ? sc[u0 + t] : mu;
+                    for (int t = 0; t < 16; t++)
+                        pu[t] = tr[t] = t < nu ? (float)or_exp64((double)sc[u0 + t] - (double)mu) : 0.f;
+                    for (int w = 1; w < 16; w *= 2)
+                        for (int t = 0; t < 16; t += 2 * w) tr[t] = tr[t] + tr[t + w];
+                    for (int e = 0; e < hd; e++) ou[e] = 0.f;
+                    for (int t = 0; t < nu; t++) {
+                        const float *vs = vl + (size_t)(u0 + t) * kd + (size_t)hk * hd;
+                        for (int e = 0; e < hd; e++) ou[e] = fmaf(pu[t], vs[e], ou[e]);
+                    }
+                    const double w = or_exp64((double)mu - (double)mx);
+                    l += w * (double)tr[0];
+                    for (int e = 0; e < hd; e++) acc[e] += w * (double)ou[e];
                 }
                 float *oh = o + (size_t)i * qd + (size_t)hq * hd;
                 for (int e = 0; e < hd; e++) oh[e] = (float)(acc[e] / l);
