@@ -34,6 +34,7 @@
 
 #include "fb_internal.h"
 #include "kq_common.cuh"
+#include "tc_common.cuh"
 
 namespace fb {
 
@@ -57,17 +58,6 @@ constexpr size_t pf_smem_bytes() {
 }
 
 // ---- tcgen05 / TMA helpers -------------------------------------------------
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-    // K-major, 128-byte swizzle: 8-row groups 1024 bytes apart (SBO = 64 x 16 B),
-    // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B)
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)64 << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
 // kind::f16 instruction descriptor: A = B = fp16, D = f32, both K-major,
 // M = 128, N = 128
 constexpr uint32_t PF_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(PF_BN >> 3) << 17) |
@@ -79,30 +69,6 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t 
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
         "l"(da), "l"(db), "r"(PF_IDESC), "r"(accumulate)
         : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Packed fp16 dequantization (two weights per instruction).  A weight's
@@ -383,14 +349,6 @@ template <int BN> struct GmCfg {
 };
 static_assert(GmCfg<128>::SMEM <= 227 * 1024 && GmCfg<256>::SMEM <= 227 * 1024, "gemm stages must fit");
 
-__device__ __forceinline__ void umma_f16_desc(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                              uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
 
 // Y[t, n_base + n] = rowscale[t] * sum_k Xh[t, k] Wh[n, k] for the chunk's
 // rows n < BN * tiles_n.  Persistent: CTA b takes tiles b, b + grid, ...
@@ -564,18 +522,6 @@ __global__ void __launch_bounds__(256) k_x_to_f16(const float *__restrict__ x, _
     }
 }
 
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static std::once_flag once;
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
 
 bool prefill_gemm_supported(const fb_qtensor *w, int64_t m) {
     return (w->dtype == FB_Q4_K || w->dtype == FB_Q6_K) && m >= 17 && w->n % PF_BN == 0 && w->k % QK == 0 &&

@@ -7,252 +7,351 @@
 // concatenated KV cache; called from crates/ferrite-wasm-host/src/
 // adapter.rs:61-70 with all prompt tokens at once) -- the reference itself
 // feeds the prompt token by token (crates/ferrite-core/src/chat_session.rs:
-// 417-424), which this path replaces.
+// 417-424), which this path replaces.  The reference's own flash-attention
+// kernel (crates/ferrite-core/kernels/flash_attention.cu:166-225) is an f32
+// stub that is never launched.
 //
-// Design (tensor cores through mma.sync.m16n8k16, f32 accumulation):
-//  * one CTA of 4 warps per (64-query block, query head); warp w owns
-//    queries 16w .. 16w + 15 of the block;
-//  * key blocks of 64 = one KV page: its K (dim-major, 16 KB) and V
-//    (token-major, 16 KB) stream into padded shared memory with cp.async
-//    (double-buffered: block kb + 1 loads while kb is processed) and reach
-//    the MMAs through ldmatrix.trans (both operands are K-major that way);
-//  * precision: q and the softmax probabilities are split into fp16 hi + lo
-//    parts (two MMAs each), so S = q.k and O = P.V carry ~22 bits of the
-//    f32 operands; K and V are fp16 in the cache already (exact);
-//  * online softmax per query row in f32 (running max, rescale by
-//    exp(m_old - m_new)), causal mask on key > query position.
+// B200 design (5th-generation tensor cores; tensor-bound at long prompts):
+//  * one CTA per (128 queries, query head); 6 warps: warps 0..3 run the
+//    softmax (thread = query row = TMEM lane), warp 4 issues the TMA copies,
+//    warp 5 allocates tensor memory and issues tcgen05.mma from one thread;
+//  * key blocks of 64 = one KV page.  The dim-major K page [128 dims][64
+//    keys] and the token-major V page [64 keys][128 dims] are copied by TMA
+//    with 128-byte swizzle straight into the MN-major layouts of the B
+//    operands (no transposes); two stages;
+//  * S = Q K^T (M = 128, N = 64, K = 128) into one of two TMEM buffers, so
+//    the MMA of block j + 1 overlaps the softmax of block j; O += P V (M =
+//    128, N = 128, K = 64) accumulates in TMEM for the whole key range;
+//  * precision: q and the probabilities enter the MMAs as fp16 hi + lo
+//    parts (two MMAs each, ~22 bits of the f32 operands); K and V are fp16 in
+//    the cache already; products accumulate in f32;
+//  * softmax in log2 units with a lazy reference max: O and the row sum are
+//    rescaled (tcgen05.ld / st) only when a row's max grows by more than 8,
+//    so p stays below 256 and most blocks never touch the accumulator;
+//  * every mbarrier wait is bounded; a timeout raises ERRBIT_WAIT_TIMEOUT and
+//    the roles stop.
 #include <math.h>
 
 #include "fb_internal.h"
 #include "kq_common.cuh"
+#include "tc_common.cuh"
 
 namespace fb {
 
-constexpr int PA_Q = 64;                 // queries per CTA
-constexpr int PA_KB = 64;                // keys per block (one page)
-constexpr int PA_HD = 128;
-constexpr int PA_KP = PA_KB * 2 + 16;    // K smem row pitch (dims are rows): 144 B
-constexpr int PA_VP = PA_HD * 2 + 16;    // V smem row pitch (keys are rows): 272 B
-constexpr int PA_K_BYTES = PA_HD * PA_KP;  // 18432
-constexpr int PA_V_BYTES = PA_KB * PA_VP;  // 17408
-constexpr int PA_STAGE = PA_K_BYTES + PA_V_BYTES;
-constexpr int PA_SMEM = 2 * PA_STAGE;  // 71680
+constexpr int TA_Q = 128;        // queries per CTA (MMA M)
+constexpr int TA_KB = 64;        // keys per block (one page)
+constexpr int TA_HD = 128;
+constexpr int TA_ST = 2;         // K/V stages
+constexpr int TA_THREADS = 192;  // warps 0..3 softmax, 4 TMA, 5 MMA
+constexpr uint32_t TA_Q_BYTES = TA_Q * TA_HD * 2;   // two 64-dim slabs of [128 rows][128 B], K-major
+constexpr uint32_t TA_K_BYTES = TA_HD * TA_KB * 2;  // [128 dims][64 keys]: MN-major B of S
+constexpr uint32_t TA_V_BYTES = TA_KB * TA_HD * 2;  // two [64 keys][64 dims] halves: MN-major B of O
+constexpr uint32_t TA_P_BYTES = TA_Q * TA_KB * 2;   // [128 rows][64 keys], K-major A of O
+constexpr size_t TA_SMEM = 1024 + 2 * (size_t)TA_Q_BYTES + TA_ST * ((size_t)TA_K_BYTES + TA_V_BYTES) +
+                           4 * (size_t)TA_P_BYTES;
+constexpr uint32_t TA_TMEM_COLS = 256;  // S buffers at columns 0 and 64, O at 128
+constexpr uint32_t TA_O_COL = 128;
+constexpr uint32_t TA_IDESC_S = umma_idesc_f16(TA_Q, TA_KB, false, true);
+constexpr uint32_t TA_IDESC_O = umma_idesc_f16(TA_Q, TA_HD, false, true);
+static_assert(TA_SMEM <= 227 * 1024, "prefill attention stages must fit");
 
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// (hi, lo) fp16 pair of two f32 values: hi = fp16(x), lo = fp16(x - hi)
-__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
-    hi = *reinterpret_cast<const uint32_t *>(&h);
-    lo = *reinterpret_cast<const uint32_t *>(&l);
+// Byte offset of 16-byte chunk c of row r in a K-major, 128-byte-swizzled
+// [rows][128 B] slab (8-row atoms of 1024 bytes, the TMA SWIZZLE_128B pattern).
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// grid (ceil(T / 64), n_heads), 128 threads.
-__global__ void __launch_bounds__(128) k_attn_prefill(const float *__restrict__ q, const __half *__restrict__ kpool,
-                                                      const __half *__restrict__ vpool,
-                                                      const int32_t *__restrict__ bt, int max_pages, int num_pages,
-                                                      int pos0, int T, int n_heads, int n_kv, float scale,
-                                                      float *__restrict__ out, uint32_t *err) {
-    extern __shared__ __align__(128) uint8_t smem[];
+// Eight f32 as fp16 hi parts and fp16 lo parts (x - hi).
+__device__ __forceinline__ void split8(const float (&x)[8], uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const __half2 a = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        const float2 af = __half22float2(a);
+        const __half2 b = __floats2half2_rn(__fsub_rn(x[2 * i], af.x), __fsub_rn(x[2 * i + 1], af.y));
+        h[i] = *reinterpret_cast<const uint32_t *>(&a);
+        l[i] = *reinterpret_cast<const uint32_t *>(&b);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// grid (ceil(T / 128), n_heads), TA_THREADS threads, TA_SMEM dynamic shared memory.
+// kmap: the K pool as rows of 64 keys ([num_pages * n_kv * 128] x 64 fp16),
+// vmap: the V pool as rows of 128 dims ([num_pages * n_kv * 64] x 128 fp16).
+__global__ void __launch_bounds__(TA_THREADS, 1)
+    k_attn_prefill_tc(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                      const float *__restrict__ q, const int32_t *__restrict__ bt, int max_pages, int num_pages,
+                      int pos0, int T, int n_heads, int n_kv, float scale, float *__restrict__ out, uint32_t *err) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t kv_full[TA_ST], kv_empty[TA_ST], s_full[2], s_free[2], p_full[2], p_free[2], o_done, fin;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort_raw;
+    volatile int &s_abort = s_abort_raw;
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sQh = sm, *sQl = sm + TA_Q_BYTES;
+    uint8_t *sK = sQl + TA_Q_BYTES;         // [stage] K page
+    uint8_t *sV = sK + TA_ST * TA_K_BYTES;  // [stage] V page (dims 0..63, then 64..127)
+    uint8_t *sP = sV + TA_ST * TA_V_BYTES;  // [buffer][hi, lo] probabilities
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, c = lane & 3;
-    const int q0 = blockIdx.x * PA_Q, h = blockIdx.y, kvh = h / (n_heads / n_kv);
-    const int qlast = min(T, q0 + PA_Q) - 1;  // last query of the CTA
-    const int nkb = (pos0 + qlast) / PA_KB + 1;
-
-    // q fragments of this warp's 16 queries (A operand, row-major 16 x 128),
-    // hi and lo parts; rows past T read zeros
-    uint32_t qa[8][4], qb[8][4];
-    {
-        const int r0 = q0 + 16 * warp + g, r1 = r0 + 8;
-        const float *p0 = q + ((int64_t)min(r0, T - 1) * n_heads + h) * PA_HD;
-        const float *p1 = q + ((int64_t)min(r1, T - 1) * n_heads + h) * PA_HD;
-        const bool v0 = r0 < T, v1 = r1 < T;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-#pragma unroll
-            for (int half = 0; half < 2; half++) {  // columns 2c (+8 for half 1)
-                const int col = 16 * kk + 2 * c + 8 * half;
-                const float2 a = v0 ? *reinterpret_cast<const float2 *>(p0 + col) : make_float2(0.f, 0.f);
-                const float2 b = v1 ? *reinterpret_cast<const float2 *>(p1 + col) : make_float2(0.f, 0.f);
-                split_h2(a.x, a.y, qa[kk][2 * half], qb[kk][2 * half]);
-                split_h2(b.x, b.y, qa[kk][2 * half + 1], qb[kk][2 * half + 1]);
-            }
+    const int q0 = blockIdx.x * TA_Q, h = blockIdx.y, kvh = h / (n_heads / n_kv);
+    const int qlast = min(T, q0 + TA_Q) - 1;
+    const int nkb = (pos0 + qlast) / TA_KB + 1;  // key blocks up to the CTA's last query
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < TA_ST; i++) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
         }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&p_free[i], 1);
+        }
+        mbar_init(&o_done, 1);
+        mbar_init(&fin, 1);
+        mbar_fence_init();
+        s_abort = 0;
     }
-    const int qpos0 = pos0 + q0 + 16 * warp + g, qpos1 = qpos0 + 8;  // positions of this thread's two rows
-
-    // stage loader: K page-head [128 dims][64 keys] and V page-head [64 keys][128 dims]
-    const uint32_t sbase = smem_u32(smem);
-    auto load = [&](int kb, int st) {
-        int page = kb < max_pages ? bt[kb] : -1;
-        if (page < 0 || page >= num_pages) {
-            if (threadIdx.x == 0) atomicOr(err, ERRBIT_BAD_PAGE);
-            page = 0;
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(TA_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (warp < 4) {
+        // q rows as fp16 hi / lo A operands (rows past T repeat the last
+        // query; their results are not stored)
+        const int r = threadIdx.x;
+        const float *qr = q + ((int64_t)min(q0 + r, T - 1) * n_heads + h) * TA_HD;
+#pragma unroll 4
+        for (int c = 0; c < 16; c++) {
+            const float4 a = *reinterpret_cast<const float4 *>(qr + 8 * c);
+            const float4 b = *reinterpret_cast<const float4 *>(qr + 8 * c + 4);
+            const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint4 hi, lo;
+            split8(x, hi, lo);
+            const uint32_t off = (uint32_t)(c >> 3) * (TA_Q * 128) + sw128_off(r, c & 7);
+            *reinterpret_cast<uint4 *>(sQh + off) = hi;
+            *reinterpret_cast<uint4 *>(sQl + off) = lo;
         }
-        const size_t off = ((size_t)page * n_kv + kvh) * (size_t)(PA_HD * PA_KB);
-        const uint8_t *ks = reinterpret_cast<const uint8_t *>(kpool + off);
-        const uint8_t *vs = reinterpret_cast<const uint8_t *>(vpool + off);
-        const uint32_t kd = sbase + st * PA_STAGE, vd = kd + PA_K_BYTES;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int ch = threadIdx.x + 128 * i;  // 1024 chunks of 16 bytes each
-            cp_async16(kd + (ch >> 3) * PA_KP + (ch & 7) * 16, ks + ch * 16);
-            cp_async16(vd + (ch >> 4) * PA_VP + (ch & 15) * 16, vs + ch * 16);
+        fence_proxy_async_smem();  // the tensor core reads them through the async proxy
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 4) {
+        // ---- TMA: block j's K and V pages into stage j % 2
+        if (lane == 0) {
+            int j = 0;
+            for (; j < nkb && !s_abort; j++) {
+                const int st = j % TA_ST;
+                if (j >= TA_ST && !mbar_wait_bounded(&kv_empty[st], (uint32_t)((j / TA_ST) - 1) & 1u)) {
+                    s_abort = 1;
+                    break;
+                }
+                int page = j < max_pages ? bt[j] : -1;
+                if (page < 0 || page >= num_pages) {
+                    atomicOr(err, ERRBIT_BAD_PAGE);
+                    page = 0;
+                }
+                const int pk = page * n_kv + kvh;
+                mbar_expect_tx(&kv_full[st], TA_K_BYTES + TA_V_BYTES);
+                tma_load_2d(sK + st * TA_K_BYTES, &kmap, 0, pk * TA_HD, &kv_full[st]);
+                tma_load_2d(sV + st * TA_V_BYTES, &vmap, 0, pk * TA_KB, &kv_full[st]);
+                tma_load_2d(sV + st * TA_V_BYTES + TA_V_BYTES / 2, &vmap, 64, pk * TA_KB, &kv_full[st]);
+            }
+            // copies in flight land before shared memory is released
+            for (int k = j > TA_ST ? j - TA_ST : 0; k < j; k++)
+                mbar_wait_bounded(&kv_full[k % TA_ST], (uint32_t)(k / TA_ST) & 1u);
         }
-        cp_async_commit();
-    };
-
-    float o[16][4];
+    } else if (warp == 5) {
+        // ---- MMA issue: S_{j+1} is issued before O_j so it overlaps block j's softmax
+        if (lane == 0) {
+            const uint32_t aQh = smem_u32(sQh), aQl = smem_u32(sQl), aK = smem_u32(sK), aV = smem_u32(sV),
+                           aP = smem_u32(sP);
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % TA_ST, sb = j & 1;
+                if (!mbar_wait_bounded(&kv_full[st], (uint32_t)(j / TA_ST) & 1u)) return false;
+                if (j >= 2 && !mbar_wait_bounded(&s_free[sb], (uint32_t)((j >> 1) - 1) & 1u)) return false;
+                tc_fence_after();
 #pragma unroll
-    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-    load(0, 0);
-    for (int kb = 0; kb < nkb; kb++) {
-        const int st = kb & 1;
-        if (kb + 1 < nkb) {
-            load(kb + 1, st ^ 1);
-            cp_async_wait<1>();
+                for (int ks = 0; ks < TA_HD / 16; ks++) {  // 16 dims: 16 K rows of the MN-major page
+                    const uint32_t qo = (uint32_t)(ks >> 2) * (TA_Q * 128) + (uint32_t)(ks & 3) * 32;
+                    const uint64_t db = umma_desc_mn_sw128(aK + st * TA_K_BYTES + ks * 2048, TA_K_BYTES, 1024);
+                    umma_f16_desc(tmem + sb * TA_KB, umma_desc_sw128(aQh + qo), db, TA_IDESC_S, ks > 0 ? 1u : 0u);
+                    umma_f16_desc(tmem + sb * TA_KB, umma_desc_sw128(aQl + qo), db, TA_IDESC_S, 1u);
+                }
+                umma_commit(&s_full[sb]);
+                return true;
+            };
+            auto issue_o = [&](int j) -> bool {
+                const int st = j % TA_ST, pb = j & 1;
+                if (!mbar_wait_bounded(&p_full[pb], (uint32_t)(j >> 1) & 1u)) return false;
+                tc_fence_after();
+                const uint32_t ph = aP + pb * 2 * TA_P_BYTES, pl = ph + TA_P_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < TA_KB / 16; ks++) {  // 16 keys: 16 K rows of both V halves
+                    const uint64_t db = umma_desc_mn_sw128(aV + st * TA_V_BYTES + ks * 2048, TA_V_BYTES / 2, 1024);
+                    umma_f16_desc(tmem + TA_O_COL, umma_desc_sw128(ph + ks * 32), db, TA_IDESC_O,
+                                  (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_f16_desc(tmem + TA_O_COL, umma_desc_sw128(pl + ks * 32), db, TA_IDESC_O, 1u);
+                }
+                umma_commit(&kv_empty[st]);
+                umma_commit(&p_free[pb]);
+                umma_commit(&o_done);
+                return true;
+            };
+            bool okm = issue_s(0);
+            for (int j = 0; okm && j < nkb && !s_abort; j++) {
+                if (j + 1 < nkb) okm = issue_s(j + 1);
+                if (okm) okm = issue_o(j);
+            }
+            if (!okm) s_abort = 1;
+            umma_commit(&fin);  // every MMA issued has completed before TMEM is released
+            mbar_wait_bounded(&fin, 0);
+        }
+    } else {
+        // ---- softmax: thread = query row r = TMEM lane of this warp's quarter
+        constexpr unsigned FULL = 0xffffffffu;
+        const int r = threadIdx.x;
+        const int qpos = pos0 + min(q0 + r, T - 1);
+        const uint32_t lt = tmem + ((uint32_t)(32 * warp) << 16);
+        const float sl2 = __fmul_rn(scale, 1.4426950408889634f);  // scores in log2 units
+        float m = -INFINITY, l = 0.f;  // reference max (log2 units) and row sum
+        bool okw = true;
+        for (int j = 0; j < nkb && okw; j++) {
+            const int sb = j & 1;
+            if (!(okw = mbar_wait_bounded(&s_full[sb], (uint32_t)(j >> 1) & 1u))) break;
+            tc_fence_after();
+            uint32_t sa[32], sc2[32];
+            tmem_ld32(lt + sb * TA_KB, sa);
+            tmem_ld32(lt + sb * TA_KB + 32, sc2);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[sb]);  // the MMA of block j + 2 may overwrite it
+            // scale, causal mask (keys after the query's position), block max
+            const int key0 = j * TA_KB;
+            float x[64];
+            float bm = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < 64; t++) {
+                const float sv = __uint_as_float(t < 32 ? sa[t] : sc2[t - 32]);
+                x[t] = key0 + t <= qpos ? __fmul_rn(sv, sl2) : -INFINITY;
+                bm = fmaxf(bm, x[t]);
+            }
+            const float mn = fmaxf(m, bm);  // finite: key 0 precedes every query
+            const bool need = j > 0 && mn > m + 8.f;
+            if (__any_sync(FULL, need)) {
+                // rescale this quarter's accumulator rows once O += P_{j-1} V_{j-1} has landed
+                if (!(okw = mbar_wait_bounded(&o_done, (uint32_t)(j - 1) & 1u))) break;
+                tc_fence_after();
+                const float al = need ? exp2f(m - mn) : 1.f;
+#pragma unroll 1
+                for (int c = 0; c < TA_HD / 32; c++) {
+                    uint32_t ov[32];
+                    tmem_ld32(lt + TA_O_COL + 32 * c, ov);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__fmul_rn(__uint_as_float(ov[i]), al));
+                    tmem_st32(lt + TA_O_COL + 32 * c, ov);
+                }
+                tc_fence_before();
+                if (need) {
+                    l = __fmul_rn(l, al);
+                    m = mn;
+                }
+            }
+            if (j == 0) m = mn;
+            // p = 2^(x - m) (<= 256), written as fp16 hi / lo A operands
+            if (j >= 2 && !(okw = mbar_wait_bounded(&p_free[sb], (uint32_t)((j >> 1) - 1) & 1u))) break;
+            uint8_t *ph = sP + sb * 2 * TA_P_BYTES, *pl = ph + TA_P_BYTES;
+            float ls = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                float p[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    p[e] = exp2f(__fsub_rn(x[8 * c + e], m));
+                    ls = __fadd_rn(ls, p[e]);
+                }
+                uint4 hi, lo;
+                split8(p, hi, lo);
+                *reinterpret_cast<uint4 *>(ph + sw128_off(r, c)) = hi;
+                *reinterpret_cast<uint4 *>(pl + sw128_off(r, c)) = lo;
+            }
+            l = __fadd_rn(l, ls);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[sb]);
+        }
+        // ---- O / l once the last P V has landed
+        if (okw) okw = mbar_wait_bounded(&o_done, (uint32_t)(nkb - 1) & 1u);
+        if (okw) {
+            tc_fence_after();
+            const float inv = l > 0.f ? __fdiv_rn(1.f, l) : 0.f;
+            float *orow = out + ((int64_t)(q0 + r) * n_heads + h) * TA_HD;
+#pragma unroll 1
+            for (int c = 0; c < TA_HD / 32; c++) {
+                uint32_t ov[32];
+                tmem_ld32(lt + TA_O_COL + 32 * c, ov);
+                if (q0 + r < T)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(orow + 32 * c + i) =
+                            make_float4(__fmul_rn(__uint_as_float(ov[i]), inv), __fmul_rn(__uint_as_float(ov[i + 1]), inv),
+                                        __fmul_rn(__uint_as_float(ov[i + 2]), inv),
+                                        __fmul_rn(__uint_as_float(ov[i + 3]), inv));
+            }
         } else {
-            cp_async_wait<0>();
+            s_abort = 1;
         }
-        __syncthreads();
-        const uint32_t kd = sbase + st * PA_STAGE, vd = kd + PA_K_BYTES;
-        // ---- S = q . k^T for 16 queries x 64 keys (8 n-tiles of 8 keys)
-        float s[8][4];
-#pragma unroll
-        for (int i = 0; i < 8; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-#pragma unroll
-            for (int np = 0; np < 4; np++) {  // n-tile pairs (2np, 2np + 1)
-                // matrices: dims 16kk + {0..7, 8..15} x keys 8(2np) .. / 8(2np+1) ..
-                const int mi = lane >> 3, rr = lane & 7;
-                const int dim = 16 * kk + (mi & 1) * 8 + rr, key = 8 * (2 * np + (mi >> 1));
-                uint32_t b[4];
-                ldsm_x4_trans(b, kd + dim * PA_KP + key * 2);
-                mma16816(s[2 * np], qa[kk], b[0], b[1]);
-                mma16816(s[2 * np], qb[kk], b[0], b[1]);
-                mma16816(s[2 * np + 1], qa[kk], b[2], b[3]);
-                mma16816(s[2 * np + 1], qb[kk], b[2], b[3]);
-            }
-        }
-        // ---- scale, causal mask, online softmax (rows g and g + 8 of the warp)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int key = kb * PA_KB + 8 * nt + 2 * c + e;
-                s[nt][e] = key <= qpos0 ? __fmul_rn(s[nt][e], scale) : -INFINITY;
-                s[nt][2 + e] = key <= qpos1 ? __fmul_rn(s[nt][2 + e], scale) : -INFINITY;
-                mx0 = fmaxf(mx0, s[nt][e]);
-                mx1 = fmaxf(mx1, s[nt][2 + e]);
-            }
-        }
-#pragma unroll
-        for (int off = 1; off <= 2; off <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-        }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        // rows with no visible key yet keep zero weight (mn = -inf)
-        const float al0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0);
-        const float al1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
-        m0 = mn0;
-        m1 = mn1;
-        float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                s[nt][e] = mn0 == -INFINITY ? 0.f : expf(s[nt][e] - mn0);
-                s[nt][2 + e] = mn1 == -INFINITY ? 0.f : expf(s[nt][2 + e] - mn1);
-                ps0 += s[nt][e];
-                ps1 += s[nt][2 + e];
-            }
-        }
-        l0 = l0 * al0 + ps0;
-        l1 = l1 * al1 + ps1;
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            o[i][0] *= al0;
-            o[i][1] *= al0;
-            o[i][2] *= al1;
-            o[i][3] *= al1;
-        }
-        // ---- O += P . V: k-steps of 16 keys (n-tiles 2j, 2j + 1 of S), 16 dim n-tiles
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            uint32_t pa[4], pb[4];
-            split_h2(s[2 * j][0], s[2 * j][1], pa[0], pb[0]);
-            split_h2(s[2 * j][2], s[2 * j][3], pa[1], pb[1]);
-            split_h2(s[2 * j + 1][0], s[2 * j + 1][1], pa[2], pb[2]);
-            split_h2(s[2 * j + 1][2], s[2 * j + 1][3], pa[3], pb[3]);
-#pragma unroll
-            for (int dp = 0; dp < 8; dp++) {  // dim n-tile pairs (2dp, 2dp + 1)
-                const int mi = lane >> 3, rr = lane & 7;
-                const int key = 16 * j + (mi & 1) * 8 + rr, dim = 8 * (2 * dp + (mi >> 1));
-                uint32_t b[4];
-                ldsm_x4_trans(b, vd + key * PA_VP + dim * 2);
-                mma16816(o[2 * dp], pa, b[0], b[1]);
-                mma16816(o[2 * dp], pb, b[0], b[1]);
-                mma16816(o[2 * dp + 1], pa, b[2], b[3]);
-                mma16816(o[2 * dp + 1], pb, b[2], b[3]);
-            }
-        }
-        __syncthreads();  // stage st is refilled by the next iteration's load
     }
-    // ---- normalise and store
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    tc_fence_before();
+    __syncthreads();
+    if (s_abort && threadIdx.x == 0) atomicOr(err, ERRBIT_WAIT_TIMEOUT);
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TA_TMEM_COLS)
+                     : "memory");
     }
-    const int r0 = q0 + 16 * warp + g, r1 = r0 + 8;
-    const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
-#pragma unroll
-    for (int dn = 0; dn < 16; dn++) {
-        const int dim = 8 * dn + 2 * c;
-        if (r0 < T)
-            *reinterpret_cast<float2 *>(out + ((int64_t)r0 * n_heads + h) * PA_HD + dim) =
-                make_float2(o[dn][0] * i0, o[dn][1] * i0);
-        if (r1 < T)
-            *reinterpret_cast<float2 *>(out + ((int64_t)r1 * n_heads + h) * PA_HD + dim) =
-                make_float2(o[dn][2] * i1, o[dn][3] * i1);
-    }
+}
+
+}  // namespace fb
+
+namespace fb {
+
+// fp16 pool viewed as rows of `inner` values, boxes of 64 values x box_rows
+// rows, 128-byte swizzle (the MN-major B layouts above).
+static CUtensorMap pool_map(const void *pool, int64_t rows, int64_t inner, uint32_t box_rows) {
+    auto encode = tensor_map_encoder();
+    FB_REQUIRE(encode != nullptr, "attn_prefill: cuTensorMapEncodeTiled is unavailable");
+    FB_REQUIRE(((uintptr_t)pool & 15) == 0, "attn_prefill: KV pools must be 16-byte aligned");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(pool), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FB_REQUIRE(cr == CUDA_SUCCESS, "attn_prefill: tensor map encoding failed");
+    return map;
 }
 
 void launch_attn_prefill(fb_ctx *ctx, const float *q, const void *kpool, const void *vpool, const int32_t *bt,
                          int max_pages, int num_pages, int pos0, int T, int n_heads, int n_kv, float scale,
                          float *out) {
-    FB_REQUIRE(T >= 1 && pos0 >= 0 && n_heads % n_kv == 0, "attn_prefill: bad shape");
-    FB_REQUIRE((pos0 + T + PA_KB - 1) / PA_KB <= max_pages, "attn_prefill: positions exceed the block table");
-    FB_CUDA(cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM));
-    dim3 grid((unsigned)((T + PA_Q - 1) / PA_Q), (unsigned)n_heads);
-    k_attn_prefill<<<grid, 128, PA_SMEM, ctx->stream>>>(q, (const __half *)kpool, (const __half *)vpool, bt, max_pages,
-                                                         num_pages, pos0, T, n_heads, n_kv, scale, out,
-                                                         ctx->err_word);
+    FB_REQUIRE(T >= 1 && pos0 >= 0 && n_kv >= 1 && n_heads % n_kv == 0, "attn_prefill: bad shape");
+    FB_REQUIRE((pos0 + T + TA_KB - 1) / TA_KB <= max_pages, "attn_prefill: positions exceed the block table");
+    FB_REQUIRE((int64_t)num_pages * n_kv * TA_HD < ((int64_t)1 << 31), "attn_prefill: KV pool too large");
+    const CUtensorMap kmap = pool_map(kpool, (int64_t)num_pages * n_kv * TA_HD, TA_KB, TA_HD);
+    const CUtensorMap vmap = pool_map(vpool, (int64_t)num_pages * n_kv * TA_KB, TA_HD, TA_KB);
+    FB_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TA_SMEM));
+    dim3 grid((unsigned)((T + TA_Q - 1) / TA_Q), (unsigned)n_heads);
+    k_attn_prefill_tc<<<grid, TA_THREADS, TA_SMEM, ctx->stream>>>(kmap, vmap, q, bt, max_pages, num_pages, pos0, T,
+                                                                   n_heads, n_kv, scale, out, ctx->err_word);
     FB_CUDA(cudaGetLastError());
 }
 
