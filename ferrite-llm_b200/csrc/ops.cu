@@ -369,13 +369,19 @@ __global__ void __launch_bounds__(256) k_add_rmsnorm_rows(float *__restrict__ x,
     for (int i = threadIdx.x; i < dim; i += 256) xn[row * dim + i] = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
 }
 
-// act[t][i] = silu(gate) * up for the rows y[t] = [gate (f) | up (f)].
+// act[t][i] = silu(gate) * up for the rows y[t] = [gate (f) | up (f)]
+// (batched prefill, the float path: silu in f32, gate / (1 + e^-gate),
+// within an ulp of the decode path's binary64 form).  grid (f / 1024, T):
+// thread = four consecutive values of one row, vectorised.
 __global__ void __launch_bounds__(256) k_swiglu_rows(const float *__restrict__ y, int f, int64_t rows,
                                                      float *__restrict__ act) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= rows * f) return;
-    const int64_t r = i / f, c = i % f;
-    act[i] = __fmul_rn(silu64(y[r * 2 * f + c]), y[r * 2 * f + f + c]);
+    const int64_t r = blockIdx.y;
+    const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (r >= rows || c >= f) return;
+    const float4 g = *reinterpret_cast<const float4 *>(y + r * 2 * f + c);
+    const float4 u = *reinterpret_cast<const float4 *>(y + r * 2 * f + f + c);
+    auto sw = [](float gv, float uv) { return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv); };
+    *reinterpret_cast<float4 *>(act + r * f + c) = make_float4(sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
 }
 
 // Prefill prologue of attention for T new tokens at positions pos0 + t: one
@@ -439,8 +445,8 @@ void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float 
 }
 
 void launch_swiglu_rows(fb_ctx *ctx, const float *y, int f, int T, float *act) {
-    const int64_t n = (int64_t)T * f;
-    k_swiglu_rows<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(y, f, T, act);
+    FB_REQUIRE(f % 4 == 0 && T >= 1 && T <= 65535, "swiglu_rows: f must be a multiple of 4, 1 <= T <= 65535");
+    k_swiglu_rows<<<dim3((unsigned)((f / 4 + 255) / 256), (unsigned)T), 256, 0, ctx->stream>>>(y, f, T, act);
     FB_CUDA(cudaGetLastError());
 }
 

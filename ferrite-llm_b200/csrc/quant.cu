@@ -459,7 +459,8 @@ __global__ void __launch_bounds__(256) k_gemv_float(const uint8_t *__restrict__ 
     const int lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= n) return;
-    double acc = 0.0;
+    double acc8[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // one chain per lane value: short FMA chains
+#pragma unroll 2
     for (int64_t b = 0; b < nb; b++) {
         float v[8];
         if constexpr (DT == 4) dq8_q4k(w, r, b, nb, lane, v);
@@ -468,8 +469,11 @@ __global__ void __launch_bounds__(256) k_gemv_float(const uint8_t *__restrict__ 
         const float4 x1 = *reinterpret_cast<const float4 *>(x + b * QK + 8 * lane + 4);
         const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-        for (int e = 0; e < 8; e++) acc = __fma_rn((double)v[e], (double)xv[e], acc);
+        for (int e = 0; e < 8; e++) acc8[e] = __fma_rn((double)v[e], (double)xv[e], acc8[e]);
     }
+    double acc = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc = __dadd_rn(acc, acc8[e]);
     acc = warp_sum64(acc);
     if (lane == 0) y[r] = __double2float_rn(acc);
 }
