@@ -232,10 +232,11 @@ bool attn_uses_cluster(fb_ctx *ctx, const AttnArgs &A, int batch);
 
 // ---- tensor parallelism (tp.cu) ----
 // Exchange region of one rank (cudaMalloc, mapped by every rank via IPC):
-//   flags    [FB_TP_MAX] u32      flags[src] = sequence number of the last
-//                                 row-parallel exchange src has pushed here
+//   flags    [FB_TP_MAX] u32      (unused by the row-parallel exchange)
 //   am_flags [FB_TP_MAX][B] u32   argmax exchange: step epoch per (src, row)
-//   inbox_o / inbox_d [W][B][H] f64  partial sums of attn_output / ffn_down
+//   inbox_o / inbox_d [W][B][H][2] u64  partial sums of attn_output /
+//                                 ffn_down: each binary64 as two words
+//                                 (seq << 32) | 32-bit half (lo, hi)
 //   am_inbox [W][B] u64           (f32 bits of the max << 32) | global index
 struct CommLayout {
     size_t flags, am_flags, inbox_o, inbox_d, am_inbox, total;
@@ -243,17 +244,20 @@ struct CommLayout {
 CommLayout comm_layout(int world, int max_batch, int hidden);
 
 // Row-parallel GEMV output: the binary64 row sums (not rounded) are stored
-// to dst[p][col * ld + row] for every rank p < world.
+// to every rank p < world as the word pair dst[p][2 (col * ld + row) + {0, 1}]
+// = (seq << 32) | lo / hi 32 bits, each an 8-byte single-copy-atomic store:
+// a reader that sees seq in both words has the value, with no fence or flag
+// (seq = (*epoch - 1) * nx + xi + 1 numbers the step's exchange points).
 struct PeerOut {
-    double *dst[FB_TP_MAX];
+    uint64_t *dst[FB_TP_MAX];
     int64_t ld;
     int world;
+    const uint32_t *epoch;  // device step counter (>= 1 inside a step)
+    int nx, xi;
 };
 // Residual + RMSNorm after a row-parallel projection (one exchange point).
 struct TpNorm {
-    const double *inbox;             // this rank's inbox [W][B][H]
-    const uint32_t *my_flags;        // this rank's flags [W]
-    uint32_t *peer_flag[FB_TP_MAX];  // &flags[rank] in rank p's region
+    const uint64_t *inbox;           // this rank's inbox [W][B][H][2] (PeerOut word pairs)
     const uint32_t *epoch;           // device step counter (>= 1 inside a step)
     double *ss_part;                 // [B][H/256] per-block sums of squares
     uint32_t *ss_tag;                // [B][H/256] exchange sequence of ss_part

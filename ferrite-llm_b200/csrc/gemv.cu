@@ -327,6 +327,8 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         for (; issued < DEPTH && issued < total; issued++) issue(issued);
     pdl_wait();
     pdl_launch();  // let the next kernel start streaming its weights
+    // row-parallel shard: the sequence number tagging this exchange's words
+    const uint32_t seq = po.world ? (*po.epoch - 1u) * (uint32_t)po.nx + (uint32_t)po.xi + 1u : 0u;
     Q8Act act = a;
     bool ok = true;
     if constexpr (DP4A) {
@@ -418,7 +420,14 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
                 const int64_t row = row0 + r;
                 if (row < n && col < m) {
                     if (po.world) {  // row-parallel shard: binary64 partials to every rank's inbox
-                        for (int p = 0; p < po.world; p++) po.dst[p][(int64_t)col * po.ld + row] = sum;
+                        const uint64_t bits = (uint64_t)__double_as_longlong(sum);
+                        const uint64_t w0 = ((uint64_t)seq << 32) | (bits & 0xffffffffull);
+                        const uint64_t w1 = ((uint64_t)seq << 32) | (bits >> 32);
+                        const int64_t wi = 2 * ((int64_t)col * po.ld + row);
+                        for (int p = 0; p < po.world; p++) {
+                            st_relaxed_sys_u64(po.dst[p] + wi, w0);
+                            st_relaxed_sys_u64(po.dst[p] + wi + 1, w1);
+                        }
                     } else {
                         y[(int64_t)col * ldy + row] = __double2float_rn(sum);
                     }
@@ -433,7 +442,6 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         for (int k = waited; k < issued; k++) mbar_wait_bounded(&wbar[k % DEPTH], (uint32_t)(k / DEPTH) & 1u);
         if (DP4A && !act_ok && threadIdx.x == 0) mbar_wait_bounded(&actbar, 0);
     }
-    if (po.world) __threadfence_system();  // peer stores performed before the grid completes
     pdl_launch();
 }
 

@@ -180,17 +180,17 @@ static PeerOut peer_out(const fb_model *m, size_t inbox_off) {
     const fb_comm *cm = m->comm;
     PeerOut po{};
     for (int p = 0; p < cm->world; p++)
-        po.dst[p] = cm->at<double>(p, inbox_off) + (size_t)cm->rank * cm->max_batch * cm->hidden;
+        po.dst[p] = cm->at<uint64_t>(p, inbox_off) + 2 * (size_t)cm->rank * cm->max_batch * cm->hidden;
     po.ld = cm->hidden;
     po.world = cm->world;
+    po.epoch = m->epoch.as<uint32_t>();
+    po.nx = 2 * m->c.n_layers;
     return po;
 }
 static TpNorm tp_norm(const fb_model *m, size_t inbox_off) {
     const fb_comm *cm = m->comm;
     TpNorm t{};
-    t.inbox = cm->at<double>(cm->rank, inbox_off);
-    t.my_flags = cm->at<uint32_t>(cm->rank, cm->L.flags);
-    for (int p = 0; p < cm->world; p++) t.peer_flag[p] = cm->at<uint32_t>(p, cm->L.flags) + cm->rank;
+    t.inbox = cm->at<uint64_t>(cm->rank, inbox_off);
     t.epoch = m->epoch.as<uint32_t>();
     t.ss_part = m->ss_part.as<double>();
     t.ss_tag = m->ss_tag.as<uint32_t>();
@@ -350,6 +350,8 @@ static void step(fb_model *m, int b, StepProbe *probe = nullptr) {
                            m->att_cnt.as<int>(), true, false);
         if (!q8_fused) launch_quantize_q8k(ctx, m->attn.as<float>(), b, qd, aa);
         mark(FB_PROF_ATTN, q8_fused ? 1 : 2);
+        po_o.xi = 2 * l;
+        po_d.xi = 2 * l + 1;
         if (tp) launch_gemv_peer(ctx, L.wo.t, aa, b, po_o);
         else launch_gemv(ctx, L.wo.t, aa, b, m->y_o.as<float>(), H);
         mark(FB_PROF_O, 1);

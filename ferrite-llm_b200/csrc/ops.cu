@@ -156,12 +156,13 @@ __global__ void __launch_bounds__(NORM_THREADS)
 // once -- the rounding the single-GPU GEMV applies to the full sum -- and
 // the residual add, RMSNorm and Q8_K follow k_residual_rmsnorm_q8k.
 // Exchange protocol (sequence number seq of this exchange point in the
-// step): one thread per destination rank publishes seq into that rank's
-// flags[rank] with a system-scope release (the GEMV grid's peer stores
-// precede it), and W threads of every CTA wait (bounded) for flags[src] >=
-// seq.  Inboxes alternate between attn_output and ffn_down, so a rank can
-// only overwrite an inbox slot after every rank has passed the exchange in
-// between, i.e. after the slot was read.
+// step): every rank's GEMV stores each partial into this rank's inbox as two
+// 8-byte words (seq << 32) | 32-bit half, and each thread here polls
+// (bounded) the W word pairs of its value until both carry seq -- no fence
+// on the writer's side and no flag round trip.  Inboxes alternate between
+// attn_output and ffn_down, so a rank can only overwrite an inbox slot after
+// every rank has passed the exchange in between, i.e. after the slot was
+// read.
 // One CTA per (256-value block, row) reduces only its own block; the blocks'
 // sums of squares meet through global slots tagged with seq.
 __global__ void __launch_bounds__(NORM_THREADS)
@@ -180,15 +181,25 @@ __global__ void __launch_bounds__(NORM_THREADS)
     pdl_wait();
     pdl_launch();
     const uint32_t seq = (*t.epoch - 1u) * (uint32_t)t.nx + (uint32_t)xi + 1u;
-    if (blk == 0 && row == 0 && tid < t.world) {
-        __threadfence_system();
-        st_release_sys(t.peer_flag[tid], seq);
-    }
-    if (tid < t.world && !wait_seq<true>(&t.my_flags[tid], seq, t.limit_ns)) atomicOr(err, ERRBIT_PEER_TIMEOUT);
-    __syncthreads();
     const int64_t plane = (int64_t)t.batch_cap * dim;
     double s = 0.0;
-    for (int r = 0; r < t.world; r++) s = __dadd_rn(s, __ldcg(t.inbox + r * plane + j));
+    bool ok = true;
+    for (int r = 0; r < t.world; r++) {
+        const uint64_t *wp = t.inbox + 2 * (r * plane + j);
+        uint64_t w0 = ld_relaxed_sys_u64(wp), w1 = ld_relaxed_sys_u64(wp + 1);
+        if ((uint32_t)(w0 >> 32) != seq || (uint32_t)(w1 >> 32) != seq) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ok && ((uint32_t)(w0 >> 32) != seq || (uint32_t)(w1 >> 32) != seq)) {
+                __nanosleep(64);
+                w0 = ld_relaxed_sys_u64(wp);
+                w1 = ld_relaxed_sys_u64(wp + 1);
+                ok = globaltimer_ns() - t0 <= t.limit_ns;
+            }
+        }
+        const double v = __longlong_as_double((long long)((w1 << 32) | (w0 & 0xffffffffull)));
+        s = __dadd_rn(s, v);
+    }
+    if (!ok) atomicOr(err, ERRBIT_PEER_TIMEOUT);
     const float xn = __fadd_rn(__double2float_rn(s), xv);
     x_out[j] = xn;
     xb[tid] = xn;

@@ -1,6 +1,7 @@
 // Tensor-parallel exchange regions (fb_comm_*): one device region per rank,
 // mapped into every rank's process with CUDA IPC so that kernels store
-// partial sums and flags straight into peers' memory over NVLink.
+// partial sums (tagged with the exchange's sequence number) straight into
+// peers' memory over NVLink.
 //
 // The reference has no tensor parallelism; its multi-GPU layer enables peer
 // access and reduces with peer copies gathered to a root device
@@ -26,9 +27,9 @@ CommLayout comm_layout(int world, int max_batch, int hidden) {
     L.am_flags = off;
     off += up256((size_t)FB_TP_MAX * max_batch * 4);
     L.inbox_o = off;
-    off += up256((size_t)world * max_batch * hidden * 8);
+    off += up256((size_t)world * max_batch * hidden * 16);
     L.inbox_d = off;
-    off += up256((size_t)world * max_batch * hidden * 8);
+    off += up256((size_t)world * max_batch * hidden * 16);
     L.am_inbox = off;
     off += up256((size_t)world * max_batch * 8);
     L.total = off;

@@ -10,7 +10,8 @@ so a near tie (oracle top-2 margin below TIE_MARGIN) is reported and the
 comparison continues.  A second model has the Llama-3-70B widths (hidden
 8192, 64 q / 8 kv heads, SwiGLU 28672, vocab 128256) at 2 layers.  The
 failure test lets one rank never step: the other rank's bounded device waits
-run out (nothing sets the flag it waits on), the step reports FB_ERR_DEVICE
+run out (nothing writes the tagged partial sums it polls for), the step
+reports FB_ERR_DEVICE
 with the peer-timeout bit and the context stays usable.  Each world size is
 skipped with fewer GPUs.
 """
