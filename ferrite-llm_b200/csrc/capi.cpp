@@ -132,6 +132,13 @@ int fb_ctx_set_pdl(fb_ctx *ctx, int enable) {
     });
 }
 
+int fb_ctx_set_prefill_weight_cache(fb_ctx *ctx, int enable) {
+    return guarded([&] {
+        FB_REQUIRE(ctx, "null ctx");
+        ctx->prefill_cache = enable != 0;
+    });
+}
+
 int fb_sync(fb_ctx *ctx) {
     return guarded([&] {
         FB_REQUIRE(ctx, "null ctx");

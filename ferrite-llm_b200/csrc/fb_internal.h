@@ -74,6 +74,7 @@ struct fb_ctx {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     bool pdl = true;
+    bool prefill_cache = true;  // fb_ctx_set_prefill_weight_cache
     int num_sms = 148;
     uint32_t *err_word = nullptr;          // device, zero-initialised
     fb::DevBuf scratch;                    // grow-only workspace
@@ -98,6 +99,8 @@ struct fb_qtensor {
     int dtype = 0;
     int64_t n = 0, k = 0;
     fb::DevBuf buf;
+    fb::DevBuf f16;           // prefill weight cache: W dequantized to fp16 [n][k] (empty: none)
+    bool f16_tried = false;   // the cache was considered (allocated or refused) once
     int64_t nb() const { return k / 256; }
     int64_t n_pad() const { return (n + 15) / 16 * 16; }
     int64_t n_tiles() const { return (n + 15) / 16; }

@@ -569,14 +569,43 @@ static int64_t two_pass_chunk_rows(int64_t n, int64_t K) {
 }
 
 // Y[m, n] = X[m, k] . W^T on the tensor cores (prefill_gemm_supported(w, m)).
+// The fp16 copy of W kept for later prompt passes (prefill weight cache), made
+// on the first long pass while max(16 GiB, a quarter of the device) stays
+// free; null when the cache is off or the memory is not there.
+static const __half *prefill_weight_cache(fb_ctx *ctx, const fb_qtensor *w) {
+    fb_qtensor *mw = const_cast<fb_qtensor *>(w);  // the cache is a derived copy, not the tensor's value
+    if (!ctx->prefill_cache) return nullptr;
+    if (!mw->f16_tried) {
+        mw->f16_tried = true;
+        size_t free_b = 0, total_b = 0;
+        FB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+        const size_t need = (size_t)w->n * w->k * 2;
+        const size_t keep = std::max((size_t)16 << 30, total_b / 4);
+        if (free_b > need && free_b - need > keep) {
+            mw->f16.alloc(need);
+            const int64_t nthr = w->n * w->nb() * 8;
+            if (w->dtype == FB_Q4_K)
+                k_dequant_rows_f16<4><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(
+                    w->main(), w->nb(), 0, w->n, mw->f16.as<__half>());
+            else
+                k_dequant_rows_f16<6><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(
+                    w->main(), w->nb(), 0, w->n, mw->f16.as<__half>());
+            FB_CUDA(cudaGetLastError());
+        }
+    }
+    return mw->f16.ptr ? mw->f16.as<__half>() : nullptr;
+}
+
 void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
     FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
     const int64_t K = w->k, N = w->n;
     const bool two_pass = m >= PF_TWO_PASS_MIN_ROWS;
-    const int64_t chunk = two_pass ? two_pass_chunk_rows(N, K) : 0;
+    const __half *wcache = two_pass ? prefill_weight_cache(ctx, w) : nullptr;
+    const int64_t chunk = two_pass ? (wcache ? N : two_pass_chunk_rows(N, K)) : 0;
     const size_t xh_bytes = ((size_t)m * K * 2 + 255) & ~(size_t)255;
     const size_t rs_bytes = ((size_t)m * 4 + 255) & ~(size_t)255;
-    uint8_t *scratch = static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + rs_bytes + (size_t)chunk * K * 2));
+    uint8_t *scratch =
+        static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + rs_bytes + (wcache ? 0 : (size_t)chunk * K * 2)));
     __half *xh = reinterpret_cast<__half *>(scratch);
     float *rowscale = reinterpret_cast<float *>(scratch + xh_bytes);
     k_x_to_f16<<<(unsigned)((m + 7) / 8), 256, 0, ctx->stream>>>(x, xh, rowscale, (int)m, K);
@@ -600,13 +629,17 @@ void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, in
     for (int64_t r0 = 0; r0 < N; r0 += chunk) {
         const int64_t rows = std::min(chunk, N - r0);
         const int64_t nthr = rows * w->nb() * 8;
-        if (w->dtype == FB_Q4_K)
-            k_dequant_rows_f16<4><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(), r0,
-                                                                                          rows, wh);
-        else
-            k_dequant_rows_f16<6><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(), r0,
-                                                                                          rows, wh);
-        FB_CUDA(cudaGetLastError());
+        if (wcache) {
+            wh = const_cast<__half *>(wcache);  // (chunk = N: one pass over the cached copy)
+        } else {
+            if (w->dtype == FB_Q4_K)
+                k_dequant_rows_f16<4><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(),
+                                                                                              r0, rows, wh);
+            else
+                k_dequant_rows_f16<6><<<(unsigned)((nthr + 255) / 256), 256, 0, ctx->stream>>>(w->main(), w->nb(),
+                                                                                              r0, rows, wh);
+            FB_CUDA(cudaGetLastError());
+        }
         // 256-column tiles (half the L2 re-reads of X per output) or 128-column
         // ones, whichever needs less time in whole waves of one tile per SM;
         // a 256-column tile is counted as 1.8 of the narrow ones (measured:

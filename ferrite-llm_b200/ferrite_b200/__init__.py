@@ -31,7 +31,7 @@ BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, Q8_K: 292}
 # Every symbol include/ferrite_b200.h declares (checked by the CPU tests).
 EXPORTED = (
     "fb_last_error", "fb_abi_version", "fb_ctx_create", "fb_ctx_destroy", "fb_ctx_set_stream", "fb_ctx_stream",
-    "fb_sync", "fb_ctx_error_word", "fb_ctx_set_pdl", "fb_qtensor_upload", "fb_qtensor_upload_dev",
+    "fb_sync", "fb_ctx_error_word", "fb_ctx_set_pdl", "fb_ctx_set_prefill_weight_cache", "fb_qtensor_upload", "fb_qtensor_upload_dev",
     "fb_qtensor_synth", "fb_qtensor_concat_rows", "fb_qtensor_info", "fb_qtensor_download", "fb_qtensor_destroy",
     "fb_dequantize", "fb_qmatmul", "fb_qmatmul_q8k", "fb_quantize_q8k", "fb_block_dots", "fb_rmsnorm", "fb_rope",
     "fb_swiglu", "fb_attn_decode", "fb_model_create", "fb_model_destroy", "fb_model_set_tensor", "fb_model_synth",
@@ -91,6 +91,7 @@ def _declare(L):
         "fb_sync": (i32, [vp]),
         "fb_ctx_error_word": (i32, [vp, P(C.c_uint32)]),
         "fb_ctx_set_pdl": (i32, [vp, i32]),
+        "fb_ctx_set_prefill_weight_cache": (i32, [vp, i32]),
         "fb_qtensor_upload": (i32, [vp, i32, i64, i64, vp, P(vp)]),
         "fb_qtensor_upload_dev": (i32, [vp, i32, i64, i64, vp, P(vp)]),
         "fb_qtensor_synth": (i32, [vp, i32, i64, i64, u64, f32, P(vp)]),
@@ -171,6 +172,11 @@ class Context:
 
     def set_pdl(self, enable: bool):
         _check(lib().fb_ctx_set_pdl(self.h, int(enable)))
+
+    def set_prefill_weight_cache(self, enable: bool):
+        """Keep fp16 copies of the projection weights for long prompt passes
+        (the default) or dequantize them on every pass."""
+        _check(lib().fb_ctx_set_prefill_weight_cache(self.h, int(enable)))
 
     def error_word(self) -> int:
         v = C.c_uint32()

@@ -83,6 +83,14 @@ int fb_sync(fb_ctx *ctx);
 int fb_ctx_error_word(fb_ctx *ctx, uint32_t *flags);
 /* Programmatic dependent launch between consecutive kernels (default on). */
 int fb_ctx_set_pdl(fb_ctx *ctx, int enable);
+/* Prompt passes of 512 rows or more dequantize each Q4_K / Q6_K projection
+ * to fp16 before its tensor-core GEMM.  With the cache on (the default) the
+ * first such pass keeps each tensor's fp16 copy (2 bytes per weight, freed
+ * with the tensor) while at least max(16 GiB, a quarter of the device) stays
+ * free, and later passes skip the dequantization; enable = 0 dequantizes on
+ * every pass and keeps nothing.  No reference counterpart (candle's CUDA
+ * path dequantizes on every call). */
+int fb_ctx_set_prefill_weight_cache(fb_ctx *ctx, int enable);
 
 /* ------------------------------------------------------------ QTensor --- */
 /* A weight matrix W[n, k] (n output features, k inputs, k % 256 == 0 for
