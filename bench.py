@@ -15,6 +15,8 @@ when decoding starts, batch 1 by default.
          per-kernel CUDA-event profile of the same workload.
   cpu_baseline  the CPU oracle (C restatement of candle's CPU quantized path)
          decoding the same random-init model on the host cores (rank 0, N=1).
+  prefill_2048, batch16  (N=1, batch 1 runs) a 2048-token prompt pass through
+         fb_model_forward, and decode at batch 16 on its own model.
 
 N > 1 (torchrun): the N ranks hold ONE tensor-parallel model (column-parallel
 q/k/v, gate/up and lm_head shards, row-parallel attn_output and ffn_down
@@ -414,6 +416,42 @@ def prefill_extra(model, cfg: dict, stream, T: int = 2048) -> dict:
             "how": "fb_model_forward of a uniform random prompt (seed 2), host ids in, host logits out"}
 
 
+def batch_extra(ctx, cfg: dict, stream, ctx_len: int, B: int = 16, steps: int = 10) -> dict:
+    """Decode at batch B on its own model (same weights and KV generator):
+    device-resident tokens, CUDA-graph steps timed with CUDA events after
+    three warm-up steps.  The step reads the weights once and B sequences'
+    KV, far above the L2 size."""
+    import torch
+
+    import ferrite_b200 as fb
+
+    m = fb.Model(ctx, dict(cfg, max_ctx=ctx_len + steps + 8, max_batch=B))
+    m.synth(SEED)
+    m.finalize()
+    m.synth_kv(SEED + 7, ctx_len)
+    tok = torch.randint(0, cfg["vocab"], (B,), dtype=torch.int32, device="cuda",
+                        generator=torch.Generator(device="cuda").manual_seed(3))
+    pos = torch.arange(ctx_len, ctx_len + steps + 4, dtype=torch.int32, device="cuda")
+    pos = pos.repeat_interleave(B).reshape(-1, B).contiguous()
+    for i in range(3):
+        m.decode_dev(tok.data_ptr(), pos[i].data_ptr(), B, next_ptr=tok.data_ptr())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(3, 3 + steps):
+        m.decode_dev(tok.data_ptr(), pos[i].data_ptr(), B, next_ptr=tok.data_ptr())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    err = ctx.error_word()
+    m.close()
+    sb = step_bytes(cfg, B, ctx_len)
+    peak, _ = peaks()
+    return {"batch": B, "kv_ctx": ctx_len, "tok_s": B / (ms * 1e-3), "ms_per_step": ms,
+            "step_roofline_frac": sb["total"] / (ms * 1e-3) / 1e9 / peak, "device_error_word": err,
+            "how": f"fb_model_decode_dev, {steps} CUDA-graph steps after 3 warm-up steps, CUDA events"}
+
+
 def workload_config(args) -> dict:
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     par = f"tp{ws}" if use_tp(args) else ("replicas" if ws > 1 else "single-gpu")
@@ -448,7 +486,7 @@ def main():
     ap.add_argument("--timeline", action="store_true",
                     help="with --persistent: print the per-phase timeline of one eager step and exit")
     ap.add_argument("--no-prefill-extra", action="store_true",
-                    help="skip the 2048-token prefill measurement added to the N=1 decode line")
+                    help="skip the 2048-token prefill and batch-16 measurements added to the N=1 decode line")
     ap.add_argument("--prefill", type=int, default=0, metavar="T",
                     help="instead of decode: time a T-token prompt pass (then 64 greedy decode steps), 1 GPU")
     ap.add_argument("--prefill-gemm", type=int, default=0, metavar="T",
@@ -608,6 +646,7 @@ def main():
         line["clocks"] = clocks
     if ws == 1 and not args.no_prefill_extra and args.model == "qwen3-8b" and B == 1:
         line["prefill_2048"] = prefill_extra(model, cfg, stream)
+        line["batch16"] = batch_extra(ctx, cfg, stream, args.ctx)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.model == "qwen3-8b":
         model.close()
         torch.cuda.empty_cache()
