@@ -2,6 +2,7 @@
 // model runtime.  Not part of the public interface.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -158,6 +159,13 @@ void qmatmul_prefill(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y,
 // n a multiple of 128.
 bool prefill_gemm_supported(const fb_qtensor *w, int64_t m);
 void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m);
+// The same from fp16 rows xh [m][k] already scaled by powers of two
+// (rowscale[m], the rule of launch_x_to_f16 / the fused producers).
+void prefill_gemm_x16(fb_ctx *ctx, const fb_qtensor *w, const __half *xh, const float *rowscale, float *y,
+                      int64_t m);
+// x [m][k] f32 -> fp16 with a per-row power-of-two scale s (the smallest
+// 2^e, e >= 0, with max |x| / s <= 32768).
+void launch_x_to_f16(fb_ctx *ctx, const float *x, __half *xh, float *rowscale, int64_t m, int64_t k);
 void launch_block_dots(fb_ctx *ctx, const fb_qtensor *w, const Q8Act &a, int32_t *out_sc, int32_t *out_min);
 void launch_rmsnorm(fb_ctx *ctx, const float *x, const float *g, float *y, int64_t rows, int64_t dim, float eps);
 void launch_rope(fb_ctx *ctx, float *x, int64_t n_tok, int64_t n_heads, int64_t hd, int64_t pos0,
@@ -182,9 +190,13 @@ void launch_synth_kv(fb_ctx *ctx, void *pool, int layer, int which, int nctx, in
 void launch_embed_rows(fb_ctx *ctx, const fb_qtensor *emb, const int32_t *tokens, int T, int vocab, int dim,
                        float *x);
 // x += y (y may be null), xn = RMSNorm(x) * g, row by row
+// (xh, rs != null: also the normalized rows as the prefill GEMM's fp16
+// operand, see launch_x_to_f16; xn may then be null)
 void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float *g, float *xn, int T, int dim,
-                             float eps);
+                             float eps, __half *xh = nullptr, float *rs = nullptr);
 void launch_swiglu_rows(fb_ctx *ctx, const float *y, int f, int T, float *act);
+// SwiGLU rows straight into the fp16 operand of the next prefill GEMM.
+void launch_swiglu_rows_x16(fb_ctx *ctx, const float *y, int f, int T, __half *xh, float *rs);
 void launch_prefill_qkv_rope(fb_ctx *ctx, const float *y, int64_t ld, int T, int pos0, int n_heads, int n_kv,
                              const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
                              const float *rope_sin, int rope_mode, float *q_out, void *kpool, void *vpool,

@@ -117,6 +117,7 @@ struct fb_model {
     bool ds_ok = false, ds_on = false;
     // batched prefill buffers (allocated on first use, rows = pf_cap)
     DevBuf pf_tok, pf_x, pf_xn, pf_yd, pf_yqkv, pf_q, pf_attn, pf_ygu, pf_act;
+    DevBuf pf_xh, pf_rs;  // fp16 GEMM operand rows written by the norm / SwiGLU kernels, their row scales
     int pf_cap = 0;
 
     size_t kv_half_layer() const { return (size_t)num_pages * lc.n_kv_heads * kPage * c.head_dim; }
@@ -863,6 +864,8 @@ static void ensure_prefill(fb_model *m, int T) {
     m->pf_attn.alloc((size_t)T * qd * 4);
     m->pf_ygu.alloc((size_t)T * 2 * lc.ffn * 4);
     m->pf_act.alloc((size_t)T * lc.ffn * 4);
+    m->pf_xh.alloc((size_t)T * std::max<size_t>(H, lc.ffn) * 2);
+    m->pf_rs.alloc((size_t)T * 4);
     m->pf_cap = T;
 }
 
@@ -875,12 +878,24 @@ static void prefill_chunk(fb_model *m, int T, int pos0, float *all_logits = null
     float *x = m->pf_x.as<float>(), *xn = m->pf_xn.as<float>(), *yd = m->pf_yd.as<float>();
     const int32_t *bt = m->block_table.as<int32_t>();  // slot 0's row
     const float scale = (float)(1.0 / sqrt((double)c.head_dim));
+    __half *xh = m->pf_xh.as<__half>();
+    float *rs = m->pf_rs.as<float>();
+    // residual add + RMSNorm rows feeding a projection
+    auto norm_then_gemm = [&](const float *add, const float *gain, const fb_qtensor *w, float *out) {
+        if (prefill_gemm_supported(w, T)) {
+            launch_add_rmsnorm_rows(ctx, x, add, gain, nullptr, T, H, c.eps, xh, rs);
+            prefill_gemm_x16(ctx, w, xh, rs, out, T);
+        } else {
+            launch_add_rmsnorm_rows(ctx, x, add, gain, xn, T, H, c.eps);
+            qmatmul_prefill(ctx, w, xn, out, T);
+        }
+    };
     launch_embed_rows(ctx, m->tok_embd.t, m->pf_tok.as<int32_t>(), T, c.vocab, H, x);
     for (int l = 0; l < c.n_layers; l++) {
         Layer &L = *m->layers[l];
-        // x += down projection of the previous layer; xn = attn_norm(x)
-        launch_add_rmsnorm_rows(ctx, x, l ? yd : nullptr, L.attn_norm.as<float>(), xn, T, H, c.eps);
-        qmatmul_prefill(ctx, L.wqkv.t, xn, m->pf_yqkv.as<float>(), T);
+        // x += down projection of the previous layer; xn = attn_norm(x), as
+        // the fp16 GEMM operand when the projection takes the tensor-core path
+        norm_then_gemm(l ? yd : nullptr, L.attn_norm.as<float>(), L.wqkv.t, m->pf_yqkv.as<float>());
         launch_prefill_qkv_rope(ctx, m->pf_yqkv.as<float>(), qd + 2 * kd, T, pos0, lc.n_heads, lc.n_kv_heads,
                                 c.qk_norm ? L.q_norm.as<float>() : nullptr,
                                 c.qk_norm ? L.k_norm.as<float>() : nullptr, c.eps, m->rope_cos.as<float>(),
@@ -889,10 +904,14 @@ static void prefill_chunk(fb_model *m, int T, int pos0, float *all_logits = null
         launch_attn_prefill(ctx, m->pf_q.as<float>(), m->kpool(l), m->vpool(l), bt, m->pages_per_seq, m->num_pages,
                             pos0, T, lc.n_heads, lc.n_kv_heads, scale, m->pf_attn.as<float>());
         qmatmul_prefill(ctx, L.wo.t, m->pf_attn.as<float>(), yd, T);
-        launch_add_rmsnorm_rows(ctx, x, yd, L.ffn_norm.as<float>(), xn, T, H, c.eps);
-        qmatmul_prefill(ctx, L.wgu.t, xn, m->pf_ygu.as<float>(), T);
-        launch_swiglu_rows(ctx, m->pf_ygu.as<float>(), F, T, m->pf_act.as<float>());
-        qmatmul_prefill(ctx, L.wdown.t, m->pf_act.as<float>(), yd, T);
+        norm_then_gemm(yd, L.ffn_norm.as<float>(), L.wgu.t, m->pf_ygu.as<float>());
+        if (prefill_gemm_supported(L.wdown.t, T)) {
+            launch_swiglu_rows_x16(ctx, m->pf_ygu.as<float>(), F, T, xh, rs);
+            prefill_gemm_x16(ctx, L.wdown.t, xh, rs, yd, T);
+        } else {
+            launch_swiglu_rows(ctx, m->pf_ygu.as<float>(), F, T, m->pf_act.as<float>());
+            qmatmul_prefill(ctx, L.wdown.t, m->pf_act.as<float>(), yd, T);
+        }
     }
     if (all_logits) {
         launch_add_rmsnorm_rows(ctx, x, yd, m->out_norm.as<float>(), xn, T, H, c.eps);

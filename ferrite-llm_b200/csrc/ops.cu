@@ -357,13 +357,34 @@ __global__ void __launch_bounds__(256) k_embed_rows(const uint8_t *__restrict__ 
         x[row * dim + i] = q4k_value(emb + q4k_offset(tok, i / QK, nbe), i % QK);
 }
 
+// The fp16 operand of the prefill GEMM from one row's values (one 256-thread
+// CTA per row; value(i) recomputes them): the power-of-two scale s = 2^e, the
+// smallest e >= 0 with max |v| / s <= 32768, into *rs and fp16(v / s) into
+// xh -- the rule of launch_x_to_f16, so the operands are the same bits.
+template <class F>
+__device__ __forceinline__ void x16_row_store(float amax, float *shm, F value, int dim, __half *xh, float *rs) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if ((threadIdx.x & 31) == 0) shm[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = shm[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) amax = fmaxf(amax, shm[w]);
+    int e = 0;
+    while (e < 120 && amax > ldexpf(32768.f, e)) e++;
+    const float inv = ldexpf(1.f, -e);
+    if (threadIdx.x == 0) *rs = ldexpf(1.f, e);
+    for (int i = threadIdx.x; i < dim; i += 256) xh[i] = __float2half_rn(__fmul_rn(value(i), inv));
+}
+
 // x[t] (+= y[t] when y != null), xn[t] = RMSNorm(x[t]) * g: the decode
 // step's residual + RMSNorm arithmetic (binary64 sum of squares), without
 // the Q8_K quantization.  One CTA per row.
 __global__ void __launch_bounds__(256) k_add_rmsnorm_rows(float *__restrict__ x, const float *__restrict__ y,
                                                           const float *__restrict__ g, float *__restrict__ xn, int dim,
-                                                          float eps) {
+                                                          float eps, __half *__restrict__ xh, float *__restrict__ rs) {
     __shared__ double sh[8];
+    __shared__ float shm[8];
     const int64_t row = blockIdx.x;
     float *xr = x + row * dim;
     double ss = 0.0;
@@ -377,7 +398,14 @@ __global__ void __launch_bounds__(256) k_add_rmsnorm_rows(float *__restrict__ x,
     }
     ss = block_sum64<8>(ss, sh);
     const float m = rms_of(ss, dim, eps);
-    for (int i = threadIdx.x; i < dim; i += 256) xn[row * dim + i] = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        const float v = __fmul_rn(__fdiv_rn(xr[i], m), g[i]);
+        if (xn) xn[row * dim + i] = v;
+        amax = fmaxf(amax, fabsf(v));
+    }
+    if (xh) x16_row_store(amax, shm, [&](int i) { return __fmul_rn(__fdiv_rn(xr[i], m), g[i]); }, dim,
+                          xh + row * dim, rs + row);
 }
 
 // act[t][i] = silu(gate) * up for the rows y[t] = [gate (f) | up (f)]
@@ -393,6 +421,27 @@ __global__ void __launch_bounds__(256) k_swiglu_rows(const float *__restrict__ y
     const float4 u = *reinterpret_cast<const float4 *>(y + r * 2 * f + f + c);
     auto sw = [](float gv, float uv) { return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv); };
     *reinterpret_cast<float4 *>(act + r * f + c) = make_float4(sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
+}
+
+// The same SwiGLU as the fp16 operand of the down projection, no f32
+// output: one CTA per row, the row's values computed once (float4 loads)
+// into shared memory, then scaled and stored by x16_row_store.
+__global__ void __launch_bounds__(256) k_swiglu_rows_x16(const float *__restrict__ y, int f,
+                                                         __half *__restrict__ xh, float *__restrict__ rs) {
+    extern __shared__ float act[];  // [f]
+    __shared__ float shm[8];
+    const int64_t r = blockIdx.x;
+    const float4 *g4 = reinterpret_cast<const float4 *>(y + r * 2 * f), *u4 = g4 + f / 4;
+    auto sw = [](float gv, float uv) { return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv); };
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < f / 4; i += 256) {
+        const float4 g = g4[i], u = u4[i];
+        const float4 a = make_float4(sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
+        reinterpret_cast<float4 *>(act)[i] = a;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+    }
+    // (x16_row_store's first __syncthreads also orders these writes before its reads)
+    x16_row_store(amax, shm, [&](int i) { return act[i]; }, f, xh + r * f, rs + r);
 }
 
 // Prefill prologue of attention for T new tokens at positions pos0 + t: one
@@ -450,8 +499,17 @@ void launch_embed_rows(fb_ctx *ctx, const fb_qtensor *emb, const int32_t *tokens
 }
 
 void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float *g, float *xn, int T, int dim,
-                             float eps) {
-    k_add_rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(x, y, g, xn, dim, eps);
+                             float eps, __half *xh, float *rs) {
+    FB_REQUIRE(xn || (xh && rs), "add_rmsnorm_rows: no output");
+    k_add_rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(x, y, g, xn, dim, eps, xh, rs);
+    FB_CUDA(cudaGetLastError());
+}
+
+void launch_swiglu_rows_x16(fb_ctx *ctx, const float *y, int f, int T, __half *xh, float *rs) {
+    FB_REQUIRE(f % 4 == 0 && (size_t)f * 4 <= 200 * 1024, "swiglu_rows_x16: f must be a multiple of 4, <= 51200");
+    const size_t smem = (size_t)f * 4;
+    FB_CUDA(cudaFuncSetAttribute(k_swiglu_rows_x16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_swiglu_rows_x16<<<(unsigned)T, 256, smem, ctx->stream>>>(y, f, xh, rs);
     FB_CUDA(cudaGetLastError());
 }
 

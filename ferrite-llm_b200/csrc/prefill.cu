@@ -596,27 +596,24 @@ static const __half *prefill_weight_cache(fb_ctx *ctx, const fb_qtensor *w) {
     return mw->f16.ptr ? mw->f16.as<__half>() : nullptr;
 }
 
-void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
-    FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
+// Y = rowscale * (Xh . Wh^T) from fp16 rows Xh [m][K] and their power-of-two
+// scales; wtmp: scratch for the weights' fp16 chunk (null: taken from the
+// context's workspace, which must then not hold Xh).
+static void prefill_gemm_impl(fb_ctx *ctx, const fb_qtensor *w, const __half *xh, const float *rowscale, float *y,
+                              int64_t m, __half *wtmp) {
     const int64_t K = w->k, N = w->n;
     const bool two_pass = m >= PF_TWO_PASS_MIN_ROWS;
     const __half *wcache = two_pass ? prefill_weight_cache(ctx, w) : nullptr;
     const int64_t chunk = two_pass ? (wcache ? N : two_pass_chunk_rows(N, K)) : 0;
-    const size_t xh_bytes = ((size_t)m * K * 2 + 255) & ~(size_t)255;
-    const size_t rs_bytes = ((size_t)m * 4 + 255) & ~(size_t)255;
-    uint8_t *scratch =
-        static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + rs_bytes + (wcache ? 0 : (size_t)chunk * K * 2)));
-    __half *xh = reinterpret_cast<__half *>(scratch);
-    float *rowscale = reinterpret_cast<float *>(scratch + xh_bytes);
-    k_x_to_f16<<<(unsigned)((m + 7) / 8), 256, 0, ctx->stream>>>(x, xh, rowscale, (int)m, K);
-    FB_CUDA(cudaGetLastError());
+    if (two_pass && !wcache && !wtmp)
+        wtmp = static_cast<__half *>(ctx->ensure_scratch((size_t)chunk * K * 2));
     if (!two_pass) {
         const CUtensorMap map = f16_map(xh, m, K, PF_BM);
         if (w->dtype == FB_Q4_K) launch_prefill_dt<4>(ctx, w, map, rowscale, y, (int)m);
         else launch_prefill_dt<6>(ctx, w, map, rowscale, y, (int)m);
         return;
     }
-    __half *wh = reinterpret_cast<__half *>(scratch + xh_bytes + rs_bytes);
+    __half *wh = wtmp;
     const CUtensorMap xmap = f16_map(xh, m, K, GM_BM);
     static std::once_flag once;
     std::call_once(once, [] {
@@ -662,6 +659,36 @@ void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, in
         }
         FB_CUDA(cudaGetLastError());
     }
+}
+
+void prefill_gemm(fb_ctx *ctx, const fb_qtensor *w, const float *x, float *y, int64_t m) {
+    FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
+    const int64_t K = w->k, N = w->n;
+    const bool two_pass = m >= PF_TWO_PASS_MIN_ROWS;
+    // the fp16 chunk of the weights shares the workspace with Xh: reserve it
+    // unless a cached copy exists (a copy made by this call is allocated on
+    // its own and leaves the reserved chunk unused)
+    const bool cached = two_pass && ctx->prefill_cache && w->f16.ptr;
+    const int64_t chunk = two_pass && !cached ? two_pass_chunk_rows(N, K) : 0;
+    const size_t xh_bytes = ((size_t)m * K * 2 + 255) & ~(size_t)255;
+    const size_t rs_bytes = ((size_t)m * 4 + 255) & ~(size_t)255;
+    uint8_t *scratch = static_cast<uint8_t *>(ctx->ensure_scratch(xh_bytes + rs_bytes + (size_t)chunk * K * 2));
+    __half *xh = reinterpret_cast<__half *>(scratch);
+    float *rowscale = reinterpret_cast<float *>(scratch + xh_bytes);
+    launch_x_to_f16(ctx, x, xh, rowscale, m, K);
+    prefill_gemm_impl(ctx, w, xh, rowscale, y, m,
+                      chunk ? reinterpret_cast<__half *>(scratch + xh_bytes + rs_bytes) : nullptr);
+}
+
+void prefill_gemm_x16(fb_ctx *ctx, const fb_qtensor *w, const __half *xh, const float *rowscale, float *y,
+                      int64_t m) {
+    FB_REQUIRE(prefill_gemm_supported(w, m), "prefill gemm: unsupported shape");
+    prefill_gemm_impl(ctx, w, xh, rowscale, y, m, nullptr);
+}
+
+void launch_x_to_f16(fb_ctx *ctx, const float *x, __half *xh, float *rowscale, int64_t m, int64_t K) {
+    k_x_to_f16<<<(unsigned)((m + 7) / 8), 256, 0, ctx->stream>>>(x, xh, rowscale, (int)m, K);
+    FB_CUDA(cudaGetLastError());
 }
 
 }  // namespace fb

@@ -94,3 +94,32 @@ def test_two_pass_equals_fused(fbctx, torch_cuda, dtype, n, k):
     fused = run(fbctx, torch_cuda, dtype, n, k, w, x[:333])
     two = run(fbctx, torch_cuda, dtype, n, k, w, x)
     assert np.array_equal(fused, two[:333])
+
+
+@pytest.mark.parametrize("dtype,n,k", [(O.Q4_K, 1024, 4096), (O.Q6_K, 4096, 12288)])
+def test_prefill_weight_cache_bit_identical(fbctx, torch_cuda, dtype, n, k):
+    """From 512 rows the first pass over a tensor keeps its fp16 copy
+    (fb_ctx_set_prefill_weight_cache, on by default) and later passes skip the
+    dequantization: the cache-filling pass, a cached pass and a run with the
+    cache off must give the same bits."""
+    torch = torch_cuda
+    w = gaussian_qweight(dtype, n, k, seed=2 * n + k)
+    x = np.random.default_rng(21).normal(0, 1, (640, k)).astype(np.float32)
+    t = fb.QTensor.upload(fbctx, dtype, n, k, w)
+    xd = torch.from_numpy(x).cuda()
+
+    def once():
+        y = torch.full((640, n), float("nan"), dtype=torch.float32, device="cuda")
+        fb.QMatMul(t).forward(xd.data_ptr(), y.data_ptr(), 640)
+        torch.cuda.synchronize()
+        return y.cpu().numpy()
+
+    try:
+        fbctx.set_prefill_weight_cache(False)
+        off = once()
+        fbctx.set_prefill_weight_cache(True)
+        fill, cached = once(), once()
+    finally:
+        fbctx.set_prefill_weight_cache(True)
+    assert fbctx.error_word() == 0
+    assert np.array_equal(off, fill) and np.array_equal(fill, cached)
