@@ -805,8 +805,11 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
         const int PPC = ATT_CHUNK / A.page_size;
         const int64_t nch = (max_seq_len + ATT_CHUNK - 1) / ATT_CHUNK;
         const int64_t nch_cap = ((int64_t)A.max_pages * A.page_size + ATT_CHUNK - 1) / ATT_CHUNK;
+        // at most ATT_MERGE1_MAX splits (one-level merge) unless the block
+        // table needs more: with one or two kv heads per GPU (tensor
+        // parallel) more splits only lengthen the merge of a small K/V
         int64_t want = std::min<int64_t>({(int64_t)ctx->num_sms / ((int64_t)A.n_kv * batch), (int64_t)A.nsplit_max,
-                                          (int64_t)ATT_SPLITS_MAX, nch});
+                                          (int64_t)ATT_MERGE1_MAX, nch});
         const int64_t lo = std::max<int64_t>(1, (nch_cap * PPC + ATT_BT_MAX - 1) / ATT_BT_MAX);
         want = std::max(want, lo);
         if (want > ATT_MERGE1_MAX) {
