@@ -158,7 +158,7 @@ __device__ __forceinline__ void lds_f32(float (&v)[G], const float *p) {
 template <int G, bool CLUSTER>
 __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     k_attn_decode(AttnArgs A, float *__restrict__ out_f32, Q8Act aq, int use_q8, int *__restrict__ counters,
-                  int depth, int bt_cap) {
+                  int bt_cap) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[ATT_MAX_DEPTH];
     __shared__ int used[ATT_MAX_DEPTH];  // units consumed per stage (the fourth of a chunk refills it)
@@ -175,7 +175,11 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     if constexpr (CLUSTER) cluster_arrive_relaxed();
     const int rank = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    // ring stages (a compile-time constant: the stage and phase of chunk j
+    // are bit operations, not divisions, in the unit loop)
+    constexpr int depth = att_depth(CLUSTER);
     const int P = A.page_size, PPC = ATT_CHUNK / P;  // pages per chunk
+    const int lgP = P == 64 ? 6 : 5;                 // page sizes 32 and 64 (checked on the host)
     const AttnLayout Ly = attn_layout(G, NW, depth, bt_cap);
     uint8_t *ring = smem;
     float *q_s = reinterpret_cast<float *>(smem + Ly.q);
@@ -246,7 +250,8 @@ __global__ void __launch_bounds__(32 * att_warps(G, CLUSTER), 1)
     const uint32_t KQS = pbytes / 4 + ATT_QPAD;               // staged K quarter stride (32 dims)
     const uint32_t KROW = 2u * P;                             // bytes between consecutive dims
     auto k_at = [&](uint8_t *kst, int d, int tc) -> __half * {  // staged K element (dim d, chunk token tc)
-        return reinterpret_cast<__half *>(kst + (tc / P) * KPG + (d >> 5) * KQS + (d & 31) * KROW + (tc % P) * 2);
+        return reinterpret_cast<__half *>(kst + (tc >> lgP) * KPG + (d >> 5) * KQS + (d & 31) * KROW +
+                                          (tc & (P - 1)) * 2);
     };
     // copy `piece` (0..3: the K quarters, 4: the V page) of page i of chunk j
     // into stage j % depth
@@ -843,11 +848,11 @@ static void launch_attn_g(fb_ctx *ctx, const AttnArgs &A, int batch, int max_seq
         auto kern = k_attn_decode<G, true>;
         FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, depth, bt_cap));
+        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, bt_cap));
     } else {
         auto kern = k_attn_decode<G, false>;
         FB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, depth, bt_cap));
+        FB_CUDA(cudaLaunchKernelEx(&cfg, kern, A, out_f32, q, aq ? 1 : 0, counters, bt_cap));
     }
 }
 

@@ -313,18 +313,28 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
         }
     }
     __syncthreads();
-    int issued = 0;
+    // producer (lane 0): records issued, and the next record's stage and
+    // global address, advanced incrementally (record c = tile c / nmine,
+    // super-block bbeg + c % nmine of that tile, stage c % DEPTH; a runtime
+    // division per record measurably slows the decode step)
+    int issued = 0, p_slot = 0, p_bl = 0;
+    const uint8_t *p_src = W + ((size_t)blockIdx.x * nb + bbeg) * REC;
+    const size_t tile_step = ((size_t)gridDim.x * nb - (size_t)nmine) * REC;  // last record of a tile -> first of the next
     const uint64_t wpol = l2_evict_first_policy();  // weights are read once per step
-    auto issue = [&](int c) {
-        const int ti = c / nmine, bl = c - ti * nmine;
-        const int64_t T = (int64_t)blockIdx.x + (int64_t)ti * gridDim.x;
-        const int slot = c % DEPTH;
-        mbar_expect_tx(&wbar[slot], REC);
-        bulk_g2s_stream(ring + (size_t)slot * REC, W + ((size_t)T * nb + bbeg + bl) * REC, REC, &wbar[slot], wpol);
+    auto issue = [&]() {
+        mbar_expect_tx(&wbar[p_slot], REC);
+        bulk_g2s_stream(ring + (size_t)p_slot * REC, p_src, REC, &wbar[p_slot], wpol);
+        issued++;
+        if (++p_slot == DEPTH) p_slot = 0;
+        p_src += REC;
+        if (++p_bl == nmine) {
+            p_bl = 0;
+            p_src += tile_step;
+        }
     };
     // weights do not depend on the previous kernel: start streaming them now
     if (lane == 0)
-        for (; issued < DEPTH && issued < total; issued++) issue(issued);
+        while (issued < DEPTH && issued < total) issue();
     pdl_wait();
     pdl_launch();  // let the next kernel start streaming its weights
     // row-parallel shard: the sequence number tagging this exchange's words
@@ -355,6 +365,8 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
     }
     const bool act_ok = ok;
     int c = 0, waited = 0;  // records visited / records whose copy has landed
+    int slot = 0;           // c % DEPTH
+    uint32_t par = 0;       // (c / DEPTH) & 1
     for (int ti = 0; ti < ntl; ti++) {
         const int64_t row0 = ((int64_t)blockIdx.x + (int64_t)ti * gridDim.x) * 16;
         double acc[NTA][4];
@@ -366,9 +378,8 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
 #pragma unroll
         for (int c2 = 0; c2 < M; c2++) accd[c2] = 0.0;
         for (int bl = 0; bl < nmine; bl++, c++) {
-            const int slot = c % DEPTH;
             if (ok) {
-                ok = mbar_wait_bounded(&wbar[slot], (uint32_t)(c / DEPTH) & 1u);
+                ok = mbar_wait_bounded(&wbar[slot], par);
                 if (ok) waited = c + 1;
             }
             if (ok) {
@@ -388,7 +399,11 @@ __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W,
             __syncwarp();
             if (lane == 0 && ok && issued < total) {
                 fence_proxy_async_smem();  // our reads of this stage precede the refill
-                issue(issued++);
+                issue();
+            }
+            if (++slot == DEPTH) {
+                slot = 0;
+                par ^= 1u;
             }
         }
         if (!ok && lane == 0) {

@@ -58,6 +58,24 @@ def test_ragged_shapes(fbctx, torch_cuda, dtype, n, k, m):
     assert_close(got, O.qmatmul(dtype, w, n, k, x), what=f"{dtype} {n}x{k} m={m}")
 
 
+@pytest.mark.parametrize("m", [5, 9, 13, 16])
+@pytest.mark.parametrize("n,k", [(2368, 4096), (2400, 2560), (4096, 1024)])
+def test_mma_path_many_tiles(fbctx, torch_cuda, n, k, m):
+    """Q4_K with m = 5..16 (the tensor-core consumer) and at least one
+    16-row tile per SM, so CTAs loop over several tiles and the record ring
+    wraps across tiles (k = 2560: 10 super-blocks, not a multiple of the
+    warps per CTA).  The row sums are the oracle's binary64 sums rounded
+    once, element for element."""
+    w = gaussian_qweight(O.Q4_K, n, k, seed=3 * n + k)
+    x = np.random.default_rng(m + n).normal(0, 1, (m, k)).astype(np.float32)
+    x[m - 1, 256:512] = 0.0  # an all-zero activation block in the last row
+    got = run(fbctx, torch_cuda, O.Q4_K, n, k, m, w, x)
+    ref = O.qmatmul(O.Q4_K, w, n, k, x)
+    assert_close(got, ref, what=f"staged {n}x{k} m={m}")
+    same = np.mean(got.view(np.uint32) == ref.view(np.uint32))
+    assert same >= 0.9999, f"{same:.6f} of the outputs bit-identical"
+
+
 def test_batch_rows_independent(fbctx, torch_cuda):
     """Each activation row's result does not depend on the other rows."""
     n, k = 512, 1024
