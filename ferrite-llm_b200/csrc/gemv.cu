@@ -280,7 +280,7 @@ template <int DT, int NT, bool DOTS, int KS>
 __global__ void __launch_bounds__(KS * 32) k_gemv(const uint8_t *__restrict__ W, int64_t n, int nb, int n_tiles,
                                                   Q8Act a, int m, float *__restrict__ y, int64_t ldy,
                                                   int32_t *__restrict__ dots_sc, int32_t *__restrict__ dots_min,
-                                                  uint32_t *err, int depth, PeerOut po) {
+                                                  uint32_t *err, int depth, const __grid_constant__ PeerOut po) {
     constexpr int REC = QRec<DT>::bytes;
     const int DEPTH = depth;
     constexpr bool DP4A = NT < 0;

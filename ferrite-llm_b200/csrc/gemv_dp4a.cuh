@@ -16,6 +16,14 @@ namespace fb {
 // bank-conflict-free.  Both halves' integer partials are added with one
 // shuffle before the binary64 combine.
 __device__ __forceinline__ int dp4(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+// Unsigned bytes of a times signed bytes of b: with a = w & 0xF0F0F0F0 the
+// high nibbles enter as 16 * q without a shift; the sum is then an exact
+// multiple of 16 and one arithmetic shift recovers the nibble dot.
+__device__ __forceinline__ int dp4us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 template <int M, bool DOTS>
 __device__ __forceinline__ void q4k_block_dp4a(const uint8_t *rec, const Q8Act &a, int b, int nb, int lane,
@@ -42,13 +50,16 @@ __device__ __forceinline__ void q4k_block_dp4a(const uint8_t *rec, const Q8Act &
             const uint4 w = wq[t];
             dot[0] = dp4(w.x & 0x0F0F0F0Fu, a0.x, dot[0]);
             dot[0] = dp4(w.y & 0x0F0F0F0Fu, a0.y, dot[0]);
-            dot[1] = dp4((w.x >> 4) & 0x0F0F0F0Fu, a0.z, dot[1]);
-            dot[1] = dp4((w.y >> 4) & 0x0F0F0F0Fu, a0.w, dot[1]);
+            dot[1] = dp4us(w.x & 0xF0F0F0F0u, a0.z, dot[1]);  // 16 x (high-nibble dot)
+            dot[1] = dp4us(w.y & 0xF0F0F0F0u, a0.w, dot[1]);
             dot[2] = dp4(w.z & 0x0F0F0F0Fu, a1.x, dot[2]);
             dot[2] = dp4(w.w & 0x0F0F0F0Fu, a1.y, dot[2]);
-            dot[3] = dp4((w.z >> 4) & 0x0F0F0F0Fu, a1.z, dot[3]);
-            dot[3] = dp4((w.w >> 4) & 0x0F0F0F0Fu, a1.w, dot[3]);
+            dot[3] = dp4us(w.z & 0xF0F0F0F0u, a1.z, dot[3]);
+            dot[3] = dp4us(w.w & 0xF0F0F0F0u, a1.w, dot[3]);
         }
+        // |16 x dot| <= 4 * 8 * 240 * 128 < 2^31: exact, a multiple of 16
+        dot[1] >>= 4;
+        dot[3] >>= 4;
         int isum = byte_of(scw, 0) * dot[0] + byte_of(scw, 1) * dot[1] + byte_of(scw, 2) * dot[2] +
                    byte_of(scw, 3) * dot[3];
         // mins: bs32 of sub-blocks 4h..4h+3 (two int16 pairs)
