@@ -361,8 +361,8 @@ __global__ void __launch_bounds__(256) k_embed_rows(const uint8_t *__restrict__ 
 // CTA per row; value(i) recomputes them): the power-of-two scale s = 2^e, the
 // smallest e >= 0 with max |v| / s <= 32768, into *rs and fp16(v / s) into
 // xh -- the rule of launch_x_to_f16, so the operands are the same bits.
-template <class F>
-__device__ __forceinline__ void x16_row_store(float amax, float *shm, F value, int dim, __half *xh, float *rs) {
+// The exponent e of that scale from each thread's partial max |v|.
+__device__ __forceinline__ int x16_row_exponent(float amax, float *shm) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     if ((threadIdx.x & 31) == 0) shm[threadIdx.x >> 5] = amax;
@@ -372,6 +372,11 @@ __device__ __forceinline__ void x16_row_store(float amax, float *shm, F value, i
     for (int w = 1; w < 8; w++) amax = fmaxf(amax, shm[w]);
     int e = 0;
     while (e < 120 && amax > ldexpf(32768.f, e)) e++;
+    return e;
+}
+template <class F>
+__device__ __forceinline__ void x16_row_store(float amax, float *shm, F value, int dim, __half *xh, float *rs) {
+    const int e = x16_row_exponent(amax, shm);
     const float inv = ldexpf(1.f, -e);
     if (threadIdx.x == 0) *rs = ldexpf(1.f, e);
     for (int i = threadIdx.x; i < dim; i += 256) xh[i] = __float2half_rn(__fmul_rn(value(i), inv));
@@ -406,6 +411,84 @@ __global__ void __launch_bounds__(256) k_add_rmsnorm_rows(float *__restrict__ x,
     }
     if (xh) x16_row_store(amax, shm, [&](int i) { return __fmul_rn(__fdiv_rn(xr[i], m), g[i]); }, dim,
                           xh + row * dim, rs + row);
+}
+
+// The same rows with the row held in registers (dim <= 1024 P, dim % 4 ==
+// 0): float4 loads, x and y read once, one division per value.  The sum of
+// squares runs in the order of the decode step's k_residual_rmsnorm_q8k
+// (thread t: float4s t, t + 256, ...; x, y, z, w in order; then the block
+// tree), so a prompt row normalizes to the same bits as a decoded one.
+template <int P>
+__global__ void __launch_bounds__(256) k_add_rmsnorm_rows4(float *__restrict__ x, const float *__restrict__ y,
+                                                           const float *__restrict__ g, float *__restrict__ xn,
+                                                           int dim, float eps, __half *__restrict__ xh,
+                                                           float *__restrict__ rs) {
+    __shared__ double sh[8];
+    __shared__ float shm[8];
+    const int64_t row = blockIdx.x;
+    float4 *x4 = reinterpret_cast<float4 *>(x + row * dim);
+    const int nv = dim / 4;
+    float4 v[P];
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+        const int i = threadIdx.x + p * 256;
+        v[p] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (y) {
+        const float4 *y4 = reinterpret_cast<const float4 *>(y + row * dim);
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int i = threadIdx.x + p * 256;
+            if (i < nv) {
+                const float4 d = y4[i];
+                v[p] = make_float4(__fadd_rn(d.x, v[p].x), __fadd_rn(d.y, v[p].y), __fadd_rn(d.z, v[p].z),
+                                   __fadd_rn(d.w, v[p].w));
+                x4[i] = v[p];
+            }
+        }
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+        if (threadIdx.x + p * 256 < nv) {
+            ss = __fma_rn((double)v[p].x, (double)v[p].x, ss);
+            ss = __fma_rn((double)v[p].y, (double)v[p].y, ss);
+            ss = __fma_rn((double)v[p].z, (double)v[p].z, ss);
+            ss = __fma_rn((double)v[p].w, (double)v[p].w, ss);
+        }
+    }
+    ss = block_sum64<8>(ss, sh);
+    const float m = rms_of(ss, dim, eps);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    float amax = 0.f;
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+        const int i = threadIdx.x + p * 256;
+        if (i < nv) {
+            const float4 gg = g4[i];
+            v[p] = make_float4(__fmul_rn(__fdiv_rn(v[p].x, m), gg.x), __fmul_rn(__fdiv_rn(v[p].y, m), gg.y),
+                               __fmul_rn(__fdiv_rn(v[p].z, m), gg.z), __fmul_rn(__fdiv_rn(v[p].w, m), gg.w));
+            if (xn) reinterpret_cast<float4 *>(xn + row * dim)[i] = v[p];
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[p].x), fabsf(v[p].y)), fmaxf(fabsf(v[p].z), fabsf(v[p].w))));
+        }
+    }
+    if (xh) {
+        const int e = x16_row_exponent(amax, shm);
+        const float inv = ldexpf(1.f, -e);
+        if (threadIdx.x == 0) rs[row] = ldexpf(1.f, e);
+        uint2 *xh4 = reinterpret_cast<uint2 *>(xh + row * dim);
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int i = threadIdx.x + p * 256;
+            if (i < nv) {
+                const __half2 a = __halves2half2(__float2half_rn(__fmul_rn(v[p].x, inv)),
+                                                 __float2half_rn(__fmul_rn(v[p].y, inv)));
+                const __half2 b = __halves2half2(__float2half_rn(__fmul_rn(v[p].z, inv)),
+                                                 __float2half_rn(__fmul_rn(v[p].w, inv)));
+                xh4[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+            }
+        }
+    }
 }
 
 // act[t][i] = silu(gate) * up for the rows y[t] = [gate (f) | up (f)]
@@ -444,11 +527,16 @@ __global__ void __launch_bounds__(256) k_swiglu_rows_x16(const float *__restrict
     x16_row_store(amax, shm, [&](int i) { return act[i]; }, f, xh + r * f, rs + r);
 }
 
-// Prefill prologue of attention for T new tokens at positions pos0 + t: one
-// warp per (token, head) of the projection output y[t] = (q | k | v): QK
-// RMSNorm (optional) and RoPE of q (-> q_out f32 [T][n_heads][hd]) and k,
-// and the fp16 KV-cache write of k (dim-major pages) and v (token-major) --
-// the decode attention prologue's arithmetic, token by token.
+// Prefill prologue of attention for T new tokens at positions pos0 + t, per
+// (token, head) of the projection output y[t] = (q | k | v): QK RMSNorm
+// (optional) and RoPE of q (-> q_out f32 [T][n_heads][hd]) and k, and the
+// fp16 KV-cache write of k (dim-major pages) and v (token-major) -- the decode
+// attention prologue's arithmetic, token by token.  One CTA per (32
+// consecutive tokens, head); warp w takes tokens w, w + 8, w + 16, w + 24 of
+// the group and issues their loads before the arithmetic.  A k head's values
+// pass through shared memory so that each dim row of a page is written as
+// consecutive tokens (64 contiguous bytes per warp, not 2-byte scatter).
+constexpr int QR_TT = 32;  // tokens per CTA
 __global__ void __launch_bounds__(256) k_prefill_qkv_rope(const float *__restrict__ y, int64_t ld, int T, int pos0,
                                                           int n_heads, int n_kv, const float *__restrict__ q_norm,
                                                           const float *__restrict__ k_norm, float eps,
@@ -457,37 +545,89 @@ __global__ void __launch_bounds__(256) k_prefill_qkv_rope(const float *__restric
                                                           float *__restrict__ q_out, __half *__restrict__ kpool,
                                                           __half *__restrict__ vpool, const int32_t *__restrict__ bt,
                                                           int page_size, int num_pages, uint32_t *err) {
-    const int lane = threadIdx.x & 31;
-    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int nh = n_heads + 2 * n_kv;
-    if (wid >= (int64_t)T * nh) return;
-    const int t = (int)(wid / nh), hh = (int)(wid % nh);
-    const int p = pos0 + t;
+    constexpr int TPW = QR_TT / 8;          // tokens per warp
+    __shared__ __half kst[128][QR_TT + 1];  // k head: [dim][token of the group]
+    __shared__ int s_page[QR_TT], s_slot[QR_TT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hh = blockIdx.y, t0 = blockIdx.x * QR_TT;
     const bool is_q = hh < n_heads, is_k = !is_q && hh < n_heads + n_kv;
-    const float4 x4 = *reinterpret_cast<const float4 *>(y + (int64_t)t * ld + (int64_t)hh * 128 + 4 * lane);
-    float v[4] = {x4.x, x4.y, x4.z, x4.w};
+    const int kvh = is_k ? hh - n_heads : hh - n_heads - n_kv;
+    if (!is_q && threadIdx.x < QR_TT) {
+        // cache page and slot of each token of the group (-1: not written)
+        const int t = t0 + (int)threadIdx.x;
+        int page = -1, slot = 0;
+        if (t < T) {
+            const int p = pos0 + t;
+            page = bt[p / page_size];
+            slot = p % page_size;
+            if (page < 0 || page >= num_pages) {
+                atomicOr(err, ERRBIT_BAD_PAGE);
+                page = -1;
+            }
+        }
+        s_page[threadIdx.x] = page;
+        s_slot[threadIdx.x] = slot;
+    }
+    float v[TPW][4];
+#pragma unroll
+    for (int i = 0; i < TPW; i++) {
+        const int t = t0 + warp + 8 * i;
+        const float4 x4 = t < T ? *reinterpret_cast<const float4 *>(y + (int64_t)t * ld + (int64_t)hh * 128 + 4 * lane)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i][0] = x4.x;
+        v[i][1] = x4.y;
+        v[i][2] = x4.z;
+        v[i][3] = x4.w;
+    }
     if (is_q || is_k) {
-        const QkHead qh = qk_head_load(lane, q_norm ? (is_q ? q_norm : k_norm) : nullptr, rope_cos + (int64_t)p * 64,
-                                       rope_sin + (int64_t)p * 64, rope_mode);
-        qk_head_apply(v, lane, qh, eps, rope_mode);
+#pragma unroll
+        for (int i = 0; i < TPW; i++) {
+            const int t = t0 + warp + 8 * i;
+            if (t < T) {  // warp-uniform
+                const int p = pos0 + t;
+                const QkHead qh = qk_head_load(lane, q_norm ? (is_q ? q_norm : k_norm) : nullptr,
+                                               rope_cos + (int64_t)p * 64, rope_sin + (int64_t)p * 64, rope_mode);
+                qk_head_apply(v[i], lane, qh, eps, rope_mode);
+            }
+        }
     }
     if (is_q) {
-        *reinterpret_cast<float4 *>(q_out + ((int64_t)t * n_heads + hh) * 128 + 4 * lane) =
-            make_float4(v[0], v[1], v[2], v[3]);
-        return;
-    }
-    const int kvh = is_k ? hh - n_heads : hh - n_heads - n_kv;
-    const int page = bt[p / page_size], slot = p % page_size;
-    if (page < 0 || page >= num_pages) {
-        if (lane == 0) atomicOr(err, ERRBIT_BAD_PAGE);
-        return;
-    }
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const int d = 4 * lane + e;
-        const __half h = __float2half_rn(v[e]);
-        if (is_k) kpool[(((size_t)page * n_kv + kvh) * 128 + d) * page_size + slot] = h;
-        else vpool[(((size_t)page * n_kv + kvh) * page_size + slot) * 128 + d] = h;
+        for (int i = 0; i < TPW; i++) {
+            const int t = t0 + warp + 8 * i;
+            if (t < T)
+                *reinterpret_cast<float4 *>(q_out + ((int64_t)t * n_heads + hh) * 128 + 4 * lane) =
+                    make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        }
+        return;  // uniform over the CTA: no barrier follows for q heads
+    }
+    if (is_k) {
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) kst[4 * lane + e][warp + 8 * i] = __float2half_rn(v[i][e]);
+    }
+    __syncthreads();  // s_page / s_slot, and the k tile
+    if (!is_k) {
+        // v: token-major pages, 8 bytes per lane and token
+#pragma unroll
+        for (int i = 0; i < TPW; i++) {
+            const int tl = warp + 8 * i, page = s_page[tl];
+            if (t0 + tl < T && page >= 0) {
+                const __half2 a = __halves2half2(__float2half_rn(v[i][0]), __float2half_rn(v[i][1]));
+                const __half2 b = __halves2half2(__float2half_rn(v[i][2]), __float2half_rn(v[i][3]));
+                *reinterpret_cast<uint2 *>(vpool + (((size_t)page * n_kv + kvh) * page_size + s_slot[tl]) * 128 +
+                                           4 * lane) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+            }
+        }
+        return;
+    }
+    // k: dim-major pages; consecutive threads take consecutive tokens of one dim
+    for (int idx = threadIdx.x; idx < 128 * QR_TT; idx += 256) {
+        const int tl = idx % QR_TT, d = idx / QR_TT, page = s_page[tl];
+        if (t0 + tl < T && page >= 0)
+            kpool[(((size_t)page * n_kv + kvh) * 128 + d) * page_size + s_slot[tl]] = kst[d][tl];
     }
 }
 
@@ -501,7 +641,12 @@ void launch_embed_rows(fb_ctx *ctx, const fb_qtensor *emb, const int32_t *tokens
 void launch_add_rmsnorm_rows(fb_ctx *ctx, float *x, const float *y, const float *g, float *xn, int T, int dim,
                              float eps, __half *xh, float *rs) {
     FB_REQUIRE(xn || (xh && rs), "add_rmsnorm_rows: no output");
-    k_add_rmsnorm_rows<<<T, 256, 0, ctx->stream>>>(x, y, g, xn, dim, eps, xh, rs);
+    cudaStream_t s = ctx->stream;
+    if (dim % 4 != 0 || dim > 8192) k_add_rmsnorm_rows<<<T, 256, 0, s>>>(x, y, g, xn, dim, eps, xh, rs);
+    else if (dim <= 1024) k_add_rmsnorm_rows4<1><<<T, 256, 0, s>>>(x, y, g, xn, dim, eps, xh, rs);
+    else if (dim <= 2048) k_add_rmsnorm_rows4<2><<<T, 256, 0, s>>>(x, y, g, xn, dim, eps, xh, rs);
+    else if (dim <= 4096) k_add_rmsnorm_rows4<4><<<T, 256, 0, s>>>(x, y, g, xn, dim, eps, xh, rs);
+    else k_add_rmsnorm_rows4<8><<<T, 256, 0, s>>>(x, y, g, xn, dim, eps, xh, rs);
     FB_CUDA(cudaGetLastError());
 }
 
@@ -523,8 +668,9 @@ void launch_prefill_qkv_rope(fb_ctx *ctx, const float *y, int64_t ld, int T, int
                              const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
                              const float *rope_sin, int rope_mode, float *q_out, void *kpool, void *vpool,
                              const int32_t *bt, int page_size, int num_pages) {
-    const int64_t warps = (int64_t)T * (n_heads + 2 * n_kv);
-    k_prefill_qkv_rope<<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(
+    FB_REQUIRE(T >= 1 && n_heads + 2 * n_kv <= 65535 && ld % 4 == 0, "prefill_qkv_rope: bad shape");
+    const dim3 grid((unsigned)((T + QR_TT - 1) / QR_TT), (unsigned)(n_heads + 2 * n_kv));
+    k_prefill_qkv_rope<<<grid, 256, 0, ctx->stream>>>(
         y, ld, T, pos0, n_heads, n_kv, q_norm, k_norm, eps, rope_cos, rope_sin, rope_mode, q_out, (__half *)kpool,
         (__half *)vpool, bt, page_size, num_pages, ctx->err_word);
     FB_CUDA(cudaGetLastError());

@@ -460,7 +460,9 @@ __global__ void __launch_bounds__(256) k_gemv_float(const uint8_t *__restrict__ 
     const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= n) return;
     double acc8[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // one chain per lane value: short FMA chains
-#pragma unroll 2
+    // four super-blocks' small weight loads in flight per warp (the loop is
+    // bound by their latency: one warp per row streams the matrix once)
+#pragma unroll 4
     for (int64_t b = 0; b < nb; b++) {
         float v[8];
         if constexpr (DT == 4) dq8_q4k(w, r, b, nb, lane, v);
