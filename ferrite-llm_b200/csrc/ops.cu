@@ -517,14 +517,27 @@ __global__ void __launch_bounds__(256) k_swiglu_rows_x16(const float *__restrict
     const float4 *g4 = reinterpret_cast<const float4 *>(y + r * 2 * f), *u4 = g4 + f / 4;
     auto sw = [](float gv, float uv) { return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), uv); };
     float amax = 0.f;
+    // four float4 pairs in flight per thread (the kernel streams the row once)
+#pragma unroll 4
     for (int i = threadIdx.x; i < f / 4; i += 256) {
         const float4 g = g4[i], u = u4[i];
         const float4 a = make_float4(sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
         reinterpret_cast<float4 *>(act)[i] = a;
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
     }
-    // (x16_row_store's first __syncthreads also orders these writes before its reads)
-    x16_row_store(amax, shm, [&](int i) { return act[i]; }, f, xh + r * f, rs + r);
+    // x16_row_store's rule, four values per thread and 8-byte stores
+    // (x16_row_exponent's __syncthreads orders the act writes before the reads)
+    const int e = x16_row_exponent(amax, shm);
+    const float inv = ldexpf(1.f, -e);
+    if (threadIdx.x == 0) rs[r] = ldexpf(1.f, e);
+    uint2 *xh4 = reinterpret_cast<uint2 *>(xh + r * f);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < f / 4; i += 256) {
+        const float4 a = reinterpret_cast<const float4 *>(act)[i];
+        const __half2 lo = __halves2half2(__float2half_rn(__fmul_rn(a.x, inv)), __float2half_rn(__fmul_rn(a.y, inv)));
+        const __half2 hi = __halves2half2(__float2half_rn(__fmul_rn(a.z, inv)), __float2half_rn(__fmul_rn(a.w, inv)));
+        xh4[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+    }
 }
 
 // Prefill prologue of attention for T new tokens at positions pos0 + t, per

@@ -502,6 +502,7 @@ __global__ void __launch_bounds__(256) k_x_to_f16(const float *__restrict__ x, _
     if (row >= T) return;
     const float *xr = x + (int64_t)row * K;
     float amax = 0.f;
+#pragma unroll 4  // several row loads in flight per lane
     for (int64_t i = 4 * lane; i < K; i += 128) {
         const float4 v = *reinterpret_cast<const float4 *>(xr + i);
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
@@ -513,6 +514,7 @@ __global__ void __launch_bounds__(256) k_x_to_f16(const float *__restrict__ x, _
     const float inv = ldexpf(1.f, -e);
     if (lane == 0) rowscale[row] = ldexpf(1.f, e);
     __half *hr = xh + (int64_t)row * K;
+#pragma unroll 4
     for (int64_t i = 4 * lane; i < K; i += 128) {
         const float4 v = *reinterpret_cast<const float4 *>(xr + i);
         const __half2 a = __floats2half2_rn(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv));
